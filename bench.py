@@ -1,0 +1,330 @@
+"""Benchmark of the B200 token loop (BASELINE metric: batch-1 decode tok/s and
+% of HBM roofline; prefill tok/s), one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config cfg2] [--ctx 1024]
+
+Workload (default): BASELINE config 2, the Llama-3.2-1B shape (Q4_0 with
+v/o/down Q8_0, f16 scales, tied, llama3 RoPE), synthetic seeded weights;
+batch-1 greedy decode at KV context --ctx (the prompt is prefilled first, then
+W untimed and K timed decode steps). Weights (871 MB) are larger than L2, so
+every step streams them from HBM.
+
+  value  decode tok/s of all ranks: K tokens per rank / max over ranks of the
+         CUDA-event time of the K graph-replayed steps (inputs in HBM)
+  e2e    the same through the drop-in API with host buffers: K kc_forward calls
+         (token and position in, the [vocab] float logits out to the host, the
+         reference's ml_bench loop with its host argmax), wall clock
+Under torchrun each rank runs an independent replica on its own GPU (sub-2B
+models do not shard profitably: "replicas only"), scaling "weak".
+
+--impl reference times the reference's own CPU build (oracle/_ref, the
+unmodified reference library; its best ISA for the host, all host threads)
+on the same workload: rank 0 only.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "isa-lm_b200"))
+
+P = argparse.ArgumentParser()
+P.add_argument("--gpus", type=int, default=1)
+P.add_argument("--steps", type=int, default=128)
+P.add_argument("--warmup", type=int, default=8)
+P.add_argument("--impl", choices=("ours", "reference"), default="ours")
+P.add_argument("--config", default="cfg2")
+P.add_argument("--ctx", type=int, default=1024)
+P.add_argument("--no-extras", action="store_true", help="skip the context sweep, prefill and CPU baseline")
+ARGS = P.parse_args()
+
+RANK = int(os.environ.get("RANK", "0"))
+WORLD = int(os.environ.get("WORLD_SIZE", "1"))
+LOCAL = int(os.environ.get("LOCAL_RANK", "0"))
+if WORLD > 1:   # one GPU per rank: the library uses device 0 of its process
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    devs = vis.split(",") if vis else [str(i) for i in range(64)]
+    os.environ["CUDA_VISIBLE_DEVICES"] = devs[LOCAL]
+
+MODEL_DIR = os.environ.get("KRAFLA_MODEL_DIR", os.path.join(ROOT, "_models"))
+PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def peaks():
+    try:
+        with open(PEAKS_PATH) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def model_bytes_per_token(cfg, ctx):
+    """Algorithmic HBM bytes of one decode token: every quantized matrix (quants
+    + f16 scales) once, the embedding row, and the F32 KV rows attended."""
+    d, L, h, v = cfg["dim"], cfg["n_layers"], cfg["hidden_dim"], cfg["vocab"]
+    qd, kvd = cfg["q_dim"], cfg["kv_dim"]
+    wt, mask = cfg["wtype"], cfg["q8_mask"]
+
+    def mat(rows, cols, bits):
+        q8 = wt == 1 or (mask & bits)
+        return rows * cols * (1 if q8 else 0.5) + rows * cols / 32 * (2 if cfg["scale_f16"] else 4)
+
+    per_layer = (mat(qd, d, 4) + mat(kvd, d, 4) + mat(kvd, d, 8) + mat(d, qd, 16) + 2 * mat(h, d, 32) + mat(d, h, 64)
+                 + 2 * d * 4)
+    shared = cfg.get("shared", 0)
+    cls = mat(v, d, 1 | 2 if shared else 2)
+    emb = d * (1 if (wt == 1 or mask & 1) else 0.5)
+    kv = 2 * L * ctx * kvd * 4
+    gemv = L * (per_layer - 2 * d * 4) + cls
+    return L * per_layer + cls + emb + kv, gemv
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region (SM clock, throttle reasons)."""
+    Q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.samples, self.stop = [], threading.Event()
+
+    def __enter__(self):
+        dev = os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0]
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", dev, f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.p = None
+        return self
+
+    def _read(self):
+        for line in self.p.stdout:
+            self.samples.append([s.strip() for s in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.p:
+            time.sleep(0.25)
+            self.p.terminate()
+            self.p.wait(timeout=5)
+
+    def summary(self):
+        sm = [float(s[0]) for s in self.samples if len(s) >= 7 and s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if len(s) >= 7 and s[1].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for s in self.samples if len(s) >= 7 for n, v in zip(names, s[3:7]) if v == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(sm)}
+
+
+def dist_init():
+    if WORLD == 1:
+        return None
+    import datetime
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(0)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    return dist
+
+
+def dist_max(dist, v):
+    if dist is None:
+        return v
+    import torch
+    t = torch.tensor([float(v)], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def prompt_tokens(vocab, n, seed=1234):
+    import numpy as np
+    return np.random.default_rng(seed).integers(0, vocab, n).astype(np.int32)
+
+
+def cpu_reference(path, cfg, ctx, steps, warmup):
+    """The reference's best CPU build on this host: prefill ctx tokens, then
+    decode `steps` greedy tokens timed (app/ml_bench.c:120-131 loop)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import ctypes as C
+    import oracle
+    ref = oracle.RefBuild()
+    cores = os.cpu_count() or 1
+    h = ref.open(path, cores, 0, True)
+    toks = prompt_tokens(cfg["vocab"], ctx)
+    tp = ref.L.ref_time_prefill(h, toks.ctypes.data_as(C.c_void_p), ctx, 0)
+    out = (C.c_int * (warmup + steps))()
+    if warmup:
+        ref.L.ref_decode_greedy(h, int(toks[-1]), ctx, warmup, out)
+    td = ref.L.ref_decode_greedy(h, int(toks[-1]), ctx + warmup, steps, out)
+    threads = ref.L.ref_threads(h)
+    ref.L.ref_close(h)
+    return {"decode_tok_s": steps / td, "prefill_tok_s": ctx / tp, "cores": threads, "isa": ref.isa,
+            "sample": f"{ctx}-token prefill, then {steps} greedy decode steps at KV context {ctx + warmup}"}
+
+
+def main():
+    import numpy as np
+    import krafla_b200 as kb
+    dist = dist_init()
+    hbm_peak, peak_kind = peaks()
+    if RANK == 0:
+        path = kb.ensure_model(ARGS.config, MODEL_DIR)
+    if dist is not None:
+        dist.barrier()
+        path = kb.ensure_model(ARGS.config, MODEL_DIR)
+    K, W = ARGS.steps, ARGS.warmup
+    model_cfg = dict(kb.CONFIGS[ARGS.config])
+
+    if ARGS.impl == "reference":
+        if RANK != 0:
+            return
+        cfg = kb.Model(path, upload=False).config
+        ctx = min(ARGS.ctx, cfg["max_seq"] - K - W)
+        cfg["shared"] = model_cfg.get("shared", 0)
+        r = cpu_reference(path, cfg, ctx, K, W)
+        line = {"metric": "batch-1 decode tok/s", "value": round(r["decode_tok_s"], 3), "unit": "tok/s",
+                "impl": "reference", "n_gpus": ARGS.gpus, "steps": K, "warmup": W,
+                "ms_per_step": round(1000.0 / r["decode_tok_s"], 3), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot, f32 accumulate", "data": "synthetic",
+                "config": {"workload": f"{ARGS.config} decode at KV context {ctx}", "model": ARGS.config,
+                           "ctx": ctx, "batch": 1},
+                "cpu_baseline": {"value": round(r["decode_tok_s"], 3), "unit": "tok/s", "cores": r["cores"],
+                                 "kind": "reference", "isa": r["isa"], "sample": r["sample"]},
+                "e2e": {"value": round(r["decode_tok_s"], 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0},
+                "prefill_tok_s": round(r["prefill_tok_s"], 1)}
+        print(json.dumps(line), flush=True)
+        return
+
+    model = kb.Model(path)
+    cfg = model.config
+    cfg["shared"] = model_cfg.get("shared", 0)
+    ctx = min(ARGS.ctx, cfg["max_seq"] - K - W - 1)
+    st = kb.State(model)
+    toks = prompt_tokens(cfg["vocab"], ctx)
+    st.prefill(toks[:-1], 0)
+    start_tok, start_pos = int(toks[-1]), ctx - 1
+
+    # --- value: device time of K graph replays (CUDA events on the launching stream)
+    with Clocks() as clk:
+        if dist is not None:
+            dist.barrier()
+        ms = st.time_decode(start_tok, start_pos, W, K)
+        if dist is not None:
+            dist.barrier()
+    ms_max = dist_max(dist, ms)
+    value = WORLD * K / (ms_max / 1000.0)
+    bpt, gemv_bytes = model_bytes_per_token(cfg, ctx + W + K // 2)
+    launches_per_step = 1 + 5 * cfg["n_layers"] + 1
+
+    # --- e2e: the drop-in API with host buffers (kc_forward + host argmax, ml_bench's loop)
+    st.prefill(toks[:-1], 0)
+    tok, pos = start_tok, start_pos
+    for _ in range(W):
+        lg = st.forward(tok, pos)
+        tok, pos = int(np.argmax(lg)), pos + 1
+    if dist is not None:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(K):
+        lg = st.forward(tok, pos)
+        tok, pos = int(np.argmax(lg)), pos + 1
+    e2e_s = dist_max(dist, time.perf_counter() - t0)
+    e2e = WORLD * K / e2e_s
+    # device-resident greedy loop through the C ABI (host tokens in and out)
+    st.prefill(toks[:-1], 0)
+    t0 = time.perf_counter()
+    st.generate_greedy(start_tok, start_pos, K)
+    greedy_s = dist_max(dist, time.perf_counter() - t0)
+
+    # --- roofline of the dominant kernel (the decode GEMV, all its launches of a step)
+    prof = st.profile_step(start_tok, start_pos)
+    gemv_ms = prof["qkv"] + prof["wo"] + prof["ffn_up"] + prof["ffn_down"] + prof["classifier"]
+    achieved = gemv_bytes / (gemv_ms / 1000.0) / 1e9
+    up_ms, up_bytes = st.time_ffn_up(0, 20)
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get(f"{ARGS.config}:gemv_kernel")
+
+    extras = {}
+    if RANK == 0 and not ARGS.no_extras:
+        sweep = {}
+        for c in (128, 1024, 4096):
+            c2 = min(c, cfg["max_seq"] - 34)
+            st.prefill(prompt_tokens(cfg["vocab"], c2)[:-1], 0)
+            m2 = st.time_decode(1, c2 - 1, 2, 32)
+            b2, _ = model_bytes_per_token(cfg, c2 + 18)
+            sweep[str(c)] = {"tok_s": round(32 / (m2 / 1000), 1),
+                             "hbm_frac": round(b2 * 32 / (m2 / 1000) / 1e9 / hbm_peak, 4)}
+        extras["decode_by_context"] = sweep
+        pre = {}
+        for n in (128, 512, 2048):
+            pt = prompt_tokens(cfg["vocab"], n, seed=7)
+            t0 = time.perf_counter()
+            st.prefill(pt, 0)
+            pre[str(n)] = round(n / (time.perf_counter() - t0), 1)
+        extras["prefill_tok_s"] = pre
+        try:
+            extras["cpu_baseline"] = cpu_reference(path, cfg, min(512, ctx), 16, 2)
+        except Exception as e:   # the reference build needs a compatible host CPU
+            extras["cpu_baseline"] = {"error": str(e)}
+
+    if RANK == 0:
+        cpu = extras.get("cpu_baseline", {})
+        line = {
+            "metric": "batch-1 decode tok/s", "value": round(value, 2), "unit": "tok/s", "n_gpus": WORLD,
+            "steps": K, "warmup": W, "ms_per_step": round(ms_max / K, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot (dp4a), f32 accumulate",
+            "data": "synthetic (seeded N(0,0.02) weights, uniform prompt ids)",
+            "config": {"workload": f"{ARGS.config} batch-1 greedy decode at KV context {ctx}",
+                       "model": ARGS.config, "ctx": ctx, "batch": 1, "kv_cache": "f32",
+                       "parallelism": f"replicas x{WORLD}", "l2": "weights 871 MB > 126 MB L2: streamed each step"},
+            "hbm_roofline_frac": round(bpt * value / WORLD / 1e9 / hbm_peak, 4),
+            "bytes_per_token": int(bpt),
+            "roofline": {"bound": "hbm", "kernel": "gemv_kernel (all decode projections of a step)",
+                         "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind, "traffic": traffic,
+                         "ffn_up_alone_gbs": round(up_bytes / (up_ms / 1000) / 1e9, 1)},
+            "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 32,
+                    "d2h_bytes_per_step": 4 * cfg["vocab"] + 32,
+                    "path": "kc_forward per token (logits to host) + host argmax"},
+            "e2e_greedy_device": {"value": round(WORLD * K / greedy_s, 2), "unit": "tok/s",
+                                  "h2d_bytes_per_step": round(32 / K, 2), "d2h_bytes_per_step": 4},
+            "gpu_launches": launches_per_step * K,
+            "clocks": clk.summary(),
+            "step_profile_ms": {k: round(v, 4) for k, v in prof.items()},
+        }
+        if cpu and "decode_tok_s" in cpu:
+            line["cpu_baseline"] = {"value": round(cpu["decode_tok_s"], 3), "unit": "tok/s", "cores": cpu["cores"],
+                                    "kind": "reference", "isa": cpu["isa"], "sample": cpu["sample"],
+                                    "prefill_tok_s": round(cpu["prefill_tok_s"], 1)}
+        elif cpu:
+            line["cpu_baseline"] = cpu
+        for k in ("decode_by_context", "prefill_tok_s"):
+            if k in extras:
+                line[k] = extras[k]
+        print(json.dumps(line), flush=True)
+    st.free()
+    model.free()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,162 @@
+/* krafla_cuda.h — C ABI of the B200 (sm_100a) implementation of Krafla's
+ * token loop (JonPark0/isa-lm): the decoder forward of model/transformer.c
+ * and the ops it binds through ops/ops.h, on HBM-resident weights.
+ *
+ * Plain C types only: no CUDA or torch types cross this boundary. Every entry
+ * point returns a status with the reference's ml_status values
+ * (core/ml.h:7-14); CUDA failures are mapped onto them (out of device memory
+ * -> KC_E_NOMEM, no sm_100 device -> KC_E_ISA, any other CUDA error -> KC_E_IO)
+ * and kc_last_error() gives the message. Nothing here aborts.
+ *
+ * Threading: one caller thread per kc_state, as the reference's ml_state.
+ */
+#ifndef KRAFLA_CUDA_H
+#define KRAFLA_CUDA_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ml_status (core/ml.h:7-14), same values */
+enum { KC_OK = 0, KC_E_IO = 1, KC_E_FORMAT = 2, KC_E_SHAPE = 3, KC_E_NOMEM = 4, KC_E_ISA = 5 };
+/* tensor and KV cache types (core/ml.h:67) */
+enum { KC_F32 = 0, KC_Q8_0 = 1, KC_Q4_0 = 2, KC_F16 = 3 };
+
+/* The model header, field for field in the order of ml_config
+ * (model/mlb.h:9-32), so that a reference build can pass &m->cfg. */
+typedef struct {
+    int dim, n_layers, n_heads, n_kv_heads, hidden_dim, vocab, max_seq, head_dim, kv_dim;
+    int q_dim;
+    float rope_theta, norm_eps;
+    int wtype;
+    unsigned q8_mask;
+    int qkv_bias, qk_norm, sliding_window, layer_flags;
+    float rope_local_theta;
+    int act, post_norms;
+    float embed_scale, attn_scale;
+    int scale_f16;
+    float attn_softcap, final_softcap;
+    int rope_type, rope_orig_max_seq;
+    float rope_factor, rope_low_freq_factor, rope_high_freq_factor;
+    float rope_attn_factor;
+} kc_config;
+
+/* A quantized matrix in host memory, the file's SoA layout (core/ml.h:69-83):
+ * q = quants (Q8: int8 [rows*cols]; Q4: uint8 [rows*cols/2], byte j = element
+ * j low nibble, j+16 high nibble), d = block scales [rows*cols/32], as f16
+ * when d_f16 is set, else float. */
+typedef struct {
+    const void *q;
+    const void *d;
+    int rows, cols, type, d_f16;
+} kc_tensor;
+
+/* One decoder layer's host arrays (model/mlb.h:42-50). Optional arrays NULL. */
+typedef struct {
+    const float *attn_norm, *ffn_norm;
+    kc_tensor wq, wk, wv, wo, w1, w2, w3;
+    const float *bq, *bk, *bv;
+    const float *q_norm, *k_norm;
+    const float *post_attn_norm, *post_ffn_norm;
+    int window, local_rope;
+} kc_layer_desc;
+
+typedef struct kc_model kc_model;
+typedef struct kc_state kc_state;
+
+/* 0 when device 0 is a Blackwell sm_100 GPU this library runs on, else
+ * KC_E_ISA: the device-side counterpart of the reference's ISA guard
+ * (core/isa_check.h, app/main_guard.c:8-15). */
+int kc_device_check(void);
+const char *kc_status_str(int status);
+/* Message of the last failure on this thread ("" if none). */
+const char *kc_last_error(void);
+
+/* Replaces ml_model_load (model/mlb.h:64, model/mlb.c:161-218): maps and
+ * validates an .mlb file with the reference's rules (parse_header,
+ * model/mlb.c:80-159; Q8 quants of -128 refused, mlb.c:34-36), keeping host
+ * views of every array. No device memory is touched. */
+int kc_model_load(kc_model **out, const char *path);
+/* The same from arrays the caller already holds (a reference ml_model):
+ * header + tensors, copied by kc_model_upload. layers: cfg->n_layers entries.
+ * For a tied classifier pass wcls == tok_emb (same q pointer). */
+int kc_model_from_host(kc_model **out, const kc_config *cfg, const kc_tensor *tok_emb, const kc_tensor *wcls,
+                       const float *final_norm, const kc_layer_desc *layers);
+/* Replaces ml_model_pack (model/pack_model.h:13-19): the one-time upload of
+ * every quantized matrix (Q4/Q8 quants + f16 or f32 block scales), norm and
+ * bias to HBM. Idempotent. */
+int kc_model_upload(kc_model *m);
+const kc_config *kc_model_config(const kc_model *m);
+/* Bytes of weights held on the device (quants + scales + float arrays). */
+size_t kc_model_device_bytes(const kc_model *m);
+void kc_model_free(kc_model *m);
+
+/* Replaces ml_state_init (model/transformer.h:56, transformer.c:51-166):
+ * device buffers, the KV cache [n_layers][max_seq][kv_dim] in HBM (kv_type
+ * KC_F32, KC_F16 or KC_Q8_0) and RoPE tables computed on the host in double
+ * exactly as the reference does. nthreads is accepted for the API's shape and
+ * ignored (the result does not depend on it, as the reference's contract
+ * says). KC_E_SHAPE for model features this build does not run. */
+int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_type);
+/* Replaces ml_prefill (transformer.h:60, transformer.c:427-438): n host
+ * tokens at positions pos0..; logits [n][vocab] (host) or NULL (classifier
+ * skipped). KC_E_SHAPE when a position or token is out of range. */
+int kc_prefill(kc_state *s, const int *tokens, int n, int pos0, float *logits);
+/* Replaces ml_forward (transformer.h:62, transformer.c:257-306): logits for
+ * `token` at `pos` in a host buffer owned by the state, valid until the next
+ * call; NULL when pos or token is out of range (or on a device error). */
+float *kc_forward(kc_state *s, int token, int pos);
+/* Greedy decode of n tokens from `token` at `pos`, entirely on the device:
+ * each step's argmax (first index of the maximum, model/sampler.c:57-61) is
+ * the next step's input. out_tokens (host, n ints) receives the n chosen
+ * tokens. The ml_run -T 0 / ml_bench decode loop (app/ml_bench.c:125-131). */
+int kc_generate_greedy(kc_state *s, int token, int pos, int n, int *out_tokens);
+/* Replaces ml_state_free (transformer.h:65). */
+void kc_state_free(kc_state *s);
+
+/* Timing helpers for bench.py (CUDA events on the state's stream; the
+ * region holds exactly `steps` greedy decode steps after `warmup` untimed
+ * ones, starting at position pos; *ms receives the device milliseconds). */
+int kc_time_decode(kc_state *s, int token, int pos, int warmup, int steps, float *ms);
+/* The device milliseconds of `reps` launches of one layer's fused gate/up
+ * kernel (the decode path's dominant kernel) on the state's stream, with an
+ * L2 flush between launches (a write larger than L2); *bytes receives the
+ * algorithmic bytes per launch (quants + scales read). */
+int kc_time_ffn_up(kc_state *s, int layer, int reps, float *ms_per_launch, double *bytes);
+/* Per-kernel-class device time of one decode step: fills ms[0..5] with the
+ * time of qkv, attention, wo, ffn-up, ffn-down and classifier launches summed
+ * over the step (instrumented with events, outside any timed region). */
+int kc_profile_step(kc_state *s, int token, int pos, float *ms);
+
+/* ---- kernel-level entry points (device pointers, stream may be NULL) ----
+ * These run the exact device code of the model path, for parity tests. */
+
+/* Replaces ml_k_quantize_q8 (kernels/scalar/k_scalar.c:39-57), bit exact. */
+int kc_quantize_q8_dev(int8_t *q, float *d, const float *x, int k, void *stream);
+/* RMSNorm (k_scalar.c:59-64) of x by w, then quantize_q8 of the result: the
+ * activation prologue of the decode projections. xn (optional, may be NULL)
+ * receives the normalized floats. */
+int kc_rmsnorm_quantize_dev(int8_t *q, float *d, float *xn, const float *x, const float *w, int n, float eps,
+                            void *stream);
+/* Replaces ml_k_matvec_q8 / ml_k_matvec_q4 (k_scalar.c:4-37) over all rows:
+ * y[r] = sum_b int32(w.x over block b) * d_w[r,b] * d_x[b]. wd holds f16
+ * scales when d_f16 is set. Uses the decode GEMV kernel. */
+int kc_matvec_dev(float *y, int type, int d_f16, const void *wq, const void *wd, int rows, int cols,
+                  const int8_t *xq, const float *xd, void *stream);
+/* The int32 block dot products s[r][b] of the same kernel code (bit exact
+ * against the scalar kernels' integer sums). */
+int kc_block_sums_dev(int32_t *s, int type, const void *wq, int rows, int cols, const int8_t *xq, void *stream);
+
+/* Device memory helpers for callers without a CUDA runtime of their own. */
+void *kc_dev_alloc(size_t bytes);
+void kc_dev_free(void *p);
+int kc_memcpy_htod(void *dst, const void *src, size_t bytes);
+int kc_memcpy_dtoh(void *dst, const void *src, size_t bytes);
+int kc_dev_sync(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,353 @@
+"""Host-side mirror of Krafla's model API (JonPark0/isa-lm) over the B200 build.
+
+The reference's C API (model/mlb.h, model/transformer.h) maps one to one:
+
+    ml_model_load  -> Model(path)                 kc_model_load
+    ml_model_pack  -> Model.upload()              kc_model_upload (HBM, once)
+    ml_state_init  -> State(model, nthreads, kv)  kc_state_init
+    ml_prefill     -> State.prefill(...)          kc_prefill
+    ml_forward     -> State.forward(token, pos)   kc_forward
+    ml_state_free  -> State.free()                kc_state_free
+
+plus State.generate_greedy (the ml_run -T 0 / ml_bench decode loop on the
+device). Every call goes through the C ABI of include/krafla_cuda.h in
+libkrafla_cuda.so; there is no other implementation behind it: when the
+library or a B200 is missing the calls raise.
+
+Status codes and their meaning are the reference's ml_status (core/ml.h:7-14).
+"""
+import ctypes as C
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libkrafla_cuda.so")
+GEN_PATH = os.path.join(_HERE, "libkrafla_mlbgen.so")
+
+OK, E_IO, E_FORMAT, E_SHAPE, E_NOMEM, E_ISA = range(6)
+F32, Q8_0, Q4_0, F16 = 0, 1, 2, 3
+STATUS = {OK: "ok", E_IO: "i/o error", E_FORMAT: "bad file format", E_SHAPE: "bad tensor shape",
+          E_NOMEM: "out of memory", E_ISA: "device lacks required architecture"}
+
+
+class KraflaError(RuntimeError):
+    """A non-zero status from the C ABI; .status holds the ml_status value."""
+
+    def __init__(self, status, what=""):
+        self.status = status
+        msg = STATUS.get(status, f"status {status}")
+        super().__init__(f"{what}: {msg}" + (f" ({what_detail()})" if what_detail() else ""))
+
+
+_lib = None
+_gen = None
+
+
+def what_detail():
+    return _lib.kc_last_error().decode() if _lib is not None else ""
+
+
+class _Config(C.Structure):
+    """kc_config: the reference's ml_config field order (model/mlb.h:9-32)."""
+    _fields_ = [(n, C.c_int) for n in ("dim", "n_layers", "n_heads", "n_kv_heads", "hidden_dim", "vocab",
+                                       "max_seq", "head_dim", "kv_dim", "q_dim")] + [
+        ("rope_theta", C.c_float), ("norm_eps", C.c_float), ("wtype", C.c_int), ("q8_mask", C.c_uint),
+        ("qkv_bias", C.c_int), ("qk_norm", C.c_int), ("sliding_window", C.c_int), ("layer_flags", C.c_int),
+        ("rope_local_theta", C.c_float), ("act", C.c_int), ("post_norms", C.c_int), ("embed_scale", C.c_float),
+        ("attn_scale", C.c_float), ("scale_f16", C.c_int), ("attn_softcap", C.c_float),
+        ("final_softcap", C.c_float), ("rope_type", C.c_int), ("rope_orig_max_seq", C.c_int),
+        ("rope_factor", C.c_float), ("rope_low_freq_factor", C.c_float), ("rope_high_freq_factor", C.c_float),
+        ("rope_attn_factor", C.c_float)]
+
+
+def lib():
+    """The loaded libkrafla_cuda.so (raises when it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} missing: build it (python -c 'import __graft_entry__ as g; g.build()')")
+        L = C.CDLL(LIB_PATH)
+        P, I, F, S = C.c_void_p, C.c_int, C.c_float, C.c_size_t
+        sig = {
+            "kc_device_check": (I, []), "kc_status_str": (C.c_char_p, [I]), "kc_last_error": (C.c_char_p, []),
+            "kc_model_load": (I, [C.POINTER(P), C.c_char_p]), "kc_model_upload": (I, [P]),
+            "kc_model_config": (C.POINTER(_Config), [P]), "kc_model_device_bytes": (S, [P]),
+            "kc_model_free": (None, [P]),
+            "kc_state_init": (I, [C.POINTER(P), P, I, I]), "kc_prefill": (I, [P, P, I, I, P]),
+            "kc_forward": (C.POINTER(F), [P, I, I]), "kc_generate_greedy": (I, [P, I, I, I, P]),
+            "kc_state_free": (None, [P]),
+            "kc_time_decode": (I, [P, I, I, I, I, C.POINTER(F)]),
+            "kc_time_ffn_up": (I, [P, I, I, C.POINTER(F), C.POINTER(C.c_double)]),
+            "kc_profile_step": (I, [P, I, I, P]),
+            "kc_quantize_q8_dev": (I, [P, P, P, I, P]), "kc_rmsnorm_quantize_dev": (I, [P, P, P, P, P, I, F, P]),
+            "kc_matvec_dev": (I, [P, I, I, P, P, I, I, P, P, P]), "kc_block_sums_dev": (I, [P, I, P, I, I, P, P]),
+            "kc_dev_alloc": (P, [S]), "kc_dev_free": (None, [P]), "kc_memcpy_htod": (I, [P, P, S]),
+            "kc_memcpy_dtoh": (I, [P, P, S]), "kc_dev_sync": (I, []),
+        }
+        for name, (res, args) in sig.items():
+            f = getattr(L, name)
+            f.restype, f.argtypes = res, args
+        _lib = L
+    return _lib
+
+
+def _check(st, what):
+    if st != OK:
+        raise KraflaError(st, what)
+
+
+def device_check():
+    """0 on a B200 (sm_100) this build runs on; raises otherwise."""
+    _check(lib().kc_device_check(), "device check")
+
+
+class Model:
+    """ml_model_load + ml_model_pack: map and validate an .mlb, upload it to HBM."""
+
+    def __init__(self, path, upload=True):
+        self._h = C.c_void_p()
+        _check(lib().kc_model_load(C.byref(self._h), os.fsencode(path)), f"load {path}")
+        if upload:
+            self.upload()
+
+    def upload(self):
+        _check(lib().kc_model_upload(self._h), "upload")
+
+    @property
+    def config(self):
+        c = lib().kc_model_config(self._h).contents
+        return {n: getattr(c, n) for n, _ in c._fields_}
+
+    @property
+    def device_bytes(self):
+        return lib().kc_model_device_bytes(self._h)
+
+    def free(self):
+        if self._h:
+            lib().kc_model_free(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class State:
+    """ml_state: decode state with its HBM KV cache (kv_type F32, F16 or Q8_0)."""
+
+    def __init__(self, model, nthreads=1, kv_type=F32):
+        self.model = model
+        self.cfg = model.config
+        self._h = C.c_void_p()
+        _check(lib().kc_state_init(C.byref(self._h), model._h, nthreads, kv_type), "state init")
+
+    def forward(self, token, pos):
+        """Logits [vocab] for token at pos (a copy), as ml_forward; None when out of range."""
+        p = lib().kc_forward(self._h, int(token), int(pos))
+        if not p:
+            err = what_detail()
+            if err:
+                raise KraflaError(E_IO, f"forward: {err}")
+            return None
+        return np.ctypeslib.as_array(p, shape=(self.cfg["vocab"],)).copy()
+
+    def prefill(self, tokens, pos0=0, logits=False):
+        """ml_prefill: runs the tokens at pos0..; returns [n, vocab] logits or None."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.empty((len(t), self.cfg["vocab"]), np.float32) if logits else None
+        st = lib().kc_prefill(self._h, t.ctypes.data_as(C.c_void_p), len(t), int(pos0),
+                              out.ctypes.data_as(C.c_void_p) if logits else None)
+        _check(st, "prefill")
+        return out
+
+    def generate_greedy(self, token, pos, n):
+        """n greedy tokens from token at pos, the loop kept on the device."""
+        out = np.empty(n, np.int32)
+        _check(lib().kc_generate_greedy(self._h, int(token), int(pos), int(n), out.ctypes.data_as(C.c_void_p)),
+               "generate")
+        return out
+
+    def time_decode(self, token, pos, warmup, steps):
+        ms = C.c_float()
+        _check(lib().kc_time_decode(self._h, int(token), int(pos), int(warmup), int(steps), C.byref(ms)),
+               "time decode")
+        return ms.value
+
+    def time_ffn_up(self, layer=0, reps=20):
+        ms, b = C.c_float(), C.c_double()
+        _check(lib().kc_time_ffn_up(self._h, layer, reps, C.byref(ms), C.byref(b)), "time ffn-up")
+        return ms.value, b.value
+
+    def profile_step(self, token, pos):
+        ms = (C.c_float * 6)()
+        _check(lib().kc_profile_step(self._h, int(token), int(pos), ms), "profile step")
+        return dict(zip(("qkv", "attention", "wo", "ffn_up", "ffn_down", "classifier"), list(ms)))
+
+    def free(self):
+        if self._h:
+            lib().kc_state_free(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+# ---------------------------------------------------------------- device arrays
+
+class DevBuf:
+    """A device allocation through the C ABI (for the kernel-level entry points)."""
+
+    def __init__(self, nbytes):
+        self.nbytes = int(nbytes)
+        self.ptr = lib().kc_dev_alloc(max(1, self.nbytes))
+        if not self.ptr:
+            raise KraflaError(E_NOMEM, "device alloc")
+
+    @classmethod
+    def of(cls, arr, pad=0):
+        a = np.ascontiguousarray(arr)
+        b = cls(a.nbytes + pad)
+        if a.nbytes:
+            _check(lib().kc_memcpy_htod(b.ptr, a.ctypes.data_as(C.c_void_p), a.nbytes), "htod")
+        return b
+
+    def get(self, dtype, count):
+        out = np.empty(count, dtype)
+        if out.nbytes:
+            _check(lib().kc_memcpy_dtoh(out.ctypes.data_as(C.c_void_p), self.ptr, out.nbytes), "dtoh")
+        return out
+
+    def __del__(self):
+        try:
+            if self.ptr:
+                lib().kc_dev_free(self.ptr)
+        except Exception:
+            pass
+
+
+def quantize_q8(x):
+    """ml_k_quantize_q8 on the device: (int8 q [k], float d [k/32])."""
+    x = np.ascontiguousarray(x, np.float32)
+    k = x.size
+    bx, bq, bd = DevBuf.of(x), DevBuf(k), DevBuf(4 * (k // 32))
+    _check(lib().kc_quantize_q8_dev(bq.ptr, bd.ptr, bx.ptr, k, None), "quantize")
+    _check(lib().kc_dev_sync(), "sync")
+    return bq.get(np.int8, k), bd.get(np.float32, k // 32)
+
+
+def rmsnorm_quantize(x, w, eps):
+    """RMSNorm then quantize_q8 on the device: (q, d, normalized floats)."""
+    x = np.ascontiguousarray(x, np.float32)
+    n = x.size
+    bx, bw, bq, bd, bn = DevBuf.of(x), DevBuf.of(np.asarray(w, np.float32)), DevBuf(n), DevBuf(4 * (n // 32)), DevBuf(4 * n)
+    _check(lib().kc_rmsnorm_quantize_dev(bq.ptr, bd.ptr, bn.ptr, bx.ptr, bw.ptr, n, C.c_float(eps), None), "rmsnorm")
+    _check(lib().kc_dev_sync(), "sync")
+    return bq.get(np.int8, n), bd.get(np.float32, n // 32), bn.get(np.float32, n)
+
+
+def matvec(wtype, wq, wd, rows, cols, xq, xd):
+    """ml_k_matvec_q8/q4 over all rows on the device. wd: float32 or float16 scales."""
+    wd = np.ascontiguousarray(wd)
+    d16 = int(wd.dtype == np.float16)
+    bw, bd = DevBuf.of(wq), DevBuf.of(wd, pad=16)   # scale rows are read in 16-byte aligned spans
+    bxq, bxd, by = DevBuf.of(np.asarray(xq, np.int8)), DevBuf.of(np.asarray(xd, np.float32)), DevBuf(4 * rows)
+    _check(lib().kc_matvec_dev(by.ptr, wtype, d16, bw.ptr, bd.ptr, rows, cols, bxq.ptr, bxd.ptr, None), "matvec")
+    _check(lib().kc_dev_sync(), "sync")
+    return by.get(np.float32, rows)
+
+
+def block_sums(wtype, wq, rows, cols, xq):
+    """int32 [rows, cols/32] block dot products on the device."""
+    bw, bx, bs = DevBuf.of(wq), DevBuf.of(np.asarray(xq, np.int8)), DevBuf(4 * rows * (cols // 32))
+    _check(lib().kc_block_sums_dev(bs.ptr, wtype, bw.ptr, rows, cols, bx.ptr, None), "block sums")
+    _check(lib().kc_dev_sync(), "sync")
+    return bs.get(np.int32, rows * (cols // 32)).reshape(rows, cols // 32)
+
+
+# ---------------------------------------------------------------- model writer
+
+class _GenConfig(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("dim", "n_layers", "n_heads", "n_kv_heads", "hidden_dim", "vocab",
+                                       "max_seq")] + [
+        ("rope_theta", C.c_float), ("norm_eps", C.c_float), ("wtype", C.c_int), ("shared", C.c_int),
+        ("rope_type", C.c_int), ("rope_factor", C.c_float), ("rope_lo", C.c_float), ("rope_hi", C.c_float),
+        ("rope_orig", C.c_int), ("q8_mask", C.c_int), ("qkv_bias", C.c_int), ("head_dim", C.c_int),
+        ("scale_f16", C.c_int), ("sigma", C.c_double), ("bias_sigma", C.c_double), ("seed", C.c_uint64),
+        ("nthreads", C.c_int)]
+
+
+def gen():
+    global _gen
+    if _gen is None:
+        if not os.path.exists(GEN_PATH):
+            raise RuntimeError(f"{GEN_PATH} missing: build it first")
+        g = C.CDLL(GEN_PATH)
+        g.kw_write_model.restype, g.kw_write_model.argtypes = C.c_int, [C.c_char_p, C.POINTER(_GenConfig)]
+        g.kw_quantize.restype = C.c_int
+        g.kw_quantize.argtypes = [C.c_int, C.c_int, C.c_void_p, C.c_long, C.c_void_p, C.c_void_p]
+        g.kw_normal.restype = None
+        g.kw_normal.argtypes = [C.c_uint64, C.c_uint64, C.c_uint64, C.c_long, C.c_double, C.c_void_p]
+        g.kw_config_size.restype = C.c_size_t
+        assert g.kw_config_size() == C.sizeof(_GenConfig), "kw_config layout mismatch"
+        _gen = g
+    return _gen
+
+
+Q8M = {"emb": 1, "cls": 2, "qk": 4, "v": 8, "o": 16, "up": 32, "down": 64}
+
+# synthetic N(0, 0.02) weights, norms 1.0, f16 block scales.
+CONFIGS = {
+    "cfg0": dict(dim=288, n_layers=6, n_heads=6, n_kv_heads=6, hidden_dim=768, vocab=32000, max_seq=256,
+                 rope_theta=10000.0, wtype="q8"),
+    "cfg1": dict(dim=896, n_layers=24, n_heads=14, n_kv_heads=2, hidden_dim=4864, vocab=151936, max_seq=512,
+                 rope_theta=1e6, wtype="q4", q8=("v", "o", "down"), shared=1, qkv_bias=1),
+    "cfg2": dict(dim=2048, n_layers=16, n_heads=32, n_kv_heads=8, hidden_dim=8192, vocab=128256, max_seq=4096,
+                 rope_theta=5e5, wtype="q4", q8=("v", "o", "down"), shared=1,
+                 rope_scaling=("llama3", 32.0, 1.0, 4.0, 8192)),
+    "cfg4": dict(dim=4096, n_layers=32, n_heads=32, n_kv_heads=8, hidden_dim=14336, vocab=128256, max_seq=8192,
+                 rope_theta=5e5, wtype="q8"),
+}
+
+
+def write_model(path, dim, n_layers, n_heads, n_kv_heads, hidden_dim, vocab, max_seq, rope_theta=10000.0,
+                norm_eps=1e-5, wtype="q8", q8=(), shared=0, qkv_bias=0, head_dim=0, rope_scaling=None,
+                scale_f16=1, sigma=0.02, bias_sigma=0.02, seed=0, nthreads=None):
+    """Writes a synthetic .mlb (seeded N(0, sigma) weights, the reference's
+    quantization rules and file layout)."""
+    c = _GenConfig()
+    c.dim, c.n_layers, c.n_heads, c.n_kv_heads = dim, n_layers, n_heads, n_kv_heads
+    c.hidden_dim, c.vocab, c.max_seq = hidden_dim, vocab, max_seq
+    c.rope_theta, c.norm_eps = rope_theta, norm_eps
+    c.wtype = 1 if wtype == "q8" else 2
+    c.shared, c.qkv_bias, c.head_dim, c.scale_f16 = int(shared), int(qkv_bias), head_dim, int(scale_f16)
+    c.q8_mask = sum(Q8M[k] for k in q8)
+    if rope_scaling:
+        kind = rope_scaling[0]
+        c.rope_type = {"llama3": 1, "linear": 2}[kind]
+        c.rope_factor = rope_scaling[1]
+        if kind == "llama3":
+            c.rope_lo, c.rope_hi, c.rope_orig = rope_scaling[2], rope_scaling[3], rope_scaling[4]
+    c.sigma, c.bias_sigma, c.seed = sigma, bias_sigma, seed
+    c.nthreads = nthreads or os.cpu_count() or 1
+    st = gen().kw_write_model(os.fsencode(path), C.byref(c))
+    if st:
+        raise OSError(st, f"writing {path}")
+
+
+def ensure_model(name, directory, seed=0, **overrides):
+    """Path of BASELINE config `name` (CONFIGS) in `directory`, written once."""
+    cfg = dict(CONFIGS[name], **overrides)
+    tag = "" if not overrides else "_" + "_".join(f"{k}{v}" for k, v in sorted(overrides.items()))
+    path = os.path.join(directory, f"{name}{tag}_s{seed}.mlb")
+    if not os.path.exists(path):
+        os.makedirs(directory, exist_ok=True)
+        tmp = path + f".tmp{os.getpid()}"
+        write_model(tmp, seed=seed, **cfg)
+        os.replace(tmp, path)
+    return path

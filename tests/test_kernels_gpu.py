@@ -1,0 +1,131 @@
+"""Kernel-level parity on the GPU, through the C ABI, against the CPU oracle.
+
+Bar (the reference's own, tests/test_kernels.c): quantized activations and
+int32 block dot products bit exact; matvec with unit scales exact; with real
+scales within 1e-5 of the sum of |terms| (TT_CLOSE of tests/tt.h:27-32).
+"""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+
+import krafla_b200 as kb
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _dev(built):
+    kb.device_check()
+
+
+@pytest.mark.parametrize("k", [32, 288, 896, 4096, 8192, 14336, 65536])
+def test_quantize_q8_bit_exact(k):
+    rng = np.random.default_rng(k)
+    x = (rng.standard_normal(k) * rng.choice([1e-3, 1, 40], k)).astype(np.float32)
+    if k >= 128:
+        x[32:64] = 0.0
+        x[64:96] = np.where(np.arange(32) % 2, 1e-37, -3e-37)
+    q, d = kb.quantize_q8(x)
+    rq, rd = oracle.quantize_q8(x)
+    assert np.array_equal(q, rq)
+    assert np.array_equal(d.view(np.uint32), rd.view(np.uint32))
+
+
+def test_quantize_q8_reference_vectors():
+    z = np.load(os.path.join(GOLDEN, "quant.npz"))
+    q, d = kb.quantize_q8(z["x"])
+    assert np.array_equal(q, z["q8_f32"])
+    assert np.array_equal(d.view(np.uint32), z["d8_f32"].view(np.uint32))
+
+
+def test_quantize_q8_known_answers():
+    x = np.zeros(64, np.float32)
+    x[0] = 127.0
+    x[1:6] = [0.5, -0.5, 1.5, 2.5, -2.5]   # tests/test_quant.c:47-60
+    x[32:64] = 1e-37                         # :64-70
+    q, d = kb.quantize_q8(x)
+    assert d[0] == 1.0 and q[1:6].tolist() == [1, -1, 2, 3, -3]
+    assert d[1] == 0.0 and (q[32:] == 0).all()
+
+
+@pytest.mark.parametrize("n", [64, 288, 2048, 4096])
+def test_rmsnorm_quantize(n):
+    rng = np.random.default_rng(n)
+    x = rng.standard_normal(n).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+    q, d, xn = kb.rmsnorm_quantize(x, w, 1e-5)
+    ref = oracle.rmsnorm(x, w, 1e-5)
+    # the sum of squares is reduced in another order: normalized values agree to float rounding
+    assert np.abs(xn - ref).max() <= 1e-6 * np.abs(ref).max()
+    # the quantization of the kernel's own normalized values is the reference rule, bit for bit
+    rq, rd = oracle.quantize_q8(xn)
+    assert np.array_equal(q, rq) and np.array_equal(d.view(np.uint32), rd.view(np.uint32))
+
+
+def make_w(rng, wtype, rows, cols, unit=False, f16=False):
+    wq = (rng.integers(-127, 128, rows * cols).astype(np.int8) if wtype == kb.Q8_0
+          else rng.integers(0, 256, rows * cols // 2).astype(np.uint8))
+    if unit:
+        wd = np.ones((rows, cols // 32), np.float32)
+    else:
+        wd = (rng.uniform(0.001, 0.05, (rows, cols // 32)) * rng.choice([-1, 1], (rows, cols // 32))).astype(np.float32)
+    if f16:
+        wd = wd.astype(np.float16)
+    return wq, wd
+
+
+def term_scale(wtype, wq, wd, rows, cols, xq, xd):
+    """Sum of |w x d_w d_x| per row (ref_scale of tests/test_kernels.c:64-83)."""
+    if wtype == kb.Q8_0:
+        w = wq.reshape(rows, -1, 32).astype(np.int64)
+    else:
+        p = wq.reshape(rows, -1, 16).astype(np.int64)
+        w = np.concatenate([(p & 15) - 8, (p >> 4) - 8], -1)
+    a = np.abs(w * xq.reshape(-1, 32)).sum(-1).astype(np.float64)
+    return (a * np.abs(wd.astype(np.float64)) * np.abs(xd)).sum(1)
+
+
+SHAPES = [(1, 32), (3, 96), (4, 256), (7, 288), (64, 896), (5, 8288), (333, 2048), (2048, 8192)]
+
+
+@pytest.mark.parametrize("wtype", [kb.Q8_0, kb.Q4_0])
+@pytest.mark.parametrize("rows,cols", SHAPES)
+def test_block_sums_bit_exact(wtype, rows, cols):
+    rng = np.random.default_rng(rows * 131 + cols)
+    wq, _ = make_w(rng, wtype, rows, cols)
+    xq = rng.integers(-127, 128, cols).astype(np.int8)
+    assert np.array_equal(kb.block_sums(wtype, wq, rows, cols, xq), oracle.block_sums(wtype, wq, rows, cols, xq))
+
+
+@pytest.mark.parametrize("wtype", [kb.Q8_0, kb.Q4_0])
+@pytest.mark.parametrize("rows,cols", SHAPES)
+def test_matvec_unit_scales_exact(wtype, rows, cols):
+    # exact while every partial sum stays below 2^24: |w x| <= 127*127 (Q8) or 8*127 (Q4) per element
+    if wtype == kb.Q8_0 and cols * 127 * 127 >= 1 << 24:
+        pytest.skip("float partial sums could round")
+    rng = np.random.default_rng(rows + cols)
+    wq, wd = make_w(rng, wtype, rows, cols, unit=True)
+    xq = rng.integers(-127, 128, cols).astype(np.int8)
+    xd = np.ones(cols // 32, np.float32)
+    y = kb.matvec(wtype, wq, wd, rows, cols, xq, xd)
+    exact = oracle.block_sums(wtype, wq, rows, cols, xq).astype(np.int64).sum(1)
+    assert np.array_equal(y, exact.astype(np.float32))
+
+
+@pytest.mark.parametrize("f16", [False, True])
+@pytest.mark.parametrize("wtype", [kb.Q8_0, kb.Q4_0])
+@pytest.mark.parametrize("rows,cols", SHAPES)
+def test_matvec_scaled(wtype, rows, cols, f16):
+    rng = np.random.default_rng(3 * rows + cols + f16)
+    wq, wd = make_w(rng, wtype, rows, cols, f16=f16)
+    xq = rng.integers(-127, 128, cols).astype(np.int8)
+    xd = rng.uniform(0.001, 0.05, cols // 32).astype(np.float32)
+    y = kb.matvec(wtype, wq, wd, rows, cols, xq, xd)
+    ref = oracle.matvec(wtype, wq, wd.astype(np.float32), rows, cols, xq, xd)
+    sc = term_scale(wtype, wq, wd, rows, cols, xq, xd)
+    tol = 1e-5 * np.maximum(sc, np.maximum(np.abs(y), np.abs(ref)))
+    assert (np.abs(y.astype(np.float64) - ref) <= tol).all()

@@ -1,0 +1,144 @@
+"""Model-level parity on the GPU through the C ABI (kc_forward / kc_prefill /
+kc_generate_greedy), against the reference's scalar logits (golden fixtures)
+and the CPU oracle.
+
+Bar: per-step logits within max|d| <= 1e-3 max|logit|;
+the greedy stream equal except at steps whose top-2 logit margin is below
+1e-4 (checked with the GPU's own tokens fed to the oracle, so one near-tie
+does not desynchronize the rest).
+"""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, MODEL_CACHE
+
+import krafla_b200 as kb
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+TOKENS = [1, 5, 9, 13, 17, 21, 25, 29, 33, 37, 41, 45, 49, 53, 57, 61]
+GOLDEN_MODELS = ["rand_q8", "rand_q4", "mix_q4", "mixf16_q4", "bias_q4", "llama3_q4", "swa_q8", "ctx_q4"]
+RTOL = 1e-3
+MARGIN = 1e-4
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _dev(built):
+    kb.device_check()
+
+
+def rel_err(a, b):
+    return np.abs(a.astype(np.float64) - b).max(axis=-1) / np.abs(b).max(axis=-1)
+
+
+def top2_margin(lg):
+    s = np.sort(lg)
+    return s[-1] - s[-2]
+
+
+@pytest.mark.parametrize("name", GOLDEN_MODELS)
+def test_forward_matches_reference_scalar_logits(name):
+    m = kb.Model(os.path.join(GOLDEN, "models", f"{name}.mlb"))
+    st = kb.State(m)
+    want = np.load(os.path.join(GOLDEN, f"{name}.logits.npy"))
+    got = np.stack([st.forward(t, p) for p, t in enumerate(TOKENS)])
+    assert rel_err(got, want).max() <= RTOL
+    for p in range(len(TOKENS)):
+        if top2_margin(want[p]) >= MARGIN:
+            assert got[p].argmax() == want[p].argmax()
+
+
+@pytest.mark.parametrize("name", ["rand_q4", "mixf16_q4", "bias_q4"])
+def test_prefill_equals_token_by_token(name):
+    # model/transformer.c:381-384: batched prefill gives the logits of decoding token by token
+    path = os.path.join(GOLDEN, "models", f"{name}.mlb")
+    m = kb.Model(path)
+    a = kb.State(m).prefill(TOKENS, 0, logits=True)
+    st = kb.State(m)
+    b = np.stack([st.forward(t, p) for p, t in enumerate(TOKENS)])
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    # prefill without logits then forward continues from the same cache
+    st2 = kb.State(m)
+    assert st2.prefill(TOKENS[:-1], 0) is None
+    c = st2.forward(TOKENS[-1], len(TOKENS) - 1)
+    assert np.array_equal(c.view(np.uint32), b[-1].view(np.uint32))
+
+
+def test_long_context_crosses_attention_splits():
+    # 150 positions (tests/test_e2e.sh:70-86 of the reference): several 32-position tiles and splits
+    path = os.path.join(GOLDEN, "models", "ctx_q4.mlb")
+    toks = [(i * 37) % 95 + 1 for i in range(1, 151)]
+    m = kb.Model(path)
+    got = kb.State(m).prefill(toks, 0, logits=True)
+    ref = oracle.OracleModel(path).prefill(toks)
+    assert rel_err(got, ref).max() <= 5e-2          # the reference's own bound for 150 positions
+    assert rel_err(got[:16], ref[:16]).max() <= RTOL
+
+
+def test_out_of_range_inputs():
+    m = kb.Model(os.path.join(GOLDEN, "models", "rand_q8.mlb"))
+    st = kb.State(m)
+    vocab, max_seq = m.config["vocab"], m.config["max_seq"]
+    assert st.forward(vocab, 0) is None
+    assert st.forward(-1, 0) is None
+    assert st.forward(1, max_seq) is None
+    with pytest.raises(kb.KraflaError) as e:
+        st.prefill([1, 2, vocab], 0)
+    assert e.value.status == kb.E_SHAPE
+    with pytest.raises(kb.KraflaError):
+        st.prefill([1] * 4, max_seq - 2)
+    assert st.forward(1, 0) is not None   # the state still works
+
+
+def teacher_forced_greedy(path, prompt, steps, kv_type=0):
+    """GPU greedy stream and the oracle run on the GPU's tokens."""
+    m = kb.Model(path)
+    st = kb.State(m, kv_type=kv_type)
+    st.prefill(prompt[:-1], 0)
+    toks = st.generate_greedy(prompt[-1], len(prompt) - 1, steps)
+    ref = oracle.OracleModel(path, kv_type=kv_type)
+    ref.prefill(prompt[:-1], 0, logits=False)
+    feed = [prompt[-1]] + toks[:-1].tolist()
+    bad = []
+    for i, t in enumerate(feed):
+        lg = ref.forward(t, len(prompt) - 1 + i)
+        if toks[i] != lg.argmax() and top2_margin(lg) >= MARGIN:
+            bad.append((i, int(toks[i]), int(lg.argmax()), float(top2_margin(lg))))
+    ref.close()
+    return toks, bad
+
+
+def test_greedy_128_small_model():
+    toks, bad = teacher_forced_greedy(os.path.join(GOLDEN, "models", "ctx_q4.mlb"), [1, 2, 3, 4], 128)
+    assert len(toks) == 128 and not bad, bad
+
+
+def test_cfg0_tiny_16_prompt_128_greedy():
+    """16 uniform prompt ids, then 128 greedy steps."""
+    path = kb.ensure_model("cfg0", MODEL_CACHE)
+    rng = np.random.default_rng(0)
+    prompt = rng.integers(0, 32000, 16).tolist()
+    m = kb.Model(path)
+    got = kb.State(m).prefill(prompt, 0, logits=True)
+    ref = oracle.OracleModel(path).prefill(prompt)
+    assert rel_err(got, ref).max() <= RTOL
+    toks, bad = teacher_forced_greedy(path, prompt, 128)
+    assert not bad, bad
+
+
+@pytest.mark.parametrize("name,prompt_len,steps", [("cfg1", 8, 24), ("cfg2", 8, 16)])
+def test_baseline_shapes_short(name, prompt_len, steps):
+    """BASELINE configs 1 and 2 (Qwen2.5-0.5B / Llama-3.2-1B shapes) over a short run."""
+    path = kb.ensure_model(name, MODEL_CACHE)
+    m = kb.Model(path)
+    vocab = m.config["vocab"]
+    prompt = np.random.default_rng(1).integers(0, vocab, prompt_len).tolist()
+    got = kb.State(m).prefill(prompt, 0, logits=True)
+    ref = oracle.OracleModel(path).prefill(prompt)
+    assert rel_err(got, ref).max() <= RTOL
+    del m
+    toks, bad = teacher_forced_greedy(path, prompt, steps)
+    assert not bad, bad
