@@ -113,6 +113,11 @@ float *kc_forward(kc_state *s, int token, int pos);
  * the next step's input. out_tokens (host, n ints) receives the n chosen
  * tokens. The ml_run -T 0 / ml_bench decode loop (app/ml_bench.c:125-131). */
 int kc_generate_greedy(kc_state *s, int token, int pos, int n, int *out_tokens);
+/* Debug view of the state after the last step: copies a device buffer to the
+ * host (which: 0 x [dim], 1 q|k|v before RoPE [q_dim + 2 kv_dim], 2 attention
+ * output [q_dim], 3 FFN hidden [hidden_dim], 4 / 5 the K / V cache
+ * [n_layers][max_seq][kv_dim]). KC_E_SHAPE when bytes is too small. */
+int kc_debug_copy(kc_state *s, int which, void *dst, size_t bytes);
 /* Replaces ml_state_free (transformer.h:65). */
 void kc_state_free(kc_state *s);
 

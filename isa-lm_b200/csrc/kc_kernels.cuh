@@ -65,6 +65,8 @@ struct GemvParams {
     float eps;
     const int8_t *xq;   /* PRO_PREQUANT */
     const float *xd;
+    const float *inv_tab;    /* PRO_RMSNORM_QUANT: when set, 1/rms of x is inv_tab[*inv_token] */
+    const int *inv_token;
     int act;            /* EPI_PAIR: 0 SiLU, 1 GELU (tanh) */
     float softcap;      /* EPI_LOGITS: final soft-cap, 0 = none */
     LoopState *ls;      /* EPI_LOGITS */
@@ -209,7 +211,11 @@ __device__ __forceinline__ void gemv_prologue(const GemvParams &p, int8_t *xq, f
         return;
     }
     float inv = 1.0f;
-    if (p.pro == PRO_RMSNORM_QUANT) {
+    if (p.pro == PRO_RMSNORM_QUANT && p.inv_tab) {
+        /* the first layer's input is an embedding row: its 1/rms was computed on
+         * the host in the reference's sequential order (see embed_inv_table) */
+        inv = p.inv_tab[*p.inv_token];
+    } else if (p.pro == PRO_RMSNORM_QUANT) {
         float ss = 0.0f;
         for (int i = tid; i < cols / 4; i += GEMV_THREADS) {
             const float4 v = ((const float4 *)p.x)[i];
@@ -739,19 +745,28 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const __grid_constant
     __syncthreads();
     if (!is_last) return;
     __threadfence();
+    /* combine: per head the split weights exp(m_s - M) / L into shared memory
+     * (one lane per split), then every output sums its splits with the loads
+     * of all splits in flight at once */
+    float *wts = sp;   /* [group][ATT_TILE >= nsplit] (the score tile is free now) */
+    for (int h = warp; h < group; h += ATT_THREADS / 32) {
+        const float *ph = p.part + (size_t)(g * group + h) * p.nsplit * stride;
+        const float m = lane < active ? __ldcg(ph + (size_t)lane * stride + hd) : -INFINITY;
+        const float l = lane < active ? __ldcg(ph + (size_t)lane * stride + hd + 1) : 0.0f;
+        const float M = warp_max(m);
+        const float e = lane < active ? expf(m - M) : 0.0f;
+        const float L = warp_sum(l * e);
+        wts[h * ATT_TILE + lane] = e / L;
+    }
+    __syncthreads();
     for (int o = tid; o < nout; o += ATT_THREADS) {
         const int h = o / hd, i = o % hd;
-        const float *base = p.part + (size_t)(g * group + h) * p.nsplit * stride;
-        float M = -INFINITY;
-        for (int s = 0; s < active; s++) M = fmaxf(M, __ldcg(base + (size_t)s * stride + hd));
-        float L = 0.0f, num = 0.0f;
-        for (int s = 0; s < active; s++) {
-            const float *ps = base + (size_t)s * stride;
-            const float w = expf(__ldcg(ps + hd) - M);
-            L = fmaf(__ldcg(ps + hd + 1), w, L);
-            num = fmaf(__ldcg(ps + i), w, num);
-        }
-        p.ao[(size_t)(g * group + h) * hd + i] = num / L;
+        const float *base = p.part + (size_t)(g * group + h) * p.nsplit * stride + i;
+        const float *w = wts + h * ATT_TILE;
+        float num = 0.0f;
+#pragma unroll 8
+        for (int s2 = 0; s2 < active; s2++) num = fmaf(__ldcg(base + (size_t)s2 * stride), w[s2], num);
+        p.ao[(size_t)(g * group + h) * hd + i] = num;
     }
     if (tid == 0) p.counter[g] = 0u;
 }

@@ -6,6 +6,7 @@
 #include <cstdio>
 #include <cstring>
 #include <new>
+#include <thread>
 #include <string>
 #include <vector>
 #include <sys/mman.h>
@@ -186,6 +187,7 @@ struct kc_state {
     float *kc = nullptr, *vc = nullptr, *rcos = nullptr, *rsin = nullptr, *lcos = nullptr, *lsin = nullptr;
     float *flush = nullptr;
     size_t flush_bytes = 0;
+    float *inv0 = nullptr;   /* [vocab]: 1/rms of each embedding row (layer 0's RMSNorm) */
     unsigned *counter = nullptr, *err = nullptr;
     LoopState *ls = nullptr;
     int *feed = nullptr, *out_tokens = nullptr;
@@ -229,9 +231,12 @@ static const int KC_MAX_SMEM = 227 * 1024;
 static int set_smem_attributes() {
     static bool done = false;
     if (done) return KC_OK;
-    CK(cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, KC_MAX_SMEM));
-    CK(cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, KC_MAX_SMEM));
-    CK(cudaFuncSetAttribute(quantize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, KC_MAX_SMEM));
+    const void *fns[] = { (const void *)gemv_kernel, (const void *)attn_kernel, (const void *)quantize_kernel };
+    for (const void *f : fns) {
+        cudaFuncAttributes a;
+        CK(cudaFuncGetAttributes(&a, f));
+        CK(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, KC_MAX_SMEM - (int)a.sharedSizeBytes));
+    }
     done = true;
     return KC_OK;
 }   /* device error word of the kernel-level entry points */
@@ -265,6 +270,70 @@ static int launch_gemv(kc_state *s, GemvParams &p, cudaStream_t st, unsigned *er
     p.err = err;
     gemv_kernel<<<ctas, GEMV_THREADS + 32, smem, st>>>(p);
     return KC_OK;
+}
+
+/* 1/rms of every embedding row, the first layer's RMSNorm factor, computed as
+ * the reference computes it: x = dequant(row) (core/quant_ref.c:4-19) times
+ * embed_scale (model/transformer.c:226-230), ss += x*x in order, inv = 1 /
+ * sqrtf(ss / n + eps) (kernels/scalar/k_scalar.c:59-64), in float with every
+ * operation rounded on its own (this file is compiled without contraction).
+ * Embedding rows are quantized: with unit norm weights their normalized values
+ * sit on exact quantization ties, which only this order resolves as the
+ * reference does. */
+static void embed_inv_table(const kc_model *m, std::vector<float> &out) {
+    const kc_config &c = m->cfg;
+    const HostMat &E = m->tok_emb;
+    const int dim = c.dim, nb = dim / QK;
+    out.assign((size_t)c.vocab, 0.0f);
+    auto scale = [&](size_t i) -> float {
+        if (E.d16) {
+            const uint16_t h = ((const uint16_t *)E.d)[i];
+            const uint32_t sign = (uint32_t)(h & 0x8000u) << 16, e = (h >> 10) & 0x1fu, mm = h & 0x3ffu;
+            if (e == 0) return (sign ? -1.0f : 1.0f) * (float)mm * (1.0f / 16777216.0f);
+            const uint32_t x = sign | (e == 31 ? 0x7f800000u | (mm << 13) : ((e + 112u) << 23) | (mm << 13));
+            float f;
+            std::memcpy(&f, &x, 4);
+            return f;
+        }
+        return ((const float *)E.d)[i];
+    };
+    auto work = [&](int t0, int t1) {
+        std::vector<float> x((size_t)dim);
+        for (int t = t0; t < t1; t++) {
+            for (int b = 0; b < nb; b++) {
+                const float d = scale((size_t)t * nb + b);
+                for (int j = 0; j < QK; j++) {
+                    int v;
+                    if (E.type == KC_Q8_0) {
+                        v = ((const int8_t *)E.q)[(size_t)t * dim + (size_t)b * QK + j];
+                    } else {
+                        const uint8_t byte = ((const uint8_t *)E.q)[((size_t)t * nb + b) * (QK / 2) + (j & 15)];
+                        v = (j < 16 ? (byte & 0xF) : (byte >> 4)) - 8;
+                    }
+                    volatile float xv = (float)v * d;
+                    float xf = xv;
+                    if (c.embed_scale != 1.0f) { volatile float t2 = xf * c.embed_scale; xf = t2; }
+                    x[(size_t)b * QK + j] = xf;
+                }
+            }
+            float ss = 0.0f;
+            for (int i = 0; i < dim; i++) {
+                volatile float sq = x[(size_t)i] * x[(size_t)i];
+                ss = ss + sq;
+            }
+            volatile float mean = ss / (float)dim;
+            volatile float arg = mean + c.norm_eps;
+            volatile float root = std::sqrt((float)arg);
+            out[(size_t)t] = 1.0f / root;
+        }
+    };
+    unsigned nt = std::thread::hardware_concurrency();
+    if (nt < 1) nt = 1;
+    if (nt > 64) nt = 64;
+    std::vector<std::thread> th;
+    for (unsigned i = 0; i < nt; i++)
+        th.emplace_back(work, (int)((long long)c.vocab * i / nt), (int)((long long)c.vocab * (i + 1) / nt));
+    for (auto &t : th) t.join();
 }
 
 static int gemv_smem(int cols) { return cols + 8 * (cols / QK) + 128; }
@@ -302,6 +371,10 @@ static void enqueue_step(kc_state *s, bool logits, cudaEvent_t *ev = nullptr, in
         /* 1. RMSNorm + quantize + Q/K/V projections (+ biases) */
         GemvParams p{};
         p.cols = c.dim; p.pro = PRO_RMSNORM_QUANT; p.x = s->x; p.norm_w = L.attn_norm; p.eps = c.norm_eps;
+        if (l == 0) {
+            p.inv_tab = s->inv0;
+            p.inv_token = &s->ls->token;
+        }
         p.seg[0] = seg_of(L.wq, EPI_STORE, s->qkv, L.bq, 2);
         p.seg[1] = seg_of(L.wk, EPI_STORE, s->qkv + c.q_dim, L.bk, 2);
         p.seg[2] = seg_of(L.wv, EPI_STORE, s->qkv + c.q_dim + c.kv_dim, L.bv, 2);
@@ -425,6 +498,7 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
         { (void **)&s->kc, sizeof(float) * lkv },
         { (void **)&s->vc, sizeof(float) * lkv },
         { (void **)&s->rcos, sizeof(float) * T * h2 },
+        { (void **)&s->inv0, sizeof(float) * (size_t)c.vocab },
         { (void **)&s->rsin, sizeof(float) * T * h2 },
     };
     if (c.rope_local_theta > 0.0f) {
@@ -469,6 +543,10 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
         if (e == cudaSuccess && s->lcos) e = cudaMemcpy(s->lcos, lc.data(), sizeof(float) * T * h2, cudaMemcpyHostToDevice);
         if (e == cudaSuccess && s->lsin) e = cudaMemcpy(s->lsin, ls_.data(), sizeof(float) * T * h2, cudaMemcpyHostToDevice);
         if (e != cudaSuccess) return fail(cuda_status(e, "rope tables"));
+        std::vector<float> inv0;
+        embed_inv_table(m, inv0);
+        e = cudaMemcpy(s->inv0, inv0.data(), sizeof(float) * c.vocab, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return fail(cuda_status(e, "embedding norms"));
     }
     st = set_smem_attributes();
     if (st != KC_OK) return fail(st);
@@ -659,6 +737,25 @@ extern "C" int kc_profile_step(kc_state *s, int token, int pos, float *ms) {
     ms[5] += t;
     for (auto &e : ev) cudaEventDestroy(e);
     return finish(s);
+}
+
+extern "C" int kc_debug_copy(kc_state *s, int which, void *dst, size_t bytes) {
+    const kc_config &c = s->c;
+    const void *src = nullptr;
+    size_t n = 0;
+    switch (which) {
+    case 0: src = s->x; n = sizeof(float) * c.dim; break;
+    case 1: src = s->qkv; n = sizeof(float) * (size_t)(c.q_dim + 2 * c.kv_dim); break;
+    case 2: src = s->ao; n = sizeof(float) * c.q_dim; break;
+    case 3: src = s->hb; n = sizeof(float) * c.hidden_dim; break;
+    case 4: src = s->kc; n = sizeof(float) * (size_t)c.n_layers * c.max_seq * c.kv_dim; break;
+    case 5: src = s->vc; n = sizeof(float) * (size_t)c.n_layers * c.max_seq * c.kv_dim; break;
+    default: return KC_E_SHAPE;
+    }
+    if (bytes < n) return KC_E_SHAPE;
+    CK(cudaStreamSynchronize(s->st));
+    CK(cudaMemcpy(dst, src, n, cudaMemcpyDeviceToHost));
+    return KC_OK;
 }
 
 /* ------------------------------------------------------------ kernel-level */

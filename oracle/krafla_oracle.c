@@ -466,6 +466,18 @@ void orc_state_free(orc_state *s) {
 }
 
 const float *orc_state_x(const orc_state *s) { return s->x; }
+/* 0 x, 1 q (after RoPE), 2 ao, 3 hb (after the activation), 4 F32 K cache, 5 F32 V cache */
+const float *orc_state_buf(const orc_state *s, int which) {
+    switch (which) {
+    case 0: return s->x;
+    case 1: return s->q;
+    case 2: return s->ao;
+    case 3: return s->hb;
+    case 4: return s->kc;
+    case 5: return s->vc;
+    }
+    return NULL;
+}
 const float *orc_rope_cos(const orc_state *s) { return s->rcos; }
 const float *orc_rope_sin(const orc_state *s) { return s->rsin; }
 

@@ -74,6 +74,8 @@ int orc_forward(orc_state *s, int token, int pos, float *logits);
 int orc_prefill(orc_state *s, const int *tokens, int n, int pos0, float *logits);
 /* Last hidden-state vector x [dim] after the latest orc_forward. */
 const float *orc_state_x(const orc_state *s);
+/* Debug views: 0 x, 1 q (after RoPE), 2 ao, 3 hb, 4 F32 K cache, 5 F32 V cache. */
+const float *orc_state_buf(const orc_state *s, int which);
 /* RoPE tables [max_seq][head_dim/2] computed as ml_state_init does. */
 const float *orc_rope_cos(const orc_state *s);
 const float *orc_rope_sin(const orc_state *s);
