@@ -121,19 +121,28 @@ int kc_debug_copy(kc_state *s, int which, void *dst, size_t bytes);
 /* Replaces ml_state_free (transformer.h:65). */
 void kc_state_free(kc_state *s);
 
-/* Timing helpers for bench.py (CUDA events on the state's stream; the
- * region holds exactly `steps` greedy decode steps after `warmup` untimed
- * ones, starting at position pos; *ms receives the device milliseconds). */
+/* Timing helper for bench.py: CUDA events on the state's stream around exactly
+ * `steps` greedy decode steps (one launch of the step kernel) after `warmup`
+ * untimed ones, starting at position pos; *ms receives the device
+ * milliseconds. */
 int kc_time_decode(kc_state *s, int token, int pos, int warmup, int steps, float *ms);
-/* The device milliseconds of `reps` launches of one layer's fused gate/up
- * kernel (the decode path's dominant kernel) on the state's stream, with an
- * L2 flush between launches (a write larger than L2); *bytes receives the
- * algorithmic bytes per launch (quants + scales read). */
-int kc_time_ffn_up(kc_state *s, int layer, int reps, float *ms_per_launch, double *bytes);
-/* Per-kernel-class device time of one decode step: fills ms[0..5] with the
- * time of qkv, attention, wo, ffn-up, ffn-down and classifier launches summed
- * over the step (instrumented with events, outside any timed region). */
-int kc_profile_step(kc_state *s, int token, int pos, float *ms);
+/* The device clock (ns) at the start of one decode step and after each of
+ * its grid barriers (as CTA 0 sees them): per layer Q/K/V, attention, O,
+ * gate/up, down, then the classifier. t: cap entries; *n: entries written. */
+int kc_step_timeline(kc_state *s, int token, int pos, unsigned long long *t, int cap, int *n);
+
+/* Per-CTA trace of one decode step (diagnostics): out[(phase * nctas + cta) *
+ * 3 + k] = device clock (ns) when CTA cta finished the phase's activation
+ * prologue (k = 0), arrived at its barrier (1) and was released (2); phases as
+ * in kc_step_timeline. cap: entries of out. */
+int kc_step_trace(kc_state *s, int token, int pos, unsigned long long *out, size_t cap, int *nphases, int *nctas);
+
+/* Event log of one decode step (diagnostics): out[(cta * 2 + who) * cap + k] =
+ * SM clock << 8 | event code, the k-th event of CTA cta's consumer (who 0:
+ * 2 activation ready, 3 ring stage ready, 4 stage done, 5 barrier arrival,
+ * 6 release) or producer (who 1: 7 waits for a free stage, 8 issued it).
+ * out holds nctas * 2 * cap entries (nctas = the SM count), zero past the end. */
+int kc_step_events(kc_state *s, int token, int pos, unsigned long long *out, unsigned cap, int *nctas);
 
 /* ---- kernel-level entry points (device pointers, stream may be NULL) ----
  * These run the exact device code of the model path, for parity tests. */

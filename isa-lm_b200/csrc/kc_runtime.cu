@@ -5,6 +5,8 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
+#include <cstdlib>
 #include <new>
 #include <thread>
 #include <string>
@@ -13,6 +15,7 @@
 
 #include "kc_internal.h"
 #include "kc_kernels.cuh"
+#include "kc_step.cuh"
 
 namespace kc {
 static thread_local std::string g_err;
@@ -185,17 +188,21 @@ struct kc_state {
     uint8_t *arena = nullptr;
     float *x = nullptr, *qkv = nullptr, *ao = nullptr, *hb = nullptr, *logits = nullptr, *part = nullptr;
     float *kc = nullptr, *vc = nullptr, *rcos = nullptr, *rsin = nullptr, *lcos = nullptr, *lsin = nullptr;
-    float *flush = nullptr;
-    size_t flush_bytes = 0;
     float *inv0 = nullptr;   /* [vocab]: 1/rms of each embedding row (layer 0's RMSNorm) */
+    float *ssp = nullptr;    /* [grid]: per-CTA sums of squares of the residual rows it wrote */
     unsigned *counter = nullptr, *err = nullptr;
     LoopState *ls = nullptr;
     int *feed = nullptr, *out_tokens = nullptr;
     float *h_logits = nullptr;
     LoopState *h_ls = nullptr;
-    cudaGraphExec_t g_logits = nullptr, g_nologits = nullptr;
-    int nsplit = 32;
     int num_sms = 148;
+    /* the persistent step kernel */
+    LayerPlan *d_plan = nullptr;
+    unsigned *bar = nullptr;
+    unsigned long long *timeline = nullptr;
+    unsigned *timeline_n = nullptr;
+    StepArgs sa{};
+    int step_smem = 0;
 };
 
 /* RoPE inverse frequency of pair i (model/transformer.c:16-38; the scaling
@@ -224,52 +231,28 @@ static double rope_inv_freq(const kc_config &c, int i) {
     return (1.0 - smooth) * inv / f + smooth * inv;
 }
 
-static unsigned *g_err_word = nullptr;
+static unsigned *g_err_word = nullptr;   /* device error word of the kernel-level entry points */
 static const int KC_MAX_SMEM = 227 * 1024;
 
 /* Opt-in to the full shared memory of an sm_100 CTA (outside any stream capture). */
 static int set_smem_attributes() {
     static bool done = false;
     if (done) return KC_OK;
-    const void *fns[] = { (const void *)gemv_kernel, (const void *)attn_kernel, (const void *)quantize_kernel };
+    const void *fns[] = { (const void *)step_kernel, (const void *)matvec_kernel, (const void *)activation_kernel };
     for (const void *f : fns) {
-        cudaFuncAttributes a;
-        CK(cudaFuncGetAttributes(&a, f));
-        CK(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, KC_MAX_SMEM - (int)a.sharedSizeBytes));
+        cudaFuncAttributes fa;
+        CK(cudaFuncGetAttributes(&fa, f));
+        CK(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, KC_MAX_SMEM - (int)fa.sharedSizeBytes));
     }
     done = true;
     return KC_OK;
-}   /* device error word of the kernel-level entry points */
+}
 
-/* Launches the GEMV over p's segments. Each segment gets CTAs in proportion
- * to its weight bytes out of the CTAs that fit on the device at once (each
- * CTA then streams a contiguous range of rows). */
-static int launch_gemv(kc_state *s, GemvParams &p, cudaStream_t st, unsigned *err) {
-    double bytes[MAX_SEGS], total = 0.0;
-    for (int i = 0; i < p.nseg; i++) {
-        const Seg &g = p.seg[i];
-        bytes[i] = (double)g.rows * (g.type == T_Q4 ? p.cols / 2 : p.cols) * (g.epi == EPI_PAIR ? 2 : 1);
-        total += bytes[i];
-    }
-    const int smem = gemv_smem_bytes(p);
-    if (smem > KC_MAX_SMEM) return KC_E_SHAPE;
-    int per_sm = 1;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_kernel, GEMV_THREADS + 32, smem);
-    if (per_sm < 1) per_sm = 1;
-    const int budget = per_sm * (s ? s->num_sms : 148);
-    int ctas = 0;
-    for (int i = 0; i < p.nseg; i++) {
-        Seg &g = p.seg[i];
-        int n = (int)((double)budget * bytes[i] / total + 0.5);
-        if (n < 1) n = 1;
-        if (n > g.rows) n = g.rows;
-        g.cta0 = ctas;
-        g.ctas = n;
-        ctas += n;
-    }
-    p.err = err;
-    gemv_kernel<<<ctas, GEMV_THREADS + 32, smem, st>>>(p);
-    return KC_OK;
+/* Ring depth that fits beside the fixed part of a streaming CTA's shared memory. */
+static int ring_stages(int slot, int act_bytes, int static_bytes) {
+    int nst = 16;
+    while (nst >= 2 && smem_fixed_bytes(nst, act_bytes) + nst * slot > KC_MAX_SMEM - static_bytes) nst--;
+    return nst;
 }
 
 /* 1/rms of every embedding row, the first layer's RMSNorm factor, computed as
@@ -336,119 +319,106 @@ static void embed_inv_table(const kc_model *m, std::vector<float> &out) {
     for (auto &t : th) t.join();
 }
 
-static int gemv_smem(int cols) { return cols + 8 * (cols / QK) + 128; }
+static PMat pmat(const DevMat &m) { return PMat{ m.q, m.d, m.rows, m.type, m.d16 }; }
 
-static Seg seg_of(const DevMat &w, int epi, float *out, const float *bias, int nr) {
-    Seg g{};
-    g.q = w.q; g.d = w.d; g.rows = w.rows; g.type = w.type; g.d16 = w.d16;
-    g.epi = epi; g.out = out; g.bias = bias; (void)nr;
-    return g;
-}
-
-/* The kernels of one decode step, in stream order. kernel_class: when
- * non-null, events are recorded around each class (profiling only). */
-static void enqueue_step(kc_state *s, bool logits, cudaEvent_t *ev = nullptr, int *nev = nullptr) {
-    kc_model *m = s->m;
+/* The persistent step kernel's plan: per-layer pointers in device memory, the
+ * ring geometry from the shared-memory budget, the attention split. */
+static int setup_step_kernel(kc_state *s) {
     const kc_config &c = s->c;
-    cudaStream_t st = s->st;
-    auto mark = [&]() {
-        if (ev) cudaEventRecord(ev[(*nev)++], st);
-    };
-    const DevMat &E = m->d_tok_emb;
-    mark();
-    if (E.d16)
-        embed_kernel<true><<<(c.dim + 255) / 256, 256, 0, st>>>(s->x, E.q, E.d, E.type, c.dim, c.vocab, c.max_seq,
-                                                                c.embed_scale, s->ls);
-    else
-        embed_kernel<false><<<(c.dim + 255) / 256, 256, 0, st>>>(s->x, E.q, E.d, E.type, c.dim, c.vocab, c.max_seq,
-                                                                 c.embed_scale, s->ls);
+    kc_model *m = s->m;
+    std::vector<LayerPlan> plan((size_t)c.n_layers);
     const size_t lkv = (size_t)c.max_seq * c.kv_dim;
-    const int group = c.n_heads / c.n_kv_heads;
-    const int att_smem = (int)sizeof(float) *
-                         (group * c.head_dim + ATT_TILE * (c.head_dim + 1) + ATT_TILE * c.head_dim + group * ATT_TILE + 3 * group);
+    int slot = 0;
+    auto fit = [&](const DevMat &w, int cols, int pair) {
+        const int b = stage_slot_bytes(w.type, w.d16, cols, pair);
+        slot = b > slot ? b : slot;
+    };
     for (int l = 0; l < c.n_layers; l++) {
         const DevLayer &L = m->d_layers[(size_t)l];
-        /* 1. RMSNorm + quantize + Q/K/V projections (+ biases) */
-        GemvParams p{};
-        p.cols = c.dim; p.pro = PRO_RMSNORM_QUANT; p.x = s->x; p.norm_w = L.attn_norm; p.eps = c.norm_eps;
-        if (l == 0) {
-            p.inv_tab = s->inv0;
-            p.inv_token = &s->ls->token;
-        }
-        p.seg[0] = seg_of(L.wq, EPI_STORE, s->qkv, L.bq, 2);
-        p.seg[1] = seg_of(L.wk, EPI_STORE, s->qkv + c.q_dim, L.bk, 2);
-        p.seg[2] = seg_of(L.wv, EPI_STORE, s->qkv + c.q_dim + c.kv_dim, L.bv, 2);
-        p.nseg = 3;
-        mark();
-        launch_gemv(s, p, st, s->err);
-        /* 2. attention (RoPE, KV store, split-K flash decode, combine) */
-        AttnParams a{};
-        a.qkv = s->qkv; a.kc = s->kc + (size_t)l * lkv; a.vc = s->vc + (size_t)l * lkv;
-        a.rcos = L.local_rope ? s->lcos : s->rcos; a.rsin = L.local_rope ? s->lsin : s->rsin;
-        a.ao = s->ao; a.part = s->part; a.counter = s->counter; a.ls = s->ls;
-        a.n_heads = c.n_heads; a.n_kv_heads = c.n_kv_heads; a.hd = c.head_dim; a.q_dim = c.q_dim; a.kv_dim = c.kv_dim;
-        a.max_seq = c.max_seq; a.window = L.window; a.nsplit = s->nsplit; a.scale = c.attn_scale; a.softcap = c.attn_softcap;
-        mark();
-        attn_kernel<<<dim3(c.n_kv_heads, s->nsplit), ATT_THREADS, att_smem, st>>>(a);
-        /* 3. quantize + output projection + residual */
-        GemvParams o{};
-        o.cols = c.q_dim; o.pro = PRO_QUANT; o.x = s->ao;
-        o.seg[0] = seg_of(L.wo, EPI_RESID, s->x, nullptr, 2);
-        o.nseg = 1;
-        mark();
-        launch_gemv(s, o, st, s->err);
-        /* 4. RMSNorm + quantize + gate/up + activation */
-        GemvParams u{};
-        u.cols = c.dim; u.pro = PRO_RMSNORM_QUANT; u.x = s->x; u.norm_w = L.ffn_norm; u.eps = c.norm_eps; u.act = c.act;
-        u.seg[0] = seg_of(L.w1, EPI_PAIR, s->hb, nullptr, 1);
-        u.seg[0].q2 = L.w3.q;
-        u.seg[0].d2 = L.w3.d;
-        u.nseg = 1;
-        mark();
-        launch_gemv(s, u, st, s->err);
-        /* 5. quantize + down projection + residual */
-        GemvParams dn{};
-        dn.cols = c.hidden_dim; dn.pro = PRO_QUANT; dn.x = s->hb;
-        dn.seg[0] = seg_of(L.w2, EPI_RESID, s->x, nullptr, 2);
-        dn.nseg = 1;
-        mark();
-        launch_gemv(s, dn, st, s->err);
+        LayerPlan &P = plan[(size_t)l];
+        P.wq = pmat(L.wq); P.wk = pmat(L.wk); P.wv = pmat(L.wv); P.wo = pmat(L.wo);
+        P.w1 = pmat(L.w1); P.w3 = pmat(L.w3); P.w2 = pmat(L.w2);
+        P.attn_norm = L.attn_norm; P.ffn_norm = L.ffn_norm; P.bq = L.bq; P.bk = L.bk; P.bv = L.bv;
+        P.kc = s->kc + (size_t)l * lkv; P.vc = s->vc + (size_t)l * lkv;
+        P.rcos = L.local_rope ? s->lcos : s->rcos; P.rsin = L.local_rope ? s->lsin : s->rsin;
+        P.window = L.window;
+        fit(L.wq, c.dim, 0); fit(L.wk, c.dim, 0); fit(L.wv, c.dim, 0); fit(L.wo, c.q_dim, 0);
+        fit(L.w1, c.dim, 1); fit(L.w2, c.hidden_dim, 0);
     }
-    mark();
-    if (logits) {
-        GemvParams h{};
-        h.cols = c.dim; h.pro = PRO_RMSNORM_QUANT; h.x = s->x; h.norm_w = m->d_final_norm; h.eps = c.norm_eps;
-        h.seg[0] = seg_of(m->d_wcls, EPI_LOGITS, s->logits, nullptr, 2);
-        h.nseg = 1;
-        h.softcap = c.final_softcap; h.ls = s->ls; h.feed = s->feed; h.out_tokens = s->out_tokens; h.vocab = c.vocab;
-        launch_gemv(s, h, st, s->err);
-    } else {
-        advance_kernel<<<1, 1, 0, st>>>(s->ls, s->feed);
+    fit(m->d_wcls, c.dim, 0);
+    CK(cudaMalloc(&s->d_plan, sizeof(LayerPlan) * plan.size()));
+    CK(cudaMemcpy(s->d_plan, plan.data(), sizeof(LayerPlan) * plan.size(), cudaMemcpyHostToDevice));
+    const int group = c.n_heads / c.n_kv_heads;
+    const int att_bytes = (int)sizeof(float) * attention_scratch_floats(group, c.head_dim);
+    int act = 0;
+    for (int cols : { c.dim, c.q_dim, c.hidden_dim }) act = std::max(act, cols + 8 * (cols / QK));
+    act = (std::max(act, att_bytes) + 15) & ~15;
+    cudaFuncAttributes fa;
+    CK(cudaFuncGetAttributes(&fa, step_kernel));
+    const int nst = ring_stages(slot, act, (int)fa.sharedSizeBytes);
+    if (nst < 2) {
+        set_error("layer shapes leave no room for the weight ring in shared memory");
+        return KC_E_SHAPE;
     }
-    mark();
-}
-
-static int capture(kc_state *s, bool logits, cudaGraphExec_t *out) {
-    cudaGraph_t g = nullptr;
-    CK(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
-    enqueue_step(s, logits);
-    cudaError_t e = cudaStreamEndCapture(s->st, &g);
-    if (e != cudaSuccess) return cuda_status(e, "graph capture");
-    e = cudaGraphInstantiate(out, g, 0);
-    cudaGraphDestroy(g);
-    if (e != cudaSuccess) return cuda_status(e, "graph instantiate");
+    s->step_smem = smem_fixed_bytes(nst, act) + nst * slot;
+    int per_sm = 0;
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, step_kernel, STEP_THREADS, s->step_smem));
+    if (per_sm < 1) {
+        set_error("the step kernel does not fit on an SM");
+        return KC_E_SHAPE;
+    }
+    StepArgs &a = s->sa;
+    a.layers = s->d_plan;
+    a.emb = pmat(m->d_tok_emb);
+    a.cls = pmat(m->d_wcls);
+    a.final_norm = m->d_final_norm;
+    a.inv0 = s->inv0;
+    a.x = s->x; a.qkv = s->qkv; a.ao = s->ao; a.hb = s->hb; a.logits = s->logits; a.part = s->part; a.ssp = s->ssp;
+    a.att_counter = s->counter; a.bar = s->bar; a.err = s->err; a.ls = s->ls; a.feed = s->feed;
+    a.out_tokens = s->out_tokens;
+    a.n_layers = c.n_layers; a.dim = c.dim; a.q_dim = c.q_dim; a.kv_dim = c.kv_dim; a.hidden = c.hidden_dim;
+    a.vocab = c.vocab; a.max_seq = c.max_seq; a.n_heads = c.n_heads; a.n_kv_heads = c.n_kv_heads; a.hd = c.head_dim;
+    a.eps = c.norm_eps; a.attn_scale = c.attn_scale; a.attn_softcap = c.attn_softcap; a.final_softcap = c.final_softcap;
+    a.embed_scale = c.embed_scale; a.act = c.act;
+    a.nsplit = std::min(MAX_NSPLIT, std::max(1, s->num_sms / c.n_kv_heads));
+    a.nstage = nst; a.slot_bytes = slot; a.act_bytes = act;
+    a.timeline = nullptr; a.timeline_n = s->timeline_n; a.timeline_cap = 4096;
     return KC_OK;
 }
+
+/* Runs nsteps token steps in one cooperative launch of the step kernel. */
+static int launch_steps(kc_state *s, int nsteps, int logits, bool timeline = false) {
+    CK(cudaMemsetAsync(s->bar, 0, sizeof(unsigned), s->st));
+    StepArgs a = s->sa;
+    a.nsteps = nsteps;
+    a.run_cls = logits;
+    if (timeline) {
+        a.timeline = s->timeline;
+        CK(cudaMemsetAsync(s->timeline_n, 0, sizeof(unsigned), s->st));
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)s->num_sms);
+    cfg.blockDim = dim3(STEP_THREADS);
+    cfg.dynamicSmemBytes = (size_t)s->step_smem;
+    cfg.stream = s->st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CK(cudaLaunchKernelEx(&cfg, step_kernel, a));
+    return KC_OK;
+}
+
+static int run_steps(kc_state *s, int nsteps, int logits) { return launch_steps(s, nsteps, logits); }
 
 extern "C" void kc_state_free(kc_state *s) {
     if (!s) return;
     if (s->st) cudaStreamSynchronize(s->st);
-    if (s->g_logits) cudaGraphExecDestroy(s->g_logits);
-    if (s->g_nologits) cudaGraphExecDestroy(s->g_nologits);
     if (s->arena) cudaFree(s->arena);
-    if (s->flush) cudaFree(s->flush);
     if (s->h_logits) cudaFreeHost(s->h_logits);
     if (s->h_ls) cudaFreeHost(s->h_ls);
+    if (s->d_plan) cudaFree(s->d_plan);
     if (s->st) cudaStreamDestroy(s->st);
     delete s;
 }
@@ -462,7 +432,7 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
     if (kv_type != KC_F32) { set_error("KV cache type not supported by this build yet"); return KC_E_SHAPE; }
     if (c.qk_norm || c.post_norms) { set_error("qk_norm / post_norms not supported by this build yet"); return KC_E_SHAPE; }
     const int group = c.n_heads / c.n_kv_heads;
-    if (group * c.head_dim > ATT_THREADS * ATT_MAX_OUT || c.head_dim % 4) {
+    if (group * c.head_dim > ATT_MAX_OUT || c.head_dim % 4) {
         set_error("attention head layout outside this build's kernel limits");
         return KC_E_SHAPE;
     }
@@ -489,9 +459,13 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
         { (void **)&s->ao, sizeof(float) * c.q_dim },
         { (void **)&s->hb, sizeof(float) * c.hidden_dim },
         { (void **)&s->logits, sizeof(float) * (size_t)LOGITS_RING * c.vocab },
-        { (void **)&s->part, sizeof(float) * (size_t)c.n_heads * s->nsplit * (c.head_dim + 2) },
+        { (void **)&s->part, sizeof(float) * (size_t)c.n_heads * MAX_NSPLIT * (c.head_dim + 2) },
+        { (void **)&s->ssp, sizeof(float) * (size_t)s->num_sms },
         { (void **)&s->counter, sizeof(unsigned) * c.n_kv_heads },
         { (void **)&s->err, sizeof(unsigned) * 4 },
+        { (void **)&s->bar, sizeof(unsigned) * 4 },
+        { (void **)&s->timeline_n, sizeof(unsigned) * 4 },
+        { (void **)&s->timeline, sizeof(unsigned long long) * 4096 },
         { (void **)&s->ls, sizeof(LoopState) },
         { (void **)&s->feed, sizeof(int) * (T + 1) },
         { (void **)&s->out_tokens, sizeof(int) * (T + 1) },
@@ -550,26 +524,10 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
     }
     st = set_smem_attributes();
     if (st != KC_OK) return fail(st);
-    {
-        const int att = (int)sizeof(float) * (group * c.head_dim + ATT_TILE * (c.head_dim + 1) + ATT_TILE * c.head_dim +
-                                              group * ATT_TILE + 3 * group);
-        GemvParams big{};
-        big.nseg = 1;
-        big.seg[0].type = T_Q8;
-        big.seg[0].d16 = 0;
-        big.seg[0].epi = EPI_PAIR;
-        const int widest = c.hidden_dim > c.dim ? (c.hidden_dim > c.q_dim ? c.hidden_dim : c.q_dim) : (c.dim > c.q_dim ? c.dim : c.q_dim);
-        big.cols = widest;
-        if (att > KC_MAX_SMEM || gemv_smem_bytes(big) > KC_MAX_SMEM) {
-            set_error("layer shapes exceed this build's shared-memory plan");
-            return fail(KC_E_SHAPE);
-        }
-    }
+    st = setup_step_kernel(s);
+    if (st != KC_OK) return fail(st);
     e = cudaStreamSynchronize(s->st);
     if (e != cudaSuccess) return fail(cuda_status(e, "state init"));
-    st = capture(s, true, &s->g_logits);
-    if (st == KC_OK) st = capture(s, false, &s->g_nologits);
-    if (st != KC_OK) return fail(st);
     *out = s;
     return KC_OK;
 }
@@ -605,9 +563,8 @@ extern "C" float *kc_forward(kc_state *s, int token, int pos) {
     const kc_config &c = s->c;
     if (pos < 0 || pos >= c.max_seq || token < 0 || token >= c.vocab) return nullptr;
     if (set_loop(s, token, pos, 0) != KC_OK) return nullptr;
-    cudaError_t e = cudaGraphLaunch(s->g_logits, s->st);
-    if (e != cudaSuccess) { cuda_status(e, "graph launch"); return nullptr; }
-    e = cudaMemcpyAsync(s->h_logits, s->logits, sizeof(float) * c.vocab, cudaMemcpyDeviceToHost, s->st);
+    if (run_steps(s, 1, 1) != KC_OK) return nullptr;
+    cudaError_t e = cudaMemcpyAsync(s->h_logits, s->logits, sizeof(float) * c.vocab, cudaMemcpyDeviceToHost, s->st);
     if (e != cudaSuccess) { cuda_status(e, "logits copy"); return nullptr; }
     if (finish(s) != KC_OK) return nullptr;
     return s->h_logits;
@@ -626,7 +583,8 @@ extern "C" int kc_prefill(kc_state *s, const int *tokens, int n, int pos0, float
     if (st != KC_OK) return st;
     for (int i0 = 0; i0 < n; i0 += LOGITS_RING) {
         const int k = n - i0 < LOGITS_RING ? n - i0 : LOGITS_RING;
-        for (int i = 0; i < k; i++) CK(cudaGraphLaunch(logits ? s->g_logits : s->g_nologits, s->st));
+        st = run_steps(s, k, logits ? 1 : 0);
+        if (st != KC_OK) return st;
         if (logits)
             CK(cudaMemcpyAsync(logits + (size_t)i0 * c.vocab, s->logits, sizeof(float) * (size_t)k * c.vocab,
                                cudaMemcpyDeviceToHost, s->st));
@@ -641,7 +599,10 @@ extern "C" int kc_generate_greedy(kc_state *s, int token, int pos, int n, int *o
     if (n == 0) return KC_OK;
     int st = set_loop(s, token, pos, 0);
     if (st != KC_OK) return st;
-    for (int i = 0; i < n; i++) CK(cudaGraphLaunch(s->g_logits, s->st));
+    for (int i = 0; i < n; i += 256) {
+        st = run_steps(s, n - i < 256 ? n - i : 256, 1);
+        if (st != KC_OK) return st;
+    }
     CK(cudaMemcpyAsync(out_tokens, s->out_tokens, sizeof(int) * n, cudaMemcpyDeviceToHost, s->st));
     return finish(s);
 }
@@ -652,13 +613,17 @@ extern "C" int kc_time_decode(kc_state *s, int token, int pos, int warmup, int s
     if (pos < 0 || pos + warmup + steps > c.max_seq || token < 0 || token >= c.vocab || steps < 1) return KC_E_SHAPE;
     int st = set_loop(s, token, pos, 0);
     if (st != KC_OK) return st;
-    for (int i = 0; i < warmup; i++) CK(cudaGraphLaunch(s->g_logits, s->st));
+    if (warmup > 0) {
+        st = run_steps(s, warmup, 1);
+        if (st != KC_OK) return st;
+    }
     cudaEvent_t e0, e1;
     CK(cudaEventCreate(&e0));
     CK(cudaEventCreate(&e1));
     cudaEventRecord(e0, s->st);
-    for (int i = 0; i < steps; i++) cudaGraphLaunch(s->g_logits, s->st);
+    st = run_steps(s, steps, 1);
     cudaEventRecord(e1, s->st);
+    if (st != KC_OK) return st;
     cudaError_t e = cudaEventSynchronize(e1);
     float t = 0.0f;
     if (e == cudaSuccess) e = cudaEventElapsedTime(&t, e0, e1);
@@ -666,76 +631,6 @@ extern "C" int kc_time_decode(kc_state *s, int token, int pos, int warmup, int s
     cudaEventDestroy(e1);
     if (e != cudaSuccess) return cuda_status(e, "decode timing");
     *ms = t;
-    return finish(s);
-}
-
-extern "C" int kc_time_ffn_up(kc_state *s, int layer, int reps, float *ms_per_launch, double *bytes) {
-    clear_error();
-    const kc_config &c = s->c;
-    if (layer < 0 || layer >= c.n_layers || reps < 1) return KC_E_SHAPE;
-    const DevLayer &L = s->m->d_layers[(size_t)layer];
-    if (!s->flush) {
-        s->flush_bytes = (size_t)256 << 20;   /* larger than the 126 MB L2 */
-        CK(cudaMalloc(&s->flush, s->flush_bytes));
-    }
-    GemvParams u{};
-    u.cols = c.dim; u.pro = PRO_RMSNORM_QUANT; u.x = s->x; u.norm_w = L.ffn_norm; u.eps = c.norm_eps; u.act = c.act;
-    u.seg[0] = seg_of(L.w1, EPI_PAIR, s->hb, nullptr, 1);
-    u.seg[0].q2 = L.w3.q;
-    u.seg[0].d2 = L.w3.d;
-    u.nseg = 1;
-    cudaEvent_t e0, e1;
-    CK(cudaEventCreate(&e0));
-    CK(cudaEventCreate(&e1));
-    float total = 0.0f;
-    for (int r = 0; r < reps + 1; r++) {
-        cudaMemsetAsync(s->flush, r & 0xff, s->flush_bytes, s->st);
-        cudaEventRecord(e0, s->st);
-        launch_gemv(s, u, s->st, s->err);
-        cudaEventRecord(e1, s->st);
-        cudaError_t e = cudaEventSynchronize(e1);
-        float t = 0.0f;
-        if (e == cudaSuccess) e = cudaEventElapsedTime(&t, e0, e1);
-        if (e != cudaSuccess) {
-            cudaEventDestroy(e0);
-            cudaEventDestroy(e1);
-            return cuda_status(e, "ffn-up timing");
-        }
-        if (r > 0) total += t;   /* the first launch is a warm-up */
-    }
-    cudaEventDestroy(e0);
-    cudaEventDestroy(e1);
-    *ms_per_launch = total / reps;
-    const HostMat &w1 = s->m->layers[(size_t)layer].w1, &w3 = s->m->layers[(size_t)layer].w3;
-    *bytes = (double)(w1.qbytes() + w1.dbytes() + w3.qbytes() + w3.dbytes());
-    return KC_OK;
-}
-
-extern "C" int kc_profile_step(kc_state *s, int token, int pos, float *ms) {
-    clear_error();
-    const kc_config &c = s->c;
-    if (pos < 0 || pos >= c.max_seq || token < 0 || token >= c.vocab) return KC_E_SHAPE;
-    int st = set_loop(s, token, pos, 0);
-    if (st != KC_OK) return st;
-    const int nev = 2 + 5 * c.n_layers + 1;
-    std::vector<cudaEvent_t> ev((size_t)nev);
-    for (auto &e : ev) CK(cudaEventCreate(&e));
-    int k = 0;
-    enqueue_step(s, true, ev.data(), &k);
-    CK(cudaStreamSynchronize(s->st));
-    for (int i = 0; i < 6; i++) ms[i] = 0.0f;
-    /* events: [embed] then per layer qkv, attn, wo, up, down, then [classifier], end */
-    float t;
-    cudaEventElapsedTime(&t, ev[0], ev[1]);
-    ms[5] += t;   /* embedding counted with the classifier ("other") */
-    for (int l = 0; l < c.n_layers; l++)
-        for (int j = 0; j < 5; j++) {
-            cudaEventElapsedTime(&t, ev[1 + 5 * l + j], ev[2 + 5 * l + j]);
-            ms[j] += t;
-        }
-    cudaEventElapsedTime(&t, ev[(size_t)k - 2], ev[(size_t)k - 1]);
-    ms[5] += t;
-    for (auto &e : ev) cudaEventDestroy(e);
     return finish(s);
 }
 
@@ -758,27 +653,95 @@ extern "C" int kc_debug_copy(kc_state *s, int which, void *dst, size_t bytes) {
     return KC_OK;
 }
 
+extern "C" int kc_step_timeline(kc_state *s, int token, int pos, unsigned long long *t, int cap, int *n) {
+    clear_error();
+    const kc_config &c = s->c;
+    if (pos < 0 || pos >= c.max_seq || token < 0 || token >= c.vocab) return KC_E_SHAPE;
+    int st = set_loop(s, token, pos, 0);
+    if (st == KC_OK) st = launch_steps(s, 1, 1, true);
+    if (st != KC_OK) return st;
+    unsigned cnt = 0;
+    CK(cudaMemcpyAsync(&cnt, s->timeline_n, sizeof cnt, cudaMemcpyDeviceToHost, s->st));
+    CK(cudaStreamSynchronize(s->st));
+    if (cnt > 4096) cnt = 4096;
+    if ((int)cnt > cap) cnt = (unsigned)cap;
+    CK(cudaMemcpy(t, s->timeline, sizeof(unsigned long long) * cnt, cudaMemcpyDeviceToHost));
+    *n = (int)cnt;
+    return finish(s);
+}
+
+extern "C" int kc_step_trace(kc_state *s, int token, int pos, unsigned long long *out, size_t cap, int *nphases,
+                             int *nctas) {
+    clear_error();
+    const kc_config &c = s->c;
+    if (pos < 0 || pos >= c.max_seq || token < 0 || token >= c.vocab) return KC_E_SHAPE;
+    const int P = 5 * c.n_layers + 1, G = s->num_sms;
+    const size_t n = (size_t)P * G * 3;
+    if (cap < n) return KC_E_SHAPE;
+    unsigned long long *d = nullptr;
+    CK(cudaMalloc(&d, n * sizeof(unsigned long long)));
+    int st = set_loop(s, token, pos, 0);
+    if (st == KC_OK) {
+        StepArgs save = s->sa;
+        s->sa.trace = d;
+        s->sa.trace_phases = (unsigned)P;
+        st = launch_steps(s, 1, 1, true);
+        s->sa = save;
+    }
+    cudaError_t e = cudaStreamSynchronize(s->st);
+    if (e == cudaSuccess) e = cudaMemcpy(out, d, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    if (e != cudaSuccess) return cuda_status(e, "trace");
+    if (st != KC_OK) return st;
+    *nphases = P;
+    *nctas = G;
+    return finish(s);
+}
+
+extern "C" int kc_step_events(kc_state *s, int token, int pos, unsigned long long *out, unsigned cap, int *nctas) {
+    clear_error();
+    const kc_config &c = s->c;
+    if (pos < 0 || pos >= c.max_seq || token < 0 || token >= c.vocab || cap == 0) return KC_E_SHAPE;
+    const int G = s->num_sms;
+    const size_t n = (size_t)G * 2 * cap;
+    unsigned long long *d = nullptr;
+    CK(cudaMalloc(&d, n * sizeof(unsigned long long)));
+    cudaError_t e = cudaMemset(d, 0, n * sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_evlog, &d, sizeof(d));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_evcap, &cap, sizeof(cap));
+    int st = e == cudaSuccess ? set_loop(s, token, pos, 0) : cuda_status(e, "events");
+    if (st == KC_OK) st = launch_steps(s, 1, 1, true);
+    e = cudaStreamSynchronize(s->st);
+    unsigned long long *null_log = nullptr;
+    const cudaError_t e2 = cudaMemcpyToSymbol(g_evlog, &null_log, sizeof(null_log));
+    if (e == cudaSuccess) e = e2;
+    if (e == cudaSuccess) e = cudaMemcpy(out, d, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    if (e != cudaSuccess) return cuda_status(e, "events");
+    if (st != KC_OK) return st;
+    *nctas = G;
+    return finish(s);
+}
+
 /* ------------------------------------------------------------ kernel-level */
+
+static int activation_smem(int n) { return 128 + n + 8 * (n / QK) + 16; }
 
 extern "C" int kc_quantize_q8_dev(int8_t *q, float *d, const float *x, int k, void *stream) {
     if (k <= 0 || k % QK) return KC_E_SHAPE;
-    GemvParams p{};
-    p.cols = k; p.pro = PRO_QUANT; p.x = x;
-    const int smem = gemv_smem(k);
+    const int smem = activation_smem(k);
     if (set_smem_attributes() != KC_OK || smem > KC_MAX_SMEM) return KC_E_SHAPE;
-    quantize_kernel<<<1, GEMV_THREADS, smem, (cudaStream_t)stream>>>(p, q, d, nullptr);
+    activation_kernel<<<1, NCT, smem, (cudaStream_t)stream>>>(x, nullptr, 0.0f, k, q, d, nullptr);
     CK(cudaGetLastError());
     return KC_OK;
 }
 
 extern "C" int kc_rmsnorm_quantize_dev(int8_t *q, float *d, float *xn, const float *x, const float *w, int n, float eps,
                                        void *stream) {
-    if (n <= 0 || n % QK) return KC_E_SHAPE;
-    GemvParams p{};
-    p.cols = n; p.pro = PRO_RMSNORM_QUANT; p.x = x; p.norm_w = w; p.eps = eps;
-    const int smem = gemv_smem(n);
+    if (n <= 0 || n % QK || !w) return KC_E_SHAPE;
+    const int smem = activation_smem(n);
     if (set_smem_attributes() != KC_OK || smem > KC_MAX_SMEM) return KC_E_SHAPE;
-    quantize_kernel<<<1, GEMV_THREADS, smem, (cudaStream_t)stream>>>(p, q, d, xn);
+    activation_kernel<<<1, NCT, smem, (cudaStream_t)stream>>>(x, w, eps, n, q, d, xn);
     CK(cudaGetLastError());
     return KC_OK;
 }
@@ -786,19 +749,26 @@ extern "C" int kc_rmsnorm_quantize_dev(int8_t *q, float *d, float *xn, const flo
 extern "C" int kc_matvec_dev(float *y, int type, int d_f16, const void *wq, const void *wd, int rows, int cols,
                              const int8_t *xq, const float *xd, void *stream) {
     if (rows <= 0 || cols <= 0 || cols % QK || (type != KC_Q8_0 && type != KC_Q4_0)) return KC_E_SHAPE;
-    GemvParams p{};
-    p.cols = cols; p.pro = PRO_PREQUANT; p.xq = xq; p.xd = xd;
-    DevMat w;
-    w.q = (const uint8_t *)wq; w.d = wd; w.rows = rows; w.cols = cols; w.type = type; w.d16 = d_f16;
-    p.seg[0] = seg_of(w, EPI_STORE, y, nullptr, 2);
-    p.nseg = 1;
     if (set_smem_attributes() != KC_OK) return KC_E_IO;
     if (!g_err_word) {
         CK(cudaMalloc(&g_err_word, sizeof(unsigned)));
         CK(cudaMemset(g_err_word, 0, sizeof(unsigned)));
     }
-    const int st = launch_gemv(nullptr, p, (cudaStream_t)stream, g_err_word);
-    if (st != KC_OK) return st;
+    MatvecArgs p{};
+    p.m = PMat{ (const uint8_t *)wq, wd, rows, type, d_f16 };
+    p.cols = cols; p.xq = xq; p.xd = xd; p.y = y; p.err = g_err_word;
+    p.slot_bytes = stage_slot_bytes(type, d_f16, cols, 0);
+    p.act_bytes = (cols + 8 * (cols / QK) + 15) & ~15;
+    cudaFuncAttributes fa;
+    CK(cudaFuncGetAttributes(&fa, matvec_kernel));
+    p.nstage = ring_stages(p.slot_bytes, p.act_bytes, (int)fa.sharedSizeBytes);
+    if (p.nstage < 2) return KC_E_SHAPE;
+    const int smem = smem_fixed_bytes(p.nstage, p.act_bytes) + p.nstage * p.slot_bytes;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int grid = rows < sms ? rows : sms;
+    matvec_kernel<<<grid, STEP_THREADS, smem, (cudaStream_t)stream>>>(p);
     CK(cudaGetLastError());
     return KC_OK;
 }

@@ -78,8 +78,9 @@ def lib():
             "kc_forward": (C.POINTER(F), [P, I, I]), "kc_generate_greedy": (I, [P, I, I, I, P]),
             "kc_state_free": (None, [P]),
             "kc_time_decode": (I, [P, I, I, I, I, C.POINTER(F)]),
-            "kc_time_ffn_up": (I, [P, I, I, C.POINTER(F), C.POINTER(C.c_double)]),
-            "kc_profile_step": (I, [P, I, I, P]),
+            "kc_step_timeline": (I, [P, I, I, P, I, C.POINTER(I)]),
+            "kc_step_trace": (I, [P, I, I, P, S, C.POINTER(I), C.POINTER(I)]),
+            "kc_step_events": (I, [P, I, I, P, C.c_uint, C.POINTER(I)]),
             "kc_quantize_q8_dev": (I, [P, P, P, I, P]), "kc_rmsnorm_quantize_dev": (I, [P, P, P, P, P, I, F, P]),
             "kc_matvec_dev": (I, [P, I, I, P, P, I, I, P, P, P]), "kc_block_sums_dev": (I, [P, I, P, I, I, P, P]),
             "kc_dev_alloc": (P, [S]), "kc_dev_free": (None, [P]), "kc_memcpy_htod": (I, [P, P, S]),
@@ -176,15 +177,31 @@ class State:
                "time decode")
         return ms.value
 
-    def time_ffn_up(self, layer=0, reps=20):
-        ms, b = C.c_float(), C.c_double()
-        _check(lib().kc_time_ffn_up(self._h, layer, reps, C.byref(ms), C.byref(b)), "time ffn-up")
-        return ms.value, b.value
+    def step_timeline(self, token, pos):
+        """Device clock (ns) at the start of one step and after each of its grid
+        barriers: per layer Q/K/V, attention, O, gate/up, down; then the classifier."""
+        t = np.zeros(4096, np.uint64)
+        n = C.c_int()
+        _check(lib().kc_step_timeline(self._h, int(token), int(pos), t.ctypes.data_as(C.c_void_p), 4096, C.byref(n)),
+               "timeline")
+        return t[:n.value].astype(np.int64)
 
-    def profile_step(self, token, pos):
-        ms = (C.c_float * 6)()
-        _check(lib().kc_profile_step(self._h, int(token), int(pos), ms), "profile step")
-        return dict(zip(("qkv", "attention", "wo", "ffn_up", "ffn_down", "classifier"), list(ms)))
+    def step_trace(self, token, pos):
+        """[phase, cta, 3] device clock (ns): activation prologue done, barrier arrival, release."""
+        cap = (5 * self.cfg["n_layers"] + 1) * 1024 * 3
+        t = np.zeros(cap, np.uint64)
+        P, G = C.c_int(), C.c_int()
+        _check(lib().kc_step_trace(self._h, int(token), int(pos), t.ctypes.data_as(C.c_void_p), cap, C.byref(P),
+                                   C.byref(G)), "trace")
+        return t[:P.value * G.value * 3].astype(np.int64).reshape(P.value, G.value, 3)
+
+    def step_events(self, token, pos, cap=4096):
+        """[cta, who, cap] event words of one step (clock << 8 | code); who 0 consumer, 1 producer."""
+        G = C.c_int()
+        out = np.zeros(1024 * 2 * cap, np.uint64)
+        _check(lib().kc_step_events(self._h, int(token), int(pos), out.ctypes.data_as(C.c_void_p), cap, C.byref(G)),
+               "events")
+        return out[:G.value * 2 * cap].reshape(G.value, 2, cap)
 
     def free(self):
         if self._h:
