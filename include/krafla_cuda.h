@@ -159,6 +159,21 @@ int kc_rmsnorm_quantize_dev(int8_t *q, float *d, float *xn, const float *x, cons
  * scales when d_f16 is set. Uses the decode GEMV kernel. */
 int kc_matvec_dev(float *y, int type, int d_f16, const void *wq, const void *wd, int rows, int cols,
                   const int8_t *xq, const float *xd, void *stream);
+/* No counterpart in the reference (its CPU kernels need no device memory).
+ * y = W . quantize_q8(x) for a float activation x on the device: the
+ * quantized x lives in a file-scope device scratch of the library, so the call
+ * allocates nothing, for callers that cannot allocate device memory per call
+ * (inside a captured CUDA graph, or a serving loop whose memory is fixed after
+ * set-up). cols <= KC_NOALLOC_MAX_COLS, else KC_E_SHAPE with no launch. The
+ * first call on each device looks up the scratch's address with that device
+ * current, so it should come before any stream capture. The scratch is one
+ * per device: calls that overlap in time (different streams or threads) race
+ * on it; calls on one stream are ordered. Same results as kc_quantize_q8_dev
+ * then kc_matvec_dev. */
+#define KC_NOALLOC_MAX_COLS 16384
+int kc_matvec_f32_noalloc(float *y, int type, int d_f16, const void *wq, const void *wd, int rows, int cols,
+                          const float *x, void *stream);
+
 /* The int32 block dot products s[r][b] of the same kernel code (bit exact
  * against the scalar kernels' integer sums). */
 int kc_block_sums_dev(int32_t *s, int type, const void *wq, int rows, int cols, const int8_t *xq, void *stream);

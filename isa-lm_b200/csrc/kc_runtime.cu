@@ -773,6 +773,66 @@ extern "C" int kc_matvec_dev(float *y, int type, int d_f16, const void *wq, cons
     return KC_OK;
 }
 
+/* ------------------------------------------------------------ no-allocation matvec */
+
+/* Device scratch of kc_matvec_f32_noalloc: the quantized activation
+ * (KC_NOALLOC_MAX_COLS int8 quants, then their block scales) and the ring's
+ * error word. Zero at module load; the error word is cleared on the call's
+ * stream at the start of every call. One copy per device, shared by all
+ * callers: calls that overlap in time (different streams or threads) race on
+ * it. */
+constexpr int NOALLOC_XD_OFF = KC_NOALLOC_MAX_COLS;
+constexpr int NOALLOC_ERR_OFF = NOALLOC_XD_OFF + (KC_NOALLOC_MAX_COLS / QK) * 4;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_ERR_OFF + 256];
+
+static unsigned char *g_noalloc_ptr[64];   /* the scratch's address on each device, set on first use */
+
+extern "C" int kc_matvec_f32_noalloc(float *y, int type, int d_f16, const void *wq, const void *wd, int rows, int cols,
+                                     const float *x, void *stream) {
+    clear_error();
+    if (rows <= 0 || cols <= 0 || cols % QK || (type != KC_Q8_0 && type != KC_Q4_0)) return KC_E_SHAPE;
+    if (cols > KC_NOALLOC_MAX_COLS) {
+        set_error("kc_matvec_f32_noalloc: cols " + std::to_string(cols) + " exceeds the scratch limit of " +
+                  std::to_string(KC_NOALLOC_MAX_COLS));
+        return KC_E_SHAPE;
+    }
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return KC_E_SHAPE;
+    if (!g_noalloc_ptr[dev]) {
+        /* once per device, with that device current (the first call should come before any stream capture) */
+        void *ptr = nullptr;
+        CK(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
+        g_noalloc_ptr[dev] = (unsigned char *)ptr;
+    }
+    if (set_smem_attributes() != KC_OK) return KC_E_IO;
+    unsigned char *scr = g_noalloc_ptr[dev];
+    int8_t *xq = (int8_t *)scr;
+    float *xd = (float *)(scr + NOALLOC_XD_OFF);
+    unsigned *err = (unsigned *)(scr + NOALLOC_ERR_OFF);
+    const cudaStream_t st = (cudaStream_t)stream;
+    CK(cudaMemsetAsync(err, 0, sizeof(unsigned), st));
+    const int asmem = 128 + cols + 8 * (cols / QK) + 16;
+    activation_kernel<<<1, NCT, asmem, st>>>(x, nullptr, 0.0f, cols, xq, xd, nullptr);
+    CK(cudaGetLastError());
+    MatvecArgs p{};
+    p.m = PMat{ (const uint8_t *)wq, wd, rows, type, d_f16 };
+    p.cols = cols; p.xq = xq; p.xd = xd; p.y = y; p.err = err;
+    p.slot_bytes = stage_slot_bytes(type, d_f16, cols, 0);
+    p.act_bytes = (cols + 8 * (cols / QK) + 15) & ~15;
+    cudaFuncAttributes fa;
+    CK(cudaFuncGetAttributes(&fa, matvec_kernel));
+    p.nstage = ring_stages(p.slot_bytes, p.act_bytes, (int)fa.sharedSizeBytes);
+    if (p.nstage < 2) return KC_E_SHAPE;
+    const int smem = smem_fixed_bytes(p.nstage, p.act_bytes) + p.nstage * p.slot_bytes;
+    int sms = 148;
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int grid = rows < sms ? rows : sms;
+    matvec_kernel<<<grid, STEP_THREADS, smem, st>>>(p);
+    CK(cudaGetLastError());
+    return KC_OK;
+}
+
 extern "C" int kc_block_sums_dev(int32_t *s, int type, const void *wq, int rows, int cols, const int8_t *xq,
                                  void *stream) {
     if (rows <= 0 || cols <= 0 || cols % QK || (type != KC_Q8_0 && type != KC_Q4_0)) return KC_E_SHAPE;

@@ -82,7 +82,8 @@ def lib():
             "kc_step_trace": (I, [P, I, I, P, S, C.POINTER(I), C.POINTER(I)]),
             "kc_step_events": (I, [P, I, I, P, C.c_uint, C.POINTER(I)]),
             "kc_quantize_q8_dev": (I, [P, P, P, I, P]), "kc_rmsnorm_quantize_dev": (I, [P, P, P, P, P, I, F, P]),
-            "kc_matvec_dev": (I, [P, I, I, P, P, I, I, P, P, P]), "kc_block_sums_dev": (I, [P, I, P, I, I, P, P]),
+            "kc_matvec_dev": (I, [P, I, I, P, P, I, I, P, P, P]),
+            "kc_matvec_f32_noalloc": (I, [P, I, I, P, P, I, I, P, P]), "kc_block_sums_dev": (I, [P, I, P, I, I, P, P]),
             "kc_dev_alloc": (P, [S]), "kc_dev_free": (None, [P]), "kc_memcpy_htod": (I, [P, P, S]),
             "kc_memcpy_dtoh": (I, [P, P, S]), "kc_dev_sync": (I, []),
         }
