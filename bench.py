@@ -257,7 +257,9 @@ def main():
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
         with open(tpath) as f:
-            traffic = json.load(f).get(f"{ARGS.config}:step_kernel")
+            t = json.load(f).get(f"{ARGS.config}:step_kernel")
+        if t:   # DRAM bytes of one captured step, times the K steps of the timed launch
+            traffic = int(t["bytes_per_step"]) * K
     st.prefill(toks[:-1], 0)
     tl = st.step_timeline(start_tok, start_pos)
     d = np.diff(tl) / 1000.0
