@@ -71,9 +71,14 @@ struct kc_model {
     int uploaded = 0;
     uint8_t *dev_base = nullptr;
     size_t dev_bytes = 0;
-    kc::DevMat d_tok_emb, d_wcls;
+    kc::DevMat d_tok_emb;
     const float *d_final_norm = nullptr;
-    std::vector<kc::DevLayer> d_layers;
+    std::vector<kc::DevLayer> d_layers;   /* norms and per-layer flags (the matrices live in the stream) */
+    /* the weight stream: every CTA's rows in the order a step reads them */
+    uint8_t *d_stream = nullptr;
+    size_t stream_bytes = 0;
+    unsigned long long *d_cta_base = nullptr;   /* [stream_G] */
+    int stream_G = 0;
 };
 
 #endif

@@ -112,6 +112,8 @@ extern "C" size_t kc_model_device_bytes(const kc_model *m) { return m->dev_bytes
 extern "C" void kc_model_free(kc_model *m) {
     if (!m) return;
     if (m->dev_base) cudaFree(m->dev_base);
+    if (m->d_stream) cudaFree(m->d_stream);
+    if (m->d_cta_base) cudaFree(m->d_cta_base);
     if (m->map) munmap(m->map, m->map_size);
     delete m;
 }
@@ -124,6 +126,123 @@ struct Item {
     const void **dst;
 };
 }  // namespace
+
+/* Types and shapes of the streamed matrices; KC_E_SHAPE when a matrix class
+ * changes type between layers or a matrix is not Q8_0/Q4_0. */
+static int stream_geom(const kc_model *m, StreamGeom &g) {
+    const kc_config &c = m->cfg;
+    const HostLayer &L0 = m->layers[0];
+    const HostMat &cls = m->shared ? m->tok_emb : m->wcls;
+    auto ty = [](const HostMat &h) { return h.type == KC_Q4_0 ? T_Q4 : T_Q8; };
+    g = StreamGeom{};
+    g.dim = c.dim; g.q_dim = c.q_dim; g.kv_dim = c.kv_dim; g.hidden = c.hidden_dim; g.vocab = c.vocab;
+    g.t_q = ty(L0.wq); g.t_k = ty(L0.wk); g.t_v = ty(L0.wv); g.t_o = ty(L0.wo);
+    g.t_up = ty(L0.w1); g.t_down = ty(L0.w2); g.t_cls = ty(cls);
+    g.d16_q = L0.wq.d16; g.d16_k = L0.wk.d16; g.d16_v = L0.wv.d16; g.d16_o = L0.wo.d16;
+    g.d16_up = L0.w1.d16; g.d16_down = L0.w2.d16; g.d16_cls = cls.d16;
+    g.b_q = L0.bq != nullptr; g.b_k = L0.bk != nullptr; g.b_v = L0.bv != nullptr;
+    auto same = [](const HostMat &a, const HostMat &b) { return a.type == b.type && a.d16 == b.d16; };
+    auto quant = [](const HostMat &h) { return h.type == KC_Q4_0 || h.type == KC_Q8_0; };
+    for (const HostLayer &H : m->layers) {
+        const bool ok = same(H.wq, L0.wq) && same(H.wk, L0.wk) && same(H.wv, L0.wv) && same(H.wo, L0.wo) &&
+                        same(H.w1, L0.w1) && same(H.w3, L0.w1) && same(H.w2, L0.w2) && (H.bq != nullptr) == g.b_q &&
+                        (H.bk != nullptr) == g.b_k && (H.bv != nullptr) == g.b_v && quant(H.wq) && quant(H.wk) &&
+                        quant(H.wv) && quant(H.wo) && quant(H.w1) && quant(H.w2);
+        if (!ok) {
+            set_error("weight types differ between layers or are not Q8_0/Q4_0");
+            return KC_E_SHAPE;
+        }
+    }
+    if (!quant(cls)) {
+        set_error("classifier is not Q8_0/Q4_0");
+        return KC_E_SHAPE;
+    }
+    return KC_OK;
+}
+
+/* One row record of the stream: quants, scales, bias, zero padding to rec. */
+static uint8_t *put_rec(uint8_t *dst, const HostMat &M, int r, const float *bias, int rec) {
+    const size_t qrow = M.type == KC_Q4_0 ? (size_t)M.cols / 2 : (size_t)M.cols, nb = (size_t)M.cols / KC_QK;
+    const size_t dsz = M.d16 ? 2 : 4;
+    std::memcpy(dst, (const uint8_t *)M.q + (size_t)r * qrow, qrow);
+    std::memcpy(dst + qrow, (const uint8_t *)M.d + (size_t)r * nb * dsz, nb * dsz);
+    size_t off = qrow + nb * dsz;
+    if (bias) {
+        std::memcpy(dst + off, bias + r, sizeof(float));
+        off += sizeof(float);
+    }
+    std::memset(dst + off, 0, (size_t)rec - off);
+    return dst + rec;
+}
+
+/* CTA j's stream: per layer the A, C, D, E phases of make_plan, then the classifier. */
+static size_t fill_stream(const kc_model *m, const PhasePlan *P, uint8_t *dst) {
+    const kc_config &c = m->cfg;
+    uint8_t *p = dst;
+    const HostMat &cls = m->shared ? m->tok_emb : m->wcls;
+    for (const HostLayer &H : m->layers) {
+        for (int s = 0; s < P[PH_A].nseg; s++) {
+            const Seg &S = P[PH_A].seg[s];
+            const bool isq = S.row0 < c.q_dim, isk = !isq && S.row0 < c.q_dim + c.kv_dim;
+            const HostMat &M = isq ? H.wq : isk ? H.wk : H.wv;
+            const float *bias = isq ? H.bq : isk ? H.bk : H.bv;
+            const int lo = isq ? 0 : isk ? c.q_dim : c.q_dim + c.kv_dim;
+            for (int r = 0; r < S.rows; r++) p = put_rec(p, M, S.row0 + r - lo, bias, S.rec);
+        }
+        const Seg &C = P[PH_C].seg[0];
+        for (int r = 0; r < C.rows; r++) p = put_rec(p, H.wo, C.row0 + r, nullptr, C.rec);
+        const Seg &D = P[PH_D].seg[0];
+        for (int r = 0; r < D.rows; r++) {
+            p = put_rec(p, H.w1, D.row0 + r, nullptr, D.rec / 2);
+            p = put_rec(p, H.w3, D.row0 + r, nullptr, D.rec / 2);
+        }
+        const Seg &E = P[PH_E].seg[0];
+        for (int r = 0; r < E.rows; r++) p = put_rec(p, H.w2, E.row0 + r, nullptr, E.rec);
+    }
+    const Seg &F = P[PH_F].seg[0];
+    for (int r = 0; r < F.rows; r++) p = put_rec(p, cls, F.row0 + r, nullptr, F.rec);
+    return (size_t)(p - dst);
+}
+
+static size_t stream_cta_bytes(const kc_model *m, const PhasePlan *P) {
+    return (size_t)m->cfg.n_layers * (size_t)(P[PH_A].bytes + P[PH_C].bytes + P[PH_D].bytes + P[PH_E].bytes) +
+           (size_t)P[PH_F].bytes;
+}
+
+/* The weight stream for a device of G SMs: every CTA's rows of every matrix,
+ * contiguous in the order the step kernel consumes them. */
+static int upload_stream(kc_model *m, int G) {
+    StreamGeom g;
+    int st = stream_geom(m, g);
+    if (st != KC_OK) return st;
+    std::vector<unsigned long long> base((size_t)G);
+    size_t total = 0, maxc = 0;
+    for (int j = 0; j < G; j++) {
+        PhasePlan P[NPHASE];
+        make_plan(g, j, G, P);
+        const size_t b = stream_cta_bytes(m, P);
+        base[(size_t)j] = total;
+        total += align256(b);
+        maxc = std::max(maxc, b);
+    }
+    CK(cudaMalloc(&m->d_stream, total ? total : 256));
+    CK(cudaMalloc(&m->d_cta_base, sizeof(unsigned long long) * (size_t)G));
+    CK(cudaMemcpy(m->d_cta_base, base.data(), sizeof(unsigned long long) * (size_t)G, cudaMemcpyHostToDevice));
+    std::vector<uint8_t> host(maxc ? maxc : 16);
+    for (int j = 0; j < G; j++) {
+        PhasePlan P[NPHASE];
+        make_plan(g, j, G, P);
+        const size_t b = fill_stream(m, P, host.data());
+        if (b != stream_cta_bytes(m, P)) {
+            set_error("weight stream size mismatch");
+            return KC_E_IO;
+        }
+        CK(cudaMemcpy(m->d_stream + base[(size_t)j], host.data(), b, cudaMemcpyHostToDevice));
+    }
+    m->stream_bytes = total;
+    m->stream_G = G;
+    return KC_OK;
+}
 
 extern "C" int kc_model_upload(kc_model *m) {
     clear_error();
@@ -147,16 +266,12 @@ extern "C" int kc_model_upload(kc_model *m) {
         DevLayer &D = m->d_layers[(size_t)l];
         vec(H.attn_norm, (size_t)c.dim, D.attn_norm);
         vec(H.ffn_norm, (size_t)c.dim, D.ffn_norm);
-        mat(H.wq, D.wq); mat(H.wk, D.wk); mat(H.wv, D.wv); mat(H.wo, D.wo);
-        mat(H.w1, D.w1); mat(H.w2, D.w2); mat(H.w3, D.w3);
-        vec(H.bq, (size_t)c.q_dim, D.bq); vec(H.bk, (size_t)c.kv_dim, D.bk); vec(H.bv, (size_t)c.kv_dim, D.bv);
         vec(H.q_norm, (size_t)c.head_dim, D.q_norm); vec(H.k_norm, (size_t)c.head_dim, D.k_norm);
         vec(H.post_attn_norm, (size_t)c.dim, D.post_attn_norm); vec(H.post_ffn_norm, (size_t)c.dim, D.post_ffn_norm);
         D.window = H.window;
         D.local_rope = H.local_rope;
     }
     vec(m->final_norm, (size_t)c.dim, m->d_final_norm);
-    if (!m->shared) mat(m->wcls, m->d_wcls);
     size_t total = 0;
     for (const Item &it : items) total += align256(it.bytes);
     uint8_t *base = nullptr;
@@ -171,9 +286,13 @@ extern "C" int kc_model_upload(kc_model *m) {
         *it.dst = base + off;
         off += align256(it.bytes);
     }
-    if (m->shared) m->d_wcls = m->d_tok_emb;
     m->dev_base = base;
-    m->dev_bytes = total;
+    int dev = 0, sms = 0;
+    CK(cudaGetDevice(&dev));
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    st = upload_stream(m, sms);
+    if (st != KC_OK) return st;
+    m->dev_bytes = total + m->stream_bytes;
     m->uploaded = 1;
     return KC_OK;
 }
@@ -249,9 +368,9 @@ static int set_smem_attributes() {
 }
 
 /* Ring depth that fits beside the fixed part of a streaming CTA's shared memory. */
-static int ring_stages(int slot, int act_bytes, int static_bytes) {
+static int ring_stages(int slot, int act_bytes, int static_bytes, int res_bytes = 0) {
     int nst = 16;
-    while (nst >= 2 && smem_fixed_bytes(nst, act_bytes) + nst * slot > KC_MAX_SMEM - static_bytes) nst--;
+    while (nst >= 2 && smem_fixed_bytes(nst, act_bytes, res_bytes) + nst * slot > KC_MAX_SMEM - static_bytes) nst--;
     return nst;
 }
 
@@ -326,26 +445,41 @@ static PMat pmat(const DevMat &m) { return PMat{ m.q, m.d, m.rows, m.type, m.d16
 static int setup_step_kernel(kc_state *s) {
     const kc_config &c = s->c;
     kc_model *m = s->m;
+    const int G = s->num_sms;
+    if (m->stream_G != G) {
+        set_error("the model was uploaded for a device with another SM count");
+        return KC_E_SHAPE;
+    }
+    if ((c.dim + G - 1) / G > OWN_MAX) {
+        set_error("dim too large for the rows of x a CTA keeps in shared memory");
+        return KC_E_SHAPE;
+    }
+    StreamGeom g;
+    int st = stream_geom(m, g);
+    if (st != KC_OK) return st;
     std::vector<LayerPlan> plan((size_t)c.n_layers);
     const size_t lkv = (size_t)c.max_seq * c.kv_dim;
-    int slot = 0;
-    auto fit = [&](const DevMat &w, int cols, int pair) {
-        const int b = stage_slot_bytes(w.type, w.d16, cols, pair);
-        slot = b > slot ? b : slot;
-    };
     for (int l = 0; l < c.n_layers; l++) {
         const DevLayer &L = m->d_layers[(size_t)l];
         LayerPlan &P = plan[(size_t)l];
-        P.wq = pmat(L.wq); P.wk = pmat(L.wk); P.wv = pmat(L.wv); P.wo = pmat(L.wo);
-        P.w1 = pmat(L.w1); P.w3 = pmat(L.w3); P.w2 = pmat(L.w2);
-        P.attn_norm = L.attn_norm; P.ffn_norm = L.ffn_norm; P.bq = L.bq; P.bk = L.bk; P.bv = L.bv;
+        P.attn_norm = L.attn_norm; P.ffn_norm = L.ffn_norm;
         P.kc = s->kc + (size_t)l * lkv; P.vc = s->vc + (size_t)l * lkv;
         P.rcos = L.local_rope ? s->lcos : s->rcos; P.rsin = L.local_rope ? s->lsin : s->rsin;
         P.window = L.window;
-        fit(L.wq, c.dim, 0); fit(L.wk, c.dim, 0); fit(L.wv, c.dim, 0); fit(L.wo, c.q_dim, 0);
-        fit(L.w1, c.dim, 1); fit(L.w2, c.hidden_dim, 0);
     }
-    fit(m->d_wcls, c.dim, 0);
+    int slot = 0, res = 0;
+    for (int j = 0; j < G; j++) {
+        PhasePlan P[NPHASE];
+        make_plan(g, j, G, P);
+        slot = std::max(slot, plan_max_chunk(P));
+        for (int p = 0; p < NPHASE; p++) {
+            int rows = 0;
+            for (int k = 0; k < P[p].nseg; k++) rows += P[p].seg[k].rows;
+            res = std::max(res, rows * (p == PH_D ? 8 : 4));
+        }
+    }
+    slot = (slot + 127) & ~127;
+    res = (res + 15) & ~15;
     CK(cudaMalloc(&s->d_plan, sizeof(LayerPlan) * plan.size()));
     CK(cudaMemcpy(s->d_plan, plan.data(), sizeof(LayerPlan) * plan.size(), cudaMemcpyHostToDevice));
     const int group = c.n_heads / c.n_kv_heads;
@@ -353,14 +487,18 @@ static int setup_step_kernel(kc_state *s) {
     int act = 0;
     for (int cols : { c.dim, c.q_dim, c.hidden_dim }) act = std::max(act, cols + 8 * (cols / QK));
     act = (std::max(act, att_bytes) + 15) & ~15;
+    if (c.dim > 4 * 2048 || c.q_dim > 8 * 2048 || c.hidden_dim > 8 * 2048) {
+        set_error("activation wider than the step kernel's prologue (dim 8192, q_dim and hidden 16384)");
+        return KC_E_SHAPE;
+    }
     cudaFuncAttributes fa;
     CK(cudaFuncGetAttributes(&fa, step_kernel));
-    const int nst = ring_stages(slot, act, (int)fa.sharedSizeBytes);
+    const int nst = ring_stages(slot, act, (int)fa.sharedSizeBytes, res);
     if (nst < 2) {
         set_error("layer shapes leave no room for the weight ring in shared memory");
         return KC_E_SHAPE;
     }
-    s->step_smem = smem_fixed_bytes(nst, act) + nst * slot;
+    s->step_smem = smem_fixed_bytes(nst, act, res) + nst * slot;
     int per_sm = 0;
     CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, step_kernel, STEP_THREADS, s->step_smem));
     if (per_sm < 1) {
@@ -370,7 +508,9 @@ static int setup_step_kernel(kc_state *s) {
     StepArgs &a = s->sa;
     a.layers = s->d_plan;
     a.emb = pmat(m->d_tok_emb);
-    a.cls = pmat(m->d_wcls);
+    a.stream = m->d_stream;
+    a.cta_base = m->d_cta_base;
+    a.geom = g;
     a.final_norm = m->d_final_norm;
     a.inv0 = s->inv0;
     a.x = s->x; a.qkv = s->qkv; a.ao = s->ao; a.hb = s->hb; a.logits = s->logits; a.part = s->part; a.ssp = s->ssp;
@@ -381,7 +521,7 @@ static int setup_step_kernel(kc_state *s) {
     a.eps = c.norm_eps; a.attn_scale = c.attn_scale; a.attn_softcap = c.attn_softcap; a.final_softcap = c.final_softcap;
     a.embed_scale = c.embed_scale; a.act = c.act;
     a.nsplit = std::min(MAX_NSPLIT, std::max(1, s->num_sms / c.n_kv_heads));
-    a.nstage = nst; a.slot_bytes = slot; a.act_bytes = act;
+    a.nstage = nst; a.slot_bytes = slot; a.act_bytes = act; a.res_bytes = res;
     a.timeline = nullptr; a.timeline_n = s->timeline_n; a.timeline_cap = 4096;
     return KC_OK;
 }

@@ -1,16 +1,18 @@
 /* The decode token loop as one persistent kernel (sm_100a), and the
  * kernel-level kernels that run the same device code.
  *
- * Streaming CTA: NCW consumer warps + 1 producer warp, one CTA per SM. Each
- * CTA owns a fixed 1/G share of the rows of every weight matrix. The producer
- * streams those rows (quants and block scales, contiguous in HBM) through a
- * shared-memory ring with bulk copies in the order the step uses them (per
- * layer: Q/K/V, O, gate+up, down; then the classifier), waiting only for free
- * ring slots, so HBM keeps streaming while the consumers wait at phase
- * boundaries.
+ * Weight stream. At upload, every CTA's rows of every matrix are laid out
+ * contiguously in HBM in the order a step consumes them — per layer the fused
+ * Q|K|V rows, the O rows, the gate|up row pairs, the down rows; then the
+ * classifier rows — each row one record: quants, block scales, bias. The
+ * producer warp of a CTA streams its own byte range into a ring of
+ * shared-memory slots, one bulk copy per chunk of whole rows (<= 32 KB), the
+ * slots handed over with full/empty mbarriers. Copies are few and large, and
+ * the ring holds the next ~190 KB of the CTA's weights across phase and layer
+ * boundaries, so HBM keeps streaming while the consumers wait at barriers.
  *
- * The consumers run the phases of a step, separated by grid barriers (an
- * arrival counter in global memory; every wait is bounded):
+ * The 16 consumer warps run the phases of a step, separated by grid barriers
+ * (an arrival counter in global memory; every wait is bounded):
  *   A  RMSNorm + quantize x (layer 0: the embedding row, its 1/rms from the
  *      host table) -> Q/K/V rows (+ biases)            model/transformer.c:270-277
  *   B  attention work items (KV head, position range): RoPE, this position's
@@ -24,10 +26,15 @@
  * Several steps run in one launch: the token of step s+1 is the argmax of
  * step s (greedy) or the next prompt token (prefill).
  *
+ * Each CTA owns the same rows of x in phases C and E; it keeps them in shared
+ * memory (the residual add reads no global memory) and publishes their sum of
+ * squares with its barrier arrival, so the next RMSNorm adds G partial sums
+ * instead of reading x twice.
+ *
  * Quantized activations follow the reference's rule bit for bit
  * (kernels/scalar/k_scalar.c:39-57); block dot products are exact int32
  * (dp4a); the float scale-accumulate is (float)s * d_w * d_x per block
- * (k_scalar.c:4-37) summed in lane and warp-tree order.
+ * (k_scalar.c:4-37) summed in lane order, then across the warp in a fixed tree.
  */
 #pragma once
 #include "kc_kernels.cuh"
@@ -41,26 +48,134 @@ struct PMat {
 };
 
 struct LayerPlan {
-    PMat wq, wk, wv, wo, w1, w3, w2;
-    const float *attn_norm, *ffn_norm, *bq, *bk, *bv;
+    const float *attn_norm, *ffn_norm;
     float *kc, *vc;                 /* this layer's F32 cache [max_seq][kv_dim] */
     const float *rcos, *rsin;       /* RoPE tables of this layer */
     int window;
 };
 
+/* ------------------------------------------------------------ the weight stream */
+
+/* Types of the streamed matrices (a matrix class has one type in every layer,
+ * model/mlb.c:172) and the shapes. */
+struct StreamGeom {
+    int dim, q_dim, kv_dim, hidden, vocab;
+    int t_q, t_k, t_v, t_o, t_up, t_down, t_cls;         /* T_Q8 / T_Q4 */
+    int d16_q, d16_k, d16_v, d16_o, d16_up, d16_down, d16_cls;
+    int b_q, b_k, b_v;                                     /* rows carry a bias */
+};
+
+/* A run of one matrix's rows in a CTA's stream. */
+struct Seg {
+    int rows;    /* rows of this CTA */
+    int row0;    /* first output row */
+    int rec;     /* bytes per record (a gate|up pair: both records) */
+    int rpc;     /* records per chunk */
+    int type, d16, bias;
+};
+
+struct PhasePlan {
+    Seg seg[3];
+    int nseg, cols;
+    long long bytes;
+};
+
+enum { PH_A = 0, PH_C = 1, PH_D = 2, PH_E = 3, PH_F = 4, NPHASE = 5 };
+constexpr int CHUNK_BYTES = 32 * 1024;   /* bytes per bulk copy (at least one record) */
+constexpr int GROUP_ROWS = 4;            /* rows per warp task (two gate|up pairs) */
+constexpr int OWN_MAX = 128;             /* rows of x a CTA may own */
+
+/* Record bytes: quants, scales, the bias when present, padded to 16. */
+__host__ __device__ inline int rec_bytes(int type, int d16, int cols, int bias) {
+    const int q = type == T_Q4 ? cols / 2 : cols, d = (cols / QK) * (d16 ? 2 : 4);
+    return (q + d + (bias ? 4 : 0) + 15) & ~15;
+}
+
+/* Rows [r0, r1) of a `rows`-row matrix owned by CTA j of G. */
+__host__ __device__ inline void share_rows(int rows, int j, int G, int &r0, int &r1) {
+    r0 = (int)((long long)rows * j / G);
+    r1 = (int)((long long)rows * (j + 1) / G);
+}
+
+__host__ __device__ inline Seg make_seg(int rows, int row0, int type, int d16, int cols, int bias, int pair) {
+    Seg s;
+    s.rows = rows;
+    s.row0 = row0;
+    s.type = type;
+    s.d16 = d16;
+    s.bias = bias;
+    s.rec = rec_bytes(type, d16, cols, bias) * (pair ? 2 : 1);
+    const int step = pair ? GROUP_ROWS / 2 : GROUP_ROWS;
+    int rpc = CHUNK_BYTES / s.rec;
+    if (rpc >= step) rpc -= rpc % step;
+    s.rpc = rpc < 1 ? 1 : rpc;
+    return s;
+}
+
+/* The phases of CTA j's stream for one layer (A, C, D, E) and the classifier (F). */
+__host__ __device__ inline void make_plan(const StreamGeom &g, int j, int G, PhasePlan *P) {
+    int r0, r1;
+    PhasePlan &A = P[PH_A];
+    A.nseg = 0;
+    A.cols = g.dim;
+    const int na = g.q_dim + 2 * g.kv_dim;
+    share_rows(na, j, G, r0, r1);
+    const int lo[3] = { 0, g.q_dim, g.q_dim + g.kv_dim }, hi[3] = { g.q_dim, g.q_dim + g.kv_dim, na };
+    const int ty[3] = { g.t_q, g.t_k, g.t_v }, dd[3] = { g.d16_q, g.d16_k, g.d16_v }, bb[3] = { g.b_q, g.b_k, g.b_v };
+    for (int m = 0; m < 3; m++) {
+        const int s0 = r0 > lo[m] ? r0 : lo[m], s1 = r1 < hi[m] ? r1 : hi[m];
+        if (s1 > s0) A.seg[A.nseg++] = make_seg(s1 - s0, s0, ty[m], dd[m], g.dim, bb[m], 0);
+    }
+    share_rows(g.dim, j, G, r0, r1);
+    P[PH_C].nseg = 1;
+    P[PH_C].cols = g.q_dim;
+    P[PH_C].seg[0] = make_seg(r1 - r0, r0, g.t_o, g.d16_o, g.q_dim, 0, 0);
+    P[PH_E].nseg = 1;
+    P[PH_E].cols = g.hidden;
+    P[PH_E].seg[0] = make_seg(r1 - r0, r0, g.t_down, g.d16_down, g.hidden, 0, 0);
+    share_rows(g.hidden, j, G, r0, r1);
+    P[PH_D].nseg = 1;
+    P[PH_D].cols = g.dim;
+    P[PH_D].seg[0] = make_seg(r1 - r0, r0, g.t_up, g.d16_up, g.dim, 0, 1);
+    share_rows(g.vocab, j, G, r0, r1);
+    P[PH_F].nseg = 1;
+    P[PH_F].cols = g.dim;
+    P[PH_F].seg[0] = make_seg(r1 - r0, r0, g.t_cls, g.d16_cls, g.dim, 0, 0);
+    for (int p = 0; p < NPHASE; p++) {
+        long long b = 0;
+        for (int s = 0; s < P[p].nseg; s++) b += (long long)P[p].seg[s].rows * P[p].seg[s].rec;
+        P[p].bytes = b;
+    }
+}
+
+/* Largest chunk of a plan: the ring's slot size. */
+__host__ __device__ inline int plan_max_chunk(const PhasePlan *P) {
+    int m = 0;
+    for (int p = 0; p < NPHASE; p++)
+        for (int s = 0; s < P[p].nseg; s++) {
+            const Seg &S = P[p].seg[s];
+            const int c = (S.rows < S.rpc ? S.rows : S.rpc) * S.rec;
+            m = c > m ? c : m;
+        }
+    return m;
+}
+
 struct StepArgs {
     const LayerPlan *layers;        /* device array [n_layers] */
-    PMat emb, cls;
+    PMat emb;
+    const uint8_t *stream;          /* the weight stream */
+    const unsigned long long *cta_base;   /* [G] byte offset of each CTA's stream */
+    StreamGeom geom;
     const float *final_norm, *inv0;
     float *x, *qkv, *ao, *hb, *logits, *part;
-    float *ssp;                     /* [G] per-CTA sum of squares of the x rows it last wrote */
+    float *ssp;                     /* [G] per-CTA sum of squares of the x rows it owns */
     unsigned *att_counter, *bar, *err;
     LoopState *ls;
     const int *feed;
     int *out_tokens;
     int n_layers, dim, q_dim, kv_dim, hidden, vocab, max_seq, n_heads, n_kv_heads, hd;
     float eps, attn_scale, attn_softcap, final_softcap, embed_scale;
-    int act, nsplit, nstage, slot_bytes, act_bytes;
+    int act, nsplit, nstage, slot_bytes, act_bytes, res_bytes;
     int nsteps, run_cls;            /* steps in this launch; run the classifier */
     unsigned long long *timeline;   /* optional: globaltimer at start and after each barrier (CTA 0) */
     unsigned *timeline_n;
@@ -88,7 +203,7 @@ __device__ __forceinline__ void ev_init(bool enabled) {
 }
 
 enum { EV_PRO_DONE = 2, EV_STAGE_READY = 3, EV_STAGE_DONE = 4, EV_ARRIVE = 5, EV_RELEASE = 6, EV_EMPTY_WAIT = 7,
-       EV_ISSUE = 8 };
+       EV_ISSUE = 8, EV_ACT_ENTRY = 9, EV_ACT_LOADED = 10, EV_ACT_INV = 11, EV_ACT_QUANT = 12 };
 
 __device__ __forceinline__ void ev(int who, unsigned code) {
     unsigned long long *log = s_evp;
@@ -163,19 +278,30 @@ __device__ __forceinline__ void wait_count(const StepArgs &a, unsigned target) {
 
 /* Grid barrier: every CTA arrives once; `expect` (the same in every CTA)
  * counts the arrivals due so far in this launch (the host zeroes the counter
- * before each launch). */
-__device__ __forceinline__ void grid_barrier(const StepArgs &a, unsigned &expect) {
+ * before each launch). With own set, warp 0 first stores the sum of squares
+ * of the CTA's nown rows of x into ssp[blockIdx.x], ordered before the
+ * arrival by thread 0's fence. */
+__device__ __forceinline__ void grid_barrier(const StepArgs &a, unsigned &expect, const float *own = nullptr,
+                                             int nown = 0) {
     consumer_sync();
     const unsigned p = expect / gridDim.x;
     expect += gridDim.x;
-    if (threadIdx.x == 0) {
-        trace_mark(a, p, 1);
-        ev(0, EV_ARRIVE);
-        __threadfence();
-        atomicAdd(a.bar, 1u);
-        wait_count(a, expect);
-        trace_mark(a, p, 2);
-        ev(0, EV_RELEASE);
+    if (threadIdx.x < 32) {
+        if (own) {
+            float t = 0.0f;
+            for (int i = threadIdx.x; i < nown; i += 32) t += own[i] * own[i];
+            t = warp_sum(t);
+            if (threadIdx.x == 0) a.ssp[blockIdx.x] = t;
+        }
+        if (threadIdx.x == 0) {
+            trace_mark(a, p, 1);
+            ev(0, EV_ARRIVE);
+            __threadfence();
+            atomicAdd(a.bar, 1u);
+            wait_count(a, expect);
+            trace_mark(a, p, 2);
+            ev(0, EV_RELEASE);
+        }
     }
     consumer_sync();
 }
@@ -186,395 +312,520 @@ struct Ring {
     uint64_t *full, *empty;
     uint8_t *base;
     int nstage, slot_bytes;
-    unsigned idx;   /* tiles issued (producer) or consumed (consumer) so far */
+    unsigned idx;   /* chunks issued (producer) or consumed (consumer) so far */
 };
 
-/* Rows [r0, r1) of a `rows`-row matrix owned by CTA j of G. */
-__device__ __forceinline__ void share_rows(int rows, int j, int G, int &r0, int &r1) {
-    r0 = (int)((long long)rows * j / G);
-    r1 = (int)((long long)rows * (j + 1) / G);
+/* Producer: waits for the chunk's slot to be free and issues its bulk copy. */
+__device__ __forceinline__ uint8_t *ring_issue(Ring &rg, unsigned bytes, unsigned *err) {
+    const int slot = (int)(rg.idx % (unsigned)rg.nstage);
+    ev(1, EV_EMPTY_WAIT);
+    if (rg.idx >= (unsigned)rg.nstage && !mbar_wait(&rg.empty[slot], (rg.idx / rg.nstage - 1) & 1u, err))
+        atomicOr(err, 2u);
+    mbar_expect_tx(&rg.full[slot], bytes);
+    return rg.base + (size_t)slot * rg.slot_bytes;
 }
 
-/* Producer: issue the tiles of rows [r0, r1) of m (and of m2 when pair). */
-__device__ __forceinline__ void produce_rows(Ring &rg, const PMat &m, const PMat *m2, int cols, int r0, int r1,
-                                             unsigned *err) {
+/* Producer: the chunks of one phase of the stream, from src on. */
+__device__ __forceinline__ void produce_phase(Ring &rg, const PhasePlan &P, const uint8_t *&src, unsigned *err) {
+    for (int s = 0; s < P.nseg; s++) {
+        const Seg &S = P.seg[s];
+        for (int r = 0; r < S.rows; r += S.rpc) {
+            const int n = min(S.rpc, S.rows - r);
+            const unsigned bytes = (unsigned)(n * S.rec);
+            const int slot = (int)(rg.idx % (unsigned)rg.nstage);
+            uint8_t *dst = ring_issue(rg, bytes, err);
+            bulk_g2s(dst, src, bytes, &rg.full[slot]);
+            src += bytes;
+            ev(1, EV_ISSUE);
+            rg.idx++;
+        }
+    }
+}
+
+/* Producer of the kernel-level matvec: rows [r0, r1) of m in the file's
+ * layout, a stage holding the quants of R rows then their scales (copied
+ * from the 16-byte boundary below them). */
+__device__ __forceinline__ void produce_rows(Ring &rg, const PMat &m, int cols, int r0, int r1, unsigned *err) {
     if (r0 >= r1) return;
-    const int pair = m2 != nullptr;
     int R, qbytes, dbytes;
-    stage_geom(m.type, m.d16, cols, pair, R, qbytes, dbytes);
+    stage_geom(m.type, m.d16, cols, 0, R, qbytes, dbytes);
     const int qrow = m.type == T_Q4 ? cols / 2 : cols, drow = (cols / QK) * (m.d16 ? 2 : 4);
     for (int ra = r0; ra < r1; ra += R) {
-        const int slot = (int)(rg.idx % (unsigned)rg.nstage);
-        ev(1, EV_EMPTY_WAIT);
-        if (rg.idx >= (unsigned)rg.nstage && !mbar_wait(&rg.empty[slot], (rg.idx / rg.nstage - 1) & 1u, err))
-            atomicOr(err, 2u);
         const int nr = min(R, r1 - ra);
         const size_t ds = (size_t)ra * drow, de = (size_t)(ra + nr) * drow;
         const size_t das = ds & ~(size_t)15, dae = (de + 15) & ~(size_t)15;
         const unsigned qb = (unsigned)(nr * qrow), db = (unsigned)(dae - das);
-        uint8_t *dst = rg.base + (size_t)slot * rg.slot_bytes;
-        mbar_expect_tx(&rg.full[slot], (qb + db) * (pair ? 2u : 1u));
+        const int slot = (int)(rg.idx % (unsigned)rg.nstage);
+        uint8_t *dst = ring_issue(rg, qb + db, err);
         bulk_g2s(dst, m.q + (size_t)ra * qrow, qb, &rg.full[slot]);
         bulk_g2s(dst + qbytes, (const uint8_t *)m.d + das, db, &rg.full[slot]);
-        if (pair) {
-            bulk_g2s(dst + qbytes + dbytes, m2->q + (size_t)ra * qrow, qb, &rg.full[slot]);
-            bulk_g2s(dst + 2 * qbytes + dbytes, (const uint8_t *)m2->d + das, db, &rg.full[slot]);
-        }
-        ev(1, EV_ISSUE);
         rg.idx++;
     }
 }
 
 /* ------------------------------------------------------------ consumers */
 
+/* The quantized activation in shared memory: elements 0..15 of block b at
+ * xlo[b], 16..31 at xhi[b] (16 bytes each, so a warp's loads of consecutive
+ * blocks are conflict-free), the block scales and 8 * the sum of each block's
+ * quants (the Q4 offset term). */
 struct Act {
-    const int8_t *xq;   /* [cols] quantized activation */
-    const float *xd;    /* [cols/32] its scales */
-    const int *xs;      /* [cols/32] 8 * sum of each block's quants */
+    const int4 *xlo, *xhi;
+    const float *xd;
+    const int *xs;
 };
 
-struct Epi {
-    int kind;           /* EPI_STORE / EPI_RESID / EPI_PAIR / EPI_LOGITS */
-    float *out;
-    const float *bias;
-    int act;            /* EPI_PAIR: 0 SiLU, 1 GELU */
-    float softcap;      /* EPI_LOGITS: final soft-cap, 0 = none */
-    int logit_row0;     /* EPI_LOGITS: offset of this step's logits row */
+struct ActW {
+    int8_t *xlo, *xhi;
+    float *xd;
+    int *xs;
 };
 
-__device__ __forceinline__ void epilogue(const Epi &e, int row, float acc, float acc2, unsigned long long &best) {
-    switch (e.kind) {
-    case EPI_STORE: e.out[row] = e.bias ? __fadd_rn(acc, e.bias[row]) : acc; break;
-    case EPI_RESID: e.out[row] = __fadd_rn(e.out[row], acc); break;
-    case EPI_PAIR: e.out[row] = act_mul(e.act, acc, acc2); break;
-    case EPI_LOGITS: {
-        float v = acc;
-        if (e.softcap > 0.0f) v = __fmul_rn(e.softcap, tanhf(__fdiv_rn(v, e.softcap)));
-        e.out[e.logit_row0 + row] = v;
-        const unsigned long long k = argmax_key(v, row);
-        best = k > best ? k : best;
-        break;
-    }
-    }
+__device__ __forceinline__ ActW act_layout(unsigned char *act, int cols) {
+    const int nb = cols / QK;
+    ActW w;
+    w.xlo = (int8_t *)act;
+    w.xhi = (int8_t *)act + nb * 16;
+    w.xd = (float *)(act + cols);
+    w.xs = (int *)(w.xd + nb);
+    return w;
 }
 
-template <bool D16>
-__device__ __forceinline__ float sm_scale(const uint8_t *dr, int b) {
-    if constexpr (D16) return __half2float(((const __half *)dr)[b]);
-    else return ((const float *)dr)[b];
+__device__ __forceinline__ Act act_view(const ActW &w) {
+    return Act{ (const int4 *)w.xlo, (const int4 *)w.xhi, w.xd, w.xs };
 }
 
-/* Dot products of nr (<= NR) weight rows held in shared memory (quants of row
- * r at q + r*qrow, scales at d + r*drow; with PAIR the second matrix at q2, d2)
- * against the activation, over the 32-chunk slices s0, s0 + sstep, ... of the
- * rows. Chunks are 16 bytes: a Q4 block or half a Q8 block. The activation of
- * a chunk is loaded once for all rows. Warp-reduced into acc[r][0..1]. */
-template <int TYPE, bool D16, bool PAIR, int NR>
-__device__ __forceinline__ void dot_rows(const uint8_t *q, const uint8_t *d, const uint8_t *q2, const uint8_t *d2,
-                                         int qrow, int drow, int nr, int s0, int sstep, int nch, const Act &x, int lane,
-                                         float (&acc)[NR][2]) {
-    constexpr int CPB = TYPE == T_Q4 ? 1 : 2;
-    const int4 *x4 = (const int4 *)x.xq;
+__device__ __forceinline__ float sm_scale(const uint8_t *dr, int b, bool d16) {
+    return d16 ? __half2float(((const __half *)dr)[b]) : ((const float *)dr)[b];
+}
+
+/* Sum over the warp of four values at once: returns, on lanes 8q..8q+7, the
+ * total of t[q] (two exchange levels, then three butterfly levels). */
+__device__ __forceinline__ float reduce4(const float (&t)[4], int lane) {
+    const bool h16 = (lane & 16) != 0, h8 = (lane & 8) != 0;
+    float k0 = h16 ? t[2] : t[0], k1 = h16 ? t[3] : t[1];
+    const float s0 = h16 ? t[0] : t[2], s1 = h16 ? t[1] : t[3];
+    k0 += __shfl_xor_sync(0xffffffffu, s0, 16);
+    k1 += __shfl_xor_sync(0xffffffffu, s1, 16);
+    float k = h8 ? k1 : k0;
+    const float s = h8 ? k0 : k1;
+    k += __shfl_xor_sync(0xffffffffu, s, 8);
+    k += __shfl_xor_sync(0xffffffffu, k, 4);
+    k += __shfl_xor_sync(0xffffffffu, k, 2);
+    k += __shfl_xor_sync(0xffffffffu, k, 1);
+    return k;
+}
+
+/* Row addressing inside a ring slot: row i's quants at q + i*qs, its scales
+ * at d + i*ds; with PAIR the second matrix's record p2 bytes further. */
+struct Lay {
+    int qs, db, ds, p2;
+};
+
+/* Dot products of nr (<= NR) rows against the activation, lane b taking
+ * blocks b, b+32, ...; each block's int32 sum is exact (dp4a), scaled as
+ * (float)s * d_w * d_x and accumulated in block order per lane. Returns
+ * reduce4 of the accumulators: {row0, row1, row2, row3}, or with PAIR
+ * {gate0, up0, gate1, up1}. */
+template <int TYPE, bool PAIR>
+__device__ __forceinline__ float dot_group(const uint8_t *q, const uint8_t *d, const Lay &L, int nb, int nr,
+                                           const Act &x, int lane, bool d16) {
+    constexpr int NR = PAIR ? GROUP_ROWS / 2 : GROUP_ROWS;
+    constexpr int NA = PAIR ? 2 : 1;
+    float acc[NR][NA];
 #pragma unroll
-    for (int r = 0; r < NR; r++) acc[r][0] = acc[r][1] = 0.0f;
-    for (int s = s0; s * 32 < nch; s += sstep) {
-        const int c = s * 32 + lane;
-        const bool ok = c < nch;
-        const int b = c / CPB;
-        if constexpr (TYPE == T_Q4) {
-            if (ok) {
-                const int4 xlo = x4[2 * b], xhi = x4[2 * b + 1];
-                const float dx = x.xd[b];
-                const int corr = x.xs[b];
+    for (int i = 0; i < NR; i++)
 #pragma unroll
-                for (int r = 0; r < NR; r++) {
-                    if (r < nr) {
-                        const uint4 w = *(const uint4 *)(q + r * qrow + 16 * c);
-                        acc[r][0] += __fmul_rn((float)(dot_q4(w, xlo, xhi) - corr), sm_scale<D16>(d + r * drow, b)) * dx;
-                        if constexpr (PAIR) {
-                            const uint4 w2 = *(const uint4 *)(q2 + r * qrow + 16 * c);
-                            acc[r][1] += __fmul_rn((float)(dot_q4(w2, xlo, xhi) - corr), sm_scale<D16>(d2 + r * drow, b)) * dx;
-                        }
+        for (int k = 0; k < NA; k++) acc[i][k] = 0.0f;
+#pragma unroll 2
+    for (int b = lane; b < nb; b += 32) {
+        const int4 xl = x.xlo[b], xh = x.xhi[b];
+        const float dx = x.xd[b];
+        const int corr = TYPE == T_Q4 ? x.xs[b] : 0;
+#pragma unroll
+        for (int i = 0; i < NR; i++) {
+            if (i < nr) {
+#pragma unroll
+                for (int k = 0; k < NA; k++) {
+                    const uint8_t *qr = q + i * L.qs + k * L.p2, *dr = d + i * L.ds + k * L.p2;
+                    int s;
+                    if constexpr (TYPE == T_Q4) {
+                        s = dot_q4(*(const uint4 *)(qr + 16 * b), xl, xh) - corr;
+                    } else {
+                        s = dot_q8(*(const uint4 *)(qr + 32 * b), xl) + dot_q8(*(const uint4 *)(qr + 32 * b + 16), xh);
                     }
+                    acc[i][k] += __fmul_rn((float)s, sm_scale(dr, b, d16)) * dx;
                 }
             }
+        }
+    }
+    float t[4];
+    if constexpr (PAIR) {
+        t[0] = acc[0][0];
+        t[1] = acc[0][NA - 1];
+        t[2] = acc[NR - 1][0];
+        t[3] = acc[NR - 1][NA - 1];
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; i++) t[i] = acc[i < NR ? i : NR - 1][0];
+    }
+    return reduce4(t, lane);
+}
+
+/* The rows [0, n) of one ring slot, in tasks of GROUP_ROWS rows (or pairs)
+ * dealt to the warps round-robin by the task's index in the phase (g0 + k),
+ * so the warps stay evenly loaded across chunks. Results (with the record's
+ * bias added) go to res[i0 + i] (pairs: res2[i0 + i] = {gate, up}); with res
+ * null, single rows are stored straight to out[i0 + i]. */
+template <int TYPE, bool PAIR>
+__device__ __forceinline__ void consume_chunk(const uint8_t *slot, const Lay &L, int n, int nb, int boff, bool d16,
+                                              int g0, int i0, const Act &x, float *res, float *out, int lane, int warp) {
+    constexpr int NR = PAIR ? GROUP_ROWS / 2 : GROUP_ROWS;
+    const int ng = (n + NR - 1) / NR;
+    for (int k = (warp - g0 % NCW + NCW) % NCW; k < ng; k += NCW) {
+        const int r = k * NR, nr = min(NR, n - r);
+        const uint8_t *q = slot + r * L.qs, *d = slot + L.db + r * L.ds;
+        float v = dot_group<TYPE, PAIR>(q, d, L, nb, nr, x, lane, d16);
+        if constexpr (PAIR) {
+            const float u = __shfl_down_sync(0xffffffffu, v, 8);
+            const int i = lane >> 4;
+            if ((lane & 15) == 0 && i < nr) ((float2 *)res)[i0 + r + i] = make_float2(v, u);
         } else {
-            const int4 xv = ok ? x4[c] : make_int4(0, 0, 0, 0);
-            const float dx = ok ? x.xd[b] : 0.0f;
-#pragma unroll
-            for (int r = 0; r < NR; r++) {
-                if (r < nr) {
-                    int t0 = ok ? dot_q8(*(const uint4 *)(q + r * qrow + 16 * c), xv) : 0;
-                    t0 += __shfl_xor_sync(0xffffffffu, t0, 1);   /* both halves of the block */
-                    if (ok && !(lane & 1)) acc[r][0] += __fmul_rn((float)t0, sm_scale<D16>(d + r * drow, b)) * dx;
-                    if constexpr (PAIR) {
-                        int t1 = ok ? dot_q8(*(const uint4 *)(q2 + r * qrow + 16 * c), xv) : 0;
-                        t1 += __shfl_xor_sync(0xffffffffu, t1, 1);
-                        if (ok && !(lane & 1)) acc[r][1] += __fmul_rn((float)t1, sm_scale<D16>(d2 + r * drow, b)) * dx;
-                    }
-                }
+            const int i = lane >> 3;
+            if ((lane & 7) == 0 && i < nr) {
+                if (boff >= 0) v = __fadd_rn(v, *(const float *)(q + i * L.qs + boff));
+                if (res) res[i0 + r + i] = v;
+                else out[i0 + r + i] = v;
             }
-        }
-    }
-#pragma unroll
-    for (int r = 0; r < NR; r++) {
-        if (r < nr) {
-            acc[r][0] = warp_sum(acc[r][0]);
-            if constexpr (PAIR) acc[r][1] = warp_sum(acc[r][1]);
         }
     }
 }
 
-/* Consumer side of rows [r0, r1) of m (and m2), tile by tile from the ring.
- * A tile of at least NCW rows is split by whole rows (NR rows per warp at a
- * time, epilogue by the warp); a smaller tile (long rows) splits each row over
- * NCW / R warps, whose partial sums meet in psum in a fixed order. */
-template <int TYPE, bool D16, bool PAIR>
-__device__ void consume_rows(Ring &rg, int cols, int r0, int r1, const Epi &e, const Act &x, float *psum,
-                             unsigned *err, unsigned long long &best) {
-    if (r0 >= r1) return;
-    const int nb = cols / QK, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    constexpr int CPB = TYPE == T_Q4 ? 1 : 2;
-    const int nch = nb * CPB;
-    const int qrow = TYPE == T_Q4 ? cols / 2 : cols, drow = nb * (D16 ? 2 : 4);
-    int R, qbytes, dbytes;
-    stage_geom(TYPE, D16, cols, PAIR, R, qbytes, dbytes);
-    for (int ra = r0; ra < r1; ra += R) {
+/* Consumer side of one segment of the stream, chunk by chunk from the ring;
+ * seg_off: the segment's first row within the phase. Returns the ring's
+ * chunk count. Everything arrives by value: nothing the loop reads lives in
+ * memory that the mbarrier operations' memory clobbers would force it to
+ * reload. */
+template <int TYPE, bool PAIR>
+__device__ __forceinline__ unsigned consume_seg(Ring rg, Seg S, int seg_off, int cols, Act x, float *res,
+                                             unsigned *err) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nb = cols / QK;
+    const int qrow = TYPE == T_Q4 ? cols / 2 : cols;
+    const bool d16 = S.d16 != 0;
+    const Lay L{ S.rec, qrow, S.rec, S.rec / 2 };
+    const int boff = S.bias ? qrow + nb * (d16 ? 2 : 4) : -1;
+    constexpr int NR = PAIR ? GROUP_ROWS / 2 : GROUP_ROWS;
+    for (int r = 0; r < S.rows; r += S.rpc) {
+        const int n = min(S.rpc, S.rows - r);
         const int slot = (int)(rg.idx % (unsigned)rg.nstage);
         if (!mbar_wait(&rg.full[slot], (rg.idx / rg.nstage) & 1u, err) && lane == 0) atomicOr(err, 2u);
         if (threadIdx.x == 0) ev(0, EV_STAGE_READY);
-        const int nr = min(R, r1 - ra);
-        const int doff = (int)(((size_t)ra * drow) & 15);
-        const uint8_t *sq = rg.base + (size_t)slot * rg.slot_bytes;
-        const uint8_t *sd = sq + qbytes + doff;
-        const uint8_t *sq2 = sq + qbytes + dbytes, *sd2 = sq2 + qbytes + doff;
-        if (R >= 2 * NCW) {
-            for (int g = 2 * warp; g < nr; g += 2 * NCW) {
-                float acc[2][2];
-                dot_rows<TYPE, D16, PAIR, 2>(sq + (size_t)g * qrow, sd + g * drow, sq2 + (size_t)g * qrow,
-                                             sd2 + g * drow, qrow, drow, min(2, nr - g), 0, 1, nch, x, lane, acc);
-                if (lane == 0) {
-                    epilogue(e, ra + g, acc[0][0], acc[0][1], best);
-                    if (g + 1 < nr) epilogue(e, ra + g + 1, acc[1][0], acc[1][1], best);
-                }
-            }
-            __syncwarp();
-            if (threadIdx.x == 0) ev(0, EV_STAGE_DONE);
-            if (lane == 0) mbar_arrive(&rg.empty[slot]);
-        } else if (R >= NCW) {
-            for (int g = warp; g < nr; g += NCW) {
-                float acc[1][2];
-                dot_rows<TYPE, D16, PAIR, 1>(sq + (size_t)g * qrow, sd + g * drow, sq2 + (size_t)g * qrow,
-                                             sd2 + g * drow, qrow, drow, 1, 0, 1, nch, x, lane, acc);
-                if (lane == 0) epilogue(e, ra + g, acc[0][0], acc[0][1], best);
-            }
-            __syncwarp();
-            if (threadIdx.x == 0) ev(0, EV_STAGE_DONE);
-            if (lane == 0) mbar_arrive(&rg.empty[slot]);
-        } else {
-            const int G = NCW / R, r = warp / G, gg = warp % G;
-            float *ps = psum + (rg.idx & 1) * 128;
-            if (r < nr) {
-                float acc[1][2];
-                dot_rows<TYPE, D16, PAIR, 1>(sq + (size_t)r * qrow, sd + r * drow, sq2 + (size_t)r * qrow,
-                                             sd2 + r * drow, qrow, drow, 1, gg, G, nch, x, lane, acc);
-                if (lane == 0) {
-                    ps[r * G + gg] = acc[0][0];
-                    ps[64 + r * G + gg] = acc[0][1];
-                }
-            }
-            __syncwarp();
-            if (threadIdx.x == 0) ev(0, EV_STAGE_DONE);
-            if (lane == 0) mbar_arrive(&rg.empty[slot]);
-            consumer_sync();
-            const int t = threadIdx.x;
-            if (t < nr) {
-                float acc = 0.0f, acc2 = 0.0f;
-                for (int k = 0; k < G; k++) {   /* a fixed order: the result does not depend on timing */
-                    acc += ps[t * G + k];
-                    acc2 += ps[64 + t * G + k];
-                }
-                epilogue(e, ra + t, acc, acc2, best);
-            }
-        }
+        consume_chunk<TYPE, PAIR>(rg.base + (size_t)slot * rg.slot_bytes, L, n, nb, boff, d16, (seg_off + r) / NR,
+                                  seg_off + r, x, res, nullptr, lane, warp);
+        __syncwarp();
+        if (threadIdx.x == 0) ev(0, EV_STAGE_DONE);
+        if (lane == 0) mbar_arrive(&rg.empty[slot]);
         rg.idx++;
     }
+    return rg.idx;
 }
 
-__device__ __forceinline__ void consume(Ring &rg, const PMat &m, const PMat *m2, int cols, int r0, int r1,
-                                        const Epi &e, const Act &x, float *psum, unsigned *err,
-                                        unsigned long long &best) {
-    if (m.type == T_Q4) {
-        if (m2) {
-            if (m.d16) consume_rows<T_Q4, true, true>(rg, cols, r0, r1, e, x, psum, err, best);
-            else consume_rows<T_Q4, false, true>(rg, cols, r0, r1, e, x, psum, err, best);
+/* All segments of a phase into res (one copy of each consumer loop: Q4/Q8,
+ * single rows or gate|up pairs), then a consumer barrier. */
+__device__ __forceinline__ void consume_phase(Ring &rg, const PhasePlan &P, bool pair, const Act &x, float *res,
+                                              unsigned *err) {
+    int off = 0;
+    for (int s = 0; s < P.nseg; s++) {
+        const Seg S = P.seg[s];
+        if (S.type == T_Q4) rg.idx = pair ? consume_seg<T_Q4, true>(rg, S, off, P.cols, x, res, err)
+                                          : consume_seg<T_Q4, false>(rg, S, off, P.cols, x, res, err);
+        else rg.idx = pair ? consume_seg<T_Q8, true>(rg, S, off, P.cols, x, res, err)
+                           : consume_seg<T_Q8, false>(rg, S, off, P.cols, x, res, err);
+        off += S.rows;
+    }
+    consumer_sync();
+}
+
+enum { FIN_STORE = 0, FIN_RESID = 1, FIN_PAIR = 2, FIN_LOGITS = 3 };
+
+/* The rows of a phase after its dot products (res, in row order from row0):
+ * store, residual add (on the CTA's rows of x in `own` and in out), act(g)*u,
+ * or logits with the first-index argmax key of the CTA's rows (returned on
+ * thread 0; 0 otherwise). */
+__device__ __noinline__ unsigned long long finish_phase(int kind, const float *res, int nrows, int row0, float *out,
+                                                        float *own, int act, float softcap, unsigned long long *cta_best) {
+    unsigned long long best = 0;
+    for (int i = threadIdx.x; i < nrows; i += NCT) {
+        const int row = row0 + i;
+        if (kind == FIN_STORE) {
+            out[row] = res[i];
+        } else if (kind == FIN_RESID) {
+            const float v = __fadd_rn(own[i], res[i]);
+            own[i] = v;
+            out[row] = v;
+        } else if (kind == FIN_PAIR) {
+            const float2 gu = ((const float2 *)res)[i];
+            out[row] = act_mul(act, gu.x, gu.y);
         } else {
-            if (m.d16) consume_rows<T_Q4, true, false>(rg, cols, r0, r1, e, x, psum, err, best);
-            else consume_rows<T_Q4, false, false>(rg, cols, r0, r1, e, x, psum, err, best);
+            float v = res[i];
+            if (softcap > 0.0f) v = __fmul_rn(softcap, tanhf(__fdiv_rn(v, softcap)));
+            out[row] = v;
+            const unsigned long long k = argmax_key(v, row);
+            best = k > best ? k : best;
         }
-    } else {
-        if (m2) {
-            if (m.d16) consume_rows<T_Q8, true, true>(rg, cols, r0, r1, e, x, psum, err, best);
-            else consume_rows<T_Q8, false, true>(rg, cols, r0, r1, e, x, psum, err, best);
-        } else {
-            if (m.d16) consume_rows<T_Q8, true, false>(rg, cols, r0, r1, e, x, psum, err, best);
-            else consume_rows<T_Q8, false, false>(rg, cols, r0, r1, e, x, psum, err, best);
+    }
+    if (kind == FIN_LOGITS) {
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+            best = other > best ? other : best;
         }
+        if ((threadIdx.x & 31) == 0) cta_best[threadIdx.x >> 5] = best;
+        consumer_sync();
+        best = 0;
+        if (threadIdx.x == 0)
+            for (int w = 0; w < NCW; w++) best = cta_best[w] > best ? cta_best[w] : best;
+    }
+    return best;
+}
+
+/* Consumer of the kernel-level matvec (rows [r0, r1) as produce_rows staged them). */
+template <int TYPE>
+__device__ void consume_rows(Ring &rg, int cols, int r0, int r1, bool d16, float *y, const Act &x, unsigned *err) {
+    if (r0 >= r1) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nb = cols / QK;
+    const int qrow = TYPE == T_Q4 ? cols / 2 : cols, drow = nb * (d16 ? 2 : 4);
+    int R, qbytes, dbytes;
+    stage_geom(TYPE, d16, cols, 0, R, qbytes, dbytes);
+    for (int ra = r0; ra < r1; ra += R) {
+        const int nr = min(R, r1 - ra);
+        const int slot = (int)(rg.idx % (unsigned)rg.nstage);
+        if (!mbar_wait(&rg.full[slot], (rg.idx / rg.nstage) & 1u, err) && lane == 0) atomicOr(err, 2u);
+        const Lay L{ qrow, qbytes + (int)(((size_t)ra * drow) & 15), drow, 0 };
+        consume_chunk<TYPE, false>(rg.base + (size_t)slot * rg.slot_bytes, L, nr, nb, -1, d16, (ra - r0) / GROUP_ROWS,
+                                   ra, x, nullptr, y, lane, warp);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&rg.empty[slot]);
+        rg.idx++;
     }
 }
 
 /* ------------------------------------------------------------ activations */
 
-enum { SRC_GLOBAL = 0, SRC_EMBED = 1, SRC_PREQUANT = 2 };
-
-constexpr int ACT_MAXP = 4;   /* passes of 64 blocks a thread keeps in registers (cols <= 8192) */
-
-/* The activation of a phase into shared memory (xq, xd, xs): quantize_q8 of
- * v, with v = RMSNorm(x) * w (k_scalar.c:59-64: o = (x * inv) * w, inv =
- * 1 / sqrt(ss / n + eps)) when norm_w is set. The source: a float vector in
- * global memory written by other CTAs (read through L2), the embedding row of
- * token tok (dequantized, times embed_scale), or an already quantized vector
- * (pq, pd). 1/rms: inv_given when > 0, else from ss = the sum of the G
- * per-CTA partial sums ssp (the residual epilogues' x^2, added in CTA order),
- * else reduced here. Each thread loads all its values before using any. */
-__device__ __noinline__ void load_activation(const StepArgs &a, int src, const float *x, int tok, const float *norm_w, float inv_given,
-                                const float *ssp, int cols, const int8_t *pq, const float *pd, int8_t *xq, float *xd,
-                                int *xs, float *red) {
-    const int nb = cols / QK, tid = threadIdx.x;
-    if (src == SRC_PREQUANT) {
-        for (int i = tid; i < cols / 16; i += NCT) ((int4 *)xq)[i] = __ldcg((const int4 *)pq + i);
-        for (int b = tid; b < nb; b += NCT) xd[b] = __ldcg(pd + b);
-        consumer_sync();
-        for (int b = tid; b < nb; b += NCT) {
-            const int4 *q4 = (const int4 *)(xq + b * QK);
-            int sum = 0;
-            for (int k = 0; k < 2; k++) {
-                const int4 w = q4[k];
-                sum = __dp4a(w.x, 0x01010101, sum);
-                sum = __dp4a(w.y, 0x01010101, sum);
-                sum = __dp4a(w.z, 0x01010101, sum);
-                sum = __dp4a(w.w, 0x01010101, sum);
-            }
-            xs[b] = 8 * sum;
-        }
-        consumer_sync();
-        return;
+/* Value i..i+3 of the embedding row of tok, dequantized (core/quant_ref.c:4-19)
+ * and times embed_scale (model/transformer.c:226-230). */
+__device__ __forceinline__ float4 embed4(const PMat &emb, float embed_scale, int tok, int cols, int i) {
+    const int nb = cols / QK, b = i / QK, j = i % QK;
+    const float sc = emb.d16 ? __half2float(((const __half *)emb.d)[(size_t)tok * nb + b])
+                               : ((const float *)emb.d)[(size_t)tok * nb + b];
+    float v[4];
+    if (emb.type == T_Q8) {
+        const char4 q4 = *(const char4 *)((const int8_t *)emb.q + (size_t)tok * cols + i);
+        v[0] = __fmul_rn((float)q4.x, sc); v[1] = __fmul_rn((float)q4.y, sc);
+        v[2] = __fmul_rn((float)q4.z, sc); v[3] = __fmul_rn((float)q4.w, sc);
+    } else {
+        const uchar4 p = *(const uchar4 *)(emb.q + ((size_t)tok * nb + b) * (QK / 2) + (j & 15));
+        const bool hi = j >= 16;
+        v[0] = __fmul_rn((float)((hi ? p.x >> 4 : p.x & 15) - 8), sc);
+        v[1] = __fmul_rn((float)((hi ? p.y >> 4 : p.y & 15) - 8), sc);
+        v[2] = __fmul_rn((float)((hi ? p.z >> 4 : p.z & 15) - 8), sc);
+        v[3] = __fmul_rn((float)((hi ? p.w >> 4 : p.w & 15) - 8), sc);
     }
-    auto load4 = [&](int i, float v[4]) {
-        if (src == SRC_GLOBAL) {
-            const float4 t = __ldcg((const float4 *)(x + i));
-            v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
-        } else {
-            const int b = i / QK, j = i % QK;
-            const float sc = a.emb.d16 ? __half2float(((const __half *)a.emb.d)[(size_t)tok * nb + b])
-                                       : ((const float *)a.emb.d)[(size_t)tok * nb + b];
-            if (a.emb.type == T_Q8) {
-                const char4 q4 = *(const char4 *)((const int8_t *)a.emb.q + (size_t)tok * cols + i);
-                v[0] = __fmul_rn((float)q4.x, sc); v[1] = __fmul_rn((float)q4.y, sc);
-                v[2] = __fmul_rn((float)q4.z, sc); v[3] = __fmul_rn((float)q4.w, sc);
-            } else {
-                const uchar4 p = *(const uchar4 *)(a.emb.q + ((size_t)tok * nb + b) * (QK / 2) + (j & 15));
-                const bool hi = j >= 16;
-                v[0] = __fmul_rn((float)((hi ? p.x >> 4 : p.x & 15) - 8), sc);
-                v[1] = __fmul_rn((float)((hi ? p.y >> 4 : p.y & 15) - 8), sc);
-                v[2] = __fmul_rn((float)((hi ? p.z >> 4 : p.z & 15) - 8), sc);
-                v[3] = __fmul_rn((float)((hi ? p.w >> 4 : p.w & 15) - 8), sc);
-            }
-            if (a.embed_scale != 1.0f)
-                for (int k = 0; k < 4; k++) v[k] = __fmul_rn(v[k], a.embed_scale);
+    if (embed_scale != 1.0f)
+        for (int k = 0; k < 4; k++) v[k] = __fmul_rn(v[k], embed_scale);
+    return make_float4(v[0], v[1], v[2], v[3]);
+}
+
+/* Value i of the embedding row of tok (any i). */
+__device__ __forceinline__ float embed1(const StepArgs &a, int tok, int cols, int i) {
+    const int nb = cols / QK, b = i / QK, j = i % QK;
+    const float sc = a.emb.d16 ? __half2float(((const __half *)a.emb.d)[(size_t)tok * nb + b])
+                               : ((const float *)a.emb.d)[(size_t)tok * nb + b];
+    int v;
+    if (a.emb.type == T_Q8) {
+        v = ((const int8_t *)a.emb.q)[(size_t)tok * cols + i];
+    } else {
+        const uint8_t byte = a.emb.q[((size_t)tok * nb + b) * (QK / 2) + (j & 15)];
+        v = (j < 16 ? (byte & 0xF) : (byte >> 4)) - 8;
+    }
+    float o = __fmul_rn((float)v, sc);
+    if (a.embed_scale != 1.0f) o = __fmul_rn(o, a.embed_scale);
+    return o;
+}
+
+/* The activation of a phase into shared memory: quantize_q8 of v, with
+ * v = RMSNorm(x) * w (k_scalar.c:59-64: o = (x * inv) * w, inv =
+ * 1 / sqrt(ss / n + eps)) when norm_w is set. Source: a float vector in global
+ * memory written by other CTAs (read through L2) or the embedding row of tok.
+ * 1/rms: inv_given when > 0, else from ss = the sum of the G per-CTA partial
+ * sums ssp, else reduced here. Every thread issues all its loads (P passes of
+ * 64 blocks, 8 lanes per block) before it uses any, so a prologue costs one
+ * round trip to L2. */
+constexpr int ACT_PASSES = 4;   /* passes of 64 blocks a thread holds in registers */
+
+/* Quantizes the 4 values of block b held by this lane (elements j0..j0+3)
+ * with the other 7 lanes of its group and stores them in the split layout. */
+__device__ __forceinline__ void put_quant(const ActW &o, int b, int nb, int j0, float u[4]) {
+    float d;
+    int sum;
+    const unsigned word = quant4(u, &d, &sum);
+    if (b < nb) {
+        *(unsigned *)((j0 < 16 ? o.xlo : o.xhi) + b * 16 + (j0 & 15)) = word;
+        if ((threadIdx.x & 7) == 0) {
+            o.xd[b] = d;
+            o.xs[b] = 8 * sum;
         }
-    };
-    constexpr int per_pass = NCT / 8;   /* blocks per pass: 8 lanes x 4 values each */
-    const int passes = (nb + per_pass - 1) / per_pass;
-    const int j0 = (tid & 7) * 4;
-    float v[ACT_MAXP][4];
-    float4 wv[ACT_MAXP];
-    const bool cached = passes <= ACT_MAXP;
-    if (cached) {
+    }
+}
+
+/* The activation of a phase into shared memory: quantize_q8 of v, with
+ * v = RMSNorm(x) * w (k_scalar.c:59-64: o = (x * inv) * w, inv =
+ * 1 / sqrt(ss / n + eps)) when norm_w is set; x is a float vector in global
+ * memory written by other CTAs (read through L2). 1/rms: from ss = the sum of
+ * the G per-CTA partial sums ssp, else reduced here. Every thread issues all
+ * its loads (up to 4 passes of 64 blocks, 8 lanes per block) before it uses
+ * any, so the prologue costs one round trip to L2; the quantize loop is not
+ * unrolled (one copy of its code). */
+__device__ __noinline__ void act_float(float eps, const float *x, const float *norm_w, const float *ssp, int cols, ActW o,
+                                       float *red) {
+    const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 7) * 4;
+    const int passes = (nb + NCT / 8 - 1) / (NCT / 8);
+    const bool norm = norm_w != nullptr;
+    if (tid == 0) ev(0, EV_ACT_ENTRY);
+    float4 v[ACT_PASSES], w[ACT_PASSES];
 #pragma unroll
-        for (int p = 0; p < ACT_MAXP; p++) {
-            const int b = p * per_pass + tid / 8;
-            if (p < passes && b < nb) {
-                load4(b * QK + j0, v[p]);
-                if (norm_w) wv[p] = *(const float4 *)(norm_w + b * QK + j0);
-            } else {
-                v[p][0] = v[p][1] = v[p][2] = v[p][3] = 0.0f;
-            }
+    for (int p = 0; p < ACT_PASSES; p++) {
+        const int b = p * (NCT / 8) + (tid >> 3);
+        v[p] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        w[p] = v[p];
+        if (p < passes && b < nb) {
+            v[p] = __ldcg((const float4 *)(x + b * QK + j0));
+            if (norm) w[p] = *(const float4 *)(norm_w + b * QK + j0);
         }
     }
-    float inv = inv_given;
-    if (norm_w && !(inv_given > 0.0f)) {
+    if (tid == 0) {
+        asm volatile("" ::"f"(v[0].x));
+        ev(0, EV_ACT_LOADED);
+    }
+    float inv = 1.0f;
+    if (norm) {
+        float ss;
         if (ssp) {
             if (tid < 32) {
                 float t = 0.0f;
-                for (int k = tid; k < gridDim.x; k += 32) t += __ldcg(ssp + k);
+                for (int k = tid; k < (int)gridDim.x; k += 32) t += __ldcg(ssp + k);
                 t = warp_sum(t);
                 if (tid == 0) red[0] = t;
             }
             consumer_sync();
+            ss = red[0];
         } else {
-            float ss = 0.0f;
-            if (cached) {
+            float t = 0.0f;
 #pragma unroll
-                for (int p = 0; p < ACT_MAXP; p++)
-                    ss += v[p][0] * v[p][0] + v[p][1] * v[p][1] + v[p][2] * v[p][2] + v[p][3] * v[p][3];
-            } else {
-                for (int i = tid * 4; i < cols; i += NCT * 4) {
-                    float t[4];
-                    load4(i, t);
-                    ss += t[0] * t[0] + t[1] * t[1] + t[2] * t[2] + t[3] * t[3];
-                }
-            }
-            block_sum(ss, red);
+            for (int p = 0; p < ACT_PASSES; p++) t += v[p].x * v[p].x + v[p].y * v[p].y + v[p].z * v[p].z + v[p].w * v[p].w;
+            ss = block_sum(t, red);
         }
-        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(red[0], (float)cols), a.eps)));
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
     }
+    if (tid == 0) ev(0, EV_ACT_INV);
+#pragma unroll 1
     for (int p = 0; p < passes; p++) {
-        const int b = p * per_pass + tid / 8;
+        float4 c = v[0], cw = w[0];
+        if (p == 1) { c = v[1]; cw = w[1]; }
+        else if (p == 2) { c = v[2]; cw = w[2]; }
+        else if (p == 3) { c = v[3]; cw = w[3]; }
+        float u[4] = { c.x, c.y, c.z, c.w };
+        if (norm) {
+            u[0] = __fmul_rn(__fmul_rn(u[0], inv), cw.x);
+            u[1] = __fmul_rn(__fmul_rn(u[1], inv), cw.y);
+            u[2] = __fmul_rn(__fmul_rn(u[2], inv), cw.z);
+            u[3] = __fmul_rn(__fmul_rn(u[3], inv), cw.w);
+        }
+        put_quant(o, p * (NCT / 8) + (tid >> 3), nb, j0, u);
+    }
+    if (tid == 0) ev(0, EV_ACT_QUANT);
+    consumer_sync();
+}
+
+/* Layer 0's activation: the embedding row of tok, its 1/rms from the host
+ * table (inv), times the norm weights. */
+__device__ __noinline__ void act_embed(PMat emb, float embed_scale, int tok, const float *norm_w, float inv, int cols,
+                                       ActW o) {
+    const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 7) * 4;
+#pragma unroll 1
+    for (int b0 = 0; b0 < nb; b0 += NCT / 8) {
+        const int b = b0 + (tid >> 3);
         float u[4] = { 0.0f, 0.0f, 0.0f, 0.0f };
-        float4 w4 = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
         if (b < nb) {
-            if (cached) {
-#pragma unroll
-                for (int pp = 0; pp < ACT_MAXP; pp++)
-                    if (pp == p) { u[0] = v[pp][0]; u[1] = v[pp][1]; u[2] = v[pp][2]; u[3] = v[pp][3]; if (norm_w) w4 = wv[pp]; }
-            } else {
-                load4(b * QK + j0, u);
-                if (norm_w) w4 = *(const float4 *)(norm_w + b * QK + j0);
-            }
-            if (norm_w) {
-                u[0] = __fmul_rn(__fmul_rn(u[0], inv), w4.x);
-                u[1] = __fmul_rn(__fmul_rn(u[1], inv), w4.y);
-                u[2] = __fmul_rn(__fmul_rn(u[2], inv), w4.z);
-                u[3] = __fmul_rn(__fmul_rn(u[3], inv), w4.w);
-            }
+            const float4 e4 = embed4(emb, embed_scale, tok, cols, b * QK + j0);
+            const float4 w4 = *(const float4 *)(norm_w + b * QK + j0);
+            u[0] = __fmul_rn(__fmul_rn(e4.x, inv), w4.x);
+            u[1] = __fmul_rn(__fmul_rn(e4.y, inv), w4.y);
+            u[2] = __fmul_rn(__fmul_rn(e4.z, inv), w4.z);
+            u[3] = __fmul_rn(__fmul_rn(e4.w, inv), w4.w);
         }
-        float d;
-        int sum;
-        const unsigned word = quant4(u, &d, &sum);
-        if (b < nb) {
-            ((unsigned *)xq)[(b * QK + j0) / 4] = word;
-            if ((tid & 7) == 0) {
-                xd[b] = d;
-                xs[b] = 8 * sum;
-            }
-        }
+        put_quant(o, b, nb, j0, u);
     }
     consumer_sync();
 }
 
-/* The sum of squares of the rows [r0, r1) of x this CTA has just written
- * into ssp[blockIdx.x]: the next RMSNorm adds the G partial sums instead of
- * reading all of x before it can scale any of it. */
-__device__ __forceinline__ void publish_ssq(const StepArgs &a, int r0, int r1, float *red) {
-    consumer_sync();
-    float t = 0.0f;
-    for (int r = r0 + (int)threadIdx.x; r < r1; r += NCT) {
-        const float v = __ldcg(a.x + r);
-        t += v * v;
+/* The same activation for any width, pass by pass (kernel-level entry points). */
+__device__ __noinline__ void act_loop(float eps, const float *x, const float *norm_w, int cols, ActW o, float *red) {
+    const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 7) * 4;
+    float inv = 1.0f;
+    if (norm_w) {
+        float t = 0.0f;
+        for (int i = tid * 4; i < cols; i += NCT * 4) {
+            const float4 v = __ldcg((const float4 *)(x + i));
+            t += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+        const float ss = block_sum(t, red);
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
     }
-    t = block_sum(t, red);
-    if (threadIdx.x == 0) a.ssp[blockIdx.x] = t;
+    for (int b0 = 0; b0 < nb; b0 += NCT / 8) {
+        const int b = b0 + (tid >> 3);
+        float u[4] = { 0.0f, 0.0f, 0.0f, 0.0f };
+        if (b < nb) {
+            const float4 v = __ldcg((const float4 *)(x + b * QK + j0));
+            u[0] = v.x; u[1] = v.y; u[2] = v.z; u[3] = v.w;
+            if (norm_w) {
+                const float4 w = *(const float4 *)(norm_w + b * QK + j0);
+                u[0] = __fmul_rn(__fmul_rn(u[0], inv), w.x);
+                u[1] = __fmul_rn(__fmul_rn(u[1], inv), w.y);
+                u[2] = __fmul_rn(__fmul_rn(u[2], inv), w.z);
+                u[3] = __fmul_rn(__fmul_rn(u[3], inv), w.w);
+            }
+        }
+        put_quant(o, b, nb, j0, u);
+    }
+    consumer_sync();
+}
+
+/* act_float for up to 4 * 2048 columns; wider vectors pass by pass. */
+__device__ __forceinline__ void load_activation(const StepArgs &a, const float *x, const float *norm_w, const float *ssp,
+                                                int cols, const ActW &o, float *red) {
+    if (cols <= ACT_PASSES * NCT / 8 * QK) act_float(a.eps, x, norm_w, ssp, cols, o, red);
+    else act_loop(a.eps, x, norm_w, cols, o, red);
+}
+
+/* An already quantized activation (kernel-level matvec) into the same layout. */
+__device__ void act_prequant(const int8_t *pq, const float *pd, int cols, const ActW &o) {
+    const int nb = cols / QK;
+    for (int i = threadIdx.x; i < cols / 16; i += NCT)
+        ((int4 *)((i & 1) ? o.xhi : o.xlo))[i >> 1] = __ldcg((const int4 *)pq + i);
+    for (int b = threadIdx.x; b < nb; b += NCT) o.xd[b] = __ldcg(pd + b);
+    consumer_sync();
+    for (int b = threadIdx.x; b < nb; b += NCT) {
+        int sum = 0;
+        const int4 lo = ((const int4 *)o.xlo)[b], hi = ((const int4 *)o.xhi)[b];
+        for (const int4 &w : { lo, hi }) {
+            sum = __dp4a(w.x, 0x01010101, sum);
+            sum = __dp4a(w.y, 0x01010101, sum);
+            sum = __dp4a(w.z, 0x01010101, sum);
+            sum = __dp4a(w.w, 0x01010101, sum);
+        }
+        o.xs[b] = 8 * sum;
+    }
+    consumer_sync();
 }
 
 /* ------------------------------------------------------------ attention */
@@ -590,7 +841,7 @@ __host__ __device__ inline int attention_scratch_floats(int group, int hd) {
  * (after RoPE) and V into the cache; scores q.k * scale (soft-capped when
  * set), online softmax and the weighted V sum over the split's positions; the
  * last CTA of the KV head to finish combines the splits into a.ao. */
-__device__ void attention_item(const StepArgs &a, const LayerPlan &L, int g, int y, int pos, float *fsm, int *flag) {
+__device__ __forceinline__ void attention_item(const StepArgs &a, const LayerPlan &L, int g, int y, int pos, float *fsm, int *flag) {
     const int hd = a.hd, group = a.n_heads / a.n_kv_heads, h2 = hd / 2, tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
     const int first = L.window && pos >= L.window ? pos + 1 - L.window : 0;
@@ -727,32 +978,36 @@ __device__ void attention_item(const StepArgs &a, const LayerPlan &L, int g, int
 
 /* ------------------------------------------------------------ shared layout */
 
-/* Dynamic shared memory of a streaming CTA: mbarriers [2][nstage], psum
- * [2][128], per-warp argmax [NCW], flag, reduction scratch [32], activation
- * (or attention scratch) of act_bytes, then the ring (128 B aligned). */
+/* Dynamic shared memory of a streaming CTA: mbarriers [2][nstage], per-warp
+ * argmax [NCW], flag, reduction scratch [32], the owned rows of x [OWN_MAX],
+ * activation (or attention scratch) of act_bytes, then the ring (128 B
+ * aligned). */
 struct Smem {
     uint64_t *full, *empty;
-    float *psum;
     unsigned long long *cta_best;
     int *flag;
     float *red;
+    float *own;
+    float *res;
     unsigned char *act;
     uint8_t *ring;
 };
 
-__host__ __device__ inline int smem_fixed_bytes(int nstage, int act_bytes) {
-    return 16 * nstage + 1024 + 8 * NCW + 16 + 128 + act_bytes + 128;
+/* res_bytes: a phase's row results (16-byte multiple). */
+__host__ __device__ inline int smem_fixed_bytes(int nstage, int act_bytes, int res_bytes = 0) {
+    return 16 * nstage + 8 * NCW + 16 + 128 + 4 * OWN_MAX + res_bytes + act_bytes + 128;
 }
 
-__device__ __forceinline__ Smem carve(unsigned char *smem, int nstage, int act_bytes) {
+__device__ __forceinline__ Smem carve(unsigned char *smem, int nstage, int act_bytes, int res_bytes = 0) {
     Smem s;
     s.full = (uint64_t *)smem;
     s.empty = s.full + nstage;
-    s.psum = (float *)(smem + 16 * nstage);
-    s.cta_best = (unsigned long long *)(s.psum + 256);
+    s.cta_best = (unsigned long long *)(s.empty + nstage);
     s.flag = (int *)(s.cta_best + NCW);
     s.red = (float *)(s.flag + 4);
-    s.act = (unsigned char *)(s.red + 32);
+    s.own = s.red + 32;
+    s.res = s.own + OWN_MAX;
+    s.act = (unsigned char *)s.res + res_bytes;
     s.ring = (uint8_t *)(((uintptr_t)(s.act + act_bytes) + 127) & ~(uintptr_t)127);
     return s;
 }
@@ -770,30 +1025,25 @@ __device__ __forceinline__ void init_ring(const Smem &s, int nstage) {
 
 /* ------------------------------------------------------------ the step kernel */
 
-__device__ void producer(const StepArgs &a, Ring rg) {
-    const int j = blockIdx.x, G = gridDim.x;
-    int r0, r1;
+__shared__ PhasePlan s_plan[NPHASE];
+
+/* Producer: this CTA's stream once per step (the classifier only when the
+ * step computes logits). */
+__device__ __forceinline__ void producer(const StepArgs &a, Ring rg) {
+    const uint8_t *base = a.stream + a.cta_base[blockIdx.x];
     for (int s = 0; s < a.nsteps; s++) {
-        for (int l = 0; l < a.n_layers; l++) {
-            const LayerPlan &L = a.layers[l];
-            share_rows(L.wq.rows, j, G, r0, r1); produce_rows(rg, L.wq, nullptr, a.dim, r0, r1, a.err);
-            share_rows(L.wk.rows, j, G, r0, r1); produce_rows(rg, L.wk, nullptr, a.dim, r0, r1, a.err);
-            share_rows(L.wv.rows, j, G, r0, r1); produce_rows(rg, L.wv, nullptr, a.dim, r0, r1, a.err);
-            share_rows(L.wo.rows, j, G, r0, r1); produce_rows(rg, L.wo, nullptr, a.q_dim, r0, r1, a.err);
-            share_rows(L.w1.rows, j, G, r0, r1); produce_rows(rg, L.w1, &L.w3, a.dim, r0, r1, a.err);
-            share_rows(L.w2.rows, j, G, r0, r1); produce_rows(rg, L.w2, nullptr, a.hidden, r0, r1, a.err);
-        }
-        if (a.run_cls) {
-            share_rows(a.cls.rows, j, G, r0, r1);
-            produce_rows(rg, a.cls, nullptr, a.dim, r0, r1, a.err);
-        }
+        const uint8_t *src = base;
+        for (int l = 0; l < a.n_layers; l++)
+            for (int p = PH_A; p <= PH_E; p++) produce_phase(rg, s_plan[p], src, a.err);
+        if (a.run_cls) produce_phase(rg, s_plan[PH_F], src, a.err);
     }
 }
 
 __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_constant__ StepArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
-    const Smem sh = carve(smem, a.nstage, a.act_bytes);
+    const Smem sh = carve(smem, a.nstage, a.act_bytes, a.res_bytes);
     ev_init(true);
+    if (threadIdx.x == 0) make_plan(a.geom, blockIdx.x, gridDim.x, s_plan);
     init_ring(sh, a.nstage);
     Ring rg{ sh.full, sh.empty, sh.ring, a.nstage, a.slot_bytes, 0u };
     if ((threadIdx.x >> 5) == NCW) {
@@ -801,8 +1051,11 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
         return;
     }
     const int j = blockIdx.x, G = gridDim.x;
+    int own0, own1;
+    share_rows(a.dim, j, G, own0, own1);
+    const int nown = own1 - own0;
     unsigned expect = 0;
-    int8_t *xq = (int8_t *)sh.act;
+    const ActW w_dim = act_layout(sh.act, a.dim), w_q = act_layout(sh.act, a.q_dim), w_h = act_layout(sh.act, a.hidden);
     if (threadIdx.x == 0) timeline_mark(a);
     for (int step = 0; step < a.nsteps; step++) {
         const int tok = __ldcg(&a.ls->token), pos = __ldcg(&a.ls->pos);
@@ -810,49 +1063,27 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
         if (!ok && threadIdx.x == 0) atomicOr(&a.ls->err, 1u);
         const int tk = ok ? tok : 0, ps = ok ? pos : 0;
         const int logit_row0 = (__ldcg(&a.ls->step) % LOGITS_RING) * a.vocab;
-        unsigned long long best = 0;
-        int r0, r1;
         for (int l = 0; l < a.n_layers; l++) {
             const LayerPlan &L = a.layers[l];
-            int cols = a.dim, nb = cols / QK;
-            float *xd = (float *)(sh.act + cols);
-            int *xs = (int *)(xd + nb);
             /* A: Q/K/V */
             if (l == 0) {
-                load_activation(a, SRC_EMBED, nullptr, tk, L.attn_norm, a.inv0[tk], nullptr, cols, nullptr, nullptr, xq, xd, xs,
-                                sh.red);
+                act_embed(a.emb, a.embed_scale, tk, L.attn_norm, a.inv0[tk], a.dim, w_dim);
                 /* the residual stream starts as the embedding row: this CTA's rows of x */
-                share_rows(a.dim, j, G, r0, r1);
-                for (int r = r0 + (int)threadIdx.x; r < r1; r += NCT) {
-                    const int b = r / QK, jj = r % QK;
-                    const float sc = a.emb.d16 ? __half2float(((const __half *)a.emb.d)[(size_t)tk * nb + b])
-                                               : ((const float *)a.emb.d)[(size_t)tk * nb + b];
-                    int v;
-                    if (a.emb.type == T_Q8) {
-                        v = ((const int8_t *)a.emb.q)[(size_t)tk * a.dim + r];
-                    } else {
-                        const uint8_t byte = a.emb.q[((size_t)tk * nb + b) * (QK / 2) + (jj & 15)];
-                        v = (jj < 16 ? (byte & 0xF) : (byte >> 4)) - 8;
-                    }
-                    float o = __fmul_rn((float)v, sc);
-                    if (a.embed_scale != 1.0f) o = __fmul_rn(o, a.embed_scale);
-                    a.x[r] = o;
+                for (int r = own0 + (int)threadIdx.x; r < own1; r += NCT) {
+                    const float e1 = embed1(a, tk, a.dim, r);
+                    a.x[r] = e1;
+                    sh.own[r - own0] = e1;
                 }
             } else {
-                load_activation(a, SRC_GLOBAL, a.x, tk, L.attn_norm, 0.0f, a.ssp, cols, nullptr, nullptr, xq, xd, xs, sh.red);
+                load_activation(a, a.x, L.attn_norm, a.ssp, a.dim, w_dim, sh.red);
             }
             trace_mark(a, expect / G, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
+            consume_phase(rg, s_plan[PH_A], false, act_view(w_dim), sh.res, a.err);
             {
-                const Act x{ xq, xd, xs };
-                share_rows(L.wq.rows, j, G, r0, r1);
-                consume(rg, L.wq, nullptr, cols, r0, r1, Epi{ EPI_STORE, a.qkv, L.bq, 0, 0.0f, 0 }, x, sh.psum, a.err, best);
-                share_rows(L.wk.rows, j, G, r0, r1);
-                consume(rg, L.wk, nullptr, cols, r0, r1, Epi{ EPI_STORE, a.qkv + a.q_dim, L.bk, 0, 0.0f, 0 }, x, sh.psum,
-                        a.err, best);
-                share_rows(L.wv.rows, j, G, r0, r1);
-                consume(rg, L.wv, nullptr, cols, r0, r1, Epi{ EPI_STORE, a.qkv + a.q_dim + a.kv_dim, L.bv, 0, 0.0f, 0 }, x,
-                        sh.psum, a.err, best);
+                const PhasePlan &P = s_plan[PH_A];
+                const int nr = P.seg[0].rows + (P.nseg > 1 ? P.seg[1].rows : 0) + (P.nseg > 2 ? P.seg[2].rows : 0);
+                finish_phase(FIN_STORE, sh.res, nr, P.nseg ? P.seg[0].row0 : 0, a.qkv, nullptr, 0, 0.0f, sh.cta_best);
             }
             grid_barrier(a, expect);
             /* B: attention */
@@ -862,60 +1093,38 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
                 attention_item(a, L, it / a.nsplit, it % a.nsplit, ps, (float *)sh.act, sh.flag);
             grid_barrier(a, expect);
             /* C: O projection + residual */
-            cols = a.q_dim; nb = cols / QK;
-            xd = (float *)(sh.act + cols); xs = (int *)(xd + nb);
-            load_activation(a, SRC_GLOBAL, a.ao, tk, nullptr, 1.0f, nullptr, cols, nullptr, nullptr, xq, xd, xs, sh.red);
+            load_activation(a, a.ao, nullptr, nullptr, a.q_dim, w_q, sh.red);
             trace_mark(a, expect / G, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
-            share_rows(L.wo.rows, j, G, r0, r1);
-            consume(rg, L.wo, nullptr, cols, r0, r1, Epi{ EPI_RESID, a.x, nullptr, 0, 0.0f, 0 }, Act{ xq, xd, xs },
-                    sh.psum, a.err, best);
-            publish_ssq(a, r0, r1, sh.red);
-            grid_barrier(a, expect);
+            consume_phase(rg, s_plan[PH_C], false, act_view(w_q), sh.res, a.err);
+            finish_phase(FIN_RESID, sh.res, nown, own0, a.x, sh.own, 0, 0.0f, sh.cta_best);
+            grid_barrier(a, expect, sh.own, nown);
             /* D: gate/up + activation */
-            cols = a.dim; nb = cols / QK;
-            xd = (float *)(sh.act + cols); xs = (int *)(xd + nb);
-            load_activation(a, SRC_GLOBAL, a.x, tk, L.ffn_norm, 0.0f, a.ssp, cols, nullptr, nullptr, xq, xd, xs, sh.red);
+            load_activation(a, a.x, L.ffn_norm, a.ssp, a.dim, w_dim, sh.red);
             trace_mark(a, expect / G, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
-            share_rows(L.w1.rows, j, G, r0, r1);
-            consume(rg, L.w1, &L.w3, cols, r0, r1, Epi{ EPI_PAIR, a.hb, nullptr, a.act, 0.0f, 0 }, Act{ xq, xd, xs },
-                    sh.psum, a.err, best);
+            consume_phase(rg, s_plan[PH_D], true, act_view(w_dim), sh.res, a.err);
+            finish_phase(FIN_PAIR, sh.res, s_plan[PH_D].seg[0].rows, s_plan[PH_D].seg[0].row0, a.hb, nullptr, a.act, 0.0f,
+                         sh.cta_best);
             grid_barrier(a, expect);
             /* E: down + residual */
-            cols = a.hidden; nb = cols / QK;
-            xd = (float *)(sh.act + cols); xs = (int *)(xd + nb);
-            load_activation(a, SRC_GLOBAL, a.hb, tk, nullptr, 1.0f, nullptr, cols, nullptr, nullptr, xq, xd, xs, sh.red);
+            load_activation(a, a.hb, nullptr, nullptr, a.hidden, w_h, sh.red);
             trace_mark(a, expect / G, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
-            share_rows(L.w2.rows, j, G, r0, r1);
-            consume(rg, L.w2, nullptr, cols, r0, r1, Epi{ EPI_RESID, a.x, nullptr, 0, 0.0f, 0 }, Act{ xq, xd, xs },
-                    sh.psum, a.err, best);
-            publish_ssq(a, r0, r1, sh.red);
-            grid_barrier(a, expect);
+            consume_phase(rg, s_plan[PH_E], false, act_view(w_h), sh.res, a.err);
+            finish_phase(FIN_RESID, sh.res, nown, own0, a.x, sh.own, 0, 0.0f, sh.cta_best);
+            grid_barrier(a, expect, sh.own, nown);
         }
         /* F: classifier + argmax */
         if (a.run_cls) {
-            const int cols = a.dim, nb = cols / QK;
-            float *xd = (float *)(sh.act + cols);
-            int *xs = (int *)(xd + nb);
-            load_activation(a, SRC_GLOBAL, a.x, tk, a.final_norm, 0.0f, a.ssp, cols, nullptr, nullptr, xq, xd, xs, sh.red);
+            load_activation(a, a.x, a.final_norm, a.ssp, a.dim, w_dim, sh.red);
             trace_mark(a, expect / G, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
-            share_rows(a.cls.rows, j, G, r0, r1);
-            consume(rg, a.cls, nullptr, cols, r0, r1, Epi{ EPI_LOGITS, a.logits, nullptr, 0, a.final_softcap, logit_row0 },
-                    Act{ xq, xd, xs }, sh.psum, a.err, best);
-            for (int o = 16; o > 0; o >>= 1) {
-                const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-                best = other > best ? other : best;
-            }
-            if ((threadIdx.x & 31) == 0) sh.cta_best[threadIdx.x >> 5] = best;
-            consumer_sync();
-            if (threadIdx.x == 0) {
-                unsigned long long b = 0;
-                for (int w = 0; w < NCW; w++) b = sh.cta_best[w] > b ? sh.cta_best[w] : b;
-                if (b) atomicMax(&a.ls->best, b);
-            }
+            consume_phase(rg, s_plan[PH_F], false, act_view(w_dim), sh.res, a.err);
+            const unsigned long long b = finish_phase(FIN_LOGITS, sh.res, s_plan[PH_F].seg[0].rows,
+                                                      s_plan[PH_F].seg[0].row0, a.logits + logit_row0, nullptr, 0,
+                                                      a.final_softcap, sh.cta_best);
+            if (threadIdx.x == 0 && b) atomicMax(&a.ls->best, b);
         }
         /* every CTA arrives; the last one advances the loop state, then
          * releases the others with one more arrival */
@@ -954,8 +1163,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
 /* ------------------------------------------------------------ kernel-level kernels */
 
 /* One matrix against one quantized activation (kc_matvec_dev): the step
- * kernel's producer and consumers over rows [0, rows), CTA j of G owning its
- * share, the activation copied in (SRC_PREQUANT). */
+ * kernel's ring and consumers over rows [0, rows), CTA j of G owning its
+ * share, the matrix in the file's layout. */
 struct MatvecArgs {
     PMat m;
     int cols;
@@ -975,18 +1184,13 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) matvec_kernel(const __grid_co
     int r0, r1;
     share_rows(p.m.rows, blockIdx.x, gridDim.x, r0, r1);
     if ((threadIdx.x >> 5) == NCW) {
-        if ((threadIdx.x & 31) == 0) produce_rows(rg, p.m, nullptr, p.cols, r0, r1, p.err);
+        if ((threadIdx.x & 31) == 0) produce_rows(rg, p.m, p.cols, r0, r1, p.err);
         return;
     }
-    const int nb = p.cols / QK;
-    int8_t *xq = (int8_t *)sh.act;
-    float *xd = (float *)(sh.act + p.cols);
-    int *xs = (int *)(xd + nb);
-    StepArgs dummy{};
-    load_activation(dummy, SRC_PREQUANT, nullptr, 0, nullptr, 1.0f, nullptr, p.cols, p.xq, p.xd, xq, xd, xs, sh.red);
-    unsigned long long best = 0;
-    consume(rg, p.m, nullptr, p.cols, r0, r1, Epi{ EPI_STORE, p.y, nullptr, 0, 0.0f, 0 }, Act{ xq, xd, xs }, sh.psum,
-            p.err, best);
+    const ActW w = act_layout(sh.act, p.cols);
+    act_prequant(p.xq, p.xd, p.cols, w);
+    if (p.m.type == T_Q4) consume_rows<T_Q4>(rg, p.cols, r0, r1, p.m.d16 != 0, p.y, act_view(w), p.err);
+    else consume_rows<T_Q8>(rg, p.cols, r0, r1, p.m.d16 != 0, p.y, act_view(w), p.err);
 }
 
 /* The activation prologue alone (kc_quantize_q8_dev, kc_rmsnorm_quantize_dev):
@@ -995,14 +1199,13 @@ __global__ void __launch_bounds__(NCT, 1) activation_kernel(const float *x, cons
                                                            float *d, float *xn) {
     extern __shared__ __align__(128) unsigned char smem[];
     float *red = (float *)smem;
-    int8_t *xq = (int8_t *)(smem + 128);
-    float *xd = (float *)(smem + 128 + n);
-    int *xs = (int *)(xd + n / QK);
-    StepArgs a{};
-    a.eps = eps;
-    load_activation(a, SRC_GLOBAL, x, 0, w, 0.0f, nullptr, n, nullptr, nullptr, xq, xd, xs, red);
-    for (int i = threadIdx.x; i < n; i += NCT) q[i] = xq[i];
-    for (int b = threadIdx.x; b < n / QK; b += NCT) d[b] = xd[b];
+    const ActW o = act_layout(smem + 128, n);
+    act_loop(eps, x, w, n, o, red);
+    for (int i = threadIdx.x; i < n; i += NCT) {
+        const int b = i / QK, j = i % QK;
+        q[i] = j < 16 ? o.xlo[b * 16 + j] : o.xhi[b * 16 + j - 16];
+    }
+    for (int b = threadIdx.x; b < n / QK; b += NCT) d[b] = o.xd[b];
     if (xn && w) {
         float ss = 0.0f;
         for (int i = threadIdx.x * 4; i < n; i += NCT * 4) {

@@ -11,12 +11,14 @@ Two bars, both the reference's own:
 - two valid implementations: after such a step logits move by ~1e-2 (the
   reference, Makefile:135-139: "one flip moves later logits by ~1%; most
   seeds have one somewhere"; its own avx2 / avx512vnni builds do the same
-  against its scalar build on these models, tests/test_refspread.py). Long
-  runs are then held to the reference's distribution criterion
-  (tests/compare_logits.py --kl 1e-3: KL <= 1e-3, top-5 overlap >= 4 of 5)
-  and its 150-position bound of 5e-2 (tests/test_e2e.sh:70-86); a greedy
-  token may differ from the oracle's only where the oracle's top-2 margin is
-  within the measured logit difference of that step.
+  against its scalar build on these models, tests/test_refspread.py).
+  Prompt positions are held to the reference's distribution criterion
+  (tests/compare_logits.py --kl 1e-3: argmax, KL <= 1e-3, top-5 overlap >= 4
+  of 5, tests/test_e2e.sh:60-68). Long greedy runs are held to the bound the
+  reference sets for its own builds with FMA over 150 positions: max|d| <=
+  5e-2 max|logit| (compare_logits.py 5e-2 --any-argmax, test_e2e.sh:72-86);
+  on top of it a greedy token may differ from the oracle's only where the
+  oracle's top-2 margin is within the measured logit difference of that step.
 """
 import os
 
@@ -63,12 +65,23 @@ def top5_overlap(a, b):
     return len(set(np.argsort(-a)[:5]) & set(np.argsort(-b)[:5]))
 
 
-def valid_pair(got, ref):
-    """The reference's criterion for two valid implementations (--kl 1e-3 mode),
-    with the argmax allowed to differ only inside the step's logit difference."""
+def argmax_ok(got, ref):
+    """Same argmax, or the two candidates within the step's logit difference."""
     d = float(np.abs(got.astype(np.float64) - ref).max())
-    arg_ok = got.argmax() == ref.argmax() or ref.max() - ref[got.argmax()] <= 2 * d + MARGIN
-    return arg_ok and top5_overlap(got, ref) >= 4 and kl(ref, got) <= 1e-3 and rel_err(got, ref) <= 5e-2
+    return got.argmax() == ref.argmax() or ref.max() - ref[got.argmax()] <= 2 * d + MARGIN
+
+
+def valid_pair(got, ref):
+    """The reference's criterion for two valid implementations one step apart
+    (--kl 1e-3 mode), with the argmax allowed to differ only inside the step's
+    logit difference."""
+    return argmax_ok(got, ref) and top5_overlap(got, ref) >= 4 and kl(ref, got) <= 1e-3 and rel_err(got, ref) <= 5e-2
+
+
+def long_run_ok(got, ref):
+    """The reference's bound for its own builds over long runs (5e-2, no argmax
+    check), plus the argmax rule above."""
+    return rel_err(got, ref) <= 5e-2 and argmax_ok(got, ref)
 
 
 @pytest.mark.parametrize("name", GOLDEN_MODELS)
@@ -128,8 +141,8 @@ def test_out_of_range_inputs():
 def teacher_forced_greedy(path, prompt, steps, kv_type=0):
     """The GPU's device-side greedy stream, then both the GPU (kc_forward) and the
     oracle run on the GPU's tokens. Returns the tokens, the steps that fail the
-    strict bar, the steps that fail the two-implementations bar, and the per-step
-    logit errors."""
+    strict bar, the steps that fail the long-run bar, and the per-step logit
+    errors."""
     m = kb.Model(path)
     st = kb.State(m, kv_type=kv_type)
     st.prefill(prompt[:-1], 0)
@@ -148,7 +161,7 @@ def teacher_forced_greedy(path, prompt, steps, kv_type=0):
         errs.append(float(rel_err(g, lg)))
         if errs[-1] > RTOL or (toks[i] != lg.argmax() and top2_margin(lg) >= MARGIN):
             strict_bad.append(i)
-        if not valid_pair(g, lg):
+        if not long_run_ok(g, lg):
             valid_bad.append((i, int(toks[i]), int(lg.argmax()), errs[-1], kl(lg, g)))
     ref.close()
     return toks, strict_bad, valid_bad, errs
