@@ -472,11 +472,7 @@ static int setup_step_kernel(kc_state *s) {
         PhasePlan P[NPHASE];
         make_plan(g, j, G, P);
         slot = std::max(slot, plan_max_chunk(P));
-        for (int p = 0; p < NPHASE; p++) {
-            int rows = 0;
-            for (int k = 0; k < P[p].nseg; k++) rows += P[p].seg[k].rows;
-            res = std::max(res, rows * (p == PH_D ? 8 : 4));
-        }
+        for (int p = 0; p < NPHASE; p++) res = std::max(res, plan_rows(P[p]) * (p == PH_D ? 8 : 4));
     }
     slot = (slot + 127) & ~127;
     res = (res + 15) & ~15;
@@ -628,7 +624,10 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
         *b.p = s->arena + off;
         off += align256(b.bytes);
     }
+    /* zero the arena and wait: the tables below are copied on the legacy
+     * stream, which does not order against this non-blocking stream */
     e = cudaMemsetAsync(s->arena, 0, total, s->st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->st);
     if (e != cudaSuccess) return fail(cuda_status(e, "memset"));
     e = cudaMallocHost(&s->h_logits, sizeof(float) * c.vocab);
     if (e == cudaSuccess) e = cudaMallocHost(&s->h_ls, sizeof(LoopState));

@@ -84,6 +84,7 @@ enum { PH_A = 0, PH_C = 1, PH_D = 2, PH_E = 3, PH_F = 4, NPHASE = 5 };
 constexpr int CHUNK_BYTES = 32 * 1024;   /* bytes per bulk copy (at least one record) */
 constexpr int GROUP_ROWS = 4;            /* rows per warp task (two gate|up pairs) */
 constexpr int OWN_MAX = 128;             /* rows of x a CTA may own */
+static_assert((NCW & (NCW - 1)) == 0, "warp round-robin uses a mask");
 
 /* Record bytes: quants, scales, the bias when present, padded to 16. */
 __host__ __device__ inline int rec_bytes(int type, int d16, int cols, int bias) {
@@ -106,7 +107,7 @@ __host__ __device__ inline Seg make_seg(int rows, int row0, int type, int d16, i
     s.bias = bias;
     s.rec = rec_bytes(type, d16, cols, bias) * (pair ? 2 : 1);
     const int step = pair ? GROUP_ROWS / 2 : GROUP_ROWS;
-    int rpc = CHUNK_BYTES / s.rec;
+    int rpc = s.rec > 0 ? CHUNK_BYTES / s.rec : 1;
     if (rpc >= step) rpc -= rpc % step;
     s.rpc = rpc < 1 ? 1 : rpc;
     return s;
@@ -115,6 +116,12 @@ __host__ __device__ inline Seg make_seg(int rows, int row0, int type, int d16, i
 /* The phases of CTA j's stream for one layer (A, C, D, E) and the classifier (F). */
 __host__ __device__ inline void make_plan(const StreamGeom &g, int j, int G, PhasePlan *P) {
     int r0, r1;
+    for (int p = 0; p < NPHASE; p++) {   /* unused segments read as empty */
+        P[p].nseg = 0;
+        P[p].cols = 0;
+        P[p].bytes = 0;
+        for (int k = 0; k < 3; k++) P[p].seg[k] = Seg{ 0, 0, 0, 1, T_Q8, 0, 0 };
+    }
     PhasePlan &A = P[PH_A];
     A.nseg = 0;
     A.cols = g.dim;
@@ -146,6 +153,13 @@ __host__ __device__ inline void make_plan(const StreamGeom &g, int j, int G, Pha
         for (int s = 0; s < P[p].nseg; s++) b += (long long)P[p].seg[s].rows * P[p].seg[s].rec;
         P[p].bytes = b;
     }
+}
+
+/* Rows of a phase (its segments are contiguous in the phase's output). */
+__host__ __device__ inline int plan_rows(const PhasePlan &P) {
+    int n = 0;
+    for (int s = 0; s < P.nseg; s++) n += P.seg[s].rows;
+    return n;
 }
 
 /* Largest chunk of a plan: the ring's slot size. */
@@ -312,17 +326,37 @@ struct Ring {
     uint64_t *full, *empty;
     uint8_t *base;
     int nstage, slot_bytes;
-    unsigned idx;   /* chunks issued (producer) or consumed (consumer) so far */
+    int slot;         /* the next chunk's slot */
+    unsigned round;   /* times the ring has wrapped: the slot's use count */
 };
+
+/* The next slot, without divisions. */
+__device__ __forceinline__ void ring_next(Ring &rg) {
+    if (++rg.slot == rg.nstage) {
+        rg.slot = 0;
+        rg.round++;
+    }
+}
+
+/* Consumer: waits until the current slot's chunk has landed. */
+__device__ __forceinline__ const uint8_t *ring_wait_full(const Ring &rg, unsigned *err) {
+    if (!mbar_wait(&rg.full[rg.slot], rg.round & 1u, err) && (threadIdx.x & 31) == 0) atomicOr(err, 2u);
+    return rg.base + (size_t)rg.slot * rg.slot_bytes;
+}
+
+/* Consumer: this warp is done with the current slot. */
+__device__ __forceinline__ void ring_release(Ring &rg) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&rg.empty[rg.slot]);
+    ring_next(rg);
+}
 
 /* Producer: waits for the chunk's slot to be free and issues its bulk copy. */
 __device__ __forceinline__ uint8_t *ring_issue(Ring &rg, unsigned bytes, unsigned *err) {
-    const int slot = (int)(rg.idx % (unsigned)rg.nstage);
     ev(1, EV_EMPTY_WAIT);
-    if (rg.idx >= (unsigned)rg.nstage && !mbar_wait(&rg.empty[slot], (rg.idx / rg.nstage - 1) & 1u, err))
-        atomicOr(err, 2u);
-    mbar_expect_tx(&rg.full[slot], bytes);
-    return rg.base + (size_t)slot * rg.slot_bytes;
+    if (rg.round > 0 && !mbar_wait(&rg.empty[rg.slot], (rg.round - 1) & 1u, err)) atomicOr(err, 2u);
+    mbar_expect_tx(&rg.full[rg.slot], bytes);
+    return rg.base + (size_t)rg.slot * rg.slot_bytes;
 }
 
 /* Producer: the chunks of one phase of the stream, from src on. */
@@ -332,12 +366,11 @@ __device__ __forceinline__ void produce_phase(Ring &rg, const PhasePlan &P, cons
         for (int r = 0; r < S.rows; r += S.rpc) {
             const int n = min(S.rpc, S.rows - r);
             const unsigned bytes = (unsigned)(n * S.rec);
-            const int slot = (int)(rg.idx % (unsigned)rg.nstage);
             uint8_t *dst = ring_issue(rg, bytes, err);
-            bulk_g2s(dst, src, bytes, &rg.full[slot]);
+            bulk_g2s(dst, src, bytes, &rg.full[rg.slot]);
             src += bytes;
             ev(1, EV_ISSUE);
-            rg.idx++;
+            ring_next(rg);
         }
     }
 }
@@ -355,11 +388,10 @@ __device__ __forceinline__ void produce_rows(Ring &rg, const PMat &m, int cols, 
         const size_t ds = (size_t)ra * drow, de = (size_t)(ra + nr) * drow;
         const size_t das = ds & ~(size_t)15, dae = (de + 15) & ~(size_t)15;
         const unsigned qb = (unsigned)(nr * qrow), db = (unsigned)(dae - das);
-        const int slot = (int)(rg.idx % (unsigned)rg.nstage);
         uint8_t *dst = ring_issue(rg, qb + db, err);
-        bulk_g2s(dst, m.q + (size_t)ra * qrow, qb, &rg.full[slot]);
-        bulk_g2s(dst + qbytes, (const uint8_t *)m.d + das, db, &rg.full[slot]);
-        rg.idx++;
+        bulk_g2s(dst, m.q + (size_t)ra * qrow, qb, &rg.full[rg.slot]);
+        bulk_g2s(dst + qbytes, (const uint8_t *)m.d + das, db, &rg.full[rg.slot]);
+        ring_next(rg);
     }
 }
 
@@ -395,8 +427,10 @@ __device__ __forceinline__ Act act_view(const ActW &w) {
     return Act{ (const int4 *)w.xlo, (const int4 *)w.xhi, w.xd, w.xs };
 }
 
-__device__ __forceinline__ float sm_scale(const uint8_t *dr, int b, bool d16) {
-    return d16 ? __half2float(((const __half *)dr)[b]) : ((const float *)dr)[b];
+template <bool D16>
+__device__ __forceinline__ float sm_scale(const uint8_t *dr, int b) {
+    if constexpr (D16) return __half2float(((const __half *)dr)[b]);
+    else return ((const float *)dr)[b];
 }
 
 /* Sum over the warp of four values at once: returns, on lanes 8q..8q+7, the
@@ -427,9 +461,9 @@ struct Lay {
  * (float)s * d_w * d_x and accumulated in block order per lane. Returns
  * reduce4 of the accumulators: {row0, row1, row2, row3}, or with PAIR
  * {gate0, up0, gate1, up1}. */
-template <int TYPE, bool PAIR>
+template <int TYPE, bool D16, bool PAIR>
 __device__ __forceinline__ float dot_group(const uint8_t *q, const uint8_t *d, const Lay &L, int nb, int nr,
-                                           const Act &x, int lane, bool d16) {
+                                           const Act &x, int lane) {
     constexpr int NR = PAIR ? GROUP_ROWS / 2 : GROUP_ROWS;
     constexpr int NA = PAIR ? 2 : 1;
     float acc[NR][NA];
@@ -454,7 +488,7 @@ __device__ __forceinline__ float dot_group(const uint8_t *q, const uint8_t *d, c
                     } else {
                         s = dot_q8(*(const uint4 *)(qr + 32 * b), xl) + dot_q8(*(const uint4 *)(qr + 32 * b + 16), xh);
                     }
-                    acc[i][k] += __fmul_rn((float)s, sm_scale(dr, b, d16)) * dx;
+                    acc[i][k] += __fmul_rn((float)s, sm_scale<D16>(dr, b)) * dx;
                 }
             }
         }
@@ -477,15 +511,15 @@ __device__ __forceinline__ float dot_group(const uint8_t *q, const uint8_t *d, c
  * so the warps stay evenly loaded across chunks. Results (with the record's
  * bias added) go to res[i0 + i] (pairs: res2[i0 + i] = {gate, up}); with res
  * null, single rows are stored straight to out[i0 + i]. */
-template <int TYPE, bool PAIR>
-__device__ __forceinline__ void consume_chunk(const uint8_t *slot, const Lay &L, int n, int nb, int boff, bool d16,
-                                              int g0, int i0, const Act &x, float *res, float *out, int lane, int warp) {
+template <int TYPE, bool D16, bool PAIR>
+__device__ __forceinline__ void consume_chunk(const uint8_t *slot, const Lay &L, int n, int nb, int boff, int g0, int i0,
+                                              const Act &x, float *res, float *out, int lane, int warp) {
     constexpr int NR = PAIR ? GROUP_ROWS / 2 : GROUP_ROWS;
     const int ng = (n + NR - 1) / NR;
-    for (int k = (warp - g0 % NCW + NCW) % NCW; k < ng; k += NCW) {
+    for (int k = (warp - g0) & (NCW - 1); k < ng; k += NCW) {
         const int r = k * NR, nr = min(NR, n - r);
         const uint8_t *q = slot + r * L.qs, *d = slot + L.db + r * L.ds;
-        float v = dot_group<TYPE, PAIR>(q, d, L, nb, nr, x, lane, d16);
+        float v = dot_group<TYPE, D16, PAIR>(q, d, L, nb, nr, x, lane);
         if constexpr (PAIR) {
             const float u = __shfl_down_sync(0xffffffffu, v, 8);
             const int i = lane >> 4;
@@ -502,45 +536,44 @@ __device__ __forceinline__ void consume_chunk(const uint8_t *slot, const Lay &L,
 }
 
 /* Consumer side of one segment of the stream, chunk by chunk from the ring;
- * seg_off: the segment's first row within the phase. Returns the ring's
- * chunk count. Everything arrives by value: nothing the loop reads lives in
- * memory that the mbarrier operations' memory clobbers would force it to
- * reload. */
-template <int TYPE, bool PAIR>
-__device__ __forceinline__ unsigned consume_seg(Ring rg, Seg S, int seg_off, int cols, Act x, float *res,
-                                             unsigned *err) {
+ * seg_off: the segment's first row within the phase. */
+template <int TYPE, bool D16, bool PAIR>
+__device__ __forceinline__ void consume_seg(Ring &rg, Seg S, int seg_off, int cols, const Act &x, float *res,
+                                            unsigned *err) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nb = cols / QK;
     const int qrow = TYPE == T_Q4 ? cols / 2 : cols;
-    const bool d16 = S.d16 != 0;
     const Lay L{ S.rec, qrow, S.rec, S.rec / 2 };
-    const int boff = S.bias ? qrow + nb * (d16 ? 2 : 4) : -1;
+    const int boff = S.bias ? qrow + nb * (D16 ? 2 : 4) : -1;
     constexpr int NR = PAIR ? GROUP_ROWS / 2 : GROUP_ROWS;
     for (int r = 0; r < S.rows; r += S.rpc) {
         const int n = min(S.rpc, S.rows - r);
-        const int slot = (int)(rg.idx % (unsigned)rg.nstage);
-        if (!mbar_wait(&rg.full[slot], (rg.idx / rg.nstage) & 1u, err) && lane == 0) atomicOr(err, 2u);
+        const uint8_t *slot = ring_wait_full(rg, err);
         if (threadIdx.x == 0) ev(0, EV_STAGE_READY);
-        consume_chunk<TYPE, PAIR>(rg.base + (size_t)slot * rg.slot_bytes, L, n, nb, boff, d16, (seg_off + r) / NR,
-                                  seg_off + r, x, res, nullptr, lane, warp);
-        __syncwarp();
+        consume_chunk<TYPE, D16, PAIR>(slot, L, n, nb, boff, (seg_off + r) / NR, seg_off + r, x, res, nullptr, lane,
+                                       warp);
         if (threadIdx.x == 0) ev(0, EV_STAGE_DONE);
-        if (lane == 0) mbar_arrive(&rg.empty[slot]);
-        rg.idx++;
+        ring_release(rg);
     }
-    return rg.idx;
 }
 
-/* All segments of a phase into res (one copy of each consumer loop: Q4/Q8,
- * single rows or gate|up pairs), then a consumer barrier. */
+/* All segments of a phase into res (one inlined copy of each consumer loop:
+ * Q4/Q8, f16/f32 scales, single rows or gate|up pairs), then a consumer
+ * barrier. */
 __device__ __forceinline__ void consume_phase(Ring &rg, const PhasePlan &P, bool pair, const Act &x, float *res,
                                               unsigned *err) {
     int off = 0;
     for (int s = 0; s < P.nseg; s++) {
         const Seg S = P.seg[s];
-        if (S.type == T_Q4) rg.idx = pair ? consume_seg<T_Q4, true>(rg, S, off, P.cols, x, res, err)
-                                          : consume_seg<T_Q4, false>(rg, S, off, P.cols, x, res, err);
-        else rg.idx = pair ? consume_seg<T_Q8, true>(rg, S, off, P.cols, x, res, err)
-                           : consume_seg<T_Q8, false>(rg, S, off, P.cols, x, res, err);
+        switch ((S.type == T_Q4 ? 4 : 0) + (S.d16 ? 2 : 0) + (pair ? 1 : 0)) {
+        case 7: consume_seg<T_Q4, true, true>(rg, S, off, P.cols, x, res, err); break;
+        case 6: consume_seg<T_Q4, true, false>(rg, S, off, P.cols, x, res, err); break;
+        case 5: consume_seg<T_Q4, false, true>(rg, S, off, P.cols, x, res, err); break;
+        case 4: consume_seg<T_Q4, false, false>(rg, S, off, P.cols, x, res, err); break;
+        case 3: consume_seg<T_Q8, true, true>(rg, S, off, P.cols, x, res, err); break;
+        case 2: consume_seg<T_Q8, true, false>(rg, S, off, P.cols, x, res, err); break;
+        case 1: consume_seg<T_Q8, false, true>(rg, S, off, P.cols, x, res, err); break;
+        default: consume_seg<T_Q8, false, false>(rg, S, off, P.cols, x, res, err); break;
+        }
         off += S.rows;
     }
     consumer_sync();
@@ -589,23 +622,19 @@ __device__ __noinline__ unsigned long long finish_phase(int kind, const float *r
 }
 
 /* Consumer of the kernel-level matvec (rows [r0, r1) as produce_rows staged them). */
-template <int TYPE>
-__device__ void consume_rows(Ring &rg, int cols, int r0, int r1, bool d16, float *y, const Act &x, unsigned *err) {
+template <int TYPE, bool D16>
+__device__ void consume_rows(Ring &rg, int cols, int r0, int r1, float *y, const Act &x, unsigned *err) {
     if (r0 >= r1) return;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nb = cols / QK;
-    const int qrow = TYPE == T_Q4 ? cols / 2 : cols, drow = nb * (d16 ? 2 : 4);
+    const int qrow = TYPE == T_Q4 ? cols / 2 : cols, drow = nb * (D16 ? 2 : 4);
     int R, qbytes, dbytes;
-    stage_geom(TYPE, d16, cols, 0, R, qbytes, dbytes);
+    stage_geom(TYPE, D16, cols, 0, R, qbytes, dbytes);
     for (int ra = r0; ra < r1; ra += R) {
         const int nr = min(R, r1 - ra);
-        const int slot = (int)(rg.idx % (unsigned)rg.nstage);
-        if (!mbar_wait(&rg.full[slot], (rg.idx / rg.nstage) & 1u, err) && lane == 0) atomicOr(err, 2u);
+        const uint8_t *slot = ring_wait_full(rg, err);
         const Lay L{ qrow, qbytes + (int)(((size_t)ra * drow) & 15), drow, 0 };
-        consume_chunk<TYPE, false>(rg.base + (size_t)slot * rg.slot_bytes, L, nr, nb, -1, d16, (ra - r0) / GROUP_ROWS,
-                                   ra, x, nullptr, y, lane, warp);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&rg.empty[slot]);
-        rg.idx++;
+        consume_chunk<TYPE, D16, false>(slot, L, nr, nb, -1, (ra - r0) / GROUP_ROWS, ra, x, nullptr, y, lane, warp);
+        ring_release(rg);
     }
 }
 
@@ -832,7 +861,7 @@ __device__ void act_prequant(const int8_t *pq, const float *pd, int cols, const 
 
 /* Shared scratch of an attention item, in floats. */
 __host__ __device__ inline int attention_scratch_floats(int group, int hd) {
-    return group * hd + ATT_TILE * (hd + 1) + ATT_TILE * hd + group * ATT_TILE + 3 * group;
+    return group * hd + ATT_TILE * (hd + 1) + ATT_TILE * hd + group * ATT_TILE + 3 * group + 2 * hd;
 }
 
 /* Attention work item (KV head g, split y) of layer L at position pos (F32
@@ -853,6 +882,7 @@ __device__ __forceinline__ void attention_item(const StepArgs &a, const LayerPla
     const int t_begin = first + y * C, t_end = min(t_begin + C, pos + 1);
     float *sq = fsm, *sk = sq + group * hd, *sv = sk + ATT_TILE * (hd + 1), *sp = sv + ATT_TILE * hd;
     float *sm = sp + group * ATT_TILE, *sl = sm + group, *sa = sl + group;
+    float *knew = sa + group, *vnew = knew + hd;   /* this position's K (after RoPE) and V */
     const float *cs = L.rcos + (size_t)pos * h2, *sn = L.rsin + (size_t)pos * h2;
     for (int idx = tid; idx < group * h2; idx += NCT) {
         const int h = idx / h2, i = idx % h2;
@@ -861,15 +891,26 @@ __device__ __forceinline__ void attention_item(const StepArgs &a, const LayerPla
         sq[h * hd + 2 * i] = __fsub_rn(__fmul_rn(qa, c), __fmul_rn(qb, s));
         sq[h * hd + 2 * i + 1] = __fadd_rn(__fmul_rn(qa, s), __fmul_rn(qb, c));
     }
+    /* the split holding pos writes that position's K and V row into the cache
+     * and keeps it in shared memory: its own tile reads take it from there, not
+     * back from global memory */
     if (t_end == pos + 1) {
         const float *kn = a.qkv + a.q_dim + (size_t)g * hd, *vn = a.qkv + a.q_dim + a.kv_dim + (size_t)g * hd;
         float *kr = L.kc + (size_t)pos * a.kv_dim + (size_t)g * hd, *vr = L.vc + (size_t)pos * a.kv_dim + (size_t)g * hd;
         for (int i = tid; i < h2; i += NCT) {
             const float ka = __ldcg(kn + 2 * i), kb = __ldcg(kn + 2 * i + 1), c = cs[i], s = sn[i];
-            kr[2 * i] = __fsub_rn(__fmul_rn(ka, c), __fmul_rn(kb, s));
-            kr[2 * i + 1] = __fadd_rn(__fmul_rn(ka, s), __fmul_rn(kb, c));
+            const float k0 = __fsub_rn(__fmul_rn(ka, c), __fmul_rn(kb, s));
+            const float k1 = __fadd_rn(__fmul_rn(ka, s), __fmul_rn(kb, c));
+            kr[2 * i] = k0;
+            kr[2 * i + 1] = k1;
+            knew[2 * i] = k0;
+            knew[2 * i + 1] = k1;
         }
-        for (int i = tid; i < hd; i += NCT) vr[i] = __ldcg(vn + i);
+        for (int i = tid; i < hd; i += NCT) {
+            const float v = __ldcg(vn + i);
+            vr[i] = v;
+            vnew[i] = v;
+        }
     }
     if (tid < group) {
         sm[tid] = -INFINITY;
@@ -886,8 +927,14 @@ __device__ __forceinline__ void attention_item(const StepArgs &a, const LayerPla
         for (int idx = tid; idx < nt * h4; idx += NCT) {
             const int t = idx / h4, c4 = idx % h4;
             const size_t off = (size_t)(t0 + t) * a.kv_dim + (size_t)g * hd + 4 * c4;
-            const float4 kv = __ldcg((const float4 *)(L.kc + off));
-            const float4 vv = __ldcg((const float4 *)(L.vc + off));
+            float4 kv, vv;
+            if (t0 + t == pos) {
+                kv = make_float4(knew[4 * c4], knew[4 * c4 + 1], knew[4 * c4 + 2], knew[4 * c4 + 3]);
+                vv = make_float4(vnew[4 * c4], vnew[4 * c4 + 1], vnew[4 * c4 + 2], vnew[4 * c4 + 3]);
+            } else {
+                kv = __ldcg((const float4 *)(L.kc + off));
+                vv = __ldcg((const float4 *)(L.vc + off));
+            }
             float *kd = sk + t * (hd + 1) + 4 * c4;
             kd[0] = kv.x; kd[1] = kv.y; kd[2] = kv.z; kd[3] = kv.w;
             *(float4 *)(sv + t * hd + 4 * c4) = vv;
@@ -1045,7 +1092,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
     ev_init(true);
     if (threadIdx.x == 0) make_plan(a.geom, blockIdx.x, gridDim.x, s_plan);
     init_ring(sh, a.nstage);
-    Ring rg{ sh.full, sh.empty, sh.ring, a.nstage, a.slot_bytes, 0u };
+    Ring rg{ sh.full, sh.empty, sh.ring, a.nstage, a.slot_bytes, 0, 0u };
     if ((threadIdx.x >> 5) == NCW) {
         if ((threadIdx.x & 31) == 0) producer(a, rg);
         return;
@@ -1082,8 +1129,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
             consume_phase(rg, s_plan[PH_A], false, act_view(w_dim), sh.res, a.err);
             {
                 const PhasePlan &P = s_plan[PH_A];
-                const int nr = P.seg[0].rows + (P.nseg > 1 ? P.seg[1].rows : 0) + (P.nseg > 2 ? P.seg[2].rows : 0);
-                finish_phase(FIN_STORE, sh.res, nr, P.nseg ? P.seg[0].row0 : 0, a.qkv, nullptr, 0, 0.0f, sh.cta_best);
+                finish_phase(FIN_STORE, sh.res, plan_rows(P), P.nseg ? P.seg[0].row0 : 0, a.qkv, nullptr, 0, 0.0f,
+                             sh.cta_best);
             }
             grid_barrier(a, expect);
             /* B: attention */
@@ -1180,7 +1227,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) matvec_kernel(const __grid_co
     const Smem sh = carve(smem, p.nstage, p.act_bytes);
     ev_init(false);
     init_ring(sh, p.nstage);
-    Ring rg{ sh.full, sh.empty, sh.ring, p.nstage, p.slot_bytes, 0u };
+    Ring rg{ sh.full, sh.empty, sh.ring, p.nstage, p.slot_bytes, 0, 0u };
     int r0, r1;
     share_rows(p.m.rows, blockIdx.x, gridDim.x, r0, r1);
     if ((threadIdx.x >> 5) == NCW) {
@@ -1189,8 +1236,13 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) matvec_kernel(const __grid_co
     }
     const ActW w = act_layout(sh.act, p.cols);
     act_prequant(p.xq, p.xd, p.cols, w);
-    if (p.m.type == T_Q4) consume_rows<T_Q4>(rg, p.cols, r0, r1, p.m.d16 != 0, p.y, act_view(w), p.err);
-    else consume_rows<T_Q8>(rg, p.cols, r0, r1, p.m.d16 != 0, p.y, act_view(w), p.err);
+    if (p.m.type == T_Q4) {
+        if (p.m.d16) consume_rows<T_Q4, true>(rg, p.cols, r0, r1, p.y, act_view(w), p.err);
+        else consume_rows<T_Q4, false>(rg, p.cols, r0, r1, p.y, act_view(w), p.err);
+    } else {
+        if (p.m.d16) consume_rows<T_Q8, true>(rg, p.cols, r0, r1, p.y, act_view(w), p.err);
+        else consume_rows<T_Q8, false>(rg, p.cols, r0, r1, p.y, act_view(w), p.err);
+    }
 }
 
 /* The activation prologue alone (kc_quantize_q8_dev, kc_rmsnorm_quantize_dev):
