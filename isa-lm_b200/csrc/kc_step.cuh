@@ -690,6 +690,7 @@ __device__ __forceinline__ float embed1(const StepArgs &a, int tok, int cols, in
  * 64 blocks, 8 lanes per block) before it uses any, so a prologue costs one
  * round trip to L2. */
 constexpr int ACT_PASSES = 4;   /* passes of 64 blocks a thread holds in registers */
+constexpr int SSP_LOADS = 8;    /* per-lane loads of the per-CTA sums: grids of up to 256 CTAs */
 
 /* Quantizes the 4 values of block b held by this lane (elements j0..j0+3)
  * with the other 7 lanes of its group and stores them in the split layout. */
@@ -720,6 +721,15 @@ __device__ __noinline__ void act_float(float eps, const float *x, const float *n
     const int passes = (nb + NCT / 8 - 1) / (NCT / 8);
     const bool norm = norm_w != nullptr;
     if (tid == 0) ev(0, EV_ACT_ENTRY);
+    /* every warp loads the G per-CTA sums of squares itself (no block
+     * reduction, no extra barrier), in the same order as every other warp */
+    const int lane = tid & 31;
+    float part[SSP_LOADS];
+#pragma unroll
+    for (int k = 0; k < SSP_LOADS; k++) {
+        const int idx = k * 32 + lane;
+        part[k] = (norm && ssp && idx < (int)gridDim.x) ? __ldcg(ssp + idx) : 0.0f;
+    }
     float4 v[ACT_PASSES], w[ACT_PASSES];
 #pragma unroll
     for (int p = 0; p < ACT_PASSES; p++) {
@@ -731,22 +741,14 @@ __device__ __noinline__ void act_float(float eps, const float *x, const float *n
             if (norm) w[p] = *(const float4 *)(norm_w + b * QK + j0);
         }
     }
-    if (tid == 0) {
-        asm volatile("" ::"f"(v[0].x));
-        ev(0, EV_ACT_LOADED);
-    }
     float inv = 1.0f;
     if (norm) {
         float ss;
         if (ssp) {
-            if (tid < 32) {
-                float t = 0.0f;
-                for (int k = tid; k < (int)gridDim.x; k += 32) t += __ldcg(ssp + k);
-                t = warp_sum(t);
-                if (tid == 0) red[0] = t;
-            }
-            consumer_sync();
-            ss = red[0];
+            float t = 0.0f;
+#pragma unroll
+            for (int k = 0; k < SSP_LOADS; k++) t += part[k];
+            ss = warp_sum(t);
         } else {
             float t = 0.0f;
 #pragma unroll
