@@ -368,9 +368,10 @@ static int set_smem_attributes() {
 }
 
 /* Ring depth that fits beside the fixed part of a streaming CTA's shared memory. */
-static int ring_stages(int slot, int act_bytes, int static_bytes, int res_bytes = 0) {
+static int ring_stages(int slot, int act_bytes, int static_bytes, int res_bytes = 0, int wbuf_bytes = 0) {
     int nst = 16;
-    while (nst >= 2 && smem_fixed_bytes(nst, act_bytes, res_bytes) + nst * slot > KC_MAX_SMEM - static_bytes) nst--;
+    while (nst >= 2 && smem_fixed_bytes(nst, act_bytes, res_bytes, wbuf_bytes) + nst * slot > KC_MAX_SMEM - static_bytes)
+        nst--;
     return nst;
 }
 
@@ -493,12 +494,13 @@ static int setup_step_kernel(kc_state *s) {
     }
     cudaFuncAttributes fa;
     CK(cudaFuncGetAttributes(&fa, step_kernel));
-    const int nst = ring_stages(slot, act, (int)fa.sharedSizeBytes, res);
+    const int wbuf = 4 * c.dim;
+    const int nst = ring_stages(slot, act, (int)fa.sharedSizeBytes, res, wbuf);
     if (nst < 2) {
         set_error("layer shapes leave no room for the weight ring in shared memory");
         return KC_E_SHAPE;
     }
-    s->step_smem = smem_fixed_bytes(nst, act, res) + nst * slot;
+    s->step_smem = smem_fixed_bytes(nst, act, res, wbuf) + nst * slot;
     int per_sm = 0;
     CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, step_kernel, STEP_THREADS, s->step_smem));
     if (per_sm < 1) {
@@ -521,7 +523,7 @@ static int setup_step_kernel(kc_state *s) {
     a.eps = c.norm_eps; a.attn_scale = c.attn_scale; a.attn_softcap = c.attn_softcap; a.final_softcap = c.final_softcap;
     a.embed_scale = c.embed_scale; a.act = c.act;
     a.nsplit = std::min(MAX_NSPLIT, std::max(1, s->num_sms / c.n_kv_heads));
-    a.nstage = nst; a.slot_bytes = slot; a.act_bytes = act; a.res_bytes = res;
+    a.nstage = nst; a.slot_bytes = slot; a.act_bytes = act; a.res_bytes = res; a.wbuf_bytes = wbuf;
     a.timeline = nullptr; a.timeline_n = s->timeline_n; a.timeline_cap = 4096;
     return KC_OK;
 }

@@ -81,7 +81,7 @@ struct PhasePlan {
 };
 
 enum { PH_A = 0, PH_C = 1, PH_D = 2, PH_E = 3, PH_F = 4, NPHASE = 5 };
-constexpr int CHUNK_BYTES = 32 * 1024;   /* bytes per bulk copy (at least one record) */
+constexpr int CHUNK_BYTES = 48 * 1024;   /* bytes per bulk copy (at least one record) */
 constexpr int GROUP_ROWS = 4;            /* rows per warp task (two gate|up pairs) */
 constexpr int OWN_MAX = 128;             /* rows of x a CTA may own */
 static_assert((NCW & (NCW - 1)) == 0, "warp round-robin uses a mask");
@@ -189,7 +189,7 @@ struct StepArgs {
     int *out_tokens;
     int n_layers, dim, q_dim, kv_dim, hidden, vocab, max_seq, n_heads, n_kv_heads, hd;
     float eps, attn_scale, attn_softcap, final_softcap, embed_scale;
-    int act, nsplit, nstage, slot_bytes, act_bytes, res_bytes;
+    int act, nsplit, nstage, slot_bytes, act_bytes, res_bytes, wbuf_bytes;
     int nsteps, run_cls;            /* steps in this launch; run the classifier */
     unsigned long long *timeline;   /* optional: globaltimer at start and after each barrier (CTA 0) */
     unsigned *timeline_n;
@@ -692,6 +692,20 @@ __device__ __forceinline__ float embed1(const StepArgs &a, int tok, int cols, in
 constexpr int ACT_PASSES = 4;   /* passes of 64 blocks a thread holds in registers */
 constexpr int SSP_LOADS = 8;    /* per-lane loads of the per-CTA sums: grids of up to 256 CTAs */
 
+/* Starts copying the norm weights that this thread's act_float slots read
+ * into wbuf (asynchronous, no wait): issued before a grid barrier, the copy
+ * overlaps the wait instead of adding a round trip after it. */
+__device__ __forceinline__ void prefetch_norm(float *wbuf, const float *nw, int cols) {
+    const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 7) * 4;
+    if (!nw) return;
+#pragma unroll
+    for (int p = 0; p < ACT_PASSES; p++) {
+        const int b = p * (NCT / 8) + (tid >> 3);
+        if (b < nb) cp_async16(wbuf + b * QK + j0, nw + b * QK + j0);
+    }
+    cp_async_commit();
+}
+
 /* Quantizes the 4 values of block b held by this lane (elements j0..j0+3)
  * with the other 7 lanes of its group and stores them in the split layout. */
 __device__ __forceinline__ void put_quant(const ActW &o, int b, int nb, int j0, float u[4]) {
@@ -716,7 +730,7 @@ __device__ __forceinline__ void put_quant(const ActW &o, int b, int nb, int j0, 
  * any, so the prologue costs one round trip to L2; the quantize loop is not
  * unrolled (one copy of its code). */
 __device__ __noinline__ void act_float(float eps, const float *x, const float *norm_w, const float *ssp, int cols, ActW o,
-                                       float *red) {
+                                       float *red, const float *wstaged) {
     const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 7) * 4;
     const int passes = (nb + NCT / 8 - 1) / (NCT / 8);
     const bool norm = norm_w != nullptr;
@@ -736,10 +750,14 @@ __device__ __noinline__ void act_float(float eps, const float *x, const float *n
         const int b = p * (NCT / 8) + (tid >> 3);
         v[p] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         w[p] = v[p];
-        if (p < passes && b < nb) {
-            v[p] = __ldcg((const float4 *)(x + b * QK + j0));
-            if (norm) w[p] = *(const float4 *)(norm_w + b * QK + j0);
-        }
+        if (p < passes && b < nb) v[p] = __ldcg((const float4 *)(x + b * QK + j0));
+    }
+    if (norm && wstaged) cp_async_wait_all();
+#pragma unroll
+    for (int p = 0; p < ACT_PASSES; p++) {
+        const int b = p * (NCT / 8) + (tid >> 3);
+        if (norm && p < passes && b < nb)
+            w[p] = *(const float4 *)((wstaged ? wstaged : norm_w) + b * QK + j0);
     }
     float inv = 1.0f;
     if (norm) {
@@ -832,9 +850,10 @@ __device__ __noinline__ void act_loop(float eps, const float *x, const float *no
 }
 
 /* act_float for up to 4 * 2048 columns; wider vectors pass by pass. */
+/* wstaged: norm_w already copied into shared memory by prefetch_norm. */
 __device__ __forceinline__ void load_activation(const StepArgs &a, const float *x, const float *norm_w, const float *ssp,
-                                                int cols, const ActW &o, float *red) {
-    if (cols <= ACT_PASSES * NCT / 8 * QK) act_float(a.eps, x, norm_w, ssp, cols, o, red);
+                                                int cols, const ActW &o, float *red, const float *wstaged = nullptr) {
+    if (cols <= ACT_PASSES * NCT / 8 * QK) act_float(a.eps, x, norm_w, ssp, cols, o, red, wstaged);
     else act_loop(a.eps, x, norm_w, cols, o, red);
 }
 
@@ -1038,16 +1057,18 @@ struct Smem {
     float *red;
     float *own;
     float *res;
+    float *wbuf;   /* the next norm phase's weights, copied in ahead of its barrier */
     unsigned char *act;
     uint8_t *ring;
 };
 
 /* res_bytes: a phase's row results (16-byte multiple). */
-__host__ __device__ inline int smem_fixed_bytes(int nstage, int act_bytes, int res_bytes = 0) {
-    return 16 * nstage + 8 * NCW + 16 + 128 + 4 * OWN_MAX + res_bytes + act_bytes + 128;
+__host__ __device__ inline int smem_fixed_bytes(int nstage, int act_bytes, int res_bytes = 0, int wbuf_bytes = 0) {
+    return 16 * nstage + 8 * NCW + 16 + 128 + 4 * OWN_MAX + res_bytes + wbuf_bytes + act_bytes + 128;
 }
 
-__device__ __forceinline__ Smem carve(unsigned char *smem, int nstage, int act_bytes, int res_bytes = 0) {
+__device__ __forceinline__ Smem carve(unsigned char *smem, int nstage, int act_bytes, int res_bytes = 0,
+                                      int wbuf_bytes = 0) {
     Smem s;
     s.full = (uint64_t *)smem;
     s.empty = s.full + nstage;
@@ -1056,7 +1077,8 @@ __device__ __forceinline__ Smem carve(unsigned char *smem, int nstage, int act_b
     s.red = (float *)(s.flag + 4);
     s.own = s.red + 32;
     s.res = s.own + OWN_MAX;
-    s.act = (unsigned char *)s.res + res_bytes;
+    s.wbuf = (float *)((unsigned char *)s.res + res_bytes);
+    s.act = (unsigned char *)s.wbuf + wbuf_bytes;
     s.ring = (uint8_t *)(((uintptr_t)(s.act + act_bytes) + 127) & ~(uintptr_t)127);
     return s;
 }
@@ -1090,7 +1112,7 @@ __device__ __forceinline__ void producer(const StepArgs &a, Ring rg) {
 
 __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_constant__ StepArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
-    const Smem sh = carve(smem, a.nstage, a.act_bytes, a.res_bytes);
+    const Smem sh = carve(smem, a.nstage, a.act_bytes, a.res_bytes, a.wbuf_bytes);
     ev_init(true);
     if (threadIdx.x == 0) make_plan(a.geom, blockIdx.x, gridDim.x, s_plan);
     init_ring(sh, a.nstage);
@@ -1113,7 +1135,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
         const int tk = ok ? tok : 0, ps = ok ? pos : 0;
         const int logit_row0 = (__ldcg(&a.ls->step) % LOGITS_RING) * a.vocab;
         for (int l = 0; l < a.n_layers; l++) {
-            const LayerPlan &L = a.layers[l];
+            const LayerPlan L = a.layers[l];
+            const float *next_norm = l + 1 < a.n_layers ? a.layers[l + 1].attn_norm : (a.run_cls ? a.final_norm : nullptr);
             /* A: Q/K/V */
             if (l == 0) {
                 act_embed(a.emb, a.embed_scale, tk, L.attn_norm, a.inv0[tk], a.dim, w_dim);
@@ -1124,7 +1147,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
                     sh.own[r - own0] = e1;
                 }
             } else {
-                load_activation(a, a.x, L.attn_norm, a.ssp, a.dim, w_dim, sh.red);
+                load_activation(a, a.x, L.attn_norm, a.ssp, a.dim, w_dim, sh.red, sh.wbuf);
             }
             trace_mark(a, expect / G, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
@@ -1147,9 +1170,10 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_C], false, act_view(w_q), sh.res, a.err);
             finish_phase(FIN_RESID, sh.res, nown, own0, a.x, sh.own, 0, 0.0f, sh.cta_best);
+            prefetch_norm(sh.wbuf, L.ffn_norm, a.dim);
             grid_barrier(a, expect, sh.own, nown);
             /* D: gate/up + activation */
-            load_activation(a, a.x, L.ffn_norm, a.ssp, a.dim, w_dim, sh.red);
+            load_activation(a, a.x, L.ffn_norm, a.ssp, a.dim, w_dim, sh.red, sh.wbuf);
             trace_mark(a, expect / G, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_D], true, act_view(w_dim), sh.res, a.err);
@@ -1162,11 +1186,12 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_E], false, act_view(w_h), sh.res, a.err);
             finish_phase(FIN_RESID, sh.res, nown, own0, a.x, sh.own, 0, 0.0f, sh.cta_best);
+            prefetch_norm(sh.wbuf, next_norm, a.dim);
             grid_barrier(a, expect, sh.own, nown);
         }
         /* F: classifier + argmax */
         if (a.run_cls) {
-            load_activation(a, a.x, a.final_norm, a.ssp, a.dim, w_dim, sh.red);
+            load_activation(a, a.x, a.final_norm, a.ssp, a.dim, w_dim, sh.red, sh.wbuf);
             trace_mark(a, expect / G, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_F], false, act_view(w_dim), sh.res, a.err);
