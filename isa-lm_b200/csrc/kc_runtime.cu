@@ -477,7 +477,8 @@ static int setup_step_kernel(kc_state *s) {
         PhasePlan P[NPHASE];
         make_plan(g, j, G, P);
         slot = std::max(slot, plan_max_chunk(P));
-        for (int p = 0; p < NPHASE; p++) res = std::max(res, plan_rows(P[p]) * (p == PH_D ? 8 : 4));
+        for (int p = 0; p < NPHASE; p++)
+            res = std::max(res, plan_rows(P[p]) * (p == PH_D ? 8 : 4 * col_slices(P[p].cols / QK, false)));
     }
     slot = (slot + 127) & ~127;
     res = (res + 15) & ~15;
@@ -574,7 +575,7 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
     if (kv_type != KC_F32) { set_error("KV cache type not supported by this build yet"); return KC_E_SHAPE; }
     if (c.qk_norm || c.post_norms) { set_error("qk_norm / post_norms not supported by this build yet"); return KC_E_SHAPE; }
     const int group = c.n_heads / c.n_kv_heads;
-    if (group * c.head_dim > ATT_MAX_OUT || c.head_dim % 4) {
+    if (group * c.head_dim > ATT_MAX_OUT || c.head_dim % 4 || c.head_dim > 4 * NCT * ATT_KV4 / ATT_TILE) {
         set_error("attention head layout outside this build's kernel limits");
         return KC_E_SHAPE;
     }

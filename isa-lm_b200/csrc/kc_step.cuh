@@ -85,6 +85,7 @@ constexpr int CHUNK_BYTES = 48 * 1024;   /* bytes per bulk copy (at least one re
 constexpr int GROUP_ROWS = 4;            /* rows per warp task (two gate|up pairs) */
 constexpr int OWN_MAX = 128;             /* rows of x a CTA may own */
 static_assert((NCW & (NCW - 1)) == 0, "warp round-robin uses a mask");
+constexpr int SSP_LOADS = 8;             /* per-lane loads of per-CTA values (sums, flags): grids of up to 256 CTAs */
 
 /* Record bytes: quants, scales, the bias when present, padded to 16. */
 __host__ __device__ inline int rec_bytes(int type, int d16, int cols, int bias) {
@@ -217,7 +218,8 @@ __device__ __forceinline__ void ev_init(bool enabled) {
 }
 
 enum { EV_PRO_DONE = 2, EV_STAGE_READY = 3, EV_STAGE_DONE = 4, EV_ARRIVE = 5, EV_RELEASE = 6, EV_EMPTY_WAIT = 7,
-       EV_ISSUE = 8, EV_ACT_ENTRY = 9, EV_ACT_LOADED = 10, EV_ACT_INV = 11, EV_ACT_QUANT = 12 };
+       EV_ISSUE = 8, EV_ACT_ENTRY = 9, EV_ACT_LOADED = 10, EV_ACT_INV = 11, EV_ACT_QUANT = 12, EV_ATT_PRE = 13,
+       EV_ATT_TILE = 14, EV_ATT_PART = 15, EV_ATT_COMBINE = 16, EV_ATT_DONE = 17 };
 
 __device__ __forceinline__ void ev(int who, unsigned code) {
     unsigned long long *log = s_evp;
@@ -290,15 +292,17 @@ __device__ __forceinline__ void wait_count(const StepArgs &a, unsigned target) {
     timeline_mark(a);
 }
 
-/* Grid barrier: every CTA arrives once; `expect` (the same in every CTA)
- * counts the arrivals due so far in this launch (the host zeroes the counter
- * before each launch). With own set, warp 0 first stores the sum of squares
- * of the CTA's nown rows of x into ssp[blockIdx.x], ordered before the
- * arrival by thread 0's fence. */
-__device__ __forceinline__ void grid_barrier(const StepArgs &a, unsigned &expect, const float *own = nullptr,
-                                             int nown = 0) {
+/* Grid barrier of the phases: every CTA arrives once on the arrival counter;
+ * `expect` (the same in every CTA) counts the arrivals due so far in this
+ * launch (the host zeroes the counter before each launch). A counter with
+ * one atomic per CTA measured faster on B200 than per-CTA flags polled by
+ * every CTA (which floods L2 with polls) or a two-level counter. With own
+ * set, warp 0 first stores the sum of squares of the CTA's nown rows of x
+ * into ssp[blockIdx.x], ordered before the arrival by thread 0's fence. */
+__device__ __forceinline__ void grid_barrier(const StepArgs &a, unsigned &expect, unsigned &pidx,
+                                             const float *own = nullptr, int nown = 0) {
     consumer_sync();
-    const unsigned p = expect / gridDim.x;
+    const unsigned p = pidx++;
     expect += gridDim.x;
     if (threadIdx.x < 32) {
         if (own) {
@@ -462,7 +466,7 @@ struct Lay {
  * reduce4 of the accumulators: {row0, row1, row2, row3}, or with PAIR
  * {gate0, up0, gate1, up1}. */
 template <int TYPE, bool D16, bool PAIR>
-__device__ __forceinline__ float dot_group(const uint8_t *q, const uint8_t *d, const Lay &L, int nb, int nr,
+__device__ __forceinline__ float dot_group(const uint8_t *q, const uint8_t *d, const Lay &L, int b_lo, int b_hi, int nr,
                                            const Act &x, int lane) {
     constexpr int NR = PAIR ? GROUP_ROWS / 2 : GROUP_ROWS;
     constexpr int NA = PAIR ? 2 : 1;
@@ -472,7 +476,7 @@ __device__ __forceinline__ float dot_group(const uint8_t *q, const uint8_t *d, c
 #pragma unroll
         for (int k = 0; k < NA; k++) acc[i][k] = 0.0f;
 #pragma unroll 2
-    for (int b = lane; b < nb; b += 32) {
+    for (int b = b_lo + lane; b < b_hi; b += 32) {
         const int4 xl = x.xlo[b], xh = x.xhi[b];
         const float dx = x.xd[b];
         const int corr = TYPE == T_Q4 ? x.xs[b] : 0;
@@ -506,20 +510,28 @@ __device__ __forceinline__ float dot_group(const uint8_t *q, const uint8_t *d, c
     return reduce4(t, lane);
 }
 
+/* Column slices of a long row: each slice (a block range) is a task of its
+ * own, so that a few long rows still keep every warp busy; the slices' partial
+ * sums are added in slice order by the finish pass. 1, 2 or 4. */
+__host__ __device__ inline int col_slices(int nb, bool pair) {
+    return pair || nb < 128 ? 1 : (nb < 256 ? 2 : 4);
+}
+
 /* The rows [0, n) of one ring slot, in tasks of GROUP_ROWS rows (or pairs)
- * dealt to the warps round-robin by the task's index in the phase (g0 + k),
- * so the warps stay evenly loaded across chunks. Results (with the record's
- * bias added) go to res[i0 + i] (pairs: res2[i0 + i] = {gate, up}); with res
- * null, single rows are stored straight to out[i0 + i]. */
+ * times ns column slices, dealt to the warps round-robin by the task's index
+ * in the phase (g0 + k), so the warps stay evenly loaded across chunks.
+ * Results go to res[(i0 + i) * ns + slice] (the record's bias added by slice
+ * 0; pairs: res2[i0 + i] = {gate, up}); with res null, single rows are stored
+ * straight to out[i0 + i] (ns 1). */
 template <int TYPE, bool D16, bool PAIR>
-__device__ __forceinline__ void consume_chunk(const uint8_t *slot, const Lay &L, int n, int nb, int boff, int g0, int i0,
-                                              const Act &x, float *res, float *out, int lane, int warp) {
+__device__ __forceinline__ void consume_chunk(const uint8_t *slot, const Lay &L, int n, int nb, int ns, int boff, int g0,
+                                              int i0, const Act &x, float *res, float *out, int lane, int warp) {
     constexpr int NR = PAIR ? GROUP_ROWS / 2 : GROUP_ROWS;
-    const int ng = (n + NR - 1) / NR;
-    for (int k = (warp - g0) & (NCW - 1); k < ng; k += NCW) {
-        const int r = k * NR, nr = min(NR, n - r);
+    const int ng = (n + NR - 1) / NR, lg = ns == 4 ? 2 : (ns == 2 ? 1 : 0);
+    for (int k = (warp - g0) & (NCW - 1); k < (ng << lg); k += NCW) {
+        const int sl = k & (ns - 1), r = (k >> lg) * NR, nr = min(NR, n - r);
         const uint8_t *q = slot + r * L.qs, *d = slot + L.db + r * L.ds;
-        float v = dot_group<TYPE, D16, PAIR>(q, d, L, nb, nr, x, lane);
+        float v = dot_group<TYPE, D16, PAIR>(q, d, L, (sl * nb) >> lg, ((sl + 1) * nb) >> lg, nr, x, lane);
         if constexpr (PAIR) {
             const float u = __shfl_down_sync(0xffffffffu, v, 8);
             const int i = lane >> 4;
@@ -527,8 +539,8 @@ __device__ __forceinline__ void consume_chunk(const uint8_t *slot, const Lay &L,
         } else {
             const int i = lane >> 3;
             if ((lane & 7) == 0 && i < nr) {
-                if (boff >= 0) v = __fadd_rn(v, *(const float *)(q + i * L.qs + boff));
-                if (res) res[i0 + r + i] = v;
+                if (boff >= 0 && sl == 0) v = __fadd_rn(v, *(const float *)(q + i * L.qs + boff));
+                if (res) res[(i0 + r + i) * ns + sl] = v;
                 else out[i0 + r + i] = v;
             }
         }
@@ -544,13 +556,14 @@ __device__ __forceinline__ void consume_seg(Ring &rg, Seg S, int seg_off, int co
     const int qrow = TYPE == T_Q4 ? cols / 2 : cols;
     const Lay L{ S.rec, qrow, S.rec, S.rec / 2 };
     const int boff = S.bias ? qrow + nb * (D16 ? 2 : 4) : -1;
+    const int ns = col_slices(nb, PAIR);
     constexpr int NR = PAIR ? GROUP_ROWS / 2 : GROUP_ROWS;
     for (int r = 0; r < S.rows; r += S.rpc) {
         const int n = min(S.rpc, S.rows - r);
         const uint8_t *slot = ring_wait_full(rg, err);
         if (threadIdx.x == 0) ev(0, EV_STAGE_READY);
-        consume_chunk<TYPE, D16, PAIR>(slot, L, n, nb, boff, (seg_off + r) / NR, seg_off + r, x, res, nullptr, lane,
-                                       warp);
+        consume_chunk<TYPE, D16, PAIR>(slot, L, n, nb, ns, boff, ((seg_off + r) / NR) * ns, seg_off + r, x, res,
+                                       nullptr, lane, warp);
         if (threadIdx.x == 0) ev(0, EV_STAGE_DONE);
         ring_release(rg);
     }
@@ -586,21 +599,27 @@ enum { FIN_STORE = 0, FIN_RESID = 1, FIN_PAIR = 2, FIN_LOGITS = 3 };
  * or logits with the first-index argmax key of the CTA's rows (returned on
  * thread 0; 0 otherwise). */
 __device__ __noinline__ unsigned long long finish_phase(int kind, const float *res, int nrows, int row0, float *out,
-                                                        float *own, int act, float softcap, unsigned long long *cta_best) {
+                                                        float *own, int act, float softcap, unsigned long long *cta_best,
+                                                        int ns) {
     unsigned long long best = 0;
     for (int i = threadIdx.x; i < nrows; i += NCT) {
         const int row = row0 + i;
+        float sum = 0.0f;
+        if (kind != FIN_PAIR) {
+            sum = res[i * ns];
+            for (int k = 1; k < ns; k++) sum = __fadd_rn(sum, res[i * ns + k]);
+        }
         if (kind == FIN_STORE) {
-            out[row] = res[i];
+            out[row] = sum;
         } else if (kind == FIN_RESID) {
-            const float v = __fadd_rn(own[i], res[i]);
+            const float v = __fadd_rn(own[i], sum);
             own[i] = v;
             out[row] = v;
         } else if (kind == FIN_PAIR) {
             const float2 gu = ((const float2 *)res)[i];
             out[row] = act_mul(act, gu.x, gu.y);
         } else {
-            float v = res[i];
+            float v = sum;
             if (softcap > 0.0f) v = __fmul_rn(softcap, tanhf(__fdiv_rn(v, softcap)));
             out[row] = v;
             const unsigned long long k = argmax_key(v, row);
@@ -633,7 +652,7 @@ __device__ void consume_rows(Ring &rg, int cols, int r0, int r1, float *y, const
         const int nr = min(R, r1 - ra);
         const uint8_t *slot = ring_wait_full(rg, err);
         const Lay L{ qrow, qbytes + (int)(((size_t)ra * drow) & 15), drow, 0 };
-        consume_chunk<TYPE, D16, false>(slot, L, nr, nb, -1, (ra - r0) / GROUP_ROWS, ra, x, nullptr, y, lane, warp);
+        consume_chunk<TYPE, D16, false>(slot, L, nr, nb, 1, -1, (ra - r0) / GROUP_ROWS, ra, x, nullptr, y, lane, warp);
         ring_release(rg);
     }
 }
@@ -690,7 +709,6 @@ __device__ __forceinline__ float embed1(const StepArgs &a, int tok, int cols, in
  * 64 blocks, 8 lanes per block) before it uses any, so a prologue costs one
  * round trip to L2. */
 constexpr int ACT_PASSES = 4;   /* passes of 64 blocks a thread holds in registers */
-constexpr int SSP_LOADS = 8;    /* per-lane loads of the per-CTA sums: grids of up to 256 CTAs */
 
 /* Starts copying the norm weights that this thread's act_float slots read
  * into wbuf (asynchronous, no wait): issued before a grid barrier, the copy
@@ -892,7 +910,7 @@ __host__ __device__ inline int attention_scratch_floats(int group, int hd) {
  * set), online softmax and the weighted V sum over the split's positions; the
  * last CTA of the KV head to finish combines the splits into a.ao. */
 __device__ __forceinline__ void attention_item(const StepArgs &a, const LayerPlan &L, int g, int y, int pos, float *fsm, int *flag) {
-    const int hd = a.hd, group = a.n_heads / a.n_kv_heads, h2 = hd / 2, tid = threadIdx.x;
+    const int hd = a.hd, group = a.n_heads / a.n_kv_heads, h2 = hd / 2, h4 = hd / 4, tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
     const int first = L.window && pos >= L.window ? pos + 1 - L.window : 0;
     const int n = pos + 1 - first;
@@ -904,6 +922,24 @@ __device__ __forceinline__ void attention_item(const StepArgs &a, const LayerPla
     float *sq = fsm, *sk = sq + group * hd, *sv = sk + ATT_TILE * (hd + 1), *sp = sv + ATT_TILE * hd;
     float *sm = sp + group * ATT_TILE, *sl = sm + group, *sa = sl + group;
     float *knew = sa + group, *vnew = knew + hd;   /* this position's K (after RoPE) and V */
+    const float *kbase = L.kc + (size_t)g * hd, *vbase = L.vc + (size_t)g * hd;
+    /* the first tile's K and V rows go into registers before anything else,
+     * so their latency overlaps the query's; each later tile is loaded while
+     * the one before is computed (the split's own position comes from knew) */
+    float4 rk[ATT_KV4], rv[ATT_KV4];
+    auto load_tile = [&](int t0) {
+        const int nt = min(ATT_TILE, t_end - t0);
+#pragma unroll
+        for (int e = 0; e < ATT_KV4; e++) {
+            const int idx = tid + e * NCT, t = idx / h4, c4 = idx % h4;
+            if (idx < nt * h4 && t0 + t != pos) {
+                const size_t off = (size_t)(t0 + t) * a.kv_dim + 4 * c4;
+                rk[e] = __ldcg((const float4 *)(kbase + off));
+                rv[e] = __ldcg((const float4 *)(vbase + off));
+            }
+        }
+    };
+    load_tile(t_begin);
     const float *cs = L.rcos + (size_t)pos * h2, *sn = L.rsin + (size_t)pos * h2;
     for (int idx = tid; idx < group * h2; idx += NCT) {
         const int h = idx / h2, i = idx % h2;
@@ -943,23 +979,24 @@ __device__ __forceinline__ void attention_item(const StepArgs &a, const LayerPla
 #pragma unroll
     for (int k = 0; k < MAXO; k++) acc[k] = 0.0f;
     consumer_sync();
+    if (tid == 0) ev(0, EV_ATT_PRE);
     for (int t0 = t_begin; t0 < t_end; t0 += ATT_TILE) {
-        const int nt = min(ATT_TILE, t_end - t0), h4 = hd / 4;
-        for (int idx = tid; idx < nt * h4; idx += NCT) {
-            const int t = idx / h4, c4 = idx % h4;
-            const size_t off = (size_t)(t0 + t) * a.kv_dim + (size_t)g * hd + 4 * c4;
-            float4 kv, vv;
-            if (t0 + t == pos) {
-                kv = make_float4(knew[4 * c4], knew[4 * c4 + 1], knew[4 * c4 + 2], knew[4 * c4 + 3]);
-                vv = make_float4(vnew[4 * c4], vnew[4 * c4 + 1], vnew[4 * c4 + 2], vnew[4 * c4 + 3]);
-            } else {
-                kv = __ldcg((const float4 *)(L.kc + off));
-                vv = __ldcg((const float4 *)(L.vc + off));
+        const int nt = min(ATT_TILE, t_end - t0);
+#pragma unroll
+        for (int e = 0; e < ATT_KV4; e++) {
+            const int idx = tid + e * NCT, t = idx / h4, c4 = idx % h4;
+            if (idx < nt * h4) {
+                float4 kv = rk[e], vv = rv[e];
+                if (t0 + t == pos) {
+                    kv = make_float4(knew[4 * c4], knew[4 * c4 + 1], knew[4 * c4 + 2], knew[4 * c4 + 3]);
+                    vv = make_float4(vnew[4 * c4], vnew[4 * c4 + 1], vnew[4 * c4 + 2], vnew[4 * c4 + 3]);
+                }
+                float *kd = sk + t * (hd + 1) + 4 * c4;
+                kd[0] = kv.x; kd[1] = kv.y; kd[2] = kv.z; kd[3] = kv.w;
+                *(float4 *)(sv + t * hd + 4 * c4) = vv;
             }
-            float *kd = sk + t * (hd + 1) + 4 * c4;
-            kd[0] = kv.x; kd[1] = kv.y; kd[2] = kv.z; kd[3] = kv.w;
-            *(float4 *)(sv + t * hd + 4 * c4) = vv;
         }
+        if (t0 + ATT_TILE < t_end) load_tile(t0 + ATT_TILE);
         consumer_sync();
         for (int idx = tid; idx < group * ATT_TILE; idx += NCT) {
             const int h = idx / ATT_TILE, t = idx % ATT_TILE;
@@ -1000,6 +1037,7 @@ __device__ __forceinline__ void attention_item(const StepArgs &a, const LayerPla
             }
         }
         consumer_sync();
+        if (tid == 0) ev(0, EV_ATT_TILE);
     }
     const int stride = hd + 2;
 #pragma unroll
@@ -1019,7 +1057,9 @@ __device__ __forceinline__ void attention_item(const StepArgs &a, const LayerPla
     consumer_sync();
     if (tid == 0) *flag = atomicAdd(&a.att_counter[g], 1u) == (unsigned)active - 1;
     consumer_sync();
+    if (tid == 0) ev(0, EV_ATT_PART);
     if (!*flag) return;
+    if (tid == 0) ev(0, EV_ATT_COMBINE);
     __threadfence();
     float *wts = sp;   /* [group][ATT_TILE >= nsplit] */
     for (int h = warp; h < group; h += NCW) {
@@ -1041,7 +1081,10 @@ __device__ __forceinline__ void attention_item(const StepArgs &a, const LayerPla
         for (int s2 = 0; s2 < active; s2++) num = fmaf(__ldcg(base + (size_t)s2 * stride), w[s2], num);
         a.ao[(size_t)(g * group + h) * hd + i] = num;
     }
-    if (tid == 0) a.att_counter[g] = 0u;
+    if (tid == 0) {
+        a.att_counter[g] = 0u;
+        ev(0, EV_ATT_DONE);
+    }
 }
 
 /* ------------------------------------------------------------ shared layout */
@@ -1125,7 +1168,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
     int own0, own1;
     share_rows(a.dim, j, G, own0, own1);
     const int nown = own1 - own0;
-    unsigned expect = 0;
+    unsigned expect = 0, pidx = 0;   /* barrier arrivals due so far, trace index */
     const ActW w_dim = act_layout(sh.act, a.dim), w_q = act_layout(sh.act, a.q_dim), w_h = act_layout(sh.act, a.hidden);
     if (threadIdx.x == 0) timeline_mark(a);
     for (int step = 0; step < a.nsteps; step++) {
@@ -1149,61 +1192,61 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
             } else {
                 load_activation(a, a.x, L.attn_norm, a.ssp, a.dim, w_dim, sh.red, sh.wbuf);
             }
-            trace_mark(a, expect / G, 0);
+            trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_A], false, act_view(w_dim), sh.res, a.err);
             {
                 const PhasePlan &P = s_plan[PH_A];
                 finish_phase(FIN_STORE, sh.res, plan_rows(P), P.nseg ? P.seg[0].row0 : 0, a.qkv, nullptr, 0, 0.0f,
-                             sh.cta_best);
+                             sh.cta_best, col_slices(a.dim / QK, false));
             }
-            grid_barrier(a, expect);
+            grid_barrier(a, expect, pidx);
             /* B: attention */
-            trace_mark(a, expect / G, 0);
+            trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             for (int it = j; it < a.n_kv_heads * a.nsplit; it += G)
                 attention_item(a, L, it / a.nsplit, it % a.nsplit, ps, (float *)sh.act, sh.flag);
-            grid_barrier(a, expect);
+            grid_barrier(a, expect, pidx);
             /* C: O projection + residual */
             load_activation(a, a.ao, nullptr, nullptr, a.q_dim, w_q, sh.red);
-            trace_mark(a, expect / G, 0);
+            trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_C], false, act_view(w_q), sh.res, a.err);
-            finish_phase(FIN_RESID, sh.res, nown, own0, a.x, sh.own, 0, 0.0f, sh.cta_best);
+            finish_phase(FIN_RESID, sh.res, nown, own0, a.x, sh.own, 0, 0.0f, sh.cta_best, col_slices(a.q_dim / QK, false));
             prefetch_norm(sh.wbuf, L.ffn_norm, a.dim);
-            grid_barrier(a, expect, sh.own, nown);
+            grid_barrier(a, expect, pidx, sh.own, nown);
             /* D: gate/up + activation */
             load_activation(a, a.x, L.ffn_norm, a.ssp, a.dim, w_dim, sh.red, sh.wbuf);
-            trace_mark(a, expect / G, 0);
+            trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_D], true, act_view(w_dim), sh.res, a.err);
             finish_phase(FIN_PAIR, sh.res, s_plan[PH_D].seg[0].rows, s_plan[PH_D].seg[0].row0, a.hb, nullptr, a.act, 0.0f,
-                         sh.cta_best);
-            grid_barrier(a, expect);
+                         sh.cta_best, 1);
+            grid_barrier(a, expect, pidx);
             /* E: down + residual */
             load_activation(a, a.hb, nullptr, nullptr, a.hidden, w_h, sh.red);
-            trace_mark(a, expect / G, 0);
+            trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_E], false, act_view(w_h), sh.res, a.err);
-            finish_phase(FIN_RESID, sh.res, nown, own0, a.x, sh.own, 0, 0.0f, sh.cta_best);
+            finish_phase(FIN_RESID, sh.res, nown, own0, a.x, sh.own, 0, 0.0f, sh.cta_best, col_slices(a.hidden / QK, false));
             prefetch_norm(sh.wbuf, next_norm, a.dim);
-            grid_barrier(a, expect, sh.own, nown);
+            grid_barrier(a, expect, pidx, sh.own, nown);
         }
         /* F: classifier + argmax */
         if (a.run_cls) {
             load_activation(a, a.x, a.final_norm, a.ssp, a.dim, w_dim, sh.red, sh.wbuf);
-            trace_mark(a, expect / G, 0);
+            trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_F], false, act_view(w_dim), sh.res, a.err);
             const unsigned long long b = finish_phase(FIN_LOGITS, sh.res, s_plan[PH_F].seg[0].rows,
                                                       s_plan[PH_F].seg[0].row0, a.logits + logit_row0, nullptr, 0,
-                                                      a.final_softcap, sh.cta_best);
+                                                      a.final_softcap, sh.cta_best, col_slices(a.dim / QK, false));
             if (threadIdx.x == 0 && b) atomicMax(&a.ls->best, b);
         }
         /* every CTA arrives; the last one advances the loop state, then
          * releases the others with one more arrival */
         consumer_sync();
-        const unsigned pfin = expect / gridDim.x;
+        const unsigned pfin = pidx++;
         expect += gridDim.x;
         if (threadIdx.x == 0) {
             trace_mark(a, pfin, 1);
