@@ -27,9 +27,8 @@ constexpr int NCW = 16;                  /* consumer warps of a streaming CTA */
 constexpr int NCT = NCW * 32;            /* consumer threads */
 constexpr int STEP_THREADS = NCT + 32;   /* + the producer warp */
 constexpr int STAGE_Q = 32 * 1024;       /* bytes of quants per ring stage (at least one row) */
-constexpr int ATT_TILE = 32;             /* positions per attention tile */
+constexpr int ATT_TILE = 64;             /* positions per attention tile (two per lane in the softmax) */
 constexpr int ATT_MAX_OUT = 2048;        /* outputs per KV head group: group * head_dim */
-constexpr int ATT_KV4 = 2;               /* float4 of K (and of V) per thread for a tile: head_dim <= 128 */
 constexpr int LOGITS_RING = 128;         /* logits rows kept on the device per call */
 constexpr int MAX_NSPLIT = 32;           /* attention splits per KV head (one lane each in the combine) */
 

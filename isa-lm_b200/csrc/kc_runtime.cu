@@ -306,7 +306,9 @@ struct kc_state {
     cudaStream_t st = nullptr;
     uint8_t *arena = nullptr;
     float *x = nullptr, *qkv = nullptr, *ao = nullptr, *hb = nullptr, *logits = nullptr, *part = nullptr;
-    float *kc = nullptr, *vc = nullptr, *rcos = nullptr, *rsin = nullptr, *lcos = nullptr, *lsin = nullptr;
+    uint8_t *kc = nullptr, *vc = nullptr;   /* [L][max_seq][kv_dim] of the KV type */
+    float *kd = nullptr, *vd = nullptr;     /* Q8 cache scales [L][max_seq][n_kv_heads] */
+    float *rcos = nullptr, *rsin = nullptr, *lcos = nullptr, *lsin = nullptr;
     float *inv0 = nullptr;   /* [vocab]: 1/rms of each embedding row (layer 0's RMSNorm) */
     float *ssp = nullptr;    /* [grid]: per-CTA sums of squares of the residual rows it wrote */
     unsigned *counter = nullptr, *err = nullptr;
@@ -349,6 +351,9 @@ static double rope_inv_freq(const kc_config &c, int i) {
     const double smooth = (orig / wavelen - lo) / (hi - lo);
     return (1.0 - smooth) * inv / f + smooth * inv;
 }
+
+/* Bytes per cache element of a KV type. */
+static size_t kv_elem_bytes(int kv_type) { return kv_type == KC_F32 ? 4 : (kv_type == KC_F16 ? 2 : 1); }
 
 static unsigned *g_err_word = nullptr;   /* device error word of the kernel-level entry points */
 static const int KC_MAX_SMEM = 227 * 1024;
@@ -463,12 +468,14 @@ static int setup_step_kernel(kc_state *s) {
     int st = stream_geom(m, g);
     if (st != KC_OK) return st;
     std::vector<LayerPlan> plan((size_t)c.n_layers);
-    const size_t lkv = (size_t)c.max_seq * c.kv_dim;
+    const size_t lkv = (size_t)c.max_seq * c.kv_dim * kv_elem_bytes(s->kv_type);
+    const size_t lkd = (size_t)c.max_seq * c.n_kv_heads;
     for (int l = 0; l < c.n_layers; l++) {
         const DevLayer &L = m->d_layers[(size_t)l];
         LayerPlan &P = plan[(size_t)l];
         P.attn_norm = L.attn_norm; P.ffn_norm = L.ffn_norm;
         P.kc = s->kc + (size_t)l * lkv; P.vc = s->vc + (size_t)l * lkv;
+        P.kd = s->kd ? s->kd + (size_t)l * lkd : nullptr; P.vd = s->vd ? s->vd + (size_t)l * lkd : nullptr;
         P.rcos = L.local_rope ? s->lcos : s->rcos; P.rsin = L.local_rope ? s->lsin : s->rsin;
         P.window = L.window;
     }
@@ -519,6 +526,7 @@ static int setup_step_kernel(kc_state *s) {
     a.x = s->x; a.qkv = s->qkv; a.ao = s->ao; a.hb = s->hb; a.logits = s->logits; a.part = s->part; a.ssp = s->ssp;
     a.att_counter = s->counter; a.bar = s->bar; a.err = s->err; a.ls = s->ls; a.feed = s->feed;
     a.out_tokens = s->out_tokens;
+    a.kv_type = s->kv_type;
     a.n_layers = c.n_layers; a.dim = c.dim; a.q_dim = c.q_dim; a.kv_dim = c.kv_dim; a.hidden = c.hidden_dim;
     a.vocab = c.vocab; a.max_seq = c.max_seq; a.n_heads = c.n_heads; a.n_kv_heads = c.n_kv_heads; a.hd = c.head_dim;
     a.eps = c.norm_eps; a.attn_scale = c.attn_scale; a.attn_softcap = c.attn_softcap; a.final_softcap = c.final_softcap;
@@ -572,10 +580,11 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
     clear_error();
     if (kv_type != KC_F32 && kv_type != KC_F16 && kv_type != KC_Q8_0) return KC_E_SHAPE;
     const kc_config &c = m->cfg;
-    if (kv_type != KC_F32) { set_error("KV cache type not supported by this build yet"); return KC_E_SHAPE; }
     if (c.qk_norm || c.post_norms) { set_error("qk_norm / post_norms not supported by this build yet"); return KC_E_SHAPE; }
     const int group = c.n_heads / c.n_kv_heads;
-    if (group * c.head_dim > ATT_MAX_OUT || c.head_dim % 4 || c.head_dim > 4 * NCT * ATT_KV4 / ATT_TILE) {
+    const int es = (int)kv_elem_bytes(kv_type);
+    if (group * c.head_dim > ATT_MAX_OUT || (c.head_dim * es) % 16 || c.head_dim % 16 ||
+        ATT_TILE * (c.head_dim * es / 16) > KVU_MAX * NCT || group > NCW) {
         set_error("attention head layout outside this build's kernel limits");
         return KC_E_SHAPE;
     }
@@ -594,7 +603,7 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
     if (e != cudaSuccess) return fail(cuda_status(e, "stream"));
 
     const size_t T = (size_t)c.max_seq, h2 = (size_t)c.head_dim / 2;
-    const size_t lkv = (size_t)c.n_layers * T * c.kv_dim;
+    const size_t lkv = (size_t)c.n_layers * T * c.kv_dim * kv_elem_bytes(kv_type);
     struct Buf { void **p; size_t bytes; };
     std::vector<Buf> bufs = {
         { (void **)&s->x, sizeof(float) * c.dim },
@@ -604,7 +613,7 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
         { (void **)&s->logits, sizeof(float) * (size_t)LOGITS_RING * c.vocab },
         { (void **)&s->part, sizeof(float) * (size_t)c.n_heads * MAX_NSPLIT * (c.head_dim + 2) },
         { (void **)&s->ssp, sizeof(float) * (size_t)s->num_sms },
-        { (void **)&s->counter, sizeof(unsigned) * c.n_kv_heads },
+        { (void **)&s->counter, sizeof(unsigned) * 2 * (size_t)c.n_kv_heads },
         { (void **)&s->err, sizeof(unsigned) * 4 },
         { (void **)&s->bar, sizeof(unsigned) * 4 },
         { (void **)&s->timeline_n, sizeof(unsigned) * 4 },
@@ -612,12 +621,16 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
         { (void **)&s->ls, sizeof(LoopState) },
         { (void **)&s->feed, sizeof(int) * (T + 1) },
         { (void **)&s->out_tokens, sizeof(int) * (T + 1) },
-        { (void **)&s->kc, sizeof(float) * lkv },
-        { (void **)&s->vc, sizeof(float) * lkv },
+        { (void **)&s->kc, lkv },
+        { (void **)&s->vc, lkv },
         { (void **)&s->rcos, sizeof(float) * T * h2 },
         { (void **)&s->inv0, sizeof(float) * (size_t)c.vocab },
         { (void **)&s->rsin, sizeof(float) * T * h2 },
     };
+    if (kv_type == KC_Q8_0) {
+        bufs.push_back({ (void **)&s->kd, sizeof(float) * (size_t)c.n_layers * T * c.n_kv_heads });
+        bufs.push_back({ (void **)&s->vd, sizeof(float) * (size_t)c.n_layers * T * c.n_kv_heads });
+    }
     if (c.rope_local_theta > 0.0f) {
         bufs.push_back({ (void **)&s->lcos, sizeof(float) * T * h2 });
         bufs.push_back({ (void **)&s->lsin, sizeof(float) * T * h2 });
@@ -789,11 +802,13 @@ extern "C" int kc_debug_copy(kc_state *s, int which, void *dst, size_t bytes) {
     case 1: src = s->qkv; n = sizeof(float) * (size_t)(c.q_dim + 2 * c.kv_dim); break;
     case 2: src = s->ao; n = sizeof(float) * c.q_dim; break;
     case 3: src = s->hb; n = sizeof(float) * c.hidden_dim; break;
-    case 4: src = s->kc; n = sizeof(float) * (size_t)c.n_layers * c.max_seq * c.kv_dim; break;
-    case 5: src = s->vc; n = sizeof(float) * (size_t)c.n_layers * c.max_seq * c.kv_dim; break;
+    case 4: src = s->kc; n = kv_elem_bytes(s->kv_type) * (size_t)c.n_layers * c.max_seq * c.kv_dim; break;
+    case 5: src = s->vc; n = kv_elem_bytes(s->kv_type) * (size_t)c.n_layers * c.max_seq * c.kv_dim; break;
+    case 6: src = s->kd; n = s->kd ? sizeof(float) * (size_t)c.n_layers * c.max_seq * c.n_kv_heads : 0; break;
+    case 7: src = s->vd; n = s->vd ? sizeof(float) * (size_t)c.n_layers * c.max_seq * c.n_kv_heads : 0; break;
     default: return KC_E_SHAPE;
     }
-    if (bytes < n) return KC_E_SHAPE;
+    if (bytes < n || !src) return KC_E_SHAPE;
     CK(cudaStreamSynchronize(s->st));
     CK(cudaMemcpy(dst, src, n, cudaMemcpyDeviceToHost));
     return KC_OK;

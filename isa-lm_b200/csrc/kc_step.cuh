@@ -38,6 +38,7 @@
  */
 #pragma once
 #include "kc_kernels.cuh"
+#include "krafla_cuda.h"
 
 namespace kc {
 
@@ -49,7 +50,8 @@ struct PMat {
 
 struct LayerPlan {
     const float *attn_norm, *ffn_norm;
-    float *kc, *vc;                 /* this layer's F32 cache [max_seq][kv_dim] */
+    void *kc, *vc;                  /* this layer's cache [max_seq][kv_dim] of the state's KV type */
+    float *kd, *vd;                 /* Q8 cache: scales [max_seq][n_kv_heads] */
     const float *rcos, *rsin;       /* RoPE tables of this layer */
     int window;
 };
@@ -189,6 +191,7 @@ struct StepArgs {
     const int *feed;
     int *out_tokens;
     int n_layers, dim, q_dim, kv_dim, hidden, vocab, max_seq, n_heads, n_kv_heads, hd;
+    int kv_type;                    /* KC_F32, KC_F16 or KC_Q8_0 */
     float eps, attn_scale, attn_softcap, final_softcap, embed_scale;
     int act, nsplit, nstage, slot_bytes, act_bytes, res_bytes, wbuf_bytes;
     int nsteps, run_cls;            /* steps in this launch; run the classifier */
@@ -898,19 +901,81 @@ __device__ void act_prequant(const int8_t *pq, const float *pd, int cols, const 
 
 /* ------------------------------------------------------------ attention */
 
-/* Shared scratch of an attention item, in floats. */
+constexpr int KVU_MAX = 4;   /* 16-byte units of K (and of V) a thread loads per tile */
+
+/* Shared scratch of an attention item, in floats (layout in att_smem; every
+ * region starts on a 16-byte boundary). */
+__host__ __device__ inline int att_pad4(int n) { return (n + 3) & ~3; }
 __host__ __device__ inline int attention_scratch_floats(int group, int hd) {
-    return group * hd + ATT_TILE * (hd + 1) + ATT_TILE * hd + group * ATT_TILE + 3 * group + 2 * hd;
+    return att_pad4(group * hd) + att_pad4((group * hd + 3) / 4) + att_pad4(group)   /* q, int8 q, its scales */
+           + att_pad4(ATT_TILE * (hd + 1)) + ATT_TILE                               /* K tile, K scales */
+           + ATT_TILE * hd + ATT_TILE                                               /* V tile, V scales */
+           + att_pad4(group * ATT_TILE) + 3 * att_pad4(group)                       /* p, m, l, alpha */
+           + att_pad4(hd) * 2 + 4                                                   /* this position's K, V, scales */
+           + group * 32;                                                            /* combine weights */
 }
 
-/* Attention work item (KV head g, split y) of layer L at position pos (F32
- * cache), on the consumer threads; fsm: shared scratch. RoPE on adjacent pairs
- * (k_scalar.c:79-94); the split holding pos first writes that position's K
- * (after RoPE) and V into the cache; scores q.k * scale (soft-capped when
- * set), online softmax and the weighted V sum over the split's positions; the
- * last CTA of the KV head to finish combines the splits into a.ao. */
-__device__ __forceinline__ void attention_item(const StepArgs &a, const LayerPlan &L, int g, int y, int pos, float *fsm, int *flag) {
-    const int hd = a.hd, group = a.n_heads / a.n_kv_heads, h2 = hd / 2, h4 = hd / 4, tid = threadIdx.x;
+struct AttSmem {
+    float *sq, *sqd, *sk, *skd, *sv, *svd, *sp, *sm, *sl, *sa, *knew, *vnew, *knd, *wts;
+    int8_t *sqq;
+};
+
+__device__ __forceinline__ AttSmem att_smem(float *f, int group, int hd) {
+    AttSmem s;
+    s.sq = f; f += att_pad4(group * hd);
+    s.sqq = (int8_t *)f; f += att_pad4((group * hd + 3) / 4);
+    s.sqd = f; f += att_pad4(group);
+    s.sk = f; f += att_pad4(ATT_TILE * (hd + 1));
+    s.skd = f; f += ATT_TILE;
+    s.sv = f; f += ATT_TILE * hd;
+    s.svd = f; f += ATT_TILE;
+    s.sp = f; f += att_pad4(group * ATT_TILE);
+    s.sm = f; f += att_pad4(group);
+    s.sl = f; f += att_pad4(group);
+    s.sa = f; f += att_pad4(group);
+    s.knew = f; f += att_pad4(hd);
+    s.vnew = f; f += att_pad4(hd);
+    s.knd = f; f += 4;
+    s.wts = f;
+    return s;
+}
+
+/* The reference's single-scale row quantization (ops/ops.c:81-96) of the n
+ * values x[0, n) by one warp (lane i takes elements i, i+32, ...): the quants
+ * into out, and as floats into back when given; returns the scale. */
+__device__ __forceinline__ float warp_quantize_row(const float *x, int n, int8_t *out, float *back, int lane) {
+    float amax = 0.0f;
+    for (int i = lane; i < n; i += 32) amax = fmaxf(amax, fabsf(x[i]));
+    amax = warp_max(amax);
+    const bool tiny = amax < 1e-30f;
+    const float id = tiny ? 0.0f : __fdiv_rn(127.0f, amax);
+    for (int i = lane; i < n; i += 32) {
+        int qi = 0;
+        if (!tiny) {
+            const float t = truncf(__fadd_rn(__fmul_rn(x[i], id), copysignf(0.5f, x[i])));
+            qi = (int)fminf(fmaxf(t, -127.0f), 127.0f);
+        }
+        out[i] = (int8_t)qi;
+        if (back) back[i] = (float)qi;
+    }
+    return tiny ? 0.0f : __fdiv_rn(amax, 127.0f);
+}
+
+/* Attention work item (KV head g, split y) of layer L at position pos, on the
+ * consumer threads; fsm: shared scratch. ops/ops.c:124-180 with the cache
+ * types of model/transformer.c:188-205 (KV: KC_F32, KC_F16 or KC_Q8_0):
+ * RoPE on adjacent pairs (k_scalar.c:79-94); the split holding pos stores
+ * that position's K (after RoPE) and V in the cache's type (f16 rounding, or
+ * the single-scale row quantization per KV head) and uses the stored values;
+ * scores q.k * scale (Q8: the query quantized per head, int32 dot,
+ * (float)s * (qd * scale) * kd), soft-capped when set; online softmax over
+ * 64-position tiles loaded one tile ahead; the weighted V sum (Q8: (p * vd)
+ * * v). The splits of a KV head then wait for each other and each combines
+ * its slice of the head group's outputs into a.ao. */
+template <int KV, int UNITS>
+__device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan &L, int g, int y, int pos, float *fsm) {
+    constexpr int ES = KV == KC_F32 ? 4 : (KV == KC_F16 ? 2 : 1);
+    const int hd = a.hd, group = a.n_heads / a.n_kv_heads, h2 = hd / 2, tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
     const int first = L.window && pos >= L.window ? pos + 1 - L.window : 0;
     const int n = pos + 1 - first;
@@ -919,24 +984,28 @@ __device__ __forceinline__ void attention_item(const StepArgs &a, const LayerPla
     const int active = (n + C - 1) / C;
     if (y >= active) return;
     const int t_begin = first + y * C, t_end = min(t_begin + C, pos + 1);
-    float *sq = fsm, *sk = sq + group * hd, *sv = sk + ATT_TILE * (hd + 1), *sp = sv + ATT_TILE * hd;
-    float *sm = sp + group * ATT_TILE, *sl = sm + group, *sa = sl + group;
-    float *knew = sa + group, *vnew = knew + hd;   /* this position's K (after RoPE) and V */
-    const float *kbase = L.kc + (size_t)g * hd, *vbase = L.vc + (size_t)g * hd;
-    /* the first tile's K and V rows go into registers before anything else,
-     * so their latency overlaps the query's; each later tile is loaded while
-     * the one before is computed (the split's own position comes from knew) */
-    float4 rk[ATT_KV4], rv[ATT_KV4];
+    const AttSmem S = att_smem(fsm, group, hd);
+    const int upr = hd * ES / 16;                      /* 16-byte units per cache row */
+    const size_t rowb = (size_t)a.kv_dim * ES;
+    const uint8_t *kb = (const uint8_t *)L.kc + (size_t)g * hd * ES, *vb = (const uint8_t *)L.vc + (size_t)g * hd * ES;
+    /* the first tile's K and V go into registers before anything else, so
+     * their latency overlaps the query's; each later tile is loaded while the
+     * one before is computed; the split's own position comes from knew/vnew */
+    uint4 rk[UNITS], rv[UNITS];
+    float rkd = 0.0f, rvd = 0.0f;
     auto load_tile = [&](int t0) {
         const int nt = min(ATT_TILE, t_end - t0);
 #pragma unroll
-        for (int e = 0; e < ATT_KV4; e++) {
-            const int idx = tid + e * NCT, t = idx / h4, c4 = idx % h4;
-            if (idx < nt * h4 && t0 + t != pos) {
-                const size_t off = (size_t)(t0 + t) * a.kv_dim + 4 * c4;
-                rk[e] = __ldcg((const float4 *)(kbase + off));
-                rv[e] = __ldcg((const float4 *)(vbase + off));
+        for (int e = 0; e < UNITS; e++) {
+            const int idx = tid + e * NCT, t = idx / upr, u = idx - t * upr;
+            if (idx < nt * upr && t0 + t != pos) {
+                rk[e] = __ldcg((const uint4 *)(kb + (size_t)(t0 + t) * rowb + 16 * u));
+                rv[e] = __ldcg((const uint4 *)(vb + (size_t)(t0 + t) * rowb + 16 * u));
             }
+        }
+        if (KV == KC_Q8_0 && tid < nt && t0 + tid != pos) {
+            rkd = __ldcg(L.kd + (size_t)(t0 + tid) * a.n_kv_heads + g);
+            rvd = __ldcg(L.vd + (size_t)(t0 + tid) * a.n_kv_heads + g);
         }
     };
     load_tile(t_begin);
@@ -945,145 +1014,250 @@ __device__ __forceinline__ void attention_item(const StepArgs &a, const LayerPla
         const int h = idx / h2, i = idx % h2;
         const float *qh = a.qkv + (size_t)(g * group + h) * hd;
         const float qa = __ldcg(qh + 2 * i), qb = __ldcg(qh + 2 * i + 1), c = cs[i], s = sn[i];
-        sq[h * hd + 2 * i] = __fsub_rn(__fmul_rn(qa, c), __fmul_rn(qb, s));
-        sq[h * hd + 2 * i + 1] = __fadd_rn(__fmul_rn(qa, s), __fmul_rn(qb, c));
+        S.sq[h * hd + 2 * i] = __fsub_rn(__fmul_rn(qa, c), __fmul_rn(qb, s));
+        S.sq[h * hd + 2 * i + 1] = __fadd_rn(__fmul_rn(qa, s), __fmul_rn(qb, c));
     }
-    /* the split holding pos writes that position's K and V row into the cache
-     * and keeps it in shared memory: its own tile reads take it from there, not
-     * back from global memory */
-    if (t_end == pos + 1) {
-        const float *kn = a.qkv + a.q_dim + (size_t)g * hd, *vn = a.qkv + a.q_dim + a.kv_dim + (size_t)g * hd;
-        float *kr = L.kc + (size_t)pos * a.kv_dim + (size_t)g * hd, *vr = L.vc + (size_t)pos * a.kv_dim + (size_t)g * hd;
-        for (int i = tid; i < h2; i += NCT) {
-            const float ka = __ldcg(kn + 2 * i), kb = __ldcg(kn + 2 * i + 1), c = cs[i], s = sn[i];
-            const float k0 = __fsub_rn(__fmul_rn(ka, c), __fmul_rn(kb, s));
-            const float k1 = __fadd_rn(__fmul_rn(ka, s), __fmul_rn(kb, c));
-            kr[2 * i] = k0;
-            kr[2 * i + 1] = k1;
-            knew[2 * i] = k0;
-            knew[2 * i + 1] = k1;
+    /* the split holding pos stores that position's K (after RoPE) and V */
+    if (t_end == pos + 1 && warp < 2) {
+        const float *src = a.qkv + a.q_dim + (warp ? a.kv_dim : 0) + (size_t)g * hd;
+        float *row = warp ? S.vnew : S.knew;
+        for (int i = lane; i < h2; i += 32) {
+            const float xa = __ldcg(src + 2 * i), xb = __ldcg(src + 2 * i + 1);
+            if (warp == 0) {
+                row[2 * i] = __fsub_rn(__fmul_rn(xa, cs[i]), __fmul_rn(xb, sn[i]));
+                row[2 * i + 1] = __fadd_rn(__fmul_rn(xa, sn[i]), __fmul_rn(xb, cs[i]));
+            } else {
+                row[2 * i] = xa;
+                row[2 * i + 1] = xb;
+            }
         }
-        for (int i = tid; i < hd; i += NCT) {
-            const float v = __ldcg(vn + i);
-            vr[i] = v;
-            vnew[i] = v;
+        __syncwarp();
+        uint8_t *dst = (uint8_t *)(warp ? L.vc : L.kc) + ((size_t)pos * a.kv_dim + (size_t)g * hd) * ES;
+        if constexpr (KV == KC_F32) {
+            for (int i = lane; i < hd; i += 32) ((float *)dst)[i] = row[i];
+        } else if constexpr (KV == KC_F16) {
+            for (int i = lane; i < hd; i += 32) {
+                const __half hv = __float2half_rn(row[i]);
+                ((__half *)dst)[i] = hv;
+                row[i] = __half2float(hv);
+            }
+        } else {
+            const float d = warp_quantize_row(row, hd, (int8_t *)dst, row, lane);
+            if (lane == 0) {
+                (warp ? L.vd : L.kd)[(size_t)pos * a.n_kv_heads + g] = d;
+                S.knd[warp] = d;
+            }
         }
     }
     if (tid < group) {
-        sm[tid] = -INFINITY;
-        sl[tid] = 0.0f;
+        S.sm[tid] = -INFINITY;
+        S.sl[tid] = 0.0f;
     }
     const int nout = group * hd;
     constexpr int MAXO = (ATT_MAX_OUT + NCT - 1) / NCT;
+    /* one thread per score (a dot over hd) and per output (a sum over the
+     * tile), each summed in the order of the reference's loops */
+    constexpr int tpd = 1, tpo = 1;
     float acc[MAXO];
 #pragma unroll
     for (int k = 0; k < MAXO; k++) acc[k] = 0.0f;
     consumer_sync();
+    if (KV == KC_Q8_0 && warp < group)
+        S.sqd[warp] = warp_quantize_row(S.sq + warp * hd, hd, S.sqq + warp * hd, nullptr, lane);
     if (tid == 0) ev(0, EV_ATT_PRE);
     for (int t0 = t_begin; t0 < t_end; t0 += ATT_TILE) {
         const int nt = min(ATT_TILE, t_end - t0);
 #pragma unroll
-        for (int e = 0; e < ATT_KV4; e++) {
-            const int idx = tid + e * NCT, t = idx / h4, c4 = idx % h4;
-            if (idx < nt * h4) {
-                float4 kv = rk[e], vv = rv[e];
-                if (t0 + t == pos) {
-                    kv = make_float4(knew[4 * c4], knew[4 * c4 + 1], knew[4 * c4 + 2], knew[4 * c4 + 3]);
-                    vv = make_float4(vnew[4 * c4], vnew[4 * c4 + 1], vnew[4 * c4 + 2], vnew[4 * c4 + 3]);
+        for (int e = 0; e < UNITS; e++) {
+            const int idx = tid + e * NCT, t = idx / upr, u = idx - t * upr;
+            if (idx < nt * upr) {
+                const bool own = t0 + t == pos;
+                if constexpr (KV == KC_Q8_0) {
+                    if (own) {
+#pragma unroll
+                        for (int k = 0; k < 16; k++) {
+                            ((int8_t *)S.sk)[t * hd + 16 * u + k] = (int8_t)S.knew[16 * u + k];
+                            S.sv[t * hd + 16 * u + k] = S.vnew[16 * u + k];
+                        }
+                    } else {
+                        *(uint4 *)((int8_t *)S.sk + t * hd + 16 * u) = rk[e];
+                        const int8_t *vq = (const int8_t *)&rv[e];
+#pragma unroll
+                        for (int k = 0; k < 16; k++) S.sv[t * hd + 16 * u + k] = (float)vq[k];
+                    }
+                } else {
+                    constexpr int PER = 16 / ES;   /* elements per unit */
+                    float kf[PER], vf[PER];
+                    if (own) {
+#pragma unroll
+                        for (int k = 0; k < PER; k++) {
+                            kf[k] = S.knew[PER * u + k];
+                            vf[k] = S.vnew[PER * u + k];
+                        }
+                    } else if constexpr (KV == KC_F32) {
+                        const float *ka = (const float *)&rk[e], *va = (const float *)&rv[e];
+#pragma unroll
+                        for (int k = 0; k < PER; k++) { kf[k] = ka[k]; vf[k] = va[k]; }
+                    } else {
+                        const __half *ka = (const __half *)&rk[e], *va = (const __half *)&rv[e];
+#pragma unroll
+                        for (int k = 0; k < PER; k++) { kf[k] = __half2float(ka[k]); vf[k] = __half2float(va[k]); }
+                    }
+#pragma unroll
+                    for (int k = 0; k < PER; k++) {
+                        S.sk[t * (hd + 1) + PER * u + k] = kf[k];
+                        S.sv[t * hd + PER * u + k] = vf[k];
+                    }
                 }
-                float *kd = sk + t * (hd + 1) + 4 * c4;
-                kd[0] = kv.x; kd[1] = kv.y; kd[2] = kv.z; kd[3] = kv.w;
-                *(float4 *)(sv + t * hd + 4 * c4) = vv;
             }
+        }
+        if (KV == KC_Q8_0 && tid < nt) {
+            const bool own = t0 + tid == pos;
+            S.skd[tid] = own ? S.knd[0] : rkd;
+            S.svd[tid] = own ? S.knd[1] : rvd;
         }
         if (t0 + ATT_TILE < t_end) load_tile(t0 + ATT_TILE);
         consumer_sync();
-        for (int idx = tid; idx < group * ATT_TILE; idx += NCT) {
-            const int h = idx / ATT_TILE, t = idx % ATT_TILE;
+        /* scores: tpd threads per (head, position); every lane takes part in
+         * the shuffles, those past the tile with zero */
+        for (int pi = tid / tpd; pi < group * ATT_TILE; pi += NCT / tpd) {
+            const int h = pi / ATT_TILE, t = pi % ATT_TILE, part = tid % tpd, span = hd / tpd;
             float s = -INFINITY;
-            if (t < nt) {
-                const float *qh = sq + h * hd, *kt = sk + t * (hd + 1);
+            if constexpr (KV == KC_Q8_0) {
+                int sum = 0;
+                if (t < nt) {
+                    const int *qw = (const int *)(S.sqq + h * hd + part * span);
+                    const int *kw = (const int *)((const int8_t *)S.sk + t * hd + part * span);
+                    for (int i = 0; i < span / 4; i++) sum = __dp4a(qw[i], kw[i], sum);
+                }
+                for (int o = tpd / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+                if (t < nt) s = __fmul_rn(__fmul_rn((float)sum, __fmul_rn(S.sqd[h], a.attn_scale)), S.skd[t]);
+            } else {
                 float dot = 0.0f;
-                for (int i = 0; i < hd; i++) dot = fmaf(qh[i], kt[i], dot);
-                s = __fmul_rn(dot, a.attn_scale);
-                if (a.attn_softcap > 0.0f) s = __fmul_rn(a.attn_softcap, tanhf(__fdiv_rn(s, a.attn_softcap)));
+                if (t < nt) {
+                    const float *qh = S.sq + h * hd + part * span, *kt = S.sk + t * (hd + 1) + part * span;
+                    for (int i = 0; i < span; i++) dot = fmaf(qh[i], kt[i], dot);
+                }
+                for (int o = tpd / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+                if (t < nt) s = __fmul_rn(dot, a.attn_scale);
             }
-            sp[h * ATT_TILE + t] = s;
+            if (t < nt && a.attn_softcap > 0.0f) s = __fmul_rn(a.attn_softcap, tanhf(__fdiv_rn(s, a.attn_softcap)));
+            if (part == 0) S.sp[h * ATT_TILE + t] = s;
         }
         consumer_sync();
         for (int h = warp; h < group; h += NCW) {
-            const float s = sp[h * ATT_TILE + lane];
-            const float m_old = sm[h], m_new = fmaxf(m_old, warp_max(s));
-            const float pr = lane < nt ? expf(s - m_new) : 0.0f;
-            const float sum = warp_sum(pr);
+            const float s0 = S.sp[h * ATT_TILE + lane], s1 = S.sp[h * ATT_TILE + 32 + lane];
+            const float m_old = S.sm[h], m_new = fmaxf(m_old, warp_max(fmaxf(s0, s1)));
+            const float p0 = lane < nt ? expf(s0 - m_new) : 0.0f, p1 = lane + 32 < nt ? expf(s1 - m_new) : 0.0f;
+            const float sum = warp_sum(p0 + p1);
             const float alpha = expf(m_old - m_new);
-            sp[h * ATT_TILE + lane] = pr;
+            S.sp[h * ATT_TILE + lane] = p0;
+            S.sp[h * ATT_TILE + 32 + lane] = p1;
             if (lane == 0) {
-                sm[h] = m_new;
-                sl[h] = sl[h] * alpha + sum;
-                sa[h] = alpha;
+                S.sm[h] = m_new;
+                S.sl[h] = S.sl[h] * alpha + sum;
+                S.sa[h] = alpha;
             }
         }
         consumer_sync();
+        /* outputs: tpo threads per (head, dimension), positions interleaved */
 #pragma unroll
         for (int k = 0; k < MAXO; k++) {
-            const int o = tid + k * NCT;
-            if (o < nout) {
-                const int h = o / hd, i = o % hd;
-                float v = acc[k] * sa[h];
-                const float *ph = sp + h * ATT_TILE;
-                for (int t = 0; t < nt; t++) v = fmaf(ph[t], sv[t * hd + i], v);
-                acc[k] = v;
+            const int o = (tid + k * NCT) / tpo, part = tid % tpo;
+            if (k * NCT < nout * tpo) {
+                float v = 0.0f;
+                if (o < nout) {
+                    const int h = o / hd, i = o % hd;
+                    v = acc[k] * S.sa[h];
+                    const float *ph = S.sp + h * ATT_TILE;
+                    for (int t = part; t < nt; t += tpo) {
+                        const float w = KV == KC_Q8_0 ? __fmul_rn(ph[t], S.svd[t]) : ph[t];
+                        v = fmaf(w, S.sv[t * hd + i], v);
+                    }
+                }
+                for (int sh = tpo / 2; sh > 0; sh >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sh);
+                if (o < nout && part == 0) acc[k] = v;
             }
         }
         consumer_sync();
         if (tid == 0) ev(0, EV_ATT_TILE);
     }
+    /* this split's partial: unnormalized outputs, running max and sum */
     const int stride = hd + 2;
 #pragma unroll
     for (int k = 0; k < MAXO; k++) {
-        const int o = tid + k * NCT;
-        if (o < nout) {
+        const int o = (tid + k * NCT) / tpo;
+        if (k * NCT < nout * tpo && o < nout && tid % tpo == 0) {
             const int h = o / hd, i = o % hd;
             a.part[((size_t)(g * group + h) * a.nsplit + y) * stride + i] = acc[k];
         }
     }
     if (tid < group) {
         float *ph = a.part + ((size_t)(g * group + tid) * a.nsplit + y) * stride;
-        ph[hd] = sm[tid];
-        ph[hd + 1] = sl[tid];
+        ph[hd] = S.sm[tid];
+        ph[hd + 1] = S.sl[tid];
     }
     __threadfence();
     consumer_sync();
-    if (tid == 0) *flag = atomicAdd(&a.att_counter[g], 1u) == (unsigned)active - 1;
+    /* the head's splits wait for each other (all resident: a bounded spin),
+     * then each combines its slice of the group's outputs */
+    unsigned *arrived = a.att_counter + g, *done = a.att_counter + a.n_kv_heads + g;
+    if (tid == 0) {
+        atomicAdd(arrived, 1u);
+        unsigned it = 0;
+        while (ld_acquire(arrived) < (unsigned)active) {
+            if (++it > (1u << 24)) {
+                atomicOr(a.err, 8u);
+                break;
+            }
+            if ((it & 1023) == 0 && ld_acquire(a.err)) break;
+        }
+        ev(0, EV_ATT_PART);
+    }
     consumer_sync();
-    if (tid == 0) ev(0, EV_ATT_PART);
-    if (!*flag) return;
-    if (tid == 0) ev(0, EV_ATT_COMBINE);
     __threadfence();
-    float *wts = sp;   /* [group][ATT_TILE >= nsplit] */
+    const int chunk = (nout + active - 1) / active, o0 = y * chunk, o1 = min(nout, o0 + chunk);
     for (int h = warp; h < group; h += NCW) {
+        if (h * hd >= o1 || (h + 1) * hd <= o0) continue;
         const float *ph = a.part + (size_t)(g * group + h) * a.nsplit * stride;
         const float m = lane < active ? __ldcg(ph + (size_t)lane * stride + hd) : -INFINITY;
         const float l = lane < active ? __ldcg(ph + (size_t)lane * stride + hd + 1) : 0.0f;
         const float M = warp_max(m);
         const float e = lane < active ? expf(m - M) : 0.0f;
         const float Ls = warp_sum(l * e);
-        wts[h * ATT_TILE + lane] = e / Ls;
+        S.wts[h * 32 + lane] = e / Ls;
     }
     consumer_sync();
-    for (int o = tid; o < nout; o += NCT) {
+    if (tid == 0) ev(0, EV_ATT_COMBINE);
+    for (int o = o0 + tid; o < o1; o += NCT) {
         const int h = o / hd, i = o % hd;
         const float *base = a.part + (size_t)(g * group + h) * a.nsplit * stride + i;
-        const float *w = wts + h * ATT_TILE;
+        const float *w = S.wts + h * 32;
         float num = 0.0f;
 #pragma unroll 8
         for (int s2 = 0; s2 < active; s2++) num = fmaf(__ldcg(base + (size_t)s2 * stride), w[s2], num);
         a.ao[(size_t)(g * group + h) * hd + i] = num;
     }
     if (tid == 0) {
-        a.att_counter[g] = 0u;
+        /* the last split through resets both counters for the next layer */
+        if (atomicAdd(done, 1u) == (unsigned)active - 1) {
+            *arrived = 0u;
+            *done = 0u;
+        }
         ev(0, EV_ATT_DONE);
+    }
+}
+
+/* UNITS: the 16-byte units of K a thread loads per tile, head_dim * bytes / 128. */
+__device__ __forceinline__ void attention_item(const StepArgs &a, const LayerPlan &L, int g, int y, int pos, float *fsm) {
+    if (a.kv_type == KC_F16) {
+        if (a.hd <= 64) attention_item_t<KC_F16, 1>(a, L, g, y, pos, fsm);
+        else attention_item_t<KC_F16, 2>(a, L, g, y, pos, fsm);
+    } else if (a.kv_type == KC_Q8_0) {
+        attention_item_t<KC_Q8_0, 1>(a, L, g, y, pos, fsm);
+    } else {
+        if (a.hd <= 64) attention_item_t<KC_F32, 2>(a, L, g, y, pos, fsm);
+        else attention_item_t<KC_F32, 4>(a, L, g, y, pos, fsm);
     }
 }
 
@@ -1205,7 +1379,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
             trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             for (int it = j; it < a.n_kv_heads * a.nsplit; it += G)
-                attention_item(a, L, it / a.nsplit, it % a.nsplit, ps, (float *)sh.act, sh.flag);
+                attention_item(a, L, it / a.nsplit, it % a.nsplit, ps, (float *)sh.act);
             grid_barrier(a, expect, pidx);
             /* C: O projection + residual */
             load_activation(a, a.ao, nullptr, nullptr, a.q_dim, w_q, sh.red);

@@ -202,3 +202,40 @@ def test_baseline_shapes_short(name, prompt_len, steps):
     del m
     toks, strict_bad, valid_bad, errs = teacher_forced_greedy(path, prompt, steps)
     assert not valid_bad, valid_bad
+
+
+@pytest.mark.parametrize("kv", [kb.F16, kb.Q8_0])
+@pytest.mark.parametrize("name", ["rand_q4", "rand_q8", "mixf16_q4"])
+def test_kv_cache_types_one_step_away(name, kv):
+    """F16 and Q8 caches (model/transformer.c:188-205): the reference holds its
+    own builds with these caches to its numpy model by the distribution
+    criterion (tests/test_e2e.sh:60-68, compare_logits.py --kl 1e-3)."""
+    path = os.path.join(GOLDEN, "models", f"{name}.mlb")
+    m = kb.Model(path)
+    got = kb.State(m, kv_type=kv).prefill(TOKENS, 0, logits=True)
+    ref = oracle.OracleModel(path, kv_type=kv).prefill(TOKENS)
+    assert all(valid_pair(got[i], ref[i]) for i in range(len(TOKENS)))
+    assert rel_err(got[:4], ref[:4]).max() <= RTOL   # before a stored-row rounding can reach the logits
+
+
+@pytest.mark.parametrize("kv", [kb.F16, kb.Q8_0])
+def test_kv_cache_types_long_context(kv):
+    # 150 positions across several tiles and splits; the reference's bound for
+    # its non-F32 caches over this run is 5e-2 without the argmax check
+    # (tests/test_e2e.sh:72-86)
+    path = os.path.join(GOLDEN, "models", "ctx_q4.mlb")
+    toks = [(i * 37) % 95 + 1 for i in range(1, 151)]
+    m = kb.Model(path)
+    got = kb.State(m, kv_type=kv).prefill(toks, 0, logits=True)
+    ref = oracle.OracleModel(path, kv_type=kv).prefill(toks)
+    assert rel_err(got, ref).max() <= 5e-2
+
+
+@pytest.mark.parametrize("kv", [kb.F16, kb.Q8_0])
+def test_kv_cache_types_prefill_equals_forward(kv):
+    path = os.path.join(GOLDEN, "models", "rand_q4.mlb")
+    m = kb.Model(path)
+    a = kb.State(m, kv_type=kv).prefill(TOKENS, 0, logits=True)
+    st = kb.State(m, kv_type=kv)
+    b = np.stack([st.forward(t, p) for p, t in enumerate(TOKENS)])
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
