@@ -69,9 +69,10 @@ def peaks():
         return 6650.0, "fallback"
 
 
-def model_bytes_per_token(cfg, ctx):
+def model_bytes_per_token(cfg, ctx, kv_bytes=4.0):
     """Algorithmic HBM bytes of one decode token: every quantized matrix (quants
-    + f16 scales) once, the embedding row, and the F32 KV rows attended."""
+    + f16 scales) once, the embedding row, and the KV rows attended (kv_bytes
+    per element: 4 F32, 2 F16, 1 + 4/head_dim Q8 with its per-row scale)."""
     d, L, h, v = cfg["dim"], cfg["n_layers"], cfg["hidden_dim"], cfg["vocab"]
     qd, kvd = cfg["q_dim"], cfg["kv_dim"]
     wt, mask = cfg["wtype"], cfg["q8_mask"]
@@ -85,7 +86,7 @@ def model_bytes_per_token(cfg, ctx):
     shared = cfg.get("shared", 0)
     cls = mat(v, d, 1 | 2 if shared else 2)
     emb = d * (1 if (wt == 1 or mask & 1) else 0.5)
-    kv = 2 * L * ctx * kvd * 4
+    kv = 2 * L * ctx * kvd * kv_bytes
     gemv = L * (per_layer - 2 * d * 4) + cls
     return L * per_layer + cls + emb + kv, gemv
 
@@ -281,6 +282,25 @@ def main():
             sweep[str(c)] = {"tok_s": round(32 / (m2 / 1000), 1),
                              "hbm_frac": round(b2 * 32 / (m2 / 1000) / 1e9 / hbm_peak, 4)}
         extras["decode_by_context"] = sweep
+        # the same decode with the F16 and Q8 caches (row f1): fewer KV bytes per token
+        kvs = {}
+        for kvname, kvt, kvb in (("f16", kb.F16, 2.0), ("q8", kb.Q8_0, 1.0 + 4.0 / cfg["head_dim"])):
+            try:
+                sk = kb.State(model, kv_type=kvt)
+                row = {}
+                for c in (1024, 4096):
+                    c2 = min(c, cfg["max_seq"] - 34)
+                    sk.prefill(prompt_tokens(cfg["vocab"], c2)[:-1], 0)
+                    m2 = sk.time_decode(1, c2 - 1, 2, 32)
+                    b2, _ = model_bytes_per_token(cfg, c2 + 18, kvb)
+                    row[str(c)] = {"tok_s": round(32 / (m2 / 1000), 1),
+                                   "hbm_frac": round(b2 * 32 / (m2 / 1000) / 1e9 / hbm_peak, 4)}
+                sk.free()
+                kvs[kvname] = row
+            except Exception as e:   # a KV type this model's head layout cannot use
+                kvs[kvname] = {"error": str(e)}
+        extras["decode_by_kv_cache"] = kvs
+
         pre = {}
         for n in (128, 512, 2048):
             pt = prompt_tokens(cfg["vocab"], n, seed=7)
@@ -324,7 +344,7 @@ def main():
                                     "prefill_tok_s": round(cpu["prefill_tok_s"], 1)}
         elif cpu:
             line["cpu_baseline"] = cpu
-        for k in ("decode_by_context", "prefill_tok_s"):
+        for k in ("decode_by_context", "decode_by_kv_cache", "prefill_tok_s"):
             if k in extras:
                 line[k] = extras[k]
         print(json.dumps(line), flush=True)

@@ -1008,7 +1008,9 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
             rvd = __ldcg(L.vd + (size_t)(t0 + tid) * a.n_kv_heads + g);
         }
     };
+    if (tid == 0) ev(0, 20);
     load_tile(t_begin);
+    if (tid == 0) ev(0, 21);
     const float *cs = L.rcos + (size_t)pos * h2, *sn = L.rsin + (size_t)pos * h2;
     for (int idx = tid; idx < group * h2; idx += NCT) {
         const int h = idx / h2, i = idx % h2;
@@ -1017,6 +1019,7 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
         S.sq[h * hd + 2 * i] = __fsub_rn(__fmul_rn(qa, c), __fmul_rn(qb, s));
         S.sq[h * hd + 2 * i + 1] = __fadd_rn(__fmul_rn(qa, s), __fmul_rn(qb, c));
     }
+    if (tid == 0) ev(0, 22);
     /* the split holding pos stores that position's K (after RoPE) and V */
     if (t_end == pos + 1 && warp < 2) {
         const float *src = a.qkv + a.q_dim + (warp ? a.kv_dim : 0) + (size_t)g * hd;
@@ -1116,8 +1119,10 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
             S.skd[tid] = own ? S.knd[0] : rkd;
             S.svd[tid] = own ? S.knd[1] : rvd;
         }
+        if (tid == 0) ev(0, 23);
         if (t0 + ATT_TILE < t_end) load_tile(t0 + ATT_TILE);
         consumer_sync();
+        if (tid == 0) ev(0, 24);
         /* scores: tpd threads per (head, position); every lane takes part in
          * the shuffles, those past the tile with zero */
         for (int pi = tid / tpd; pi < group * ATT_TILE; pi += NCT / tpd) {
@@ -1145,6 +1150,7 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
             if (part == 0) S.sp[h * ATT_TILE + t] = s;
         }
         consumer_sync();
+        if (tid == 0) ev(0, 25);
         for (int h = warp; h < group; h += NCW) {
             const float s0 = S.sp[h * ATT_TILE + lane], s1 = S.sp[h * ATT_TILE + 32 + lane];
             const float m_old = S.sm[h], m_new = fmaxf(m_old, warp_max(fmaxf(s0, s1)));
@@ -1160,6 +1166,7 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
             }
         }
         consumer_sync();
+        if (tid == 0) ev(0, 26);
         /* outputs: tpo threads per (head, dimension), positions interleaved */
 #pragma unroll
         for (int k = 0; k < MAXO; k++) {
@@ -1199,11 +1206,13 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
     }
     __threadfence();
     consumer_sync();
+    if (tid == 0) ev(0, 27);
     /* the head's splits wait for each other (all resident: a bounded spin),
      * then each combines its slice of the group's outputs */
     unsigned *arrived = a.att_counter + g, *done = a.att_counter + a.n_kv_heads + g;
     if (tid == 0) {
         atomicAdd(arrived, 1u);
+        ev(0, 28);
         unsigned it = 0;
         while (ld_acquire(arrived) < (unsigned)active) {
             if (++it > (1u << 24)) {
