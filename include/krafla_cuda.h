@@ -102,8 +102,18 @@ void kc_model_free(kc_model *m);
 int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_type);
 /* Replaces ml_prefill (transformer.h:60, transformer.c:427-438): n host
  * tokens at positions pos0..; logits [n][vocab] (host) or NULL (classifier
- * skipped). KC_E_SHAPE when a position or token is out of range. */
+ * skipped). KC_E_SHAPE when a position or token is out of range.
+ * With the state's batch > 1 (the default) the tokens go through the model in
+ * chunks of up to batch tokens, each projection one int8 tensor-core GEMM
+ * whose per-row float accumulation follows the reference's packed kernels;
+ * with batch 1 they run one decode step each, and the logits equal those of
+ * kc_forward bit for bit. */
 int kc_prefill(kc_state *s, const int *tokens, int n, int pos0, float *logits);
+/* Prompt tokens per batched prefill step: the ml_state.batch field
+ * (model/transformer.h:30-31) that ml_run --batch sets (app/ml_run.c:274,347);
+ * 1..KC_BATCH_MAX, 1 = token by token. KC_E_SHAPE outside that range. */
+#define KC_BATCH_MAX 1024
+int kc_set_batch(kc_state *s, int batch);
 /* Replaces ml_forward (transformer.h:62, transformer.c:257-306): logits for
  * `token` at `pos` in a host buffer owned by the state, valid until the next
  * call; NULL when pos or token is out of range (or on a device error). */
@@ -179,6 +189,14 @@ int kc_matvec_f32_noalloc(float *y, int type, int d_f16, const void *wq, const v
 int kc_block_sums_dev(int32_t *s, int type, const void *wq, int rows, int cols, const int8_t *xq, void *stream);
 
 /* Device memory helpers for callers without a CUDA runtime of their own. */
+/* Replaces ml_matmul (ops/ops.c:51-79, the batched products of prefill) on
+ * device buffers: y[t * rows + r] = sum_b s(r, t, b) * (d_w[r][b] * d_x[t][b])
+ * for n quantized activation rows xq [n][cols], xd [n][cols/32], each block dot
+ * an exact int32 from the int8 tensor cores and the float sum over blocks in
+ * block order as the reference's packed kernels accumulate it. The weights are
+ * repacked into temporary device memory per call. */
+int kc_matmul_dev(float *y, int type, int d_f16, const void *wq, const void *wd, int rows, int cols,
+                  const int8_t *xq, const float *xd, int n, void *stream);
 void *kc_dev_alloc(size_t bytes);
 void kc_dev_free(void *p);
 int kc_memcpy_htod(void *dst, const void *src, size_t bytes);

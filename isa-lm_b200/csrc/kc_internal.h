@@ -50,6 +50,9 @@ struct DevLayer {
     int window = 0, local_rope = 0;
 };
 
+struct PfModel;     /* packed weights of the batched prefill (kc_prefill.cu) */
+struct PfScratch;   /* its per-state buffers */
+
 /* Parses and validates the header of an .mlb (model/mlb.c:80-159). */
 int parse_header(kc_config *cfg, int *shared, const uint8_t *h);
 /* Takes the arrays of a mapped .mlb (model/mlb.c:161-218). */
@@ -79,6 +82,8 @@ struct kc_model {
     size_t stream_bytes = 0;
     unsigned long long *d_cta_base = nullptr;   /* [stream_G] */
     int stream_G = 0;
+    /* the batched prefill's packed weights, built on first use */
+    kc::PfModel *pf = nullptr;
 };
 
 #endif

@@ -136,6 +136,27 @@ __device__ __forceinline__ unsigned quant4(const float v[4], float *d, int *sum)
     return word;
 }
 
+/* The reference's single-scale row quantization (ops/ops.c:81-96) of the n
+ * values x[0, n) by one warp (lane i takes elements i, i+32, ...): the quants
+ * into out, and as floats into back when given; returns the scale. */
+__device__ __forceinline__ float warp_quantize_row(const float *x, int n, int8_t *out, float *back, int lane) {
+    float amax = 0.0f;
+    for (int i = lane; i < n; i += 32) amax = fmaxf(amax, fabsf(x[i]));
+    amax = warp_max(amax);
+    const bool tiny = amax < 1e-30f;
+    const float id = tiny ? 0.0f : __fdiv_rn(127.0f, amax);
+    for (int i = lane; i < n; i += 32) {
+        int qi = 0;
+        if (!tiny) {
+            const float t = truncf(__fadd_rn(__fmul_rn(x[i], id), copysignf(0.5f, x[i])));
+            qi = (int)fminf(fmaxf(t, -127.0f), 127.0f);
+        }
+        out[i] = (int8_t)qi;
+        if (back) back[i] = (float)qi;
+    }
+    return tiny ? 0.0f : __fdiv_rn(amax, 127.0f);
+}
+
 /* ---- mbarrier / bulk-copy primitives (PTX ISA: mbarrier, cp.async.bulk) ---- */
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }

@@ -1,0 +1,993 @@
+/* Batched prompt prefill on sm_100a: ml_prefill / prefill_step
+ * (model/transformer.c:385-438) with the matrix products on the tensor cores.
+ *
+ * A chunk of up to `batch` prompt tokens goes through each layer as the
+ * reference's prefill_step takes it: per token RMSNorm and the Q8_0 activation
+ * rule, one matrix product per projection shared by every token of the chunk,
+ * per token bias / RoPE / KV store, the batched attention (ops/ops.c:186-238)
+ * and the residual adds.
+ *
+ * Projections: int8 GEMMs on tcgen05 (kind::i8, s8 x s8 -> s32 in TMEM). One
+ * MMA covers one 32-wide K block, so every (row, token) block dot is an exact
+ * int32, as the reference's dpbusd sums are; the epilogue warps read it from
+ * TMEM and accumulate in float in block order, acc = fma(s, d_w * d_x, acc),
+ * the per-row chain of the reference's packed kernels
+ * (kernels/avx512vnni/k_avx512vnni.c:128-186). Weights are repacked once per
+ * model into the MMA's shared-memory operand layout (Q4 nibbles widened to
+ * int8, scales to float), and each quantized activation chunk is written in
+ * the same layout, so a pipeline stage is one bulk copy per operand.
+ *
+ * CTA of the GEMM: warp 0 issues the bulk copies, warp 1 owns TMEM and issues
+ * the MMAs, warps 2..9 are the epilogue (two per TMEM lane quarter, each 16
+ * token columns of a 128-row x 32-token tile).
+ */
+#include <cmath>
+#include <cstring>
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "kc_internal.h"
+#include "kc_kernels.cuh"
+#include "kc_prefill.h"
+
+namespace kc {
+
+constexpr int PF_M = 128;                              /* weight rows per tile: the TMEM lanes */
+constexpr int PF_N = 32;                               /* tokens per tile: TMEM columns per buffer */
+constexpr int PF_KB = 4;                               /* K blocks per pipeline stage */
+constexpr int PF_NST = 5;                              /* pipeline stages */
+constexpr int PF_NBUF = 8;                             /* TMEM accumulator buffers */
+constexpr int PF_EPI_WARPS = 8;                        /* two per TMEM lane quarter */
+constexpr int PF_THREADS = 32 * (2 + PF_EPI_WARPS);
+constexpr int PF_COLS = PF_N * 4 / PF_EPI_WARPS;       /* token columns per epilogue warp */
+constexpr int PF_A_BLK = PF_M * QK;                    /* bytes of one K block of a weight tile */
+constexpr int PF_B_BLK = PF_N * QK;                    /* bytes of one K block of a token tile */
+constexpr int PF_STAGE = PF_KB * (PF_A_BLK + PF_B_BLK);
+constexpr int PF_TMEM_COLS = PF_NBUF * PF_N;
+constexpr int PF_SMEM = 1024 + PF_NST * PF_STAGE + 256;
+static_assert(PF_TMEM_COLS >= 32 && (PF_TMEM_COLS & (PF_TMEM_COLS - 1)) == 0, "TMEM columns: a power of two");
+static_assert(PF_COLS == 16, "the epilogue loads 16 TMEM columns at a time");
+static_assert((2 * PF_NST + 2 * PF_NBUF) * 8 + 4 <= 256, "barrier room");
+
+/* Byte (r, k) of one K block (rows x 32 bytes) in the MMA's K-major layout
+ * without swizzle: core matrices of 8 rows x 16 bytes (128 contiguous bytes),
+ * the two 16-byte K halves of a row group 128 bytes apart, row groups 256
+ * bytes apart. */
+__host__ __device__ inline int tile_off(int r, int k) { return (r >> 3) * 256 + (k >> 4) * 128 + (r & 7) * 16 + (k & 15); }
+
+/* Shared-memory matrix descriptor of a K block in that layout (tcgen05
+ * descriptor: start >> 4, leading-dimension offset 128 >> 4 (between the K
+ * halves), stride offset 256 >> 4 (between row groups), version 1, no swizzle). */
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(256 >> 4) << 32) |
+           (1ull << 46);
+}
+/* Instruction descriptor: s32 accumulators, A and B signed 8-bit, both K-major,
+ * N = PF_N, M = PF_M. */
+constexpr uint32_t PF_IDESC =
+    (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(PF_N >> 3) << 17) | ((uint32_t)(PF_M >> 4) << 24);
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_alloc(uint32_t *slot, int ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tc_dealloc(uint32_t taddr, int ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_mma_i8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+            d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+        "[%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+/* Error bit of the prefill kernels: a pipeline wait gave up. */
+constexpr unsigned PF_ERR_WAIT = 4u;
+
+enum { PF_STORE = 0, PF_RESID = 1 };
+
+struct PfGemm {
+    const int8_t *wq;    /* [mt][nbk] K blocks of PF_A_BLK bytes */
+    const float *wd;     /* [mt][nbk][PF_M] */
+    const float *bias;   /* [rows] or null */
+    const int8_t *xq;    /* [nt][nbk] K blocks of PF_B_BLK bytes */
+    const float *xd;     /* [nt][nbk][PF_N] */
+    float *out;          /* out[t * ldo + row] */
+    int ldo, rows, T, nbk, mode;
+    float softcap;
+    unsigned *err;
+};
+
+/* Y[t][row] = sum_b s(row, t, b) * (d_w[row][b] * d_x[t][b]) over one
+ * 128-row x 32-token tile (blockIdx.y, blockIdx.x): stored, or added to out
+ * (residual), with the row's bias and the logit soft-cap when given. */
+__global__ void __launch_bounds__(PF_THREADS, 2) pf_gemm_kernel(const __grid_constant__ PfGemm g) {
+    extern __shared__ unsigned char pf_smem_raw[];
+    unsigned char *sm = (unsigned char *)(((uintptr_t)pf_smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t *full = (uint64_t *)(sm + PF_NST * PF_STAGE), *empty = full + PF_NST;
+    uint64_t *tfull = empty + PF_NST, *tempty = tfull + PF_NBUF;
+    uint32_t *tslot = (uint32_t *)(tempty + PF_NBUF);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = blockIdx.x, m = blockIdx.y, nbk = g.nbk;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < PF_NST; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < PF_NBUF; i++) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], PF_EPI_WARPS);
+        }
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tc_alloc(tslot, PF_TMEM_COLS);
+        tc_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    if (warp == 0) {
+        if (lane == 0) {
+            const int nst = (nbk + PF_KB - 1) / PF_KB;
+            for (int st = 0; st < nst; st++) {
+                const int s = st % PF_NST;
+                if (!mbar_wait(&empty[s], ((st / PF_NST) & 1) ^ 1, g.err)) {
+                    atomicOr(g.err, PF_ERR_WAIT);
+                    break;
+                }
+                const int kbs = min(PF_KB, nbk - st * PF_KB);
+                unsigned char *a = sm + s * PF_STAGE, *b = a + PF_KB * PF_A_BLK;
+                mbar_expect_tx(&full[s], (unsigned)(kbs * (PF_A_BLK + PF_B_BLK)));
+                bulk_g2s(a, g.wq + ((size_t)m * nbk + (size_t)st * PF_KB) * PF_A_BLK, kbs * PF_A_BLK, &full[s]);
+                bulk_g2s(b, g.xq + ((size_t)n * nbk + (size_t)st * PF_KB) * PF_B_BLK, kbs * PF_B_BLK, &full[s]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            for (int kb = 0; kb < nbk; kb++) {
+                const int st = kb / PF_KB, j = kb - st * PF_KB, s = st % PF_NST, buf = kb % PF_NBUF;
+                if (j == 0 && !mbar_wait(&full[s], (st / PF_NST) & 1, g.err)) {
+                    atomicOr(g.err, PF_ERR_WAIT);
+                    break;
+                }
+                if (!mbar_wait(&tempty[buf], ((kb / PF_NBUF) & 1) ^ 1, g.err)) {
+                    atomicOr(g.err, PF_ERR_WAIT);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a = smem_u32(sm + s * PF_STAGE) + j * PF_A_BLK;
+                const uint32_t b = smem_u32(sm + s * PF_STAGE + PF_KB * PF_A_BLK) + j * PF_B_BLK;
+                tc_mma_i8(tmem + (uint32_t)(buf * PF_N), umma_desc(a), umma_desc(b), PF_IDESC, 0u);
+                tc_commit(&tfull[buf]);
+                if (j == PF_KB - 1 || kb == nbk - 1) tc_commit(&empty[s]);
+            }
+        }
+    } else {
+        /* epilogue: TMEM lane quarter q (the warp's rank in its warpgroup),
+         * token columns c0 .. c0+15 of the tile */
+        const int e = warp - 2, q = warp & 3, c0 = (e >> 2) * PF_COLS;
+        const int row = m * PF_M + q * 32 + lane;
+        const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
+        const float *wd = g.wd + (size_t)m * nbk * PF_M + q * 32 + lane;
+        const float *xd = g.xd + (size_t)n * nbk * PF_N + c0;
+        float acc[PF_COLS];
+#pragma unroll
+        for (int c = 0; c < PF_COLS; c++) acc[c] = 0.0f;
+        bool ok = true;
+        for (int kb = 0; kb < nbk; kb++) {
+            const int buf = kb % PF_NBUF;
+            const float dw = __ldg(wd + (size_t)kb * PF_M);
+            float dx[PF_COLS];
+#pragma unroll
+            for (int i = 0; i < PF_COLS / 4; i++) {
+                const float4 v = __ldg((const float4 *)(xd + (size_t)kb * PF_N) + i);
+                dx[4 * i] = v.x;
+                dx[4 * i + 1] = v.y;
+                dx[4 * i + 2] = v.z;
+                dx[4 * i + 3] = v.w;
+            }
+            const bool w = mbar_wait(&tfull[buf], (kb / PF_NBUF) & 1, g.err);
+            if (!__all_sync(0xffffffffu, w)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t s[PF_COLS];
+            tc_ld16(tq + (uint32_t)(buf * PF_N), s);
+            tc_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
+#pragma unroll
+            for (int c = 0; c < PF_COLS; c++) acc[c] = __fmaf_rn((float)(int)s[c], __fmul_rn(dw, dx[c]), acc[c]);
+        }
+        if (!ok) {
+            if (lane == 0) atomicOr(g.err, PF_ERR_WAIT);
+        } else if (row < g.rows) {
+            const float bias = g.bias ? g.bias[row] : 0.0f;
+#pragma unroll
+            for (int c = 0; c < PF_COLS; c++) {
+                const int t = n * PF_N + c0 + c;
+                if (t < g.T) {
+                    float y = acc[c];
+                    if (g.bias) y = __fadd_rn(y, bias);
+                    if (g.softcap > 0.0f) y = __fmul_rn(g.softcap, tanhf(__fdiv_rn(y, g.softcap)));
+                    float *o = g.out + (size_t)t * g.ldo + row;
+                    *o = g.mode == PF_RESID ? __fadd_rn(*o, y) : y;
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tc_dealloc(tmem, PF_TMEM_COLS);
+}
+
+/* ------------------------------------------------------------ activations */
+
+enum { PQ_NORM = 0, PQ_PLAIN = 1, PQ_GATED = 2 };
+
+struct PfQuant {
+    const float *x;      /* x[t * ldx + i] */
+    int ldx;
+    const float *w;      /* norm weights (PQ_NORM) */
+    float eps;
+    int mode, act, cols, T, nbk;
+    int8_t *xq;          /* [nt][nbk] K blocks of PF_B_BLK bytes */
+    float *xd;           /* [nt][nbk][PF_N] */
+};
+
+/* One token per CTA (grid: the token tiles' rows, padding tokens quantize to
+ * zero): v = RMSNorm(x) * w (k_scalar.c:59-64, o = (x * inv) * w), x itself,
+ * or act(g) * u from a [g | u] row (model/transformer.c:233-236); then the
+ * Q8_0 rule per 32-block (k_scalar.c:39-57) into the GEMM's token-tile layout. */
+__global__ void __launch_bounds__(256) pf_quant_kernel(const PfQuant a) {
+    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nt = t / PF_N, tr = t - nt * PF_N;
+    __shared__ float red[8];
+    const bool live = t < a.T;
+    const float *xr = a.x + (size_t)(live ? t : 0) * a.ldx;
+    float inv = 1.0f;
+    if (a.mode == PQ_NORM) {
+        float ss = 0.0f;
+        if (live)
+            for (int i = tid; i < a.cols; i += 256) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        ss = red[0];
+        for (int w = 1; w < 8; w++) ss = __fadd_rn(ss, red[w]);
+        inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)a.cols), a.eps)));
+    }
+    for (int b0 = warp * 4; b0 < a.nbk; b0 += 32) {
+        const int b = b0 + (lane >> 3), j0 = (lane & 7) * 4;
+        float v[4] = { 0.0f, 0.0f, 0.0f, 0.0f };
+        if (live && b < a.nbk) {
+            const int i = b * QK + j0;
+            if (a.mode == PQ_GATED) {
+#pragma unroll
+                for (int k = 0; k < 4; k++) v[k] = act_mul(a.act, xr[i + k], xr[a.cols + i + k]);
+            } else {
+                const float4 x4 = *(const float4 *)(xr + i);
+                v[0] = x4.x; v[1] = x4.y; v[2] = x4.z; v[3] = x4.w;
+                if (a.mode == PQ_NORM) {
+                    const float4 w4 = *(const float4 *)(a.w + i);
+                    v[0] = __fmul_rn(__fmul_rn(v[0], inv), w4.x);
+                    v[1] = __fmul_rn(__fmul_rn(v[1], inv), w4.y);
+                    v[2] = __fmul_rn(__fmul_rn(v[2], inv), w4.z);
+                    v[3] = __fmul_rn(__fmul_rn(v[3], inv), w4.w);
+                }
+            }
+        }
+        float d;
+        int sum;
+        const unsigned word = quant4(v, &d, &sum);
+        if (b < a.nbk) {
+            int8_t *blk = a.xq + ((size_t)nt * a.nbk + b) * PF_B_BLK;
+            *(unsigned *)(blk + tile_off(tr, j0)) = word;
+            if ((lane & 7) == 0) a.xd[((size_t)nt * a.nbk + b) * PF_N + tr] = d;
+        }
+    }
+}
+
+struct PfEmbed {
+    const uint8_t *q;
+    const void *d;
+    int type, d16;
+    float scale;
+    const int *tok;
+    int cols;
+    float *x;
+};
+
+/* x[t] = dequant(tok_emb[tok[t]]) * embed_scale (model/transformer.c:226-230,
+ * core/quant_ref.c:4-19). */
+__global__ void __launch_bounds__(256) pf_embed_kernel(const PfEmbed a) {
+    const int t = blockIdx.x, tok = a.tok[t], nb = a.cols / QK;
+    for (int i = threadIdx.x; i < a.cols; i += 256) {
+        const int b = i / QK, j = i % QK;
+        const float sc = a.d16 ? __half2float(((const __half *)a.d)[(size_t)tok * nb + b])
+                               : ((const float *)a.d)[(size_t)tok * nb + b];
+        int v;
+        if (a.type == T_Q8) {
+            v = ((const int8_t *)a.q)[(size_t)tok * a.cols + i];
+        } else {
+            const uint8_t byte = a.q[((size_t)tok * nb + b) * (QK / 2) + (j & 15)];
+            v = (j < 16 ? (byte & 0xF) : (byte >> 4)) - 8;
+        }
+        float o = __fmul_rn((float)v, sc);
+        if (a.scale != 1.0f) o = __fmul_rn(o, a.scale);
+        a.x[(size_t)t * a.cols + i] = o;
+    }
+}
+
+struct PfRope {
+    float *qkv;                  /* [T][q_dim + 2 kv_dim], q | k | v */
+    int ldq;
+    const float *rcos, *rsin;    /* [max_seq][hd / 2] */
+    void *kc, *vc;               /* this layer's cache rows [max_seq][kv_dim] */
+    float *kd, *vd;              /* Q8 cache: row scales [max_seq][n_kv] */
+    int8_t *qq;                  /* Q8 cache: quantized query heads [T][q_dim] */
+    float *qd;                   /* their scales [T][n_heads] */
+    int pos0, hd, n_heads, n_kv, q_dim, kv_dim, kv_type;
+};
+
+/* One token per CTA: RoPE on adjacent pairs of every q and k head
+ * (k_scalar.c:79-94) at position pos0 + t, then the K and V rows into the
+ * cache in its type (model/transformer.c:188-205: f16 rounding, or the
+ * single-scale row quantization per KV head, ops/ops.c:81-96) and, for a Q8
+ * cache, the query heads quantized the same way (ops/ops.c:229-233). */
+__global__ void __launch_bounds__(256) pf_rope_kernel(const PfRope a) {
+    const int t = blockIdx.x, p = a.pos0 + t, h2 = a.hd / 2;
+    float *q = a.qkv + (size_t)t * a.ldq, *k = q + a.q_dim, *v = k + a.kv_dim;
+    const float *cs = a.rcos + (size_t)p * h2, *sn = a.rsin + (size_t)p * h2;
+    const int nq = a.n_heads * h2, nk = a.n_kv * h2;
+    for (int idx = threadIdx.x; idx < nq + nk; idx += 256) {
+        const bool isq = idx < nq;
+        const int r = isq ? idx : idx - nq, h = r / h2, i = r - h * h2;
+        float *e = (isq ? q : k) + h * a.hd + 2 * i;
+        const float xa = e[0], xb = e[1], c = cs[i], s = sn[i];
+        e[0] = __fsub_rn(__fmul_rn(xa, c), __fmul_rn(xb, s));
+        e[1] = __fadd_rn(__fmul_rn(xa, s), __fmul_rn(xb, c));
+    }
+    __syncthreads();
+    const size_t row = (size_t)p * a.kv_dim;
+    if (a.kv_type == KC_F32) {
+        for (int i = threadIdx.x; i < a.kv_dim; i += 256) {
+            ((float *)a.kc)[row + i] = k[i];
+            ((float *)a.vc)[row + i] = v[i];
+        }
+    } else if (a.kv_type == KC_F16) {
+        for (int i = threadIdx.x; i < a.kv_dim; i += 256) {
+            ((__half *)a.kc)[row + i] = __float2half_rn(k[i]);
+            ((__half *)a.vc)[row + i] = __float2half_rn(v[i]);
+        }
+    } else {
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        for (int j = warp; j < 2 * a.n_kv + a.n_heads; j += 8) {
+            if (j < 2 * a.n_kv) {
+                const bool isv = j >= a.n_kv;
+                const int g = isv ? j - a.n_kv : j;
+                int8_t *dst = (int8_t *)(isv ? a.vc : a.kc) + row + (size_t)g * a.hd;
+                const float d = warp_quantize_row((isv ? v : k) + g * a.hd, a.hd, dst, nullptr, lane);
+                if (lane == 0) (isv ? a.vd : a.kd)[(size_t)p * a.n_kv + g] = d;
+            } else {
+                const int h = j - 2 * a.n_kv;
+                const float d =
+                    warp_quantize_row(q + h * a.hd, a.hd, a.qq + (size_t)t * a.q_dim + h * a.hd, nullptr, lane);
+                if (lane == 0) a.qd[(size_t)t * a.n_heads + h] = d;
+            }
+        }
+    }
+}
+
+/* ------------------------------------------------------------ attention */
+
+constexpr int PA_THREADS = 128;
+constexpr int PA_MAXG = 16;                          /* query heads per KV head */
+constexpr int PA_MAXO = ATT_MAX_OUT / PA_THREADS;    /* outputs per thread */
+
+struct PfAttn {
+    const float *qkv;            /* rotated query heads at qkv[t * ldq + h * hd] */
+    int ldq;
+    const int8_t *qq;            /* Q8 cache: quantized query heads */
+    const float *qd;
+    const void *kc, *vc;
+    const float *kd, *vd;
+    float *out;                  /* [T][q_dim] */
+    int pos0, hd, n_heads, n_kv, q_dim, kv_dim, window, npos;
+    float scale, softcap;
+};
+
+__device__ __forceinline__ float block_reduce(float v, float *red, bool is_max) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = is_max ? warp_max(v) : warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float r = red[0];
+    for (int w = 1; w < PA_THREADS / 32; w++) r = is_max ? fmaxf(r, red[w]) : __fadd_rn(r, red[w]);
+    return r;
+}
+
+/* Attention of token t (position pos0 + t) for the query heads of KV head g
+ * (ops/ops.c:124-180, attend): scores q.k * scale summed over the head
+ * dimension in order (Q8 cache: int32 dot of the quantized query and row,
+ * (float)s * (qd * scale) * kd), the optional soft-cap, softmax (all -inf:
+ * uniform, k_scalar.c:66-77), then out = sum_t p_t * V_t in position order
+ * (Q8: (p_t * vd_t) * v). Scores live in shared memory, npos per head. */
+template <int KV>
+__global__ void __launch_bounds__(PA_THREADS) pf_attn_kernel(const PfAttn a) {
+    extern __shared__ float pa_smem[];
+    constexpr int ES = KV == KC_F32 ? 4 : (KV == KC_F16 ? 2 : 1);
+    const int t = blockIdx.x, g = blockIdx.y, tid = threadIdx.x;
+    const int group = a.n_heads / a.n_kv, hd = a.hd, p = a.pos0 + t;
+    const int first = a.window && p >= a.window ? p + 1 - a.window : 0, n = p + 1 - first;
+    float *sq = pa_smem;                        /* [group][hd] query heads (Q8: as int8 words) */
+    float *sc = sq + group * hd;                /* [group][npos] */
+    __shared__ float red[PA_THREADS / 32];
+    __shared__ float cq[PA_MAXG];
+    const float *qsrc = a.qkv + (size_t)t * a.ldq + (size_t)g * group * hd;
+    if constexpr (KV == KC_Q8_0) {
+        const int8_t *qq = a.qq + (size_t)t * a.q_dim + (size_t)g * group * hd;
+        for (int i = tid; i < group * hd / 4; i += PA_THREADS) ((int *)sq)[i] = ((const int *)qq)[i];
+        if (tid < group) cq[tid] = __fmul_rn(a.qd[(size_t)t * a.n_heads + g * group + tid], a.scale);
+    } else {
+        for (int i = tid; i < group * hd; i += PA_THREADS) sq[i] = qsrc[i];
+    }
+    __syncthreads();
+    const size_t rowb = (size_t)a.kv_dim * ES;
+    const uint8_t *kb = (const uint8_t *)a.kc + (size_t)g * hd * ES, *vb = (const uint8_t *)a.vc + (size_t)g * hd * ES;
+    for (int i = tid; i < n; i += PA_THREADS) {
+        const int j = first + i;
+        const uint8_t *kr = kb + (size_t)j * rowb;
+        float acc[PA_MAXG];
+        int isum[PA_MAXG];
+#pragma unroll
+        for (int h = 0; h < PA_MAXG; h++) {
+            acc[h] = 0.0f;
+            isum[h] = 0;
+        }
+        for (int d0 = 0; d0 < hd; d0 += 4) {
+            if constexpr (KV == KC_Q8_0) {
+                const int kw = *(const int *)(kr + d0);
+#pragma unroll
+                for (int h = 0; h < PA_MAXG; h++)
+                    if (h < group) isum[h] = __dp4a(((const int *)sq)[(h * hd + d0) >> 2], kw, isum[h]);
+            } else {
+                float k4[4];
+                if constexpr (KV == KC_F32) {
+                    const float4 v = *(const float4 *)(kr + 4 * d0);
+                    k4[0] = v.x; k4[1] = v.y; k4[2] = v.z; k4[3] = v.w;
+                } else {
+                    const uint2 u = *(const uint2 *)(kr + 2 * d0);
+                    const float2 lo = __half22float2(*(const __half2 *)&u.x), hi = __half22float2(*(const __half2 *)&u.y);
+                    k4[0] = lo.x; k4[1] = lo.y; k4[2] = hi.x; k4[3] = hi.y;
+                }
+#pragma unroll
+                for (int h = 0; h < PA_MAXG; h++)
+                    if (h < group) {
+                        const float4 q4 = *(const float4 *)(sq + h * hd + d0);
+                        acc[h] = __fadd_rn(acc[h], __fmul_rn(q4.x, k4[0]));
+                        acc[h] = __fadd_rn(acc[h], __fmul_rn(q4.y, k4[1]));
+                        acc[h] = __fadd_rn(acc[h], __fmul_rn(q4.z, k4[2]));
+                        acc[h] = __fadd_rn(acc[h], __fmul_rn(q4.w, k4[3]));
+                    }
+            }
+        }
+        const float kd = KV == KC_Q8_0 ? a.kd[(size_t)j * a.n_kv + g] : 0.0f;
+#pragma unroll
+        for (int h = 0; h < PA_MAXG; h++)
+            if (h < group) {
+                float s = KV == KC_Q8_0 ? __fmul_rn(__fmul_rn((float)isum[h], cq[h]), kd) : __fmul_rn(acc[h], a.scale);
+                if (a.softcap > 0.0f) s = __fmul_rn(a.softcap, tanhf(__fdiv_rn(s, a.softcap)));
+                sc[h * a.npos + i] = s;
+            }
+    }
+    __syncthreads();
+    for (int h = 0; h < group; h++) {
+        float *r = sc + h * a.npos;
+        float mx = -INFINITY;
+        for (int i = tid; i < n; i += PA_THREADS) mx = fmaxf(mx, r[i]);
+        mx = block_reduce(mx, red, true);
+        if (mx == -INFINITY) {
+            const float u = __fdiv_rn(1.0f, (float)n);
+            for (int i = tid; i < n; i += PA_THREADS) r[i] = u;
+            continue;
+        }
+        float sum = 0.0f;
+        for (int i = tid; i < n; i += PA_THREADS) {
+            const float e = expf(__fsub_rn(r[i], mx));
+            r[i] = e;
+            sum = __fadd_rn(sum, e);
+        }
+        sum = block_reduce(sum, red, false);
+        const float inv = __fdiv_rn(1.0f, sum);
+        for (int i = tid; i < n; i += PA_THREADS) r[i] = __fmul_rn(r[i], inv);
+    }
+    __syncthreads();
+    const int nout = group * hd;
+    float acc[PA_MAXO];
+    int oh[PA_MAXO], od[PA_MAXO];
+#pragma unroll
+    for (int k = 0; k < PA_MAXO; k++) {
+        const int o = tid + k * PA_THREADS;
+        acc[k] = 0.0f;
+        oh[k] = o < nout ? o / hd : 0;
+        od[k] = o < nout ? o % hd : 0;
+    }
+    for (int i = 0; i < n; i++) {
+        const int j = first + i;
+        const uint8_t *vr = vb + (size_t)j * rowb;
+        const float vd = KV == KC_Q8_0 ? a.vd[(size_t)j * a.n_kv + g] : 0.0f;
+#pragma unroll
+        for (int k = 0; k < PA_MAXO; k++) {
+            if (tid + k * PA_THREADS < nout) {
+                const float pr = sc[oh[k] * a.npos + i];
+                if constexpr (KV == KC_F32) {
+                    acc[k] = __fadd_rn(acc[k], __fmul_rn(pr, ((const float *)vr)[od[k]]));
+                } else if constexpr (KV == KC_F16) {
+                    acc[k] = __fadd_rn(acc[k], __fmul_rn(pr, __half2float(((const __half *)vr)[od[k]])));
+                } else {
+                    const float w = __fmul_rn(pr, vd);
+                    acc[k] = __fadd_rn(acc[k], __fmul_rn(w, (float)((const int8_t *)vr)[od[k]]));
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < PA_MAXO; k++)
+        if (tid + k * PA_THREADS < nout)
+            a.out[(size_t)t * a.q_dim + (size_t)g * group * hd + oh[k] * hd + od[k]] = acc[k];
+}
+
+/* ------------------------------------------------------------ weight repack */
+
+/* Row r, block b of a file matrix (Q8: int8 rows; Q4: 16 bytes per block,
+ * byte j = element j low nibble and j+16 high nibble, value nibble - 8) into
+ * row row0 + r of the packed matrix: int8 quants in the MMA tile layout and
+ * the block scale as float. */
+__global__ void pf_pack_kernel(const uint8_t *q, const void *d, int type, int d16, int rows, int cols, int row0,
+                               int nbk, int8_t *wq, float *wd) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int nb = cols / QK;
+    if (i >= (size_t)rows * nb) return;
+    const int r = (int)(i / nb), b = (int)(i - (size_t)r * nb);
+    const int R = row0 + r, m = R / PF_M, rr = R - m * PF_M;
+    alignas(16) int8_t v[QK];
+    if (type == T_Q8) {
+        const uint4 *src = (const uint4 *)(q + (size_t)r * cols + (size_t)b * QK);
+        *(uint4 *)v = src[0];
+        *(uint4 *)(v + 16) = src[1];
+    } else {
+        const uint8_t *src = q + ((size_t)r * nb + b) * (QK / 2);
+        for (int j = 0; j < 16; j++) {
+            v[j] = (int8_t)((src[j] & 15) - 8);
+            v[j + 16] = (int8_t)((src[j] >> 4) - 8);
+        }
+    }
+    int8_t *dst = wq + ((size_t)m * nbk + b) * PF_A_BLK;
+    *(uint4 *)(dst + tile_off(rr, 0)) = *(const uint4 *)v;
+    *(uint4 *)(dst + tile_off(rr, 16)) = *(const uint4 *)(v + 16);
+    wd[((size_t)m * nbk + b) * PF_M + rr] =
+        d16 ? __half2float(((const __half *)d)[(size_t)r * nb + b]) : ((const float *)d)[(size_t)r * nb + b];
+}
+
+/* Token t's quantized activation row (int8 [cols], scales [cols/32]) into
+ * the GEMM's token-tile layout. */
+__global__ void pf_pack_act_kernel(const int8_t *xq, const float *xd, int n, int cols, int8_t *tq, float *td) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int nb = cols / QK, tpad = (n + PF_N - 1) / PF_N * PF_N;
+    if (i >= (size_t)tpad * nb) return;
+    const int t = (int)(i / nb), b = (int)(i - (size_t)t * nb), nt = t / PF_N, tr = t - nt * PF_N;
+    uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+    float d = 0.0f;
+    if (t < n) {
+        const uint4 *src = (const uint4 *)(xq + (size_t)t * cols + (size_t)b * QK);
+        lo = src[0];
+        hi = src[1];
+        d = xd[(size_t)t * nb + b];
+    }
+    int8_t *blk = tq + ((size_t)nt * nb + b) * PF_B_BLK;
+    *(uint4 *)(blk + tile_off(tr, 0)) = lo;
+    *(uint4 *)(blk + tile_off(tr, 16)) = hi;
+    td[((size_t)nt * nb + b) * PF_N + tr] = d;
+}
+
+/* ------------------------------------------------------------ host side */
+
+namespace {
+
+int cuda_err(cudaError_t e, const char *what) {
+    if (e == cudaSuccess) return KC_OK;
+    set_error(std::string("prefill: ") + what + ": " + cudaGetErrorString(e));
+    (void)cudaGetLastError();
+    return e == cudaErrorMemoryAllocation ? KC_E_NOMEM : KC_E_IO;
+}
+#define PCK(call, what)                                    \
+    do {                                                   \
+        const cudaError_t e_ = (call);                     \
+        if (e_ != cudaSuccess) return cuda_err(e_, what);  \
+    } while (0)
+
+size_t up256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+/* One packed GEMM operand. */
+struct PfMat {
+    int8_t *q = nullptr;
+    float *d = nullptr;
+    float *bias = nullptr;
+    int rows = 0, cols = 0, mt = 0, nbk = 0;
+};
+
+struct PfLayerW {
+    PfMat qkv, wo, w13, w2;
+};
+
+}  // namespace
+
+struct PfModel {
+    std::vector<PfLayerW> layers;
+    PfMat cls;
+    bool have_cls = false;
+    std::vector<void *> allocs;
+    size_t bytes = 0;
+    ~PfModel() {
+        for (void *p : allocs) cudaFree(p);
+    }
+};
+
+struct PfScratch {
+    int tc = 0;                  /* tokens per chunk (a multiple of PF_N) */
+    size_t npos = 0;
+    void *base = nullptr;
+    float *x = nullptr, *qkv = nullptr, *ao = nullptr, *gu = nullptr, *xd = nullptr, *qd = nullptr;
+    int8_t *xq = nullptr, *qq = nullptr;
+    int *tok = nullptr;
+    ~PfScratch() {
+        if (base) cudaFree(base);
+    }
+};
+
+namespace {
+
+int alloc_mat(PfModel &P, PfMat &M, int rows, int cols, cudaStream_t st) {
+    M.rows = rows;
+    M.cols = cols;
+    M.mt = (rows + PF_M - 1) / PF_M;
+    M.nbk = cols / QK;
+    const size_t qb = (size_t)M.mt * M.nbk * PF_A_BLK, db = (size_t)M.mt * M.nbk * PF_M * sizeof(float);
+    void *q = nullptr, *d = nullptr;
+    PCK(cudaMalloc(&q, qb), "packed weights");
+    P.allocs.push_back(q);
+    PCK(cudaMalloc(&d, db), "packed scales");
+    P.allocs.push_back(d);
+    P.bytes += qb + db;
+    PCK(cudaMemsetAsync(q, 0, qb, st), "memset");
+    PCK(cudaMemsetAsync(d, 0, db, st), "memset");
+    M.q = (int8_t *)q;
+    M.d = (float *)d;
+    return KC_OK;
+}
+
+/* Staging buffers for one file matrix on its way to the pack kernel. */
+struct Staging {
+    uint8_t *q = nullptr;
+    void *d = nullptr;
+    size_t qcap = 0, dcap = 0;
+    ~Staging() {
+        if (q) cudaFree(q);
+        if (d) cudaFree(d);
+    }
+};
+
+int pack_part(const HostMat &H, int row0, PfMat &M, Staging &sg, cudaStream_t st) {
+    if (H.cols != M.cols || row0 + H.rows > M.rows || (H.type != KC_Q8_0 && H.type != KC_Q4_0)) {
+        set_error("prefill: a matrix does not fit its packed operand");
+        return KC_E_SHAPE;
+    }
+    const size_t qb = H.qbytes(), db = H.dbytes();
+    PCK(cudaStreamSynchronize(st), "staging");
+    if (qb > sg.qcap) {
+        if (sg.q) cudaFree(sg.q);
+        sg.q = nullptr;
+        PCK(cudaMalloc(&sg.q, qb), "staging");
+        sg.qcap = qb;
+    }
+    if (db > sg.dcap) {
+        if (sg.d) cudaFree(sg.d);
+        sg.d = nullptr;
+        PCK(cudaMalloc(&sg.d, db), "staging");
+        sg.dcap = db;
+    }
+    PCK(cudaMemcpyAsync(sg.q, H.q, qb, cudaMemcpyHostToDevice, st), "weights upload");
+    PCK(cudaMemcpyAsync(sg.d, H.d, db, cudaMemcpyHostToDevice, st), "scales upload");
+    const size_t items = (size_t)H.rows * (H.cols / QK);
+    pf_pack_kernel<<<(unsigned)((items + 255) / 256), 256, 0, st>>>(sg.q, sg.d, H.type == KC_Q4_0 ? T_Q4 : T_Q8,
+                                                                     H.d16, H.rows, H.cols, row0, M.nbk, M.q, M.d);
+    PCK(cudaGetLastError(), "pack kernel");
+    return KC_OK;
+}
+
+/* The stacked bias of a packed operand from the layer's host arrays. */
+int stack_bias(PfModel &P, PfMat &M, const std::vector<std::pair<const float *, int>> &parts, cudaStream_t st) {
+    void *b = nullptr;
+    PCK(cudaMalloc(&b, sizeof(float) * (size_t)M.rows), "bias");
+    P.allocs.push_back(b);
+    size_t off = 0;
+    for (const auto &pr : parts) {
+        PCK(cudaMemcpyAsync((float *)b + off, pr.first, sizeof(float) * (size_t)pr.second, cudaMemcpyHostToDevice, st),
+            "bias copy");
+        off += (size_t)pr.second;
+    }
+    M.bias = (float *)b;
+    return KC_OK;
+}
+
+int build_layers(kc_model *m, PfModel &P, cudaStream_t st) {
+    const kc_config &c = m->cfg;
+    Staging sg;
+    P.layers.resize((size_t)c.n_layers);
+    for (int l = 0; l < c.n_layers; l++) {
+        const HostLayer &H = m->layers[(size_t)l];
+        PfLayerW &W = P.layers[(size_t)l];
+        int r;
+        if ((r = alloc_mat(P, W.qkv, c.q_dim + 2 * c.kv_dim, c.dim, st)) != KC_OK) return r;
+        if ((r = pack_part(H.wq, 0, W.qkv, sg, st)) != KC_OK) return r;
+        if ((r = pack_part(H.wk, c.q_dim, W.qkv, sg, st)) != KC_OK) return r;
+        if ((r = pack_part(H.wv, c.q_dim + c.kv_dim, W.qkv, sg, st)) != KC_OK) return r;
+        if (H.bq && (r = stack_bias(P, W.qkv, { { H.bq, c.q_dim }, { H.bk, c.kv_dim }, { H.bv, c.kv_dim } }, st)) != KC_OK)
+            return r;
+        if ((r = alloc_mat(P, W.wo, c.dim, c.q_dim, st)) != KC_OK) return r;
+        if ((r = pack_part(H.wo, 0, W.wo, sg, st)) != KC_OK) return r;
+        if ((r = alloc_mat(P, W.w13, 2 * c.hidden_dim, c.dim, st)) != KC_OK) return r;
+        if ((r = pack_part(H.w1, 0, W.w13, sg, st)) != KC_OK) return r;
+        if ((r = pack_part(H.w3, c.hidden_dim, W.w13, sg, st)) != KC_OK) return r;
+        if ((r = alloc_mat(P, W.w2, c.dim, c.hidden_dim, st)) != KC_OK) return r;
+        if ((r = pack_part(H.w2, 0, W.w2, sg, st)) != KC_OK) return r;
+    }
+    PCK(cudaStreamSynchronize(st), "weight repack");
+    return KC_OK;
+}
+
+int build_cls(kc_model *m, PfModel &P, cudaStream_t st) {
+    Staging sg;
+    int r = alloc_mat(P, P.cls, m->cfg.vocab, m->cfg.dim, st);
+    if (r == KC_OK) r = pack_part(m->wcls, 0, P.cls, sg, st);
+    if (r != KC_OK) return r;
+    PCK(cudaStreamSynchronize(st), "classifier repack");
+    P.have_cls = true;
+    return KC_OK;
+}
+
+int attn_smem_bytes(const kc_config &c, size_t npos) {
+    const int group = c.n_heads / c.n_kv_heads;
+    return (int)(sizeof(float) * ((size_t)group * c.head_dim + (size_t)group * npos));
+}
+
+int ensure_scratch(PfScratch *&S, const kc_config &c, int tc, size_t npos) {
+    if (S && S->tc >= tc && S->npos >= npos) return KC_OK;
+    delete S;
+    S = new (std::nothrow) PfScratch();
+    if (!S) return KC_E_NOMEM;
+    const size_t T = (size_t)tc, wide = (size_t)std::max(std::max(c.dim, c.q_dim), c.hidden_dim);
+    struct B { void **p; size_t bytes; };
+    std::vector<B> bufs = {
+        { (void **)&S->x, sizeof(float) * T * c.dim },
+        { (void **)&S->qkv, sizeof(float) * T * (size_t)(c.q_dim + 2 * c.kv_dim) },
+        { (void **)&S->ao, sizeof(float) * T * c.q_dim },
+        { (void **)&S->gu, sizeof(float) * T * 2 * (size_t)c.hidden_dim },
+        { (void **)&S->xq, T * wide },
+        { (void **)&S->xd, sizeof(float) * T * (wide / QK) },
+        { (void **)&S->qq, T * c.q_dim },
+        { (void **)&S->qd, sizeof(float) * T * c.n_heads },
+        { (void **)&S->tok, sizeof(int) * T },
+    };
+    size_t total = 0;
+    for (const B &b : bufs) total += up256(b.bytes);
+    PCK(cudaMalloc(&S->base, total), "prefill scratch");
+    size_t off = 0;
+    for (const B &b : bufs) {
+        *b.p = (uint8_t *)S->base + off;
+        off += up256(b.bytes);
+    }
+    S->tc = tc;
+    S->npos = npos;
+    return KC_OK;
+}
+
+void launch_quant(const PfScratch &S, const float *x, int ldx, const float *w, float eps, int mode, int act, int cols,
+                  int T, cudaStream_t st) {
+    PfQuant q{ x, ldx, w, eps, mode, act, cols, T, cols / QK, S.xq, S.xd };
+    const int tpad = (T + PF_N - 1) / PF_N * PF_N;
+    pf_quant_kernel<<<tpad, 256, 0, st>>>(q);
+}
+
+void launch_gemm(const PfMat &W, const PfScratch &S, int T, float *out, int ldo, int mode, float softcap,
+                 unsigned *err, cudaStream_t st, int tok0 = 0) {
+    PfGemm g;
+    g.wq = W.q; g.wd = W.d; g.bias = W.bias;
+    g.xq = S.xq + (size_t)(tok0 / PF_N) * W.nbk * PF_B_BLK;
+    g.xd = S.xd + (size_t)(tok0 / PF_N) * W.nbk * PF_N;
+    g.out = out; g.ldo = ldo; g.rows = W.rows; g.T = T; g.nbk = W.nbk; g.mode = mode; g.softcap = softcap; g.err = err;
+    const dim3 grid((unsigned)((T + PF_N - 1) / PF_N), (unsigned)W.mt);
+    pf_gemm_kernel<<<grid, PF_THREADS, PF_SMEM, st>>>(g);
+}
+
+int set_attributes(int attn_smem) {
+    static int done_gemm = 0;
+    if (!done_gemm) {
+        PCK(cudaFuncSetAttribute(pf_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM), "gemm smem");
+        done_gemm = 1;
+    }
+    PCK(cudaFuncSetAttribute(pf_attn_kernel<KC_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem), "attn");
+    PCK(cudaFuncSetAttribute(pf_attn_kernel<KC_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem), "attn");
+    PCK(cudaFuncSetAttribute(pf_attn_kernel<KC_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem), "attn");
+    return KC_OK;
+}
+
+}  // namespace
+
+/* Shared memory the batched attention needs for a chunk reaching position
+ * last_pos; > PF_ATTN_SMEM_MAX means the batched path cannot take it. */
+bool pf_fits(const kc_config &c, int kv_type, int last_pos) {
+    (void)kv_type;
+    const int group = c.n_heads / c.n_kv_heads;
+    if (group > PA_MAXG || group * c.head_dim > ATT_MAX_OUT || c.head_dim % 4) return false;
+    if (c.dim % QK || c.q_dim % QK || c.hidden_dim % QK) return false;
+    return attn_smem_bytes(c, (size_t)last_pos + 1) <= PF_ATTN_SMEM_MAX;
+}
+
+void pf_free_model(PfModel *p) { delete p; }
+void pf_free_scratch(PfScratch *p) { delete p; }
+size_t pf_model_bytes(const PfModel *p) { return p ? p->bytes : 0; }
+
+int pf_prefill(const PfRun &r, const int *tokens, int n, int pos0, float *logits) {
+    const kc_config &c = r.m->cfg;
+    cudaStream_t st = r.st;
+    if (!r.m->pf) {
+        PfModel *P = new (std::nothrow) PfModel();
+        if (!P) return KC_E_NOMEM;
+        const int rc = build_layers(r.m, *P, st);
+        if (rc != KC_OK) {
+            delete P;
+            return rc;
+        }
+        r.m->pf = P;
+    }
+    PfModel &P = *r.m->pf;
+    if (logits && !P.have_cls) {
+        const int rc = build_cls(r.m, P, st);
+        if (rc != KC_OK) return rc;
+    }
+    const int tc = std::max(PF_N, std::min(r.batch, n) + PF_N - 1) / PF_N * PF_N;
+    const size_t npos = (size_t)pos0 + n;
+    int rc = ensure_scratch(*r.scratch, c, tc, npos);
+    if (rc != KC_OK) return rc;
+    PfScratch &S = **r.scratch;
+    const int asmem = attn_smem_bytes(c, npos);
+    rc = set_attributes(asmem);
+    if (rc != KC_OK) return rc;
+    const int group = c.n_heads / c.n_kv_heads, ldq = c.q_dim + 2 * c.kv_dim;
+    PCK(cudaMemsetAsync(r.err, 0, sizeof(unsigned), st), "error word");
+    for (int i0 = 0; i0 < n; i0 += tc) {
+        const int T = std::min(tc, n - i0), p0 = pos0 + i0;
+        PCK(cudaMemcpyAsync(S.tok, tokens + i0, sizeof(int) * (size_t)T, cudaMemcpyHostToDevice, st), "tokens");
+        PfEmbed e{ r.emb_q, r.emb_d, r.emb_type, r.emb_d16, c.embed_scale, S.tok, c.dim, S.x };
+        pf_embed_kernel<<<T, 256, 0, st>>>(e);
+        for (int l = 0; l < c.n_layers; l++) {
+            const PfLayerW &W = P.layers[(size_t)l];
+            const PfLayerRun &L = r.layers[l];
+            launch_quant(S, S.x, c.dim, L.attn_norm, c.norm_eps, PQ_NORM, c.act, c.dim, T, st);
+            launch_gemm(W.qkv, S, T, S.qkv, ldq, PF_STORE, 0.0f, r.err, st);
+            PfRope ro{ S.qkv, ldq, L.rcos, L.rsin, L.kc, L.vc, L.kd, L.vd, S.qq, S.qd,
+                       p0, c.head_dim, c.n_heads, c.n_kv_heads, c.q_dim, c.kv_dim, r.kv_type };
+            pf_rope_kernel<<<T, 256, 0, st>>>(ro);
+            PfAttn at{ S.qkv, ldq, S.qq, S.qd, L.kc, L.vc, L.kd, L.vd, S.ao,
+                       p0, c.head_dim, c.n_heads, c.n_kv_heads, c.q_dim, c.kv_dim, L.window, (int)(npos),
+                       c.attn_scale, c.attn_softcap };
+            const dim3 ag((unsigned)T, (unsigned)c.n_kv_heads);
+            if (r.kv_type == KC_F32) pf_attn_kernel<KC_F32><<<ag, PA_THREADS, asmem, st>>>(at);
+            else if (r.kv_type == KC_F16) pf_attn_kernel<KC_F16><<<ag, PA_THREADS, asmem, st>>>(at);
+            else pf_attn_kernel<KC_Q8_0><<<ag, PA_THREADS, asmem, st>>>(at);
+            launch_quant(S, S.ao, c.q_dim, nullptr, 0.0f, PQ_PLAIN, c.act, c.q_dim, T, st);
+            launch_gemm(W.wo, S, T, S.x, c.dim, PF_RESID, 0.0f, r.err, st);
+            launch_quant(S, S.x, c.dim, L.ffn_norm, c.norm_eps, PQ_NORM, c.act, c.dim, T, st);
+            launch_gemm(W.w13, S, T, S.gu, 2 * c.hidden_dim, PF_STORE, 0.0f, r.err, st);
+            launch_quant(S, S.gu, 2 * c.hidden_dim, nullptr, 0.0f, PQ_GATED, c.act, c.hidden_dim, T, st);
+            launch_gemm(W.w2, S, T, S.x, c.dim, PF_RESID, 0.0f, r.err, st);
+        }
+        (void)group;
+        PCK(cudaGetLastError(), "prefill launch");
+        if (logits) {
+            launch_quant(S, S.x, c.dim, r.final_norm, c.norm_eps, PQ_NORM, c.act, c.dim, T, st);
+            for (int s0 = 0; s0 < T; s0 += r.logits_rows) {
+                const int k = std::min(r.logits_rows, T - s0);
+                launch_gemm(P.cls, S, k, r.logits_dev, c.vocab, PF_STORE, c.final_softcap, r.err, st, s0);
+                PCK(cudaGetLastError(), "classifier launch");
+                PCK(cudaMemcpyAsync(logits + (size_t)(i0 + s0) * c.vocab, r.logits_dev, sizeof(float) * (size_t)k * c.vocab,
+                                    cudaMemcpyDeviceToHost, st),
+                    "logits copy");
+            }
+        }
+    }
+    unsigned err = 0;
+    PCK(cudaMemcpyAsync(&err, r.err, sizeof err, cudaMemcpyDeviceToHost, st), "error word");
+    PCK(cudaStreamSynchronize(st), "prefill");
+    if (err) {
+        set_error("prefill: a pipeline wait gave up (error word " + std::to_string(err) + ")");
+        return KC_E_IO;
+    }
+    return KC_OK;
+}
+
+}  // namespace kc
+
+using namespace kc;
+
+/* ml_matmul (ops/ops.c:51-79) on device buffers: y[t * rows + r] = W x_t for n
+ * quantized activation rows, through the prefill's packed weights and tensor-core
+ * GEMM (weights repacked per call into temporary device memory). */
+extern "C" int kc_matmul_dev(float *y, int type, int d_f16, const void *wq, const void *wd, int rows, int cols,
+                             const int8_t *xq, const float *xd, int n, void *stream) {
+    clear_error();
+    if (rows <= 0 || cols <= 0 || n <= 0 || cols % QK || (type != KC_Q8_0 && type != KC_Q4_0)) return KC_E_SHAPE;
+    cudaStream_t st = (cudaStream_t)stream;
+    PfModel P;
+    PfMat W;
+    int rc = alloc_mat(P, W, rows, cols, st);
+    if (rc != KC_OK) return rc;
+    const size_t items = (size_t)rows * (cols / QK);
+    pf_pack_kernel<<<(unsigned)((items + 255) / 256), 256, 0, st>>>((const uint8_t *)wq, wd, type == KC_Q4_0 ? T_Q4 : T_Q8,
+                                                                     d_f16, rows, cols, 0, W.nbk, W.q, W.d);
+    const int tpad = (n + PF_N - 1) / PF_N * PF_N;
+    PfScratch S;
+    void *buf = nullptr;
+    const size_t qb = up256((size_t)tpad * cols), db = sizeof(float) * (size_t)tpad * (cols / QK);
+    PCK(cudaMalloc(&buf, qb + db), "activation tiles");
+    S.base = buf;
+    S.xq = (int8_t *)buf;
+    S.xd = (float *)((uint8_t *)buf + qb);
+    const size_t aitems = (size_t)tpad * (cols / QK);
+    pf_pack_act_kernel<<<(unsigned)((aitems + 255) / 256), 256, 0, st>>>(xq, xd, n, cols, S.xq, S.xd);
+    unsigned *err = nullptr;
+    PCK(cudaMalloc(&err, sizeof(unsigned)), "error word");
+    rc = set_attributes(48 * 1024);
+    if (rc == KC_OK) {
+        cudaMemsetAsync(err, 0, sizeof(unsigned), st);
+        launch_gemm(W, S, n, y, rows, PF_STORE, 0.0f, err, st);
+        unsigned h = 0;
+        cudaMemcpyAsync(&h, err, sizeof h, cudaMemcpyDeviceToHost, st);
+        const cudaError_t e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) rc = cuda_err(e, "matmul");
+        else if (h) {
+            set_error("matmul: a pipeline wait gave up");
+            rc = KC_E_IO;
+        }
+    }
+    cudaFree(err);
+    return rc;
+}

@@ -1,0 +1,52 @@
+/* Batched prefill (kc_prefill.cu): what the runtime hands it. Host-only
+ * declarations, shared by kc_runtime.cu and kc_prefill.cu. */
+#ifndef KC_PREFILL_H
+#define KC_PREFILL_H
+#include <cuda_runtime.h>
+
+#include "kc_internal.h"
+
+namespace kc {
+
+/* Shared memory the batched attention may use for its score rows. */
+constexpr int PF_ATTN_SMEM_MAX = 200 * 1024;
+
+/* One layer as the batched path sees it: device norms, this state's cache
+ * rows of the layer, the RoPE tables it uses and its attention window. */
+struct PfLayerRun {
+    const float *attn_norm, *ffn_norm;
+    void *kc, *vc;
+    float *kd, *vd;
+    const float *rcos, *rsin;
+    int window;
+};
+
+struct PfRun {
+    kc_model *m;
+    int kv_type;
+    const PfLayerRun *layers;          /* [n_layers] */
+    const uint8_t *emb_q;              /* the device embedding table */
+    const void *emb_d;
+    int emb_type, emb_d16;             /* T_Q8 / T_Q4, f16 scales */
+    const float *final_norm;
+    float *logits_dev;                 /* [logits_rows][vocab] */
+    int logits_rows;
+    unsigned *err;                     /* device error word */
+    cudaStream_t st;
+    PfScratch **scratch;               /* owned by the state */
+    int batch;                         /* tokens per chunk */
+};
+
+/* True when the batched kernels take this model and a chunk reaching
+ * position last_pos. */
+bool pf_fits(const kc_config &c, int kv_type, int last_pos);
+/* Runs the n tokens at pos0.. (logits: host [n][vocab] or null); builds the
+ * packed weights on first use. */
+int pf_prefill(const PfRun &r, const int *tokens, int n, int pos0, float *logits);
+void pf_free_model(PfModel *p);
+void pf_free_scratch(PfScratch *p);
+size_t pf_model_bytes(const PfModel *p);
+
+}  // namespace kc
+
+#endif

@@ -16,6 +16,7 @@
 #include "kc_internal.h"
 #include "kc_kernels.cuh"
 #include "kc_step.cuh"
+#include "kc_prefill.h"
 
 namespace kc {
 static thread_local std::string g_err;
@@ -107,13 +108,14 @@ extern "C" int kc_model_from_host(kc_model **out, const kc_config *cfg, const kc
 }
 
 extern "C" const kc_config *kc_model_config(const kc_model *m) { return &m->cfg; }
-extern "C" size_t kc_model_device_bytes(const kc_model *m) { return m->dev_bytes; }
+extern "C" size_t kc_model_device_bytes(const kc_model *m) { return m->dev_bytes + pf_model_bytes(m->pf); }
 
 extern "C" void kc_model_free(kc_model *m) {
     if (!m) return;
     if (m->dev_base) cudaFree(m->dev_base);
     if (m->d_stream) cudaFree(m->d_stream);
     if (m->d_cta_base) cudaFree(m->d_cta_base);
+    pf_free_model(m->pf);
     if (m->map) munmap(m->map, m->map_size);
     delete m;
 }
@@ -324,6 +326,9 @@ struct kc_state {
     unsigned *timeline_n = nullptr;
     StepArgs sa{};
     int step_smem = 0;
+    /* prompt tokens per batched prefill step (ml_state.batch); 1: token by token */
+    int batch = KC_BATCH_MAX;
+    PfScratch *pfs = nullptr;
 };
 
 /* RoPE inverse frequency of pair i (model/transformer.c:16-38; the scaling
@@ -570,6 +575,7 @@ extern "C" void kc_state_free(kc_state *s) {
     if (s->h_logits) cudaFreeHost(s->h_logits);
     if (s->h_ls) cudaFreeHost(s->h_ls);
     if (s->d_plan) cudaFree(s->d_plan);
+    pf_free_scratch(s->pfs);
     if (s->st) cudaStreamDestroy(s->st);
     delete s;
 }
@@ -729,13 +735,10 @@ extern "C" float *kc_forward(kc_state *s, int token, int pos) {
     return s->h_logits;
 }
 
-extern "C" int kc_prefill(kc_state *s, const int *tokens, int n, int pos0, float *logits) {
-    clear_error();
+/* ml_prefill through the step kernel, one token per step: the logits of
+ * token-by-token decoding bit for bit (ml_state.batch == 1). */
+static int prefill_tokenwise(kc_state *s, const int *tokens, int n, int pos0, float *logits) {
     const kc_config &c = s->c;
-    if (n < 0 || pos0 < 0 || pos0 + n > c.max_seq) return KC_E_SHAPE;
-    for (int i = 0; i < n; i++)
-        if (tokens[i] < 0 || tokens[i] >= c.vocab) return KC_E_SHAPE;
-    if (n == 0) return KC_OK;
     CK(cudaMemcpyAsync(s->feed, tokens, sizeof(int) * n, cudaMemcpyHostToDevice, s->st));
     CK(cudaMemsetAsync(s->feed + n, 0, sizeof(int), s->st));
     int st = set_loop(s, tokens[0], pos0, 1);
@@ -749,6 +752,67 @@ extern "C" int kc_prefill(kc_state *s, const int *tokens, int n, int pos0, float
                                cudaMemcpyDeviceToHost, s->st));
     }
     return finish(s);
+}
+
+/* ml_prefill in chunks of up to s->batch tokens through the batched path
+ * (tensor-core GEMMs, kc_prefill.cu). */
+static int prefill_batched(kc_state *s, const int *tokens, int n, int pos0, float *logits) {
+    const kc_config &c = s->c;
+    kc_model *m = s->m;
+    std::vector<PfLayerRun> L((size_t)c.n_layers);
+    const size_t lkv = (size_t)c.max_seq * c.kv_dim * kv_elem_bytes(s->kv_type);
+    const size_t lkd = (size_t)c.max_seq * c.n_kv_heads;
+    for (int l = 0; l < c.n_layers; l++) {
+        const DevLayer &D = m->d_layers[(size_t)l];
+        PfLayerRun &P = L[(size_t)l];
+        P.attn_norm = D.attn_norm;
+        P.ffn_norm = D.ffn_norm;
+        P.kc = s->kc + (size_t)l * lkv;
+        P.vc = s->vc + (size_t)l * lkv;
+        P.kd = s->kd ? s->kd + (size_t)l * lkd : nullptr;
+        P.vd = s->vd ? s->vd + (size_t)l * lkd : nullptr;
+        P.rcos = D.local_rope ? s->lcos : s->rcos;
+        P.rsin = D.local_rope ? s->lsin : s->rsin;
+        P.window = D.window;
+    }
+    PfRun r;
+    r.m = m;
+    r.kv_type = s->kv_type;
+    r.layers = L.data();
+    r.emb_q = m->d_tok_emb.q;
+    r.emb_d = m->d_tok_emb.d;
+    r.emb_type = m->d_tok_emb.type;
+    r.emb_d16 = m->d_tok_emb.d16;
+    r.final_norm = m->d_final_norm;
+    r.logits_dev = s->logits;
+    r.logits_rows = LOGITS_RING;
+    r.err = s->err + 1;
+    r.st = s->st;
+    r.scratch = &s->pfs;
+    r.batch = s->batch;
+    return pf_prefill(r, tokens, n, pos0, logits);
+}
+
+extern "C" int kc_prefill(kc_state *s, const int *tokens, int n, int pos0, float *logits) {
+    clear_error();
+    const kc_config &c = s->c;
+    if (n < 0 || pos0 < 0 || pos0 + n > c.max_seq) return KC_E_SHAPE;
+    for (int i = 0; i < n; i++)
+        if (tokens[i] < 0 || tokens[i] >= c.vocab) return KC_E_SHAPE;
+    if (n == 0) return KC_OK;
+    if (s->batch > 1 && n > 1 && pf_fits(c, s->kv_type, pos0 + n - 1))
+        return prefill_batched(s, tokens, n, pos0, logits);
+    return prefill_tokenwise(s, tokens, n, pos0, logits);
+}
+
+extern "C" int kc_set_batch(kc_state *s, int batch) {
+    clear_error();
+    if (batch < 1 || batch > KC_BATCH_MAX) {
+        set_error("batch must be 1.." + std::to_string(KC_BATCH_MAX));
+        return KC_E_SHAPE;
+    }
+    s->batch = batch;
+    return KC_OK;
 }
 
 extern "C" int kc_generate_greedy(kc_state *s, int token, int pos, int n, int *out_tokens) {

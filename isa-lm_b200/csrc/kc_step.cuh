@@ -940,27 +940,6 @@ __device__ __forceinline__ AttSmem att_smem(float *f, int group, int hd) {
     return s;
 }
 
-/* The reference's single-scale row quantization (ops/ops.c:81-96) of the n
- * values x[0, n) by one warp (lane i takes elements i, i+32, ...): the quants
- * into out, and as floats into back when given; returns the scale. */
-__device__ __forceinline__ float warp_quantize_row(const float *x, int n, int8_t *out, float *back, int lane) {
-    float amax = 0.0f;
-    for (int i = lane; i < n; i += 32) amax = fmaxf(amax, fabsf(x[i]));
-    amax = warp_max(amax);
-    const bool tiny = amax < 1e-30f;
-    const float id = tiny ? 0.0f : __fdiv_rn(127.0f, amax);
-    for (int i = lane; i < n; i += 32) {
-        int qi = 0;
-        if (!tiny) {
-            const float t = truncf(__fadd_rn(__fmul_rn(x[i], id), copysignf(0.5f, x[i])));
-            qi = (int)fminf(fmaxf(t, -127.0f), 127.0f);
-        }
-        out[i] = (int8_t)qi;
-        if (back) back[i] = (float)qi;
-    }
-    return tiny ? 0.0f : __fdiv_rn(amax, 127.0f);
-}
-
 /* Attention work item (KV head g, split y) of layer L at position pos, on the
  * consumer threads; fsm: shared scratch. ops/ops.c:124-180 with the cache
  * types of model/transformer.c:188-205 (KV: KC_F32, KC_F16 or KC_Q8_0):

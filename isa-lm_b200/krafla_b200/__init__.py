@@ -6,6 +6,7 @@ The reference's C API (model/mlb.h, model/transformer.h) maps one to one:
     ml_model_pack  -> Model.upload()              kc_model_upload (HBM, once)
     ml_state_init  -> State(model, nthreads, kv)  kc_state_init
     ml_prefill     -> State.prefill(...)          kc_prefill
+    ml_state.batch -> State.set_batch(b)          kc_set_batch
     ml_forward     -> State.forward(token, pos)   kc_forward
     ml_state_free  -> State.free()                kc_state_free
 
@@ -75,6 +76,7 @@ def lib():
             "kc_model_config": (C.POINTER(_Config), [P]), "kc_model_device_bytes": (S, [P]),
             "kc_model_free": (None, [P]),
             "kc_state_init": (I, [C.POINTER(P), P, I, I]), "kc_prefill": (I, [P, P, I, I, P]),
+            "kc_set_batch": (I, [P, I]),
             "kc_forward": (C.POINTER(F), [P, I, I]), "kc_generate_greedy": (I, [P, I, I, I, P]),
             "kc_state_free": (None, [P]),
             "kc_time_decode": (I, [P, I, I, I, I, C.POINTER(F)]),
@@ -83,7 +85,8 @@ def lib():
             "kc_step_events": (I, [P, I, I, P, C.c_uint, C.POINTER(I)]),
             "kc_quantize_q8_dev": (I, [P, P, P, I, P]), "kc_rmsnorm_quantize_dev": (I, [P, P, P, P, P, I, F, P]),
             "kc_matvec_dev": (I, [P, I, I, P, P, I, I, P, P, P]),
-            "kc_matvec_f32_noalloc": (I, [P, I, I, P, P, I, I, P, P]), "kc_block_sums_dev": (I, [P, I, P, I, I, P, P]),
+            "kc_matvec_f32_noalloc": (I, [P, I, I, P, P, I, I, P, P]),
+            "kc_matmul_dev": (I, [P, I, I, P, P, I, I, P, P, I, P]), "kc_block_sums_dev": (I, [P, I, P, I, I, P, P]),
             "kc_dev_alloc": (P, [S]), "kc_dev_free": (None, [P]), "kc_memcpy_htod": (I, [P, P, S]),
             "kc_memcpy_dtoh": (I, [P, P, S]), "kc_dev_sync": (I, []),
         }
@@ -164,6 +167,11 @@ class State:
                               out.ctypes.data_as(C.c_void_p) if logits else None)
         _check(st, "prefill")
         return out
+
+    def set_batch(self, batch):
+        """ml_state.batch: prompt tokens per batched prefill step (1 = token by token)."""
+        _check(lib().kc_set_batch(self._h, int(batch)), "set batch")
+        return self
 
     def generate_greedy(self, token, pos, n):
         """n greedy tokens from token at pos, the loop kept on the device."""
@@ -278,6 +286,19 @@ def matvec(wtype, wq, wd, rows, cols, xq, xd):
     _check(lib().kc_matvec_dev(by.ptr, wtype, d16, bw.ptr, bd.ptr, rows, cols, bxq.ptr, bxd.ptr, None), "matvec")
     _check(lib().kc_dev_sync(), "sync")
     return by.get(np.float32, rows)
+
+
+def matmul(wtype, wq, wd, rows, cols, xq, xd):
+    """ml_matmul on the device for n quantized rows xq [n, cols], xd [n, cols/32]: y [n, rows]."""
+    wd = np.ascontiguousarray(wd)
+    d16 = int(wd.dtype == np.float16)
+    xq = np.ascontiguousarray(xq, np.int8)
+    n = xq.shape[0]
+    bw, bd = DevBuf.of(wq), DevBuf.of(wd, pad=16)
+    bxq, bxd, by = DevBuf.of(xq), DevBuf.of(np.ascontiguousarray(xd, np.float32)), DevBuf(4 * rows * n)
+    _check(lib().kc_matmul_dev(by.ptr, wtype, d16, bw.ptr, bd.ptr, rows, cols, bxq.ptr, bxd.ptr, n, None), "matmul")
+    _check(lib().kc_dev_sync(), "sync")
+    return by.get(np.float32, rows * n).reshape(n, rows)
 
 
 def block_sums(wtype, wq, rows, cols, xq):

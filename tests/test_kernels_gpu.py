@@ -129,3 +129,45 @@ def test_matvec_scaled(wtype, rows, cols, f16):
     sc = term_scale(wtype, wq, wd, rows, cols, xq, xd)
     tol = 1e-5 * np.maximum(sc, np.maximum(np.abs(y), np.abs(ref)))
     assert (np.abs(y.astype(np.float64) - ref) <= tol).all()
+
+
+MM_SHAPES = [(1, 32, 1), (7, 288, 5), (64, 896, 33), (333, 2048, 70), (2048, 8192, 40), (130, 14336, 3)]
+
+
+@pytest.mark.parametrize("wtype", [kb.Q8_0, kb.Q4_0])
+@pytest.mark.parametrize("rows,cols,n", MM_SHAPES)
+def test_matmul_unit_scales_exact(wtype, rows, cols, n):
+    # ml_matmul (ops/ops.c:51-79) on the int8 tensor cores: every block dot is an
+    # exact int32, so with unit scales each row sum is exact below 2^24
+    if wtype == kb.Q8_0 and cols * 127 * 127 >= 1 << 24:
+        pytest.skip("float partial sums could round")
+    rng = np.random.default_rng(rows * 7 + cols + n)
+    wq, wd = make_w(rng, wtype, rows, cols, unit=True)
+    xq = rng.integers(-127, 128, (n, cols)).astype(np.int8)
+    xd = np.ones((n, cols // 32), np.float32)
+    y = kb.matmul(wtype, wq, wd, rows, cols, xq, xd)
+    for t in range(n):
+        exact = oracle.block_sums(wtype, wq, rows, cols, xq[t]).astype(np.int64).sum(1)
+        assert np.array_equal(y[t], exact.astype(np.float32)), t
+
+
+@pytest.mark.parametrize("f16", [False, True])
+@pytest.mark.parametrize("wtype", [kb.Q8_0, kb.Q4_0])
+@pytest.mark.parametrize("rows,cols,n", MM_SHAPES)
+def test_matmul_scaled(wtype, rows, cols, n, f16):
+    # per token the reference's matvec within TT_CLOSE (1e-5 of the sum of |terms|)
+    rng = np.random.default_rng(5 * rows + cols + n + f16)
+    wq, wd = make_w(rng, wtype, rows, cols, f16=f16)
+    xq = rng.integers(-127, 128, (n, cols)).astype(np.int8)
+    xd = rng.uniform(0.001, 0.05, (n, cols // 32)).astype(np.float32)
+    y = kb.matmul(wtype, wq, wd, rows, cols, xq, xd)
+    for t in range(n):
+        ref = oracle.matvec(wtype, wq, wd.astype(np.float32), rows, cols, xq[t], xd[t])
+        sc = term_scale(wtype, wq, wd, rows, cols, xq[t], xd[t])
+        tol = 1e-5 * np.maximum(sc, np.maximum(np.abs(y[t]), np.abs(ref)))
+        assert (np.abs(y[t].astype(np.float64) - ref) <= tol).all(), t
+
+
+def test_matmul_rejects_bad_shapes():
+    assert kb.lib().kc_matmul_dev(None, kb.Q8_0, 0, None, None, 4, 33, None, None, 1, None) == kb.E_SHAPE
+    assert kb.lib().kc_matmul_dev(None, kb.Q8_0, 0, None, None, 4, 32, None, None, 0, None) == kb.E_SHAPE
