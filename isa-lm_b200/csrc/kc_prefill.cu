@@ -36,18 +36,21 @@ namespace kc {
 constexpr int PF_M = 128;                              /* weight rows per tile: the TMEM lanes */
 constexpr int PF_N = 32;                               /* tokens per tile: TMEM columns per buffer */
 constexpr int PF_KB = 4;                               /* K blocks per pipeline stage */
-constexpr int PF_NST = 5;                              /* pipeline stages */
+constexpr int PF_NST = 4;                              /* pipeline stages */
 constexpr int PF_NBUF = 8;                             /* TMEM accumulator buffers */
 constexpr int PF_EPI_WARPS = 8;                        /* two per TMEM lane quarter */
 constexpr int PF_THREADS = 32 * (2 + PF_EPI_WARPS);
 constexpr int PF_COLS = PF_N * 4 / PF_EPI_WARPS;       /* token columns per epilogue warp */
 constexpr int PF_A_BLK = PF_M * QK;                    /* bytes of one K block of a weight tile */
 constexpr int PF_B_BLK = PF_N * QK;                    /* bytes of one K block of a token tile */
-constexpr int PF_STAGE = PF_KB * (PF_A_BLK + PF_B_BLK);
+constexpr int PF_DW_BLK = PF_M * 4;                    /* weight scales of one K block (float) */
+constexpr int PF_DX_BLK = PF_N * 4;                    /* token scales of one K block (float) */
+constexpr int PF_STAGE = PF_KB * (PF_A_BLK + PF_B_BLK + PF_DW_BLK + PF_DX_BLK);
 constexpr int PF_TMEM_COLS = PF_NBUF * PF_N;
 constexpr int PF_SMEM = 1024 + PF_NST * PF_STAGE + 256;
 static_assert(PF_TMEM_COLS >= 32 && (PF_TMEM_COLS & (PF_TMEM_COLS - 1)) == 0, "TMEM columns: a power of two");
 static_assert(PF_COLS == 16, "the epilogue loads 16 TMEM columns at a time");
+static_assert(PF_STAGE % 256 == 0, "stage alignment");
 static_assert((2 * PF_NST + 2 * PF_NBUF) * 8 + 4 <= 256, "barrier room");
 
 /* Byte (r, k) of one K block (rows x 32 bytes) in the MMA's K-major layout
@@ -120,7 +123,11 @@ struct PfGemm {
 
 /* Y[t][row] = sum_b s(row, t, b) * (d_w[row][b] * d_x[t][b]) over one
  * 128-row x 32-token tile (blockIdx.y, blockIdx.x): stored, or added to out
- * (residual), with the row's bias and the logit soft-cap when given. */
+ * (residual), with the row's bias and the logit soft-cap when given.
+ * A pipeline stage holds PF_KB K blocks: weight quants, token quants, weight
+ * scales, token scales, each one bulk copy. The stage is released when its
+ * MMAs have completed (tcgen05.commit) and every epilogue warp has read its
+ * scales; a TMEM buffer when every epilogue warp has loaded it. */
 __global__ void __launch_bounds__(PF_THREADS, 2) pf_gemm_kernel(const __grid_constant__ PfGemm g) {
     extern __shared__ unsigned char pf_smem_raw[];
     unsigned char *sm = (unsigned char *)(((uintptr_t)pf_smem_raw + 1023) & ~(uintptr_t)1023);
@@ -129,10 +136,11 @@ __global__ void __launch_bounds__(PF_THREADS, 2) pf_gemm_kernel(const __grid_con
     uint32_t *tslot = (uint32_t *)(tempty + PF_NBUF);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n = blockIdx.x, m = blockIdx.y, nbk = g.nbk;
+    constexpr int OFF_B = PF_KB * PF_A_BLK, OFF_DW = OFF_B + PF_KB * PF_B_BLK, OFF_DX = OFF_DW + PF_KB * PF_DW_BLK;
     if (threadIdx.x == 0) {
         for (int i = 0; i < PF_NST; i++) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 1);
+            mbar_init(&empty[i], 1 + PF_EPI_WARPS);
         }
         for (int i = 0; i < PF_NBUF; i++) {
             mbar_init(&tfull[i], 1);
@@ -158,10 +166,13 @@ __global__ void __launch_bounds__(PF_THREADS, 2) pf_gemm_kernel(const __grid_con
                     break;
                 }
                 const int kbs = min(PF_KB, nbk - st * PF_KB);
-                unsigned char *a = sm + s * PF_STAGE, *b = a + PF_KB * PF_A_BLK;
-                mbar_expect_tx(&full[s], (unsigned)(kbs * (PF_A_BLK + PF_B_BLK)));
-                bulk_g2s(a, g.wq + ((size_t)m * nbk + (size_t)st * PF_KB) * PF_A_BLK, kbs * PF_A_BLK, &full[s]);
-                bulk_g2s(b, g.xq + ((size_t)n * nbk + (size_t)st * PF_KB) * PF_B_BLK, kbs * PF_B_BLK, &full[s]);
+                const size_t wb = (size_t)m * nbk + (size_t)st * PF_KB, xb = (size_t)n * nbk + (size_t)st * PF_KB;
+                unsigned char *stage = sm + s * PF_STAGE;
+                mbar_expect_tx(&full[s], (unsigned)(kbs * (PF_A_BLK + PF_B_BLK + PF_DW_BLK + PF_DX_BLK)));
+                bulk_g2s(stage, g.wq + wb * PF_A_BLK, kbs * PF_A_BLK, &full[s]);
+                bulk_g2s(stage + OFF_B, g.xq + xb * PF_B_BLK, kbs * PF_B_BLK, &full[s]);
+                bulk_g2s(stage + OFF_DW, g.wd + wb * PF_M, kbs * PF_DW_BLK, &full[s]);
+                bulk_g2s(stage + OFF_DX, g.xd + xb * PF_N, kbs * PF_DX_BLK, &full[s]);
             }
         }
     } else if (warp == 1) {
@@ -178,7 +189,7 @@ __global__ void __launch_bounds__(PF_THREADS, 2) pf_gemm_kernel(const __grid_con
                 }
                 tc_fence_after();
                 const uint32_t a = smem_u32(sm + s * PF_STAGE) + j * PF_A_BLK;
-                const uint32_t b = smem_u32(sm + s * PF_STAGE + PF_KB * PF_A_BLK) + j * PF_B_BLK;
+                const uint32_t b = smem_u32(sm + s * PF_STAGE + OFF_B) + j * PF_B_BLK;
                 tc_mma_i8(tmem + (uint32_t)(buf * PF_N), umma_desc(a), umma_desc(b), PF_IDESC, 0u);
                 tc_commit(&tfull[buf]);
                 if (j == PF_KB - 1 || kb == nbk - 1) tc_commit(&empty[s]);
@@ -186,44 +197,66 @@ __global__ void __launch_bounds__(PF_THREADS, 2) pf_gemm_kernel(const __grid_con
         }
     } else {
         /* epilogue: TMEM lane quarter q (the warp's rank in its warpgroup),
-         * token columns c0 .. c0+15 of the tile */
+         * token columns c0 .. c0+15 of the tile; the TMEM load of K block
+         * kb + 1 is in flight while K block kb is accumulated */
         const int e = warp - 2, q = warp & 3, c0 = (e >> 2) * PF_COLS;
         const int row = m * PF_M + q * 32 + lane;
         const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
-        const float *wd = g.wd + (size_t)m * nbk * PF_M + q * 32 + lane;
-        const float *xd = g.xd + (size_t)n * nbk * PF_N + c0;
         float acc[PF_COLS];
 #pragma unroll
         for (int c = 0; c < PF_COLS; c++) acc[c] = 0.0f;
-        bool ok = true;
-        for (int kb = 0; kb < nbk; kb++) {
-            const int buf = kb % PF_NBUF;
-            const float dw = __ldg(wd + (size_t)kb * PF_M);
-            float dx[PF_COLS];
-#pragma unroll
-            for (int i = 0; i < PF_COLS / 4; i++) {
-                const float4 v = __ldg((const float4 *)(xd + (size_t)kb * PF_N) + i);
-                dx[4 * i] = v.x;
-                dx[4 * i + 1] = v.y;
-                dx[4 * i + 2] = v.z;
-                dx[4 * i + 3] = v.w;
-            }
-            const bool w = mbar_wait(&tfull[buf], (kb / PF_NBUF) & 1, g.err);
-            if (!__all_sync(0xffffffffu, w)) {
-                ok = false;
-                break;
-            }
+        uint32_t cur[PF_COLS], nxt[PF_COLS];
+        bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[0], 0, g.err));
+        if (ok) {
             tc_fence_after();
-            uint32_t s[PF_COLS];
-            tc_ld16(tq + (uint32_t)(buf * PF_N), s);
+            tc_ld16(tq, cur);
             tc_wait_ld();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[buf]);
+            if (lane == 0) mbar_arrive(&tempty[0]);
+        }
+        for (int kb = 0; ok && kb < nbk; kb++) {
+            const int st = kb / PF_KB, j = kb - st * PF_KB, s = st % PF_NST;
+            if (j == 0 && !__all_sync(0xffffffffu, mbar_wait(&full[s], (st / PF_NST) & 1, g.err))) {
+                ok = false;
+                break;
+            }
+            const bool more = kb + 1 < nbk;
+            const int nbuf = (kb + 1) % PF_NBUF;
+            if (more) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&tfull[nbuf], ((kb + 1) / PF_NBUF) & 1, g.err))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                tc_ld16(tq + (uint32_t)(nbuf * PF_N), nxt);
+            }
+            const unsigned char *stage = sm + s * PF_STAGE;
+            const float dw = ((const float *)(stage + OFF_DW))[j * PF_M + q * 32 + lane];
+            const float4 *dx4 = (const float4 *)(stage + OFF_DX + j * PF_DX_BLK) + c0 / 4;
 #pragma unroll
-            for (int c = 0; c < PF_COLS; c++) acc[c] = __fmaf_rn((float)(int)s[c], __fmul_rn(dw, dx[c]), acc[c]);
+            for (int i = 0; i < PF_COLS / 4; i++) {
+                const float4 v = dx4[i];
+                acc[4 * i] = __fmaf_rn((float)(int)cur[4 * i], __fmul_rn(dw, v.x), acc[4 * i]);
+                acc[4 * i + 1] = __fmaf_rn((float)(int)cur[4 * i + 1], __fmul_rn(dw, v.y), acc[4 * i + 1]);
+                acc[4 * i + 2] = __fmaf_rn((float)(int)cur[4 * i + 2], __fmul_rn(dw, v.z), acc[4 * i + 2]);
+                acc[4 * i + 3] = __fmaf_rn((float)(int)cur[4 * i + 3], __fmul_rn(dw, v.w), acc[4 * i + 3]);
+            }
+            if (j == PF_KB - 1 || !more) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+            }
+            if (more) {
+                tc_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[nbuf]);
+#pragma unroll
+                for (int c = 0; c < PF_COLS; c++) cur[c] = nxt[c];
+            }
         }
         if (!ok) {
+            tc_wait_ld();
             if (lane == 0) atomicOr(g.err, PF_ERR_WAIT);
         } else if (row < g.rows) {
             const float bias = g.bias ? g.bias[row] : 0.0f;
@@ -406,7 +439,8 @@ __global__ void __launch_bounds__(256) pf_rope_kernel(const PfRope a) {
 
 /* ------------------------------------------------------------ attention */
 
-constexpr int PA_THREADS = 128;
+constexpr int PA_THREADS = 256;
+constexpr int PA_TILE = 64;                          /* cache positions per shared-memory tile */
 constexpr int PA_MAXG = 16;                          /* query heads per KV head */
 constexpr int PA_MAXO = ATT_MAX_OUT / PA_THREADS;    /* outputs per thread */
 
@@ -421,6 +455,18 @@ struct PfAttn {
     int pos0, hd, n_heads, n_kv, q_dim, kv_dim, window, npos;
     float scale, softcap;
 };
+
+/* Shared memory of pf_attn_kernel: query heads, the score rows (npos per
+ * head, a multiple of 4), two cache tiles of PA_TILE rows at a pitch of the
+ * row's bytes + 16 (16-byte reads of different rows hit different banks),
+ * and the Q8 row scales of the two tiles. */
+__host__ __device__ inline int pa_pitch(int hd, int es) { return hd * es + 16; }
+__host__ __device__ inline size_t pa_smem_bytes(int group, int hd, int es, int npos) {
+    return sizeof(float) * ((size_t)group * hd + (size_t)group * npos) + 2 * (size_t)PA_TILE * pa_pitch(hd, es) +
+           sizeof(float) * 2 * PA_TILE;
+}
+
+__device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 __device__ __forceinline__ float block_reduce(float v, float *red, bool is_max) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -438,78 +484,94 @@ __device__ __forceinline__ float block_reduce(float v, float *red, bool is_max) 
  * dimension in order (Q8 cache: int32 dot of the quantized query and row,
  * (float)s * (qd * scale) * kd), the optional soft-cap, softmax (all -inf:
  * uniform, k_scalar.c:66-77), then out = sum_t p_t * V_t in position order
- * (Q8: (p_t * vd_t) * v). Scores live in shared memory, npos per head. */
+ * (Q8: (p_t * vd_t) * v). The cache is read in tiles of PA_TILE positions
+ * staged through shared memory (cp.async, one tile ahead); the scores of
+ * every position stay in shared memory between the passes. */
 template <int KV>
 __global__ void __launch_bounds__(PA_THREADS) pf_attn_kernel(const PfAttn a) {
-    extern __shared__ float pa_smem[];
+    extern __shared__ __align__(16) unsigned char pa_raw[];
     constexpr int ES = KV == KC_F32 ? 4 : (KV == KC_F16 ? 2 : 1);
     const int t = blockIdx.x, g = blockIdx.y, tid = threadIdx.x;
     const int group = a.n_heads / a.n_kv, hd = a.hd, p = a.pos0 + t;
     const int first = a.window && p >= a.window ? p + 1 - a.window : 0, n = p + 1 - first;
-    float *sq = pa_smem;                        /* [group][hd] query heads (Q8: as int8 words) */
-    float *sc = sq + group * hd;                /* [group][npos] */
+    const int rowb = hd * ES, pitch = rowb + 16, upr = rowb / 16;
+    float *sq = (float *)pa_raw;                                   /* [group][hd] (Q8: int8 quants) */
+    float *sc = sq + group * hd;                                   /* [group][npos] */
+    unsigned char *tiles = (unsigned char *)(sc + (size_t)group * a.npos);
+    float *srd = (float *)(tiles + 2 * PA_TILE * pitch);           /* [2][PA_TILE] Q8 row scales */
     __shared__ float red[PA_THREADS / 32];
     __shared__ float cq[PA_MAXG];
-    const float *qsrc = a.qkv + (size_t)t * a.ldq + (size_t)g * group * hd;
     if constexpr (KV == KC_Q8_0) {
         const int8_t *qq = a.qq + (size_t)t * a.q_dim + (size_t)g * group * hd;
         for (int i = tid; i < group * hd / 4; i += PA_THREADS) ((int *)sq)[i] = ((const int *)qq)[i];
         if (tid < group) cq[tid] = __fmul_rn(a.qd[(size_t)t * a.n_heads + g * group + tid], a.scale);
     } else {
+        const float *qsrc = a.qkv + (size_t)t * a.ldq + (size_t)g * group * hd;
         for (int i = tid; i < group * hd; i += PA_THREADS) sq[i] = qsrc[i];
     }
-    __syncthreads();
-    const size_t rowb = (size_t)a.kv_dim * ES;
-    const uint8_t *kb = (const uint8_t *)a.kc + (size_t)g * hd * ES, *vb = (const uint8_t *)a.vc + (size_t)g * hd * ES;
-    for (int i = tid; i < n; i += PA_THREADS) {
-        const int j = first + i;
-        const uint8_t *kr = kb + (size_t)j * rowb;
-        float acc[PA_MAXG];
-        int isum[PA_MAXG];
-#pragma unroll
-        for (int h = 0; h < PA_MAXG; h++) {
-            acc[h] = 0.0f;
-            isum[h] = 0;
+    const size_t ld = (size_t)a.kv_dim * ES;
+    const uint8_t *kbase = (const uint8_t *)a.kc + (size_t)g * rowb, *vbase = (const uint8_t *)a.vc + (size_t)g * rowb;
+    const int ntiles = (n + PA_TILE - 1) / PA_TILE;
+    auto load_tile = [&](const uint8_t *base, const float *rd, int k) {
+        const int t0 = k * PA_TILE, nt = min(PA_TILE, n - t0);
+        unsigned char *dst = tiles + (k & 1) * PA_TILE * pitch;
+        for (int u = tid; u < nt * upr; u += PA_THREADS) {
+            const int r = u / upr, c = u - r * upr;
+            cp_async16(dst + r * pitch + 16 * c, base + (size_t)(first + t0 + r) * ld + 16 * c);
         }
-        for (int d0 = 0; d0 < hd; d0 += 4) {
-            if constexpr (KV == KC_Q8_0) {
-                const int kw = *(const int *)(kr + d0);
-#pragma unroll
-                for (int h = 0; h < PA_MAXG; h++)
-                    if (h < group) isum[h] = __dp4a(((const int *)sq)[(h * hd + d0) >> 2], kw, isum[h]);
-            } else {
-                float k4[4];
-                if constexpr (KV == KC_F32) {
-                    const float4 v = *(const float4 *)(kr + 4 * d0);
-                    k4[0] = v.x; k4[1] = v.y; k4[2] = v.z; k4[3] = v.w;
+        cp_async_commit();
+        if (KV == KC_Q8_0 && tid < nt) srd[(k & 1) * PA_TILE + tid] = rd[(size_t)(first + t0 + tid) * a.n_kv + g];
+    };
+    /* scores: thread -> tile position tid % PA_TILE, heads tid / PA_TILE + 4k */
+    load_tile(kbase, a.kd, 0);
+    for (int k = 0; k < ntiles; k++) {
+        if (k + 1 < ntiles) {
+            load_tile(kbase, a.kd, k + 1);
+            cp_async_wait_one();
+        } else {
+            cp_async_wait_all();
+        }
+        __syncthreads();
+        const int i = tid & (PA_TILE - 1), nt = min(PA_TILE, n - k * PA_TILE);
+        const unsigned char *row = tiles + (k & 1) * PA_TILE * pitch + i * pitch;
+        if (i < nt) {
+            for (int h = tid / PA_TILE; h < group; h += PA_THREADS / PA_TILE) {
+                float s;
+                if constexpr (KV == KC_Q8_0) {
+                    int isum = 0;
+                    for (int w = 0; w < hd / 4; w++) isum = __dp4a(((const int *)sq)[h * hd / 4 + w], ((const int *)row)[w], isum);
+                    s = __fmul_rn(__fmul_rn((float)isum, cq[h]), srd[(k & 1) * PA_TILE + i]);
                 } else {
-                    const uint2 u = *(const uint2 *)(kr + 2 * d0);
-                    const float2 lo = __half22float2(*(const __half2 *)&u.x), hi = __half22float2(*(const __half2 *)&u.y);
-                    k4[0] = lo.x; k4[1] = lo.y; k4[2] = hi.x; k4[3] = hi.y;
-                }
-#pragma unroll
-                for (int h = 0; h < PA_MAXG; h++)
-                    if (h < group) {
-                        const float4 q4 = *(const float4 *)(sq + h * hd + d0);
-                        acc[h] = __fadd_rn(acc[h], __fmul_rn(q4.x, k4[0]));
-                        acc[h] = __fadd_rn(acc[h], __fmul_rn(q4.y, k4[1]));
-                        acc[h] = __fadd_rn(acc[h], __fmul_rn(q4.z, k4[2]));
-                        acc[h] = __fadd_rn(acc[h], __fmul_rn(q4.w, k4[3]));
+                    float acc = 0.0f;
+                    const float *qh = sq + h * hd;
+                    for (int d0 = 0; d0 < hd; d0 += 4) {
+                        float k4[4];
+                        if constexpr (KV == KC_F32) {
+                            const float4 v = *(const float4 *)(row + 4 * d0);
+                            k4[0] = v.x; k4[1] = v.y; k4[2] = v.z; k4[3] = v.w;
+                        } else {
+                            const uint2 u = *(const uint2 *)(row + 2 * d0);
+                            const float2 lo = __half22float2(*(const __half2 *)&u.x), hi = __half22float2(*(const __half2 *)&u.y);
+                            k4[0] = lo.x; k4[1] = lo.y; k4[2] = hi.x; k4[3] = hi.y;
+                        }
+                        const float4 q4 = *(const float4 *)(qh + d0);
+                        acc = __fadd_rn(acc, __fmul_rn(q4.x, k4[0]));
+                        acc = __fadd_rn(acc, __fmul_rn(q4.y, k4[1]));
+                        acc = __fadd_rn(acc, __fmul_rn(q4.z, k4[2]));
+                        acc = __fadd_rn(acc, __fmul_rn(q4.w, k4[3]));
                     }
+                    s = __fmul_rn(acc, a.scale);
+                }
+                if (a.softcap > 0.0f) s = __fmul_rn(a.softcap, tanhf(__fdiv_rn(s, a.softcap)));
+                sc[(size_t)h * a.npos + k * PA_TILE + i] = s;
             }
         }
-        const float kd = KV == KC_Q8_0 ? a.kd[(size_t)j * a.n_kv + g] : 0.0f;
-#pragma unroll
-        for (int h = 0; h < PA_MAXG; h++)
-            if (h < group) {
-                float s = KV == KC_Q8_0 ? __fmul_rn(__fmul_rn((float)isum[h], cq[h]), kd) : __fmul_rn(acc[h], a.scale);
-                if (a.softcap > 0.0f) s = __fmul_rn(a.softcap, tanhf(__fdiv_rn(s, a.softcap)));
-                sc[h * a.npos + i] = s;
-            }
+        __syncthreads();
     }
-    __syncthreads();
+    /* V tile 0 streams in while the softmax runs */
+    load_tile(vbase, a.vd, 0);
     for (int h = 0; h < group; h++) {
-        float *r = sc + h * a.npos;
+        float *r = sc + (size_t)h * a.npos;
         float mx = -INFINITY;
         for (int i = tid; i < n; i += PA_THREADS) mx = fmaxf(mx, r[i]);
         mx = block_reduce(mx, red, true);
@@ -528,7 +590,7 @@ __global__ void __launch_bounds__(PA_THREADS) pf_attn_kernel(const PfAttn a) {
         const float inv = __fdiv_rn(1.0f, sum);
         for (int i = tid; i < n; i += PA_THREADS) r[i] = __fmul_rn(r[i], inv);
     }
-    __syncthreads();
+    /* out = sum_t p_t V_t: thread -> outputs tid + k * PA_THREADS, (head, dim) */
     const int nout = group * hd;
     float acc[PA_MAXO];
     int oh[PA_MAXO], od[PA_MAXO];
@@ -539,24 +601,36 @@ __global__ void __launch_bounds__(PA_THREADS) pf_attn_kernel(const PfAttn a) {
         oh[k] = o < nout ? o / hd : 0;
         od[k] = o < nout ? o % hd : 0;
     }
-    for (int i = 0; i < n; i++) {
-        const int j = first + i;
-        const uint8_t *vr = vb + (size_t)j * rowb;
-        const float vd = KV == KC_Q8_0 ? a.vd[(size_t)j * a.n_kv + g] : 0.0f;
+    for (int k = 0; k < ntiles; k++) {
+        if (k + 1 < ntiles) {
+            load_tile(vbase, a.vd, k + 1);
+            cp_async_wait_one();
+        } else {
+            cp_async_wait_all();
+        }
+        __syncthreads();
+        const int nt = min(PA_TILE, n - k * PA_TILE);
+        const unsigned char *T = tiles + (k & 1) * PA_TILE * pitch;
 #pragma unroll
-        for (int k = 0; k < PA_MAXO; k++) {
-            if (tid + k * PA_THREADS < nout) {
-                const float pr = sc[oh[k] * a.npos + i];
-                if constexpr (KV == KC_F32) {
-                    acc[k] = __fadd_rn(acc[k], __fmul_rn(pr, ((const float *)vr)[od[k]]));
-                } else if constexpr (KV == KC_F16) {
-                    acc[k] = __fadd_rn(acc[k], __fmul_rn(pr, __half2float(((const __half *)vr)[od[k]])));
-                } else {
-                    const float w = __fmul_rn(pr, vd);
-                    acc[k] = __fadd_rn(acc[k], __fmul_rn(w, (float)((const int8_t *)vr)[od[k]]));
+        for (int kk = 0; kk < PA_MAXO; kk++) {
+            if (tid + kk * PA_THREADS < nout) {
+                const float *pr = sc + (size_t)oh[kk] * a.npos + k * PA_TILE;
+                float s = acc[kk];
+                for (int i = 0; i < nt; i++) {
+                    const unsigned char *row = T + i * pitch;
+                    if constexpr (KV == KC_F32) {
+                        s = __fadd_rn(s, __fmul_rn(pr[i], ((const float *)row)[od[kk]]));
+                    } else if constexpr (KV == KC_F16) {
+                        s = __fadd_rn(s, __fmul_rn(pr[i], __half2float(((const __half *)row)[od[kk]])));
+                    } else {
+                        const float w = __fmul_rn(pr[i], srd[(k & 1) * PA_TILE + i]);
+                        s = __fadd_rn(s, __fmul_rn(w, (float)((const int8_t *)row)[od[kk]]));
+                    }
                 }
+                acc[kk] = s;
             }
         }
+        __syncthreads();
     }
 #pragma unroll
     for (int k = 0; k < PA_MAXO; k++)
@@ -783,9 +857,10 @@ int build_cls(kc_model *m, PfModel &P, cudaStream_t st) {
     return KC_OK;
 }
 
-int attn_smem_bytes(const kc_config &c, size_t npos) {
-    const int group = c.n_heads / c.n_kv_heads;
-    return (int)(sizeof(float) * ((size_t)group * c.head_dim + (size_t)group * npos));
+size_t kv_es(int kv_type) { return kv_type == KC_F32 ? 4 : (kv_type == KC_F16 ? 2 : 1); }
+int pad_npos(size_t npos) { return (int)((npos + 3) & ~(size_t)3); }
+int attn_smem_bytes(const kc_config &c, int kv_type, size_t npos) {
+    return (int)pa_smem_bytes(c.n_heads / c.n_kv_heads, c.head_dim, (int)kv_es(kv_type), pad_npos(npos));
 }
 
 int ensure_scratch(PfScratch *&S, const kc_config &c, int tc, size_t npos) {
@@ -854,11 +929,11 @@ int set_attributes(int attn_smem) {
 /* Shared memory the batched attention needs for a chunk reaching position
  * last_pos; > PF_ATTN_SMEM_MAX means the batched path cannot take it. */
 bool pf_fits(const kc_config &c, int kv_type, int last_pos) {
-    (void)kv_type;
     const int group = c.n_heads / c.n_kv_heads;
     if (group > PA_MAXG || group * c.head_dim > ATT_MAX_OUT || c.head_dim % 4) return false;
     if (c.dim % QK || c.q_dim % QK || c.hidden_dim % QK) return false;
-    return attn_smem_bytes(c, (size_t)last_pos + 1) <= PF_ATTN_SMEM_MAX;
+    if ((c.head_dim * (int)kv_es(kv_type)) % 16) return false;
+    return attn_smem_bytes(c, kv_type, (size_t)last_pos + 1) <= PF_ATTN_SMEM_MAX;
 }
 
 void pf_free_model(PfModel *p) { delete p; }
@@ -888,7 +963,7 @@ int pf_prefill(const PfRun &r, const int *tokens, int n, int pos0, float *logits
     int rc = ensure_scratch(*r.scratch, c, tc, npos);
     if (rc != KC_OK) return rc;
     PfScratch &S = **r.scratch;
-    const int asmem = attn_smem_bytes(c, npos);
+    const int asmem = attn_smem_bytes(c, r.kv_type, npos);
     rc = set_attributes(asmem);
     if (rc != KC_OK) return rc;
     const int group = c.n_heads / c.n_kv_heads, ldq = c.q_dim + 2 * c.kv_dim;
@@ -907,7 +982,7 @@ int pf_prefill(const PfRun &r, const int *tokens, int n, int pos0, float *logits
                        p0, c.head_dim, c.n_heads, c.n_kv_heads, c.q_dim, c.kv_dim, r.kv_type };
             pf_rope_kernel<<<T, 256, 0, st>>>(ro);
             PfAttn at{ S.qkv, ldq, S.qq, S.qd, L.kc, L.vc, L.kd, L.vd, S.ao,
-                       p0, c.head_dim, c.n_heads, c.n_kv_heads, c.q_dim, c.kv_dim, L.window, (int)(npos),
+                       p0, c.head_dim, c.n_heads, c.n_kv_heads, c.q_dim, c.kv_dim, L.window, pad_npos(npos),
                        c.attn_scale, c.attn_softcap };
             const dim3 ag((unsigned)T, (unsigned)c.n_kv_heads);
             if (r.kv_type == KC_F32) pf_attn_kernel<KC_F32><<<ag, PA_THREADS, asmem, st>>>(at);
