@@ -37,7 +37,7 @@ constexpr int PF_M = 128;                              /* weight rows per tile: 
 constexpr int PF_N = 32;                               /* tokens per tile: TMEM columns per buffer */
 constexpr int PF_KB = 4;                               /* K blocks per pipeline stage */
 constexpr int PF_NST = 4;                              /* pipeline stages */
-constexpr int PF_NBUF = 8;                             /* TMEM accumulator buffers */
+constexpr int PF_NBUF = 4;                             /* TMEM buffers, each two K blocks x PF_N columns */
 constexpr int PF_EPI_WARPS = 8;                        /* two per TMEM lane quarter */
 constexpr int PF_THREADS = 32 * (2 + PF_EPI_WARPS);
 constexpr int PF_COLS = PF_N * 4 / PF_EPI_WARPS;       /* token columns per epilogue warp */
@@ -46,11 +46,12 @@ constexpr int PF_B_BLK = PF_N * QK;                    /* bytes of one K block o
 constexpr int PF_DW_BLK = PF_M * 4;                    /* weight scales of one K block (float) */
 constexpr int PF_DX_BLK = PF_N * 4;                    /* token scales of one K block (float) */
 constexpr int PF_STAGE = PF_KB * (PF_A_BLK + PF_B_BLK + PF_DW_BLK + PF_DX_BLK);
-constexpr int PF_TMEM_COLS = PF_NBUF * PF_N;
+constexpr int PF_TMEM_COLS = PF_NBUF * 2 * PF_N;
 constexpr int PF_SMEM = 1024 + PF_NST * PF_STAGE + 256;
 static_assert(PF_TMEM_COLS >= 32 && (PF_TMEM_COLS & (PF_TMEM_COLS - 1)) == 0, "TMEM columns: a power of two");
 static_assert(PF_COLS == 16, "the epilogue loads 16 TMEM columns at a time");
 static_assert(PF_STAGE % 256 == 0, "stage alignment");
+static_assert(PF_KB % 2 == 0, "a stage holds whole K-block pairs");
 static_assert((2 * PF_NST + 2 * PF_NBUF) * 8 + 4 <= 256, "barrier room");
 
 /* Byte (r, k) of one K block (rows x 32 bytes) in the MMA's K-major layout
@@ -103,6 +104,40 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
         : "r"(taddr));
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+/* Pairs of floats in one 64-bit register for the paired FP32 instructions
+ * (add/sub/mul/fma .f32x2): each lane of the pair rounds as the scalar
+ * instruction does. */
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float &a, float &b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2sub(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2mul(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+/* An int32 with |s| < 2^22 as a float, exactly, without the conversion unit:
+ * the bits 0x4B400000 + s are the float 1.5 * 2^23 + s (the mantissa of
+ * 1.5 * 2^23 has ulp 1 and room for s on either side), and subtracting
+ * 1.5 * 2^23 leaves s. A 32-element int8 block dot is at most 32 * 127 * 127. */
+constexpr int PF_MAGIC_BITS = 0x4B400000;
+constexpr float PF_MAGIC = 12582912.0f;
+__device__ __forceinline__ float magic_float(uint32_t s) { return __int_as_float((int)s + PF_MAGIC_BITS); }
 
 /* Error bit of the prefill kernels: a pipeline wait gave up. */
 constexpr unsigned PF_ERR_WAIT = 4u;
@@ -176,83 +211,81 @@ __global__ void __launch_bounds__(PF_THREADS, 2) pf_gemm_kernel(const __grid_con
             }
         }
     } else if (warp == 1) {
+        /* MMA issue: K blocks in pairs, one TMEM buffer (2 x PF_N columns) and
+         * one commit per pair */
         if (lane == 0) {
-            for (int kb = 0; kb < nbk; kb++) {
-                const int st = kb / PF_KB, j = kb - st * PF_KB, s = st % PF_NST, buf = kb % PF_NBUF;
+            for (int ks = 0; 2 * ks < nbk; ks++) {
+                const int kb = 2 * ks, st = kb / PF_KB, j = kb - st * PF_KB, s = st % PF_NST, buf = ks % PF_NBUF;
                 if (j == 0 && !mbar_wait(&full[s], (st / PF_NST) & 1, g.err)) {
                     atomicOr(g.err, PF_ERR_WAIT);
                     break;
                 }
-                if (!mbar_wait(&tempty[buf], ((kb / PF_NBUF) & 1) ^ 1, g.err)) {
+                if (!mbar_wait(&tempty[buf], ((ks / PF_NBUF) & 1) ^ 1, g.err)) {
                     atomicOr(g.err, PF_ERR_WAIT);
                     break;
                 }
                 tc_fence_after();
                 const uint32_t a = smem_u32(sm + s * PF_STAGE) + j * PF_A_BLK;
                 const uint32_t b = smem_u32(sm + s * PF_STAGE + OFF_B) + j * PF_B_BLK;
-                tc_mma_i8(tmem + (uint32_t)(buf * PF_N), umma_desc(a), umma_desc(b), PF_IDESC, 0u);
+                const uint32_t d = tmem + (uint32_t)(buf * 2 * PF_N);
+                tc_mma_i8(d, umma_desc(a), umma_desc(b), PF_IDESC, 0u);
+                if (kb + 1 < nbk) tc_mma_i8(d + PF_N, umma_desc(a + PF_A_BLK), umma_desc(b + PF_B_BLK), PF_IDESC, 0u);
                 tc_commit(&tfull[buf]);
-                if (j == PF_KB - 1 || kb == nbk - 1) tc_commit(&empty[s]);
+                if (j + 2 == PF_KB || kb + 2 >= nbk) tc_commit(&empty[s]);
             }
         }
     } else {
         /* epilogue: TMEM lane quarter q (the warp's rank in its warpgroup),
-         * token columns c0 .. c0+15 of the tile; the TMEM load of K block
-         * kb + 1 is in flight while K block kb is accumulated */
+         * token columns c0 .. c0+15 of the tile; K blocks in pairs, the TMEM
+         * loads of pair ks + 1 in flight while pair ks is accumulated */
         const int e = warp - 2, q = warp & 3, c0 = (e >> 2) * PF_COLS;
         const int row = m * PF_M + q * 32 + lane;
         const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
-        float acc[PF_COLS];
+        uint64_t acc[PF_COLS / 2];   /* column pairs */
 #pragma unroll
-        for (int c = 0; c < PF_COLS; c++) acc[c] = 0.0f;
-        uint32_t cur[PF_COLS], nxt[PF_COLS];
-        bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[0], 0, g.err));
-        if (ok) {
-            tc_fence_after();
-            tc_ld16(tq, cur);
-            tc_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[0]);
-        }
-        for (int kb = 0; ok && kb < nbk; kb++) {
-            const int st = kb / PF_KB, j = kb - st * PF_KB, s = st % PF_NST;
+        for (int c = 0; c < PF_COLS / 2; c++) acc[c] = 0ull;
+        const uint64_t magic2 = f2pack(PF_MAGIC, PF_MAGIC);
+        const int nks = (nbk + 1) / 2;
+        bool ok = true;
+        /* acc = fma((float)s, d_w * d_x, acc) for K block j of the stage, two columns per instruction */
+        auto accumulate = [&](const uint32_t (&v)[PF_COLS], const unsigned char *stage, int j) {
+            const float dw = ((const float *)(stage + OFF_DW))[j * PF_M + q * 32 + lane];
+            const uint64_t dw2 = f2pack(dw, dw);
+            const float4 *dx4 = (const float4 *)(stage + OFF_DX + j * PF_DX_BLK) + c0 / 4;
+#pragma unroll
+            for (int i = 0; i < PF_COLS / 4; i++) {
+                const float4 x = dx4[i];
+                const uint64_t m01 = f2mul(dw2, f2pack(x.x, x.y)), m23 = f2mul(dw2, f2pack(x.z, x.w));
+                const uint64_t s01 = f2sub(f2pack(magic_float(v[4 * i]), magic_float(v[4 * i + 1])), magic2);
+                const uint64_t s23 = f2sub(f2pack(magic_float(v[4 * i + 2]), magic_float(v[4 * i + 3])), magic2);
+                acc[2 * i] = f2fma(s01, m01, acc[2 * i]);
+                acc[2 * i + 1] = f2fma(s23, m23, acc[2 * i + 1]);
+            }
+        };
+        for (int ks = 0; ks < nks; ks++) {
+            const int kb = 2 * ks, st = kb / PF_KB, j = kb - st * PF_KB, s = st % PF_NST, buf = ks % PF_NBUF;
             if (j == 0 && !__all_sync(0xffffffffu, mbar_wait(&full[s], (st / PF_NST) & 1, g.err))) {
                 ok = false;
                 break;
             }
-            const bool more = kb + 1 < nbk;
-            const int nbuf = (kb + 1) % PF_NBUF;
-            if (more) {
-                if (!__all_sync(0xffffffffu, mbar_wait(&tfull[nbuf], ((kb + 1) / PF_NBUF) & 1, g.err))) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                tc_ld16(tq + (uint32_t)(nbuf * PF_N), nxt);
+            if (!__all_sync(0xffffffffu, mbar_wait(&tfull[buf], (ks / PF_NBUF) & 1, g.err))) {
+                ok = false;
+                break;
             }
+            tc_fence_after();
+            uint32_t va[PF_COLS], vb[PF_COLS];
+            tc_ld16(tq + (uint32_t)(buf * 2 * PF_N), va);
+            tc_ld16(tq + (uint32_t)(buf * 2 * PF_N + PF_N), vb);
+            tc_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
             const unsigned char *stage = sm + s * PF_STAGE;
-            const float dw = ((const float *)(stage + OFF_DW))[j * PF_M + q * 32 + lane];
-            const float4 *dx4 = (const float4 *)(stage + OFF_DX + j * PF_DX_BLK) + c0 / 4;
-#pragma unroll
-            for (int i = 0; i < PF_COLS / 4; i++) {
-                const float4 v = dx4[i];
-                acc[4 * i] = __fmaf_rn((float)(int)cur[4 * i], __fmul_rn(dw, v.x), acc[4 * i]);
-                acc[4 * i + 1] = __fmaf_rn((float)(int)cur[4 * i + 1], __fmul_rn(dw, v.y), acc[4 * i + 1]);
-                acc[4 * i + 2] = __fmaf_rn((float)(int)cur[4 * i + 2], __fmul_rn(dw, v.z), acc[4 * i + 2]);
-                acc[4 * i + 3] = __fmaf_rn((float)(int)cur[4 * i + 3], __fmul_rn(dw, v.w), acc[4 * i + 3]);
-            }
-            if (j == PF_KB - 1 || !more) {
+            accumulate(va, stage, j);
+            if (kb + 1 < nbk) accumulate(vb, stage, j + 1);
+            if (j + 2 == PF_KB || kb + 2 >= nbk) {
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
-            }
-            if (more) {
-                tc_wait_ld();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&tempty[nbuf]);
-#pragma unroll
-                for (int c = 0; c < PF_COLS; c++) cur[c] = nxt[c];
             }
         }
         if (!ok) {
@@ -260,11 +293,14 @@ __global__ void __launch_bounds__(PF_THREADS, 2) pf_gemm_kernel(const __grid_con
             if (lane == 0) atomicOr(g.err, PF_ERR_WAIT);
         } else if (row < g.rows) {
             const float bias = g.bias ? g.bias[row] : 0.0f;
+            float res[PF_COLS];
+#pragma unroll
+            for (int c = 0; c < PF_COLS / 2; c++) f2unpack(acc[c], res[2 * c], res[2 * c + 1]);
 #pragma unroll
             for (int c = 0; c < PF_COLS; c++) {
                 const int t = n * PF_N + c0 + c;
                 if (t < g.T) {
-                    float y = acc[c];
+                    float y = res[c];
                     if (g.bias) y = __fadd_rn(y, bias);
                     if (g.softcap > 0.0f) y = __fmul_rn(g.softcap, tanhf(__fdiv_rn(y, g.softcap)));
                     float *o = g.out + (size_t)t * g.ldo + row;
