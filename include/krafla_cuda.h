@@ -93,6 +93,21 @@ const kc_config *kc_model_config(const kc_model *m);
 size_t kc_model_device_bytes(const kc_model *m);
 void kc_model_free(kc_model *m);
 
+/* Tensor parallelism (no counterpart in the reference, which runs on one
+ * device): splits a loaded model, before kc_model_upload, into rank's share of
+ * world ranks, one process and one GPU per rank, Megatron style: Q/K/V rows by
+ * heads and the KV cache by KV head, gate/up rows, O and down by columns (the
+ * ranks' partial outputs are summed on the device after each), classifier rows
+ * by vocabulary (the ranks exchange their best logit). world 1..KC_TP_MAX with
+ * n_heads, n_kv_heads, q_dim/32 and hidden_dim/32 divisible by world.
+ * kc_model_config keeps returning the file's configuration. */
+#define KC_TP_MAX 8
+int kc_model_shard(kc_model *m, int rank, int world);
+/* This rank's share (9 ints): rank, world, n_heads, n_kv_heads, q_dim, kv_dim,
+ * hidden_dim held here, first classifier row, classifier rows. */
+int kc_model_shard_info(const kc_model *m, int *out);
+/* Makes `device` the current CUDA device of the calling thread (a rank's GPU). */
+int kc_set_device(int device);
 /* Replaces ml_state_init (model/transformer.h:56, transformer.c:51-166):
  * device buffers, the KV cache [n_layers][max_seq][kv_dim] in HBM (kv_type
  * KC_F32, KC_F16 or KC_Q8_0) and RoPE tables computed on the host in double
@@ -128,6 +143,13 @@ int kc_generate_greedy(kc_state *s, int token, int pos, int n, int *out_tokens);
  * output [q_dim], 3 FFN hidden [hidden_dim], 4 / 5 the K / V cache
  * [n_layers][max_seq][kv_dim]). KC_E_SHAPE when bytes is too small. */
 int kc_debug_copy(kc_state *s, int which, void *dst, size_t bytes);
+/* A sharded state's exchange buffer handle (CUDA IPC, KC_TP_HANDLE_BYTES
+ * bytes) for the other ranks; then kc_tp_connect with every rank's handle in
+ * rank order opens them. Until connected a sharded state refuses to run
+ * (KC_E_SHAPE). Every rank must then make the same sequence of calls. */
+#define KC_TP_HANDLE_BYTES 64
+int kc_tp_handle(kc_state *s, void *out, size_t cap);
+int kc_tp_connect(kc_state *s, const void *handles);
 /* Replaces ml_state_free (transformer.h:65). */
 void kc_state_free(kc_state *s);
 

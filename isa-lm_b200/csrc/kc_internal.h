@@ -84,6 +84,16 @@ struct kc_model {
     int stream_G = 0;
     /* the batched prefill's packed weights, built on first use */
     kc::PfModel *pf = nullptr;
+    /* tensor parallelism (kc_model_shard): after sharding, cfg holds this rank's
+     * dimensions (heads, q/kv widths, hidden) with the full vocab, cfg_full the
+     * file's; the classifier rows held here are [cls_row0, cls_row0 + cls_rows) */
+    int tp_rank = 0, tp_world = 1;
+    kc_config cfg_full{};
+    int cls_row0 = 0, cls_rows = 0;
+    std::vector<std::vector<uint8_t>> shard_bufs;   /* column slices copied out of the file */
 };
+
+/* Classifier rows this model (or rank) holds. */
+inline int model_cls_rows(const kc_model *m) { return m->tp_world > 1 ? m->cls_rows : m->cfg.vocab; }
 
 #endif

@@ -107,7 +107,91 @@ extern "C" int kc_model_from_host(kc_model **out, const kc_config *cfg, const kc
     return KC_OK;
 }
 
-extern "C" const kc_config *kc_model_config(const kc_model *m) { return &m->cfg; }
+extern "C" const kc_config *kc_model_config(const kc_model *m) { return m->tp_world > 1 ? &m->cfg_full : &m->cfg; }
+
+extern "C" int kc_model_shard_info(const kc_model *m, int *out) {
+    const kc_config &c = m->cfg;
+    const int v[9] = { m->tp_rank, m->tp_world, c.n_heads, c.n_kv_heads, c.q_dim, c.kv_dim, c.hidden_dim,
+                       m->cls_row0, model_cls_rows(m) };
+    std::memcpy(out, v, sizeof v);
+    return KC_OK;
+}
+
+extern "C" int kc_set_device(int device) {
+    clear_error();
+    CK(cudaSetDevice(device));
+    return KC_OK;
+}
+
+/* Rows [r0, r0 + n) of a file matrix: a view. */
+static HostMat row_view(const HostMat &M, int r0, int n) {
+    HostMat v = M;
+    const size_t qrow = M.type == KC_Q4_0 ? (size_t)M.cols / 2 : (size_t)M.cols;
+    const size_t drow = (size_t)(M.cols / KC_QK) * (M.d16 ? 2 : 4);
+    v.q = (const uint8_t *)M.q + (size_t)r0 * qrow;
+    v.d = (const uint8_t *)M.d + (size_t)r0 * drow;
+    v.rows = n;
+    return v;
+}
+
+/* Columns [c0, c0 + n) of every row (c0, n multiples of 32): a copy kept by the model. */
+static HostMat col_slice(kc_model *m, const HostMat &M, int c0, int n) {
+    const size_t nb = (size_t)M.cols / KC_QK, b0 = (size_t)c0 / KC_QK, wb = (size_t)n / KC_QK;
+    const size_t bq = M.type == KC_Q4_0 ? KC_QK / 2 : KC_QK, ds = M.d16 ? 2 : 4;
+    std::vector<uint8_t> q((size_t)M.rows * wb * bq), d((size_t)M.rows * wb * ds);
+    for (size_t r = 0; r < (size_t)M.rows; r++) {
+        std::memcpy(q.data() + r * wb * bq, (const uint8_t *)M.q + (r * nb + b0) * bq, wb * bq);
+        std::memcpy(d.data() + r * wb * ds, (const uint8_t *)M.d + (r * nb + b0) * ds, wb * ds);
+    }
+    m->shard_bufs.push_back(std::move(q));
+    m->shard_bufs.push_back(std::move(d));
+    HostMat v = M;
+    v.q = m->shard_bufs[m->shard_bufs.size() - 2].data();
+    v.d = m->shard_bufs.back().data();
+    v.cols = n;
+    return v;
+}
+
+extern "C" int kc_model_shard(kc_model *m, int rank, int world) {
+    clear_error();
+    const kc_config c = m->cfg;
+    if (m->uploaded || m->tp_world > 1) {
+        set_error("shard a model once, before kc_model_upload");
+        return KC_E_SHAPE;
+    }
+    if (world < 1 || world > KC_TP_MAX || rank < 0 || rank >= world) return KC_E_SHAPE;
+    if (world == 1) return KC_OK;
+    if (c.n_heads % world || c.n_kv_heads % world || (c.q_dim / world) % KC_QK || c.q_dim % world ||
+        (c.hidden_dim / world) % KC_QK || c.hidden_dim % world) {
+        set_error("heads, q_dim/32 and hidden_dim/32 must divide by the number of ranks");
+        return KC_E_SHAPE;
+    }
+    const int qd = c.q_dim / world, kvd = c.kv_dim / world, hid = c.hidden_dim / world;
+    for (HostLayer &H : m->layers) {
+        H.wq = row_view(H.wq, rank * qd, qd);
+        H.wk = row_view(H.wk, rank * kvd, kvd);
+        H.wv = row_view(H.wv, rank * kvd, kvd);
+        if (H.bq) { H.bq += (size_t)rank * qd; H.bk += (size_t)rank * kvd; H.bv += (size_t)rank * kvd; }
+        H.wo = col_slice(m, H.wo, rank * qd, qd);
+        H.w1 = row_view(H.w1, rank * hid, hid);
+        H.w3 = row_view(H.w3, rank * hid, hid);
+        H.w2 = col_slice(m, H.w2, rank * hid, hid);
+    }
+    const int v0 = (int)((long long)c.vocab * rank / world), v1 = (int)((long long)c.vocab * (rank + 1) / world);
+    m->wcls = row_view(m->shared ? m->tok_emb : m->wcls, v0, v1 - v0);
+    m->shared = 0;
+    m->cls_row0 = v0;
+    m->cls_rows = v1 - v0;
+    m->cfg_full = c;
+    m->cfg.n_heads = c.n_heads / world;
+    m->cfg.n_kv_heads = c.n_kv_heads / world;
+    m->cfg.q_dim = qd;
+    m->cfg.kv_dim = kvd;
+    m->cfg.hidden_dim = hid;
+    m->tp_rank = rank;
+    m->tp_world = world;
+    return KC_OK;
+}
 extern "C" size_t kc_model_device_bytes(const kc_model *m) { return m->dev_bytes + pf_model_bytes(m->pf); }
 
 extern "C" void kc_model_free(kc_model *m) {
@@ -137,7 +221,7 @@ static int stream_geom(const kc_model *m, StreamGeom &g) {
     const HostMat &cls = m->shared ? m->tok_emb : m->wcls;
     auto ty = [](const HostMat &h) { return h.type == KC_Q4_0 ? T_Q4 : T_Q8; };
     g = StreamGeom{};
-    g.dim = c.dim; g.q_dim = c.q_dim; g.kv_dim = c.kv_dim; g.hidden = c.hidden_dim; g.vocab = c.vocab;
+    g.dim = c.dim; g.q_dim = c.q_dim; g.kv_dim = c.kv_dim; g.hidden = c.hidden_dim; g.vocab = model_cls_rows(m);
     g.t_q = ty(L0.wq); g.t_k = ty(L0.wk); g.t_v = ty(L0.wv); g.t_o = ty(L0.wo);
     g.t_up = ty(L0.w1); g.t_down = ty(L0.w2); g.t_cls = ty(cls);
     g.d16_q = L0.wq.d16; g.d16_k = L0.wk.d16; g.d16_v = L0.wv.d16; g.d16_o = L0.wo.d16;
@@ -329,6 +413,13 @@ struct kc_state {
     /* prompt tokens per batched prefill step (ml_state.batch); 1: token by token */
     int batch = KC_BATCH_MAX;
     PfScratch *pfs = nullptr;
+    /* tensor parallelism: this rank's exchange buffer (IPC-exported), the
+     * other ranks' buffers once connected, steps launched so far */
+    uint8_t *tp_box = nullptr;
+    cudaIpcMemHandle_t tp_handle{};
+    uint8_t *tp_peer[KC_TP_MAX] = {};
+    int tp_connected = 0;
+    unsigned long long tp_steps = 0;
 };
 
 /* RoPE inverse frequency of pair i (model/transformer.c:16-38; the scaling
@@ -536,6 +627,9 @@ static int setup_step_kernel(kc_state *s) {
     a.vocab = c.vocab; a.max_seq = c.max_seq; a.n_heads = c.n_heads; a.n_kv_heads = c.n_kv_heads; a.hd = c.head_dim;
     a.eps = c.norm_eps; a.attn_scale = c.attn_scale; a.attn_softcap = c.attn_softcap; a.final_softcap = c.final_softcap;
     a.embed_scale = c.embed_scale; a.act = c.act;
+    a.cls_row0 = m->cls_row0;
+    a.tp_rank = 0; a.tp_world = 1; a.tp_step0 = 0;
+    for (int r = 0; r < KC_TP_MAX; r++) a.tp_box[r] = nullptr;
     a.nsplit = std::min(MAX_NSPLIT, std::max(1, s->num_sms / c.n_kv_heads));
     a.nstage = nst; a.slot_bytes = slot; a.act_bytes = act; a.res_bytes = res; a.wbuf_bytes = wbuf;
     a.timeline = nullptr; a.timeline_n = s->timeline_n; a.timeline_cap = 4096;
@@ -544,8 +638,14 @@ static int setup_step_kernel(kc_state *s) {
 
 /* Runs nsteps token steps in one cooperative launch of the step kernel. */
 static int launch_steps(kc_state *s, int nsteps, int logits, bool timeline = false) {
+    if (s->m->tp_world > 1 && !s->tp_connected) {
+        set_error("tensor-parallel state not connected (kc_tp_connect)");
+        return KC_E_SHAPE;
+    }
     CK(cudaMemsetAsync(s->bar, 0, sizeof(unsigned), s->st));
     StepArgs a = s->sa;
+    a.tp_step0 = s->tp_steps;
+    s->tp_steps += (unsigned long long)nsteps;
     a.nsteps = nsteps;
     a.run_cls = logits;
     if (timeline) {
@@ -568,6 +668,34 @@ static int launch_steps(kc_state *s, int nsteps, int logits, bool timeline = fal
 
 static int run_steps(kc_state *s, int nsteps, int logits) { return launch_steps(s, nsteps, logits); }
 
+/* A sharded state's exchange buffer (one allocation, exported by CUDA IPC):
+ * partial rows y [2][world][dim], CTA flags [2][world][G], best keys [world]
+ * and their flags [world], the logits ring [LOGITS_RING][vocab] (every rank's
+ * classifier rows land in every rank's ring). Zeroed: flag values start at 1. */
+static int tp_alloc(kc_state *s) {
+    const kc_config &c = s->c;
+    kc_model *m = s->m;
+    const size_t W = (size_t)m->tp_world, G = (size_t)s->num_sms;
+    const size_t off_flag = align256(sizeof(float) * 2 * W * c.dim);
+    const size_t off_best = off_flag + align256(sizeof(unsigned) * 2 * W * G);
+    const size_t off_bflag = off_best + align256(sizeof(unsigned long long) * W);
+    const size_t off_logits = off_bflag + align256(sizeof(unsigned) * W);
+    const size_t total = off_logits + align256(sizeof(float) * (size_t)LOGITS_RING * c.vocab);
+    CK(cudaMalloc(&s->tp_box, total));
+    CK(cudaMemset(s->tp_box, 0, total));
+    CK(cudaIpcGetMemHandle(&s->tp_handle, s->tp_box));
+    s->logits = (float *)(s->tp_box + off_logits);
+    StepArgs &a = s->sa;
+    a.logits = s->logits;
+    a.tp_rank = m->tp_rank;
+    a.tp_world = m->tp_world;
+    a.tp_off_flag = off_flag;
+    a.tp_off_best = off_best;
+    a.tp_off_bflag = off_bflag;
+    a.tp_off_logits = off_logits;
+    return KC_OK;
+}
+
 extern "C" void kc_state_free(kc_state *s) {
     if (!s) return;
     if (s->st) cudaStreamSynchronize(s->st);
@@ -575,6 +703,9 @@ extern "C" void kc_state_free(kc_state *s) {
     if (s->h_logits) cudaFreeHost(s->h_logits);
     if (s->h_ls) cudaFreeHost(s->h_ls);
     if (s->d_plan) cudaFree(s->d_plan);
+    for (int r = 0; r < KC_TP_MAX; r++)
+        if (s->tp_peer[r]) cudaIpcCloseMemHandle(s->tp_peer[r]);
+    if (s->tp_box) cudaFree(s->tp_box);
     pf_free_scratch(s->pfs);
     if (s->st) cudaStreamDestroy(s->st);
     delete s;
@@ -691,9 +822,42 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
     if (st != KC_OK) return fail(st);
     st = setup_step_kernel(s);
     if (st != KC_OK) return fail(st);
+    if (m->tp_world > 1) {
+        st = tp_alloc(s);
+        if (st != KC_OK) return fail(st);
+    }
     e = cudaStreamSynchronize(s->st);
     if (e != cudaSuccess) return fail(cuda_status(e, "state init"));
     *out = s;
+    return KC_OK;
+}
+
+extern "C" int kc_tp_handle(kc_state *s, void *out, size_t cap) {
+    clear_error();
+    if (!s->tp_box || cap < KC_TP_HANDLE_BYTES || sizeof(cudaIpcMemHandle_t) > KC_TP_HANDLE_BYTES) return KC_E_SHAPE;
+    std::memset(out, 0, KC_TP_HANDLE_BYTES);
+    std::memcpy(out, &s->tp_handle, sizeof(cudaIpcMemHandle_t));
+    return KC_OK;
+}
+
+extern "C" int kc_tp_connect(kc_state *s, const void *handles) {
+    clear_error();
+    kc_model *m = s->m;
+    if (!s->tp_box || s->tp_connected) return KC_E_SHAPE;
+    const uint8_t *h = (const uint8_t *)handles;
+    for (int r = 0; r < m->tp_world; r++) {
+        if (r == m->tp_rank) {
+            s->sa.tp_box[r] = s->tp_box;
+            continue;
+        }
+        cudaIpcMemHandle_t ih;
+        std::memcpy(&ih, h + (size_t)r * KC_TP_HANDLE_BYTES, sizeof ih);
+        void *p = nullptr;
+        CK(cudaIpcOpenMemHandle(&p, ih, cudaIpcMemLazyEnablePeerAccess));
+        s->tp_peer[r] = (uint8_t *)p;
+        s->sa.tp_box[r] = (uint8_t *)p;
+    }
+    s->tp_connected = 1;
     return KC_OK;
 }
 
@@ -800,7 +964,7 @@ extern "C" int kc_prefill(kc_state *s, const int *tokens, int n, int pos0, float
     for (int i = 0; i < n; i++)
         if (tokens[i] < 0 || tokens[i] >= c.vocab) return KC_E_SHAPE;
     if (n == 0) return KC_OK;
-    if (s->batch > 1 && n > 1 && pf_fits(c, s->kv_type, pos0 + n - 1))
+    if (s->batch > 1 && n > 1 && s->m->tp_world == 1 && pf_fits(c, s->kv_type, pos0 + n - 1))
         return prefill_batched(s, tokens, n, pos0, logits);
     return prefill_tokenwise(s, tokens, n, pos0, logits);
 }

@@ -200,6 +200,17 @@ struct StepArgs {
     unsigned timeline_cap;
     unsigned long long *trace;      /* optional: [phase][G][3] per CTA: prologue done, arrived, released */
     unsigned trace_phases;
+    /* tensor parallelism: this rank's classifier rows start at cls_row0; with
+     * tp_world > 1, tp_box[r] is rank r's exchange buffer (the own one too):
+     * partial rows y [2][world][dim] at 0, CTA flags [2][world][G] at
+     * tp_off_flag, best logit keys [world] at tp_off_best and their flags at
+     * tp_off_bflag, the logits ring at tp_off_logits. tp_step0: the steps of
+     * earlier launches (flag values grow by one per exchange). */
+    int cls_row0;
+    int tp_rank, tp_world;
+    unsigned long long tp_step0;
+    unsigned char *tp_box[KC_TP_MAX];
+    unsigned long long tp_off_flag, tp_off_best, tp_off_bflag, tp_off_logits;
 };
 
 /* ------------------------------------------------------------ event log (diagnostics) */
@@ -325,6 +336,81 @@ __device__ __forceinline__ void grid_barrier(const StepArgs &a, unsigned &expect
         }
     }
     consumer_sync();
+}
+
+/* ------------------------------------------------------------ tensor parallelism */
+
+constexpr unsigned TP_ERR = 16u;   /* error bit: a rank's partial rows or best key never came */
+
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+/* Bounded wait (one thread) until *f >= seq; false after ~1 s or when the
+ * error word is set. */
+__device__ __forceinline__ bool tp_wait(const unsigned *f, unsigned seq, unsigned *err) {
+    for (unsigned it = 0; it < (1u << 22); it++) {
+        if (ld_acquire_sys(f) >= seq) return true;
+        if ((it & 255) == 255 && ld_acquire(err)) return false;
+    }
+    atomicOr(err, TP_ERR);
+    return false;
+}
+__device__ __forceinline__ unsigned tp_seq(const StepArgs &a, int step, int l, int ph) {
+    return (unsigned)((a.tp_step0 + (unsigned long long)step) * (2ull * a.n_layers) + 2ull * l + ph + 1ull);
+}
+
+/* The residual add after a row-parallel projection (O: ph 0, down: ph 1)
+ * across ranks: the CTA's partial rows (its column slices summed in order)
+ * go to slot [ph][rank] of every rank's exchange buffer, then one flag per
+ * rank; once every rank's flag for this CTA has come, x[row] += the partials
+ * summed in rank order. Every rank runs the same grid, so CTA j of every rank
+ * owns the same rows of x. */
+__device__ __noinline__ void tp_resid(const StepArgs &a, const float *res, int nrows, int row0, float *out,
+                                      float *own, int ns, int ph, unsigned seq) {
+    const int me = a.tp_rank, W = a.tp_world, D = a.dim, G = gridDim.x, c = blockIdx.x;
+    for (int i = threadIdx.x; i < nrows; i += NCT) {
+        float sum = res[i * ns];
+        for (int k = 1; k < ns; k++) sum = __fadd_rn(sum, res[i * ns + k]);
+        for (int r = 0; r < W; r++) ((float *)a.tp_box[r])[((size_t)ph * W + me) * D + row0 + i] = sum;
+    }
+    __threadfence_system();
+    consumer_sync();
+    if (threadIdx.x < W) {
+        st_release_sys((unsigned *)(a.tp_box[threadIdx.x] + a.tp_off_flag) + ((size_t)ph * W + me) * G + c, seq);
+        tp_wait((const unsigned *)(a.tp_box[me] + a.tp_off_flag) + ((size_t)ph * W + threadIdx.x) * G + c, seq, a.err);
+        __threadfence_system();
+    }
+    consumer_sync();
+    const float *y = (const float *)a.tp_box[me] + (size_t)ph * W * D;
+    for (int i = threadIdx.x; i < nrows; i += NCT) {
+        float tot = __ldcv(y + row0 + i);
+        for (int r = 1; r < W; r++) tot = __fadd_rn(tot, __ldcv(y + (size_t)r * D + row0 + i));
+        const float v = __fadd_rn(own[i], tot);
+        own[i] = v;
+        out[row0 + i] = v;
+    }
+}
+
+/* The rank's best logit key to every rank, then the maximum over ranks (one
+ * thread, the CTA that finishes the step). */
+__device__ __noinline__ unsigned long long tp_argmax(const StepArgs &a, unsigned long long b, unsigned seq) {
+    const int me = a.tp_rank, W = a.tp_world;
+    for (int r = 0; r < W; r++) ((unsigned long long *)(a.tp_box[r] + a.tp_off_best))[me] = b;
+    __threadfence_system();
+    for (int r = 0; r < W; r++) st_release_sys((unsigned *)(a.tp_box[r] + a.tp_off_bflag) + me, seq);
+    unsigned long long best = 0;
+    for (int r = 0; r < W; r++) {
+        tp_wait((const unsigned *)(a.tp_box[me] + a.tp_off_bflag) + r, seq, a.err);
+        __threadfence_system();
+        const unsigned long long k = __ldcv((const unsigned long long *)(a.tp_box[me] + a.tp_off_best) + r);
+        best = k > best ? k : best;
+    }
+    return best;
 }
 
 /* ------------------------------------------------------------ the ring */
@@ -1374,7 +1460,11 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
             trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_C], false, act_view(w_q), sh.res, a.err);
-            finish_phase(FIN_RESID, sh.res, nown, own0, a.x, sh.own, 0, 0.0f, sh.cta_best, col_slices(a.q_dim / QK, false));
+            if (a.tp_world > 1)
+                tp_resid(a, sh.res, nown, own0, a.x, sh.own, col_slices(a.q_dim / QK, false), 0, tp_seq(a, step, l, 0));
+            else
+                finish_phase(FIN_RESID, sh.res, nown, own0, a.x, sh.own, 0, 0.0f, sh.cta_best,
+                             col_slices(a.q_dim / QK, false));
             prefetch_norm(sh.wbuf, L.ffn_norm, a.dim);
             grid_barrier(a, expect, pidx, sh.own, nown);
             /* D: gate/up + activation */
@@ -1390,7 +1480,11 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
             trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_E], false, act_view(w_h), sh.res, a.err);
-            finish_phase(FIN_RESID, sh.res, nown, own0, a.x, sh.own, 0, 0.0f, sh.cta_best, col_slices(a.hidden / QK, false));
+            if (a.tp_world > 1)
+                tp_resid(a, sh.res, nown, own0, a.x, sh.own, col_slices(a.hidden / QK, false), 1, tp_seq(a, step, l, 1));
+            else
+                finish_phase(FIN_RESID, sh.res, nown, own0, a.x, sh.own, 0, 0.0f, sh.cta_best,
+                             col_slices(a.hidden / QK, false));
             prefetch_norm(sh.wbuf, next_norm, a.dim);
             grid_barrier(a, expect, pidx, sh.own, nown);
         }
@@ -1400,10 +1494,22 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
             trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_F], false, act_view(w_dim), sh.res, a.err);
-            const unsigned long long b = finish_phase(FIN_LOGITS, sh.res, s_plan[PH_F].seg[0].rows,
-                                                      s_plan[PH_F].seg[0].row0, a.logits + logit_row0, nullptr, 0,
-                                                      a.final_softcap, sh.cta_best, col_slices(a.dim / QK, false));
+            const Seg &F = s_plan[PH_F].seg[0];
+            const unsigned long long b =
+                finish_phase(FIN_LOGITS, sh.res, F.rows, a.cls_row0 + F.row0, a.logits + logit_row0, nullptr, 0,
+                             a.final_softcap, sh.cta_best, col_slices(a.dim / QK, false));
             if (threadIdx.x == 0 && b) atomicMax(&a.ls->best, b);
+            if (a.tp_world > 1) {
+                /* this rank's logits rows into every other rank's ring (each thread
+                 * re-reads the rows it wrote itself) */
+                for (int i = threadIdx.x; i < F.rows; i += NCT) {
+                    const size_t o = (size_t)logit_row0 + a.cls_row0 + F.row0 + i;
+                    const float v = a.logits[o];
+                    for (int r = 0; r < a.tp_world; r++)
+                        if (r != a.tp_rank) ((float *)(a.tp_box[r] + a.tp_off_logits))[o] = v;
+                }
+                __threadfence_system();
+            }
         }
         /* every CTA arrives; the last one advances the loop state, then
          * releases the others with one more arrival */
@@ -1418,7 +1524,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
                 LoopState *ls = a.ls;
                 const int st = ls->step;
                 if (a.run_cls) {
-                    const unsigned long long b = atomicAdd(&ls->best, 0ull);
+                    unsigned long long b = atomicAdd(&ls->best, 0ull);
+                    if (a.tp_world > 1) b = tp_argmax(a, b, (unsigned)(a.tp_step0 + (unsigned long long)step + 1ull));
                     const int next = (int)(0xffffffffu - (unsigned)(b & 0xffffffffull));
                     a.out_tokens[st] = next;
                     ls->token = ls->feed_mode ? a.feed[st + 1] : next;

@@ -28,6 +28,7 @@ GEN_PATH = os.path.join(_HERE, "libkrafla_mlbgen.so")
 
 OK, E_IO, E_FORMAT, E_SHAPE, E_NOMEM, E_ISA = range(6)
 F32, Q8_0, Q4_0, F16 = 0, 1, 2, 3
+TP_MAX, TP_HANDLE_BYTES = 8, 64          # KC_TP_MAX, KC_TP_HANDLE_BYTES of include/krafla_cuda.h
 STATUS = {OK: "ok", E_IO: "i/o error", E_FORMAT: "bad file format", E_SHAPE: "bad tensor shape",
           E_NOMEM: "out of memory", E_ISA: "device lacks required architecture"}
 
@@ -76,7 +77,8 @@ def lib():
             "kc_model_config": (C.POINTER(_Config), [P]), "kc_model_device_bytes": (S, [P]),
             "kc_model_free": (None, [P]),
             "kc_state_init": (I, [C.POINTER(P), P, I, I]), "kc_prefill": (I, [P, P, I, I, P]),
-            "kc_set_batch": (I, [P, I]),
+            "kc_set_batch": (I, [P, I]), "kc_model_shard": (I, [P, I, I]), "kc_model_shard_info": (I, [P, P]),
+            "kc_set_device": (I, [I]), "kc_tp_handle": (I, [P, P, S]), "kc_tp_connect": (I, [P, P]),
             "kc_forward": (C.POINTER(F), [P, I, I]), "kc_generate_greedy": (I, [P, I, I, I, P]),
             "kc_state_free": (None, [P]),
             "kc_time_decode": (I, [P, I, I, I, I, C.POINTER(F)]),
@@ -102,6 +104,21 @@ def _check(st, what):
         raise KraflaError(st, what)
 
 
+def set_device(device):
+    """The calling thread's CUDA device for this library (one rank, one GPU)."""
+    _check(lib().kc_set_device(int(device)), "set device")
+
+
+def exchange_handles(handle, dist):
+    """Every rank's tensor-parallel handle, in rank order, through an initialised
+    torch.distributed process group (any backend: objects travel on the CPU)."""
+    out = [None] * dist.get_world_size()
+    dist.all_gather_object(out, bytes(handle))
+    if any(not isinstance(h, bytes) or len(h) != TP_HANDLE_BYTES for h in out):
+        raise KraflaError(E_SHAPE, "tp handles: a rank sent a malformed handle")
+    return out
+
+
 def device_check():
     """0 on a B200 (sm_100) this build runs on; raises otherwise."""
     _check(lib().kc_device_check(), "device check")
@@ -118,6 +135,18 @@ class Model:
 
     def upload(self):
         _check(lib().kc_model_upload(self._h), "upload")
+
+    def shard(self, rank, world):
+        """Keep rank's tensor-parallel share of world (before upload)."""
+        _check(lib().kc_model_shard(self._h, int(rank), int(world)), "shard")
+        return self
+
+    @property
+    def shard_info(self):
+        v = (C.c_int * 9)()
+        _check(lib().kc_model_shard_info(self._h, v), "shard info")
+        keys = ("rank", "world", "n_heads", "n_kv_heads", "q_dim", "kv_dim", "hidden_dim", "cls_row0", "cls_rows")
+        return dict(zip(keys, list(v)))
 
     @property
     def config(self):
@@ -167,6 +196,18 @@ class State:
                               out.ctypes.data_as(C.c_void_p) if logits else None)
         _check(st, "prefill")
         return out
+
+    def tp_handle(self):
+        """This rank's exchange-buffer handle (bytes) for the other ranks."""
+        buf = C.create_string_buffer(TP_HANDLE_BYTES)
+        _check(lib().kc_tp_handle(self._h, buf, TP_HANDLE_BYTES), "tp handle")
+        return buf.raw
+
+    def tp_connect(self, handles):
+        """Open every rank's exchange buffer (handles in rank order)."""
+        blob = b"".join(bytes(h) for h in handles)
+        _check(lib().kc_tp_connect(self._h, blob), "tp connect")
+        return self
 
     def set_batch(self, batch):
         """ml_state.batch: prompt tokens per batched prefill step (1 = token by token)."""
