@@ -18,6 +18,13 @@ every step streams them from HBM.
 Under torchrun each rank runs an independent replica on its own GPU (sub-2B
 models do not shard profitably: "replicas only"), scaling "weak".
 
+  tp     BASELINE config 4 (Llama-3-8B shape, Q8_0) batch-1 greedy decode at
+         KV context 2048, tensor parallel over all ranks (one model across the
+         N GPUs, the O and down partial sums exchanged inside the step kernel
+         over NVLink): tok/s of the one token stream (max over ranks of the
+         CUDA-event time), scaling "strong". At N=1 (without --no-extras) the
+         same decode on one GPU, the reference point of the scaling.
+
 --impl reference times the reference's own CPU build (oracle/_ref, the
 unmodified reference library; its best ISA for the host, all host threads)
 on the same workload: rank 0 only.
@@ -42,15 +49,17 @@ P.add_argument("--impl", choices=("ours", "reference"), default="ours")
 P.add_argument("--config", default="cfg2")
 P.add_argument("--ctx", type=int, default=1024)
 P.add_argument("--no-extras", action="store_true", help="skip the context sweep, prefill and CPU baseline")
+P.add_argument("--tp-config", default="cfg4", help="model of the tensor-parallel decode ('none' to skip)")
+P.add_argument("--tp-ctx", type=int, default=2048)
 ARGS = P.parse_args()
 
 RANK = int(os.environ.get("RANK", "0"))
 WORLD = int(os.environ.get("WORLD_SIZE", "1"))
 LOCAL = int(os.environ.get("LOCAL_RANK", "0"))
-if WORLD > 1:   # one GPU per rank: the library uses device 0 of its process
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-    devs = vis.split(",") if vis else [str(i) for i in range(64)]
-    os.environ["CUDA_VISIBLE_DEVICES"] = devs[LOCAL]
+# one GPU per rank: device LOCAL_RANK; every device stays visible, since a
+# tensor-parallel rank maps the other ranks' exchange buffers (CUDA IPC)
+_VIS = os.environ.get("CUDA_VISIBLE_DEVICES")
+PHYS_DEV = (_VIS.split(",") if _VIS else [str(i) for i in range(64)])[LOCAL]
 
 MODEL_DIR = os.environ.get("KRAFLA_MODEL_DIR", os.path.join(ROOT, "_models"))
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -117,7 +126,7 @@ class Clocks:
         self.samples, self.stop = [], threading.Event()
 
     def __enter__(self):
-        dev = os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0]
+        dev = PHYS_DEV
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", dev, f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
                                        "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
@@ -152,7 +161,7 @@ def dist_init():
     import datetime
     import torch
     import torch.distributed as dist
-    torch.cuda.set_device(0)
+    torch.cuda.set_device(LOCAL)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
     return dist
 
@@ -192,10 +201,52 @@ def cpu_reference(path, cfg, ctx, steps, warmup):
             "sample": f"{ctx}-token prefill, then {steps} greedy decode steps at KV context {ctx + warmup}"}
 
 
+def tp_decode(dist, K, W, hbm_peak):
+    """Config --tp-config decode at KV context --tp-ctx, tensor parallel over the
+    WORLD ranks (kc_model_shard + kc_tp_connect); None when skipped."""
+    import krafla_b200 as kb
+    name = ARGS.tp_config
+    if name == "none" or name not in kb.CONFIGS:
+        return None
+    if RANK == 0:
+        path = kb.ensure_model(name, MODEL_DIR)
+    if dist is not None:
+        dist.barrier()
+        path = kb.ensure_model(name, MODEL_DIR)
+    model = kb.Model(path, upload=False)
+    if WORLD > 1:
+        model.shard(RANK, WORLD)
+    st = kb.State(model)
+    if WORLD > 1:
+        st.tp_connect(kb.exchange_handles(st.tp_handle(), dist))
+    cfg = model.config
+    cfg["shared"] = kb.CONFIGS[name].get("shared", 0)
+    ctx = min(ARGS.tp_ctx, cfg["max_seq"] - K - W - 1)
+    toks = prompt_tokens(cfg["vocab"], ctx, seed=99)
+    st.prefill(toks[:-1], 0)
+    if dist is not None:
+        dist.barrier()
+    ms = dist_max(dist, st.time_decode(int(toks[-1]), ctx - 1, W, K))
+    tok_s = K / (ms / 1000.0)
+    bpt, _ = model_bytes_per_token(cfg, ctx + W + K // 2)
+    if dist is not None:
+        dist.barrier()   # every rank's kernels are done before any exchange buffer goes
+    st.free()
+    model.free()
+    if dist is not None:
+        dist.barrier()
+    return {"config": name, "workload": f"{name} batch-1 greedy decode at KV context {ctx}, tensor parallel",
+            "parallelism": f"tp{WORLD}", "n_gpus": WORLD, "scaling": "strong", "tok_s": round(tok_s, 2),
+            "ms_per_token": round(ms / K, 4), "steps": K, "warmup": W, "bytes_per_token": int(bpt),
+            "hbm_frac_per_gpu": round(bpt / WORLD * tok_s / 1e9 / hbm_peak, 4),
+            "exchange": "O and down partials: per-CTA peer stores + flags inside the step kernel (no NCCL on the token path)"}
+
+
 def main():
     import numpy as np
     import krafla_b200 as kb
     dist = dist_init()
+    kb.set_device(LOCAL)
     hbm_peak, peak_kind = peaks()
     if RANK == 0:
         path = kb.ensure_model(ARGS.config, MODEL_DIR)
@@ -288,7 +339,7 @@ def main():
         phases["classifier"] = round(float(d[5 * L:].sum()), 2)
 
     extras = {}
-    if RANK == 0 and not ARGS.no_extras:
+    if RANK == 0 and WORLD == 1 and not ARGS.no_extras:   # extras and the CPU baseline: N=1 only
         sweep = {}
         for c in (128, 1024, 4096):
             c2 = min(c, cfg["max_seq"] - 34)
@@ -343,6 +394,12 @@ def main():
         except Exception as e:   # the reference build needs a compatible host CPU
             extras["cpu_baseline"] = {"error": str(e)}
 
+    st.free()
+    model.free()
+    tp = None
+    if WORLD > 1 or not ARGS.no_extras:
+        tp = tp_decode(dist, min(K, 64), max(W, 3), hbm_peak)
+
     if RANK == 0:
         cpu = extras.get("cpu_baseline", {})
         line = {
@@ -377,9 +434,9 @@ def main():
         for k in ("decode_by_context", "decode_by_kv_cache", "prefill_tok_s", "prefill_roofline"):
             if k in extras:
                 line[k] = extras[k]
+        if tp is not None:
+            line["tp"] = tp
         print(json.dumps(line), flush=True)
-    st.free()
-    model.free()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

@@ -669,15 +669,15 @@ static int launch_steps(kc_state *s, int nsteps, int logits, bool timeline = fal
 static int run_steps(kc_state *s, int nsteps, int logits) { return launch_steps(s, nsteps, logits); }
 
 /* A sharded state's exchange buffer (one allocation, exported by CUDA IPC):
- * partial rows y [2][world][dim], CTA flags [2][world][G], best keys [world]
- * and their flags [world], the logits ring [LOGITS_RING][vocab] (every rank's
- * classifier rows land in every rank's ring). Zeroed: flag values start at 1. */
+ * partial rows y [2][world][dim] as 64-bit words (sequence number | float),
+ * best keys [world] and their flags [world], the logits ring
+ * [LOGITS_RING][vocab] (every rank's classifier rows land in every rank's
+ * ring). Zeroed: sequence numbers start at 1. */
 static int tp_alloc(kc_state *s) {
     const kc_config &c = s->c;
     kc_model *m = s->m;
-    const size_t W = (size_t)m->tp_world, G = (size_t)s->num_sms;
-    const size_t off_flag = align256(sizeof(float) * 2 * W * c.dim);
-    const size_t off_best = off_flag + align256(sizeof(unsigned) * 2 * W * G);
+    const size_t W = (size_t)m->tp_world;
+    const size_t off_best = align256(sizeof(unsigned long long) * 2 * W * c.dim);
     const size_t off_bflag = off_best + align256(sizeof(unsigned long long) * W);
     const size_t off_logits = off_bflag + align256(sizeof(unsigned) * W);
     const size_t total = off_logits + align256(sizeof(float) * (size_t)LOGITS_RING * c.vocab);
@@ -689,7 +689,6 @@ static int tp_alloc(kc_state *s) {
     a.logits = s->logits;
     a.tp_rank = m->tp_rank;
     a.tp_world = m->tp_world;
-    a.tp_off_flag = off_flag;
     a.tp_off_best = off_best;
     a.tp_off_bflag = off_bflag;
     a.tp_off_logits = off_logits;

@@ -202,15 +202,15 @@ struct StepArgs {
     unsigned trace_phases;
     /* tensor parallelism: this rank's classifier rows start at cls_row0; with
      * tp_world > 1, tp_box[r] is rank r's exchange buffer (the own one too):
-     * partial rows y [2][world][dim] at 0, CTA flags [2][world][G] at
-     * tp_off_flag, best logit keys [world] at tp_off_best and their flags at
+     * partial rows y [2][world][dim] (64-bit words: sequence number | float)
+     * at 0, best logit keys [world] at tp_off_best and their flags at
      * tp_off_bflag, the logits ring at tp_off_logits. tp_step0: the steps of
-     * earlier launches (flag values grow by one per exchange). */
+     * earlier launches (sequence numbers grow by one per exchange). */
     int cls_row0;
     int tp_rank, tp_world;
     unsigned long long tp_step0;
     unsigned char *tp_box[KC_TP_MAX];
-    unsigned long long tp_off_flag, tp_off_best, tp_off_bflag, tp_off_logits;
+    unsigned long long tp_off_best, tp_off_bflag, tp_off_logits;
 };
 
 /* ------------------------------------------------------------ event log (diagnostics) */
@@ -364,32 +364,52 @@ __device__ __forceinline__ unsigned tp_seq(const StepArgs &a, int step, int l, i
     return (unsigned)((a.tp_step0 + (unsigned long long)step) * (2ull * a.n_layers) + 2ull * l + ph + 1ull);
 }
 
+__device__ __forceinline__ void st_sys_u64(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_sys_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
 /* The residual add after a row-parallel projection (O: ph 0, down: ph 1)
- * across ranks: the CTA's partial rows (its column slices summed in order)
- * go to slot [ph][rank] of every rank's exchange buffer, then one flag per
- * rank; once every rank's flag for this CTA has come, x[row] += the partials
- * summed in rank order. Every rank runs the same grid, so CTA j of every rank
- * owns the same rows of x. */
+ * across ranks. Each partial row travels as one 64-bit word, sequence number
+ * in the high half and the float in the low half: an aligned 8-byte store is
+ * seen whole or not at all, so the word is its own flag and no fence or
+ * barrier sits between the ranks. The thread of row i stores its partial
+ * (the row's column slices summed in order) into slot [ph][rank][row] of every
+ * rank's exchange buffer, then waits in its own buffer for every rank's word
+ * of that row carrying this exchange's number and adds them in rank order:
+ * x[row] += y_0 + y_1 + ... Every rank runs the same grid, so CTA j of every
+ * rank owns the same rows of x; a rank can store the next exchange's words
+ * into a slot only after this rank has passed the exchange in between. */
 __device__ __noinline__ void tp_resid(const StepArgs &a, const float *res, int nrows, int row0, float *out,
                                       float *own, int ns, int ph, unsigned seq) {
-    const int me = a.tp_rank, W = a.tp_world, D = a.dim, G = gridDim.x, c = blockIdx.x;
+    const int me = a.tp_rank, W = a.tp_world, D = a.dim;
     for (int i = threadIdx.x; i < nrows; i += NCT) {
         float sum = res[i * ns];
         for (int k = 1; k < ns; k++) sum = __fadd_rn(sum, res[i * ns + k]);
-        for (int r = 0; r < W; r++) ((float *)a.tp_box[r])[((size_t)ph * W + me) * D + row0 + i] = sum;
+        const unsigned long long word = ((unsigned long long)seq << 32) | __float_as_uint(sum);
+        for (int r = 0; r < W; r++)
+            st_sys_u64((unsigned long long *)a.tp_box[r] + ((size_t)ph * W + me) * D + row0 + i, word);
     }
-    __threadfence_system();
-    consumer_sync();
-    if (threadIdx.x < W) {
-        st_release_sys((unsigned *)(a.tp_box[threadIdx.x] + a.tp_off_flag) + ((size_t)ph * W + me) * G + c, seq);
-        tp_wait((const unsigned *)(a.tp_box[me] + a.tp_off_flag) + ((size_t)ph * W + threadIdx.x) * G + c, seq, a.err);
-        __threadfence_system();
-    }
-    consumer_sync();
-    const float *y = (const float *)a.tp_box[me] + (size_t)ph * W * D;
+    const unsigned long long *y = (const unsigned long long *)a.tp_box[me] + (size_t)ph * W * D;
     for (int i = threadIdx.x; i < nrows; i += NCT) {
-        float tot = __ldcv(y + row0 + i);
-        for (int r = 1; r < W; r++) tot = __fadd_rn(tot, __ldcv(y + (size_t)r * D + row0 + i));
+        float tot = 0.0f;
+        for (int r = 0; r < W; r++) {
+            const unsigned long long *p = y + (size_t)r * D + row0 + i;
+            unsigned long long w = ld_sys_u64(p);
+            for (unsigned it = 0; (unsigned)(w >> 32) != seq; it++) {
+                if (it > (1u << 22) || ((it & 255) == 255 && ld_acquire(a.err))) {
+                    atomicOr(a.err, TP_ERR);
+                    break;
+                }
+                w = ld_sys_u64(p);
+            }
+            const float v = __uint_as_float((unsigned)w);
+            tot = r == 0 ? v : __fadd_rn(tot, v);
+        }
         const float v = __fadd_rn(own[i], tot);
         own[i] = v;
         out[row0 + i] = v;

@@ -287,6 +287,28 @@ def test_baseline_shapes_short(name, prompt_len, steps):
     assert not valid_bad, (valid_bad, spread)
 
 
+def test_cfg4_shape_decode_and_prefill():
+    """BASELINE config 4 (Llama-3-8B shape: head_dim 128, hidden 14336, all Q8_0)
+    on one GPU: a short prompt through the batched prefill and decode steps on its
+    cache, each position against the oracle, with the long-run bound derived from
+    the reference's own SIMD build on the same positions."""
+    path = kb.ensure_model("cfg4", MODEL_CACHE)
+    vocab = kb.Model(path, upload=False).config["vocab"]
+    prompt = np.random.default_rng(4).integers(0, vocab, 6).tolist()
+    m = kb.Model(path)
+    st = kb.State(m)
+    got = np.concatenate([st.prefill(prompt[:4], 0, logits=True),
+                          np.stack([st.forward(prompt[p], p) for p in (4, 5)])])
+    st.free()
+    m.free()
+    ref = oracle.OracleModel(path).prefill(prompt)
+    spread = reference_simd_spread(path, prompt)
+    bound, kl_bound = (5e-2, 1e-3) if spread is None else (max(5e-2, 1.25 * spread[0]), max(1e-3, 1.25 * spread[1]))
+    for i in range(len(prompt)):
+        assert argmax_ok(got[i], ref[i]) and top5_overlap(got[i], ref[i]) >= 4, i
+        assert rel_err(got[i], ref[i]) <= bound and kl(ref[i], got[i]) <= kl_bound, (i, spread)
+
+
 @pytest.mark.parametrize("kv", [kb.F16, kb.Q8_0])
 @pytest.mark.parametrize("name", ["rand_q4", "rand_q8", "mixf16_q4"])
 def test_kv_cache_types_one_step_away(name, kv):
