@@ -239,7 +239,7 @@ def tp_decode(dist, K, W, hbm_peak):
             "parallelism": f"tp{WORLD}", "n_gpus": WORLD, "scaling": "strong", "tok_s": round(tok_s, 2),
             "ms_per_token": round(ms / K, 4), "steps": K, "warmup": W, "bytes_per_token": int(bpt),
             "hbm_frac_per_gpu": round(bpt / WORLD * tok_s / 1e9 / hbm_peak, 4),
-            "exchange": "O and down partials: per-CTA peer stores + flags inside the step kernel (no NCCL on the token path)"}
+            "exchange": "O and down partials as tagged 64-bit NVLink peer stores inside the step kernel (no NCCL on the token path)"}
 
 
 def main():
