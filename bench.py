@@ -367,6 +367,15 @@ def main():
             except Exception as e:   # a KV type this model's head layout cannot use
                 kvs[kvname] = {"error": str(e)}
         extras["decode_by_kv_cache"] = kvs
+        # sampled generation on the device (top-k 40, top-p 0.95, T 0.8, penalty 1.1 over 64): step + sample kernel
+        # per token, no logits copy
+        smp = kb.Sampler(st, temperature=0.8, topk=40, topp=0.95, repeat_penalty=1.1, repeat_last_n=64, seed=1)
+        st.prefill(toks[:-1], 0)
+        t0 = time.perf_counter()
+        st.generate_sampled(smp, start_tok, start_pos, 32)
+        extras["e2e_sampled_device"] = {"value": round(32 / (time.perf_counter() - t0), 2), "unit": "tok/s",
+                                        "sampler": "T 0.8, top-k 40, top-p 0.95, repeat penalty 1.1 / 64"}
+        smp.free()
 
         # prefill (config 3): the batched tensor-core path, wall clock around the
         # whole host call (best of 3, after one call that packs the weights)
@@ -431,7 +440,7 @@ def main():
                                     "prefill_tok_s": round(cpu["prefill_tok_s"], 1)}
         elif cpu:
             line["cpu_baseline"] = cpu
-        for k in ("decode_by_context", "decode_by_kv_cache", "prefill_tok_s", "prefill_roofline"):
+        for k in ("decode_by_context", "decode_by_kv_cache", "e2e_sampled_device", "prefill_tok_s", "prefill_roofline"):
             if k in extras:
                 line[k] = extras[k]
         if tp is not None:

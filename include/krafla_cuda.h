@@ -138,6 +138,34 @@ float *kc_forward(kc_state *s, int token, int pos);
  * the next step's input. out_tokens (host, n ints) receives the n chosen
  * tokens. The ml_run -T 0 / ml_bench decode loop (app/ml_bench.c:125-131). */
 int kc_generate_greedy(kc_state *s, int token, int pos, int n, int *out_tokens);
+/* Sampling on the device (model/sampler.h): the options of ml_sampler_opts,
+ * field for field, so a reference build can pass &opts. */
+typedef struct {
+    float temperature;     /* 0 = greedy */
+    float topp;            /* 0 or 1 = off */
+    int topk;              /* 0 = off */
+    float repeat_penalty;  /* 1 = off */
+    int repeat_last_n;
+    uint64_t seed;         /* 0: the reference's default seed */
+} kc_sampler_opts;
+typedef struct kc_sampler kc_sampler;
+/* Replaces ml_sampler_init (model/sampler.c:6-19) for a state: the xorshift64*
+ * state and the recent-token ring live in device memory. */
+int kc_sampler_init(kc_sampler **out, kc_state *s, const kc_sampler_opts *o);
+/* Replaces ml_sampler_accept (:23-28): records a context token for the penalty. */
+int kc_sampler_accept(kc_sampler *p, int token);
+/* Replaces ml_sample (:157-165) on the logits of the state's last step, on the
+ * device (the logits stay there): penalty, greedy at temperature 0, else
+ * softmax, top-k / top-p / multinomial with the same random stream and tie
+ * rules; records the token as accepted. */
+int kc_sample(kc_sampler *p, int *token);
+/* n tokens from `token` at `pos`: per step one decode step and one device
+ * sample (no logits copy); out_tokens (host, n ints). */
+int kc_generate_sampled(kc_state *s, kc_sampler *p, int token, int pos, int n, int *out_tokens);
+/* The sampler's xorshift64* state (tests and resumption). */
+int kc_sampler_rng(kc_sampler *p, uint64_t *rng);
+void kc_sampler_free(kc_sampler *p);
+
 /* Debug view of the state after the last step: copies a device buffer to the
  * host (which: 0 x [dim], 1 q|k|v before RoPE [q_dim + 2 kv_dim], 2 attention
  * output [q_dim], 3 FFN hidden [hidden_dim], 4 / 5 the K / V cache

@@ -17,6 +17,7 @@
 #include "kc_kernels.cuh"
 #include "kc_step.cuh"
 #include "kc_prefill.h"
+#include "kc_sampler.cuh"
 
 namespace kc {
 static thread_local std::string g_err;
@@ -420,6 +421,8 @@ struct kc_state {
     uint8_t *tp_peer[KC_TP_MAX] = {};
     int tp_connected = 0;
     unsigned long long tp_steps = 0;
+    /* the logits ring row of the last call's last token (kc_sample); -1: none */
+    int last_row = -1;
 };
 
 /* RoPE inverse frequency of pair i (model/transformer.c:16-38; the scaling
@@ -642,6 +645,7 @@ static int launch_steps(kc_state *s, int nsteps, int logits, bool timeline = fal
         set_error("tensor-parallel state not connected (kc_tp_connect)");
         return KC_E_SHAPE;
     }
+    s->last_row = -1;   /* the caller names the row when its last token's logits are kept */
     CK(cudaMemsetAsync(s->bar, 0, sizeof(unsigned), s->st));
     StepArgs a = s->sa;
     a.tp_step0 = s->tp_steps;
@@ -890,8 +894,10 @@ extern "C" float *kc_forward(kc_state *s, int token, int pos) {
     clear_error();
     const kc_config &c = s->c;
     if (pos < 0 || pos >= c.max_seq || token < 0 || token >= c.vocab) return nullptr;
+    s->last_row = -1;
     if (set_loop(s, token, pos, 0) != KC_OK) return nullptr;
     if (run_steps(s, 1, 1) != KC_OK) return nullptr;
+    s->last_row = 0;
     cudaError_t e = cudaMemcpyAsync(s->h_logits, s->logits, sizeof(float) * c.vocab, cudaMemcpyDeviceToHost, s->st);
     if (e != cudaSuccess) { cuda_status(e, "logits copy"); return nullptr; }
     if (finish(s) != KC_OK) return nullptr;
@@ -914,6 +920,7 @@ static int prefill_tokenwise(kc_state *s, const int *tokens, int n, int pos0, fl
             CK(cudaMemcpyAsync(logits + (size_t)i0 * c.vocab, s->logits, sizeof(float) * (size_t)k * c.vocab,
                                cudaMemcpyDeviceToHost, s->st));
     }
+    if (logits) s->last_row = (n - 1) % LOGITS_RING;
     return finish(s);
 }
 
@@ -921,6 +928,7 @@ static int prefill_tokenwise(kc_state *s, const int *tokens, int n, int pos0, fl
  * (tensor-core GEMMs, kc_prefill.cu). */
 static int prefill_batched(kc_state *s, const int *tokens, int n, int pos0, float *logits) {
     const kc_config &c = s->c;
+    s->last_row = -1;
     kc_model *m = s->m;
     std::vector<PfLayerRun> L((size_t)c.n_layers);
     const size_t lkv = (size_t)c.max_seq * c.kv_dim * kv_elem_bytes(s->kv_type);
@@ -989,6 +997,7 @@ extern "C" int kc_generate_greedy(kc_state *s, int token, int pos, int n, int *o
         st = run_steps(s, n - i < 256 ? n - i : 256, 1);
         if (st != KC_OK) return st;
     }
+    s->last_row = (n - 1) % LOGITS_RING;
     CK(cudaMemcpyAsync(out_tokens, s->out_tokens, sizeof(int) * n, cudaMemcpyDeviceToHost, s->st));
     return finish(s);
 }
@@ -1244,3 +1253,140 @@ extern "C" void kc_dev_free(void *p) { if (p) cudaFree(p); }
 extern "C" int kc_memcpy_htod(void *dst, const void *src, size_t n) { CK(cudaMemcpy(dst, src, n, cudaMemcpyHostToDevice)); return KC_OK; }
 extern "C" int kc_memcpy_dtoh(void *dst, const void *src, size_t n) { CK(cudaMemcpy(dst, src, n, cudaMemcpyDeviceToHost)); return KC_OK; }
 extern "C" int kc_dev_sync(void) { CK(cudaDeviceSynchronize()); return KC_OK; }
+
+/* ------------------------------------------------------------------ sampler */
+
+struct kc_sampler {
+    kc_state *s = nullptr;
+    kc_sampler_opts o{};
+    uint8_t *arena = nullptr;
+    SampleArgs a{};
+    SamplerDev host{};        /* mirror of the device state, refreshed after each call */
+    std::vector<int> ring;    /* mirror of the device ring */
+};
+
+extern "C" void kc_sampler_free(kc_sampler *p) {
+    if (!p) return;
+    if (p->arena) cudaFree(p->arena);
+    delete p;
+}
+
+extern "C" int kc_sampler_init(kc_sampler **out, kc_state *s, const kc_sampler_opts *o) {
+    clear_error();
+    *out = nullptr;
+    if (!(o->temperature >= 0.0f) || o->topk < 0) return KC_E_SHAPE;
+    kc_sampler *p = new (std::nothrow) kc_sampler();
+    if (!p) return KC_E_NOMEM;
+    p->s = s;
+    p->o = *o;
+    if (p->o.repeat_last_n < 0) p->o.repeat_last_n = 0;
+    const size_t V = (size_t)s->c.vocab, RL = (size_t)(p->o.repeat_last_n > 0 ? p->o.repeat_last_n : 1);
+    const size_t sz[] = { sizeof(SamplerDev), sizeof(int) * RL, sizeof(float) * V, sizeof(unsigned) * V,
+                          sizeof(unsigned) * V, sizeof(int) * V, sizeof(int) * V, sizeof(int) };
+    size_t total = 0;
+    for (size_t b : sz) total += align256(b);
+    cudaError_t e = cudaMalloc(&p->arena, total);
+    if (e != cudaSuccess) {
+        kc_sampler_free(p);
+        return cuda_status(e, "sampler");
+    }
+    uint8_t *q = p->arena;
+    void *ptr[8];
+    for (int i = 0; i < 8; i++) {
+        ptr[i] = q;
+        q += align256(sz[i]);
+    }
+    SampleArgs &a = p->a;
+    a.vocab = s->c.vocab;
+    a.temperature = p->o.temperature;
+    a.topp = p->o.topp;
+    a.topk = p->o.topk;
+    a.repeat_penalty = p->o.repeat_penalty;
+    a.repeat_last_n = p->o.repeat_last_n;
+    a.st = (SamplerDev *)ptr[0];
+    a.recent = (int *)ptr[1];
+    a.p = (float *)ptr[2];
+    a.ka = (unsigned *)ptr[3];
+    a.kb = (unsigned *)ptr[4];
+    a.va = (int *)ptr[5];
+    a.vb = (int *)ptr[6];
+    a.token_out = (int *)ptr[7];
+    p->host.rng = p->o.seed ? p->o.seed : 0x9E3779B97F4A7C15ull;   /* model/sampler.c:10 */
+    p->ring.assign(RL, 0);
+    e = cudaMemcpy(a.st, &p->host, sizeof p->host, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(a.recent, p->ring.data(), sizeof(int) * RL, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        kc_sampler_free(p);
+        return cuda_status(e, "sampler");
+    }
+    *out = p;
+    return KC_OK;
+}
+
+/* The device state and ring back into the host mirror. */
+static int sampler_pull(kc_sampler *p) {
+    CK(cudaMemcpyAsync(&p->host, p->a.st, sizeof p->host, cudaMemcpyDeviceToHost, p->s->st));
+    CK(cudaMemcpyAsync(p->ring.data(), p->a.recent, sizeof(int) * p->ring.size(), cudaMemcpyDeviceToHost, p->s->st));
+    CK(cudaStreamSynchronize(p->s->st));
+    return KC_OK;
+}
+
+extern "C" int kc_sampler_accept(kc_sampler *p, int token) {
+    clear_error();
+    const int rl = p->o.repeat_last_n;
+    if (rl <= 0 || token < 0 || token >= p->s->c.vocab) return KC_OK;
+    p->ring[(size_t)p->host.recent_at] = token;
+    p->host.recent_at = (p->host.recent_at + 1) % rl;
+    if (p->host.n_recent < rl) p->host.n_recent++;
+    CK(cudaMemcpyAsync(p->a.st, &p->host, sizeof p->host, cudaMemcpyHostToDevice, p->s->st));
+    CK(cudaMemcpyAsync(p->a.recent, p->ring.data(), sizeof(int) * p->ring.size(), cudaMemcpyHostToDevice, p->s->st));
+    CK(cudaStreamSynchronize(p->s->st));
+    return KC_OK;
+}
+
+extern "C" int kc_sampler_rng(kc_sampler *p, uint64_t *rng) {
+    *rng = p->host.rng;
+    return KC_OK;
+}
+
+extern "C" int kc_sample(kc_sampler *p, int *token) {
+    clear_error();
+    kc_state *s = p->s;
+    if (s->last_row < 0) {
+        set_error("no logits of a last token on the device: run kc_forward first");
+        return KC_E_SHAPE;
+    }
+    SampleArgs a = p->a;
+    a.logits = s->logits + (size_t)s->last_row * s->c.vocab;
+    a.ls = nullptr;
+    a.out_tokens = nullptr;
+    sample_kernel<<<1, SM_THREADS, 0, s->st>>>(a);
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(token, a.token_out, sizeof(int), cudaMemcpyDeviceToHost, s->st));
+    return sampler_pull(p);
+}
+
+extern "C" int kc_generate_sampled(kc_state *s, kc_sampler *p, int token, int pos, int n, int *out_tokens) {
+    clear_error();
+    const kc_config &c = s->c;
+    if (p->s != s || n < 0 || pos < 0 || pos + n > c.max_seq || token < 0 || token >= c.vocab) return KC_E_SHAPE;
+    if (n == 0) return KC_OK;
+    int st = set_loop(s, token, pos, 0);
+    if (st != KC_OK) return st;
+    for (int i = 0; i < n; i++) {
+        st = run_steps(s, 1, 1);
+        if (st != KC_OK) return st;
+        SampleArgs a = p->a;
+        a.logits = s->logits + (size_t)(i % LOGITS_RING) * c.vocab;
+        a.ls = s->ls;
+        a.out_tokens = s->out_tokens;
+        sample_kernel<<<1, SM_THREADS, 0, s->st>>>(a);
+        CK(cudaGetLastError());
+    }
+    CK(cudaMemcpyAsync(out_tokens, s->out_tokens, sizeof(int) * n, cudaMemcpyDeviceToHost, s->st));
+    st = finish(s);
+    if (st != KC_OK) return st;
+    s->last_row = (n - 1) % LOGITS_RING;
+    return sampler_pull(p);
+}
+

@@ -79,6 +79,9 @@ def lib():
             "kc_state_init": (I, [C.POINTER(P), P, I, I]), "kc_prefill": (I, [P, P, I, I, P]),
             "kc_set_batch": (I, [P, I]), "kc_model_shard": (I, [P, I, I]), "kc_model_shard_info": (I, [P, P]),
             "kc_set_device": (I, [I]), "kc_tp_handle": (I, [P, P, S]), "kc_tp_connect": (I, [P, P]),
+            "kc_sampler_init": (I, [C.POINTER(P), P, P]), "kc_sampler_accept": (I, [P, I]),
+            "kc_sample": (I, [P, C.POINTER(I)]), "kc_generate_sampled": (I, [P, P, I, I, I, P]),
+            "kc_sampler_rng": (I, [P, C.POINTER(C.c_uint64)]), "kc_sampler_free": (None, [P]),
             "kc_forward": (C.POINTER(F), [P, I, I]), "kc_generate_greedy": (I, [P, I, I, I, P]),
             "kc_state_free": (None, [P]),
             "kc_time_decode": (I, [P, I, I, I, I, C.POINTER(F)]),
@@ -102,6 +105,47 @@ def lib():
 def _check(st, what):
     if st != OK:
         raise KraflaError(st, what)
+
+
+class _SamplerOpts(C.Structure):
+    _fields_ = [("temperature", C.c_float), ("topp", C.c_float), ("topk", C.c_int), ("repeat_penalty", C.c_float),
+                ("repeat_last_n", C.c_int), ("seed", C.c_uint64)]
+
+
+class Sampler:
+    """ml_sampler on the device for a State: kc_sampler_init / accept / kc_sample."""
+
+    def __init__(self, state, temperature=0.0, topp=0.0, topk=0, repeat_penalty=1.0, repeat_last_n=0, seed=0):
+        self.state = state
+        self._h = C.c_void_p()
+        o = _SamplerOpts(temperature, topp, topk, repeat_penalty, repeat_last_n, seed)
+        _check(lib().kc_sampler_init(C.byref(self._h), state._h, C.byref(o)), "sampler init")
+
+    def accept(self, token):
+        _check(lib().kc_sampler_accept(self._h, int(token)), "sampler accept")
+
+    def sample(self):
+        """ml_sample on the state's last logits (on the device)."""
+        t = C.c_int()
+        _check(lib().kc_sample(self._h, C.byref(t)), "sample")
+        return t.value
+
+    @property
+    def rng(self):
+        r = C.c_uint64()
+        lib().kc_sampler_rng(self._h, C.byref(r))
+        return r.value
+
+    def free(self):
+        if self._h:
+            lib().kc_sampler_free(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
 
 
 def set_device(device):
@@ -213,6 +257,13 @@ class State:
         """ml_state.batch: prompt tokens per batched prefill step (1 = token by token)."""
         _check(lib().kc_set_batch(self._h, int(batch)), "set batch")
         return self
+
+    def generate_sampled(self, sampler, token, pos, n):
+        """n tokens from token at pos, each sampled on the device by `sampler`."""
+        out = np.empty(n, np.int32)
+        _check(lib().kc_generate_sampled(self._h, sampler._h, int(token), int(pos), int(n),
+                                         out.ctypes.data_as(C.c_void_p)), "generate sampled")
+        return out
 
     def generate_greedy(self, token, pos, n):
         """n greedy tokens from token at pos, the loop kept on the device."""

@@ -651,3 +651,166 @@ int orc_prefill(orc_state *s, const int *tokens, int n, int pos0, float *logits)
     }
     return ORC_OK;
 }
+
+/* ------------------------------------------------------------------ sampler
+ * model/sampler.c restated: penalty (:30-42), xorshift64* (:44-49), argmax
+ * (:51-55), softmax (kernels/scalar/k_scalar.c:66-77), the multinomial draw
+ * (:57-64), top-k (:80-106; the k best in (p desc, id asc) order), sample_sorted
+ * (:108-131), sample_topp (:133-155). Each call also reports how close the
+ * draw came to a boundary between two tokens (relative to the mass it was
+ * drawn from), so that a test can tell an implementation whose float sums
+ * differ by rounding from one that picks another token. */
+struct orc_sampler {
+    orc_sampler_opts o;
+    uint64_t rng;
+    int vocab, n_recent, recent_at;
+    int *recent;
+    float *probs;
+    int *order;
+};
+
+int orc_sampler_new(orc_sampler **out, int vocab, const orc_sampler_opts *o) {
+    orc_sampler *s = calloc(1, sizeof *s);
+    if (!s) return 4;
+    s->o = *o;
+    if (s->o.repeat_last_n < 0) s->o.repeat_last_n = 0;
+    s->vocab = vocab;
+    s->rng = o->seed ? o->seed : 0x9E3779B97F4A7C15ull;
+    s->recent = calloc((size_t)(s->o.repeat_last_n > 0 ? s->o.repeat_last_n : 1), sizeof(int));
+    s->probs = malloc(sizeof(float) * (size_t)vocab);
+    s->order = malloc(sizeof(int) * (size_t)vocab);
+    if (!s->recent || !s->probs || !s->order) { orc_sampler_free(s); return 4; }
+    *out = s;
+    return 0;
+}
+
+void orc_sampler_free(orc_sampler *s) {
+    if (!s) return;
+    free(s->recent);
+    free(s->probs);
+    free(s->order);
+    free(s);
+}
+
+void orc_sampler_accept(orc_sampler *s, int token) {
+    if (s->o.repeat_last_n <= 0 || token < 0 || token >= s->vocab) return;
+    s->recent[s->recent_at] = token;
+    s->recent_at = (s->recent_at + 1) % s->o.repeat_last_n;
+    if (s->n_recent < s->o.repeat_last_n) s->n_recent++;
+}
+
+uint64_t orc_sampler_rng(const orc_sampler *s) { return s->rng; }
+
+static float orc_coin(uint64_t *st) {
+    uint64_t x = *st;
+    x ^= x >> 12;
+    x ^= x << 25;
+    x ^= x >> 27;
+    *st = x;
+    return (float)((uint32_t)((x * 0x2545F4914F6CDD1Dull) >> 32) >> 8) / 16777216.0f;
+}
+
+static const float *g_sort_p;
+static int by_prob_then_id(const void *a, const void *b) {
+    const int x = *(const int *)a, y = *(const int *)b;
+    if (g_sort_p[x] > g_sort_p[y]) return -1;
+    if (g_sort_p[x] < g_sort_p[y]) return 1;
+    return x - y;
+}
+
+/* distance of r from the two boundaries of the interval it falls in (the
+ * cumulative sums of `seq`, ids into p, m of them, in order), over mass */
+static float draw_margin(const float *p, const int *seq, int m, float r, float mass) {
+    float lo = 0.0f, hi = 0.0f;
+    for (int i = 0; i < m; i++) {
+        hi = lo + p[seq ? seq[i] : i];
+        if (r < hi) break;
+        lo = hi;
+    }
+    const float d = fminf(fabsf(r - lo), fabsf(hi - r));
+    return mass > 0.0f ? d / mass : d;
+}
+
+/* One ml_sample over logits[vocab] (overwritten by the penalty, as the
+ * reference's are); *margin: see above (INFINITY for greedy). */
+int orc_sample(orc_sampler *s, float *logits, float *margin) {
+    const int n = s->vocab;
+    *margin = INFINITY;
+    if (s->o.repeat_penalty != 1.0f)
+        for (int i = 0; i < s->n_recent; i++) {
+            const int t = s->recent[i];
+            int seen = 0;
+            for (int j = 0; j < i; j++) seen |= s->recent[j] == t;
+            if (seen || t >= n) continue;
+            logits[t] = logits[t] > 0.0f ? logits[t] / s->o.repeat_penalty : logits[t] * s->o.repeat_penalty;
+        }
+    if (s->o.temperature == 0.0f) {
+        int best = 0;
+        for (int i = 1; i < n; i++) if (logits[i] > logits[best]) best = i;
+        return best;
+    }
+    float *p = s->probs;
+    for (int i = 0; i < n; i++) p[i] = logits[i] / s->o.temperature;
+    orc_softmax(p, n);
+    const float coin = orc_coin(&s->rng);
+    const float topp = s->o.topp;
+    if (s->o.topk > 0 && s->o.topk < n) {
+        for (int i = 0; i < n; i++) s->order[i] = i;
+        g_sort_p = p;
+        qsort(s->order, (size_t)n, sizeof(int), by_prob_then_id);
+        const int m = s->o.topk;
+        float total = 0.0f;
+        for (int i = 0; i < m; i++) total += p[s->order[i]];
+        int last = m - 1;
+        if (topp > 0.0f && topp < 1.0f) {
+            float cum = 0.0f;
+            for (int i = 0; i < m; i++) {
+                cum += p[s->order[i]];
+                if (cum > topp * total) { last = i; break; }
+            }
+            total = cum;
+        }
+        const float r = coin * total;
+        *margin = draw_margin(p, s->order, last + 1, r, total);
+        float cdf = 0.0f;
+        for (int i = 0; i <= last; i++) {
+            cdf += p[s->order[i]];
+            if (r < cdf) return s->order[i];
+        }
+        return s->order[last];
+    }
+    if (topp <= 0.0f || topp >= 1.0f) {
+        *margin = draw_margin(p, NULL, n, coin, 1.0f);
+        float cdf = 0.0f;
+        for (int i = 0; i < n; i++) {
+            cdf += p[i];
+            if (coin < cdf) return i;
+        }
+        return n - 1;
+    }
+    const float cutoff = n > 1 ? (1.0f - topp) / (float)(n - 1) : 0.0f;
+    int m = 0;
+    for (int i = 0; i < n; i++)
+        if (p[i] >= cutoff) s->order[m++] = i;
+    if (m == 0) {
+        int best = 0;
+        for (int i = 1; i < n; i++) if (p[i] > p[best]) best = i;
+        return best;
+    }
+    g_sort_p = p;
+    qsort(s->order, (size_t)m, sizeof(int), by_prob_then_id);
+    float cum = 0.0f;
+    int last = m - 1;
+    for (int i = 0; i < m; i++) {
+        cum += p[s->order[i]];
+        if (cum > topp) { last = i; break; }
+    }
+    const float r = coin * cum;
+    *margin = draw_margin(p, s->order, last + 1, r, cum);
+    float cdf = 0.0f;
+    for (int i = 0; i <= last; i++) {
+        cdf += p[s->order[i]];
+        if (r < cdf) return s->order[i];
+    }
+    return s->order[last];
+}

@@ -83,4 +83,20 @@ const float *orc_rope_sin(const orc_state *s);
 #ifdef __cplusplus
 }
 #endif
+/* model/sampler.h restated (test infrastructure): options field for field
+ * as ml_sampler_opts. */
+typedef struct {
+    float temperature, topp;
+    int topk;
+    float repeat_penalty;
+    int repeat_last_n;
+    uint64_t seed;
+} orc_sampler_opts;
+typedef struct orc_sampler orc_sampler;
+int orc_sampler_new(orc_sampler **out, int vocab, const orc_sampler_opts *o);
+void orc_sampler_free(orc_sampler *s);
+void orc_sampler_accept(orc_sampler *s, int token);
+uint64_t orc_sampler_rng(const orc_sampler *s);
+int orc_sample(orc_sampler *s, float *logits, float *margin);
+
 #endif

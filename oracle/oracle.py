@@ -43,12 +43,60 @@ def orc():
             "orc_model_config": (None, [P, P]), "orc_state_new": (I, [C.POINTER(P), P, I, I]),
             "orc_state_free": (None, [P]), "orc_forward": (I, [P, I, I, P]), "orc_prefill": (I, [P, P, I, I, P]),
             "orc_state_x": (C.POINTER(F), [P]),
+            "orc_sampler_new": (I, [C.POINTER(P), I, P]), "orc_sampler_free": (None, [P]),
+            "orc_sampler_accept": (None, [P, I]), "orc_sampler_rng": (C.c_uint64, [P]),
+            "orc_sample": (I, [P, P, C.POINTER(F)]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
             f.restype, f.argtypes = res, args
         _orc = L
     return _orc
+
+
+class SamplerOpts(C.Structure):
+    """ml_sampler_opts (model/sampler.h), field for field."""
+    _fields_ = [("temperature", C.c_float), ("topp", C.c_float), ("topk", C.c_int), ("repeat_penalty", C.c_float),
+                ("repeat_last_n", C.c_int), ("seed", C.c_uint64)]
+
+
+def sampler_opts(temperature=0.0, topp=0.0, topk=0, repeat_penalty=1.0, repeat_last_n=0, seed=0):
+    return SamplerOpts(temperature, topp, topk, repeat_penalty, repeat_last_n, seed)
+
+
+class OracleSampler:
+    """The oracle's restatement of the reference sampler: sample() returns the
+    token and the draw's distance from the nearest token boundary (relative)."""
+
+    def __init__(self, vocab, opts):
+        self.h = C.c_void_p()
+        if orc().orc_sampler_new(C.byref(self.h), vocab, C.byref(opts)):
+            raise MemoryError("oracle sampler")
+        self.vocab = vocab
+
+    def accept(self, token):
+        orc().orc_sampler_accept(self.h, int(token))
+
+    def sample(self, logits):
+        lg = np.array(logits, np.float32, copy=True)
+        m = C.c_float()
+        tok = orc().orc_sample(self.h, _ptr(lg), C.byref(m))
+        return int(tok), float(m.value)
+
+    @property
+    def rng(self):
+        return int(orc().orc_sampler_rng(self.h))
+
+    def close(self):
+        if self.h:
+            orc().orc_sampler_free(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def _ptr(a):
@@ -175,6 +223,7 @@ class RefBuild:
             "ref_threads": (I, [P]), "ref_set_batch": (None, [P, I]),
             "ref_quantize_q8": (None, [P, P, P, I]), "ref_quantize_q8_scalar": (None, [P, P, P, I]),
             "ref_matvec_scalar": (None, [P, I, P, P, I, I, P, P, I, I]),
+            "ref_sample_seq": (I, [P, I, P, I, P, I, P, C.POINTER(C.c_uint64)]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -189,3 +238,17 @@ class RefBuild:
         if st:
             raise RuntimeError(f"reference ml_model_load/ml_state_init {path}: status {st}")
         return h
+
+    def sample_seq(self, opts, vocab, context, logits):
+        """The reference's ml_sampler over rows of logits (each choice accepted):
+        (tokens, final rng state)."""
+        lg = np.array(logits, np.float32, copy=True).reshape(-1, vocab)
+        ctx = np.ascontiguousarray(context, np.int32)
+        out = np.zeros(lg.shape[0], np.int32)
+        rng = C.c_uint64()
+        st = self.L.ref_sample_seq(C.byref(opts), vocab, _ptr(ctx), len(ctx), _ptr(lg), lg.shape[0], _ptr(out),
+                                   C.byref(rng))
+        if st:
+            raise RuntimeError(f"reference sampler: status {st}")
+        return out, int(rng.value)
+

@@ -128,3 +128,21 @@ float ref_f16_to_f32(uint16_t h) { return ml_f16_to_f32(h); }
 /* RoPE tables of the state: [max_seq][head_dim/2]. */
 const float *ref_rope_cos(ref_ctx *c) { return c->s.rope_cos; }
 const float *ref_rope_sin(ref_ctx *c) { return c->s.rope_sin; }
+
+/* The reference's own sampler (model/sampler.h): init, accept the context
+ * tokens, then for each logits row ml_sample and accept its choice. */
+#include "model/sampler.h"
+int ref_sample_seq(const ml_sampler_opts *o, int vocab, const int *context, int n_context, float *logits, int rows,
+                   int *out, uint64_t *rng_out) {
+    ml_sampler s;
+    ml_status st = ml_sampler_init(&s, vocab, o);
+    if (st != ML_OK) return st;
+    for (int i = 0; i < n_context; i++) ml_sampler_accept(&s, context[i]);
+    for (int r = 0; r < rows; r++) {
+        out[r] = ml_sample(&s, logits + (size_t)r * vocab, vocab);
+        ml_sampler_accept(&s, out[r]);
+    }
+    *rng_out = s.rng;
+    ml_sampler_free(&s);
+    return ML_OK;
+}
