@@ -413,6 +413,23 @@ __global__ void __launch_bounds__(256) pf_embed_kernel(const PfEmbed a) {
     }
 }
 
+/* Post-norm models: x += RMSNorm(y) * w for every token (model/transformer.c:238-243), one token per CTA. */
+__global__ void __launch_bounds__(256) pf_post_kernel(float *x, const float *y, const float *w, int cols, float eps) {
+    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __shared__ float red[8];
+    const float *yr = y + (size_t)t * cols;
+    float *xr = x + (size_t)t * cols;
+    float ss = 0.0f;
+    for (int i = tid; i < cols; i += 256) ss = __fadd_rn(ss, __fmul_rn(yr[i], yr[i]));
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    ss = red[0];
+    for (int k = 1; k < 8; k++) ss = __fadd_rn(ss, red[k]);
+    const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
+    for (int i = tid; i < cols; i += 256) xr[i] = __fadd_rn(xr[i], __fmul_rn(__fmul_rn(yr[i], inv), w[i]));
+}
+
 struct PfRope {
     float *qkv;                  /* [T][q_dim + 2 kv_dim], q | k | v */
     int ldq;
@@ -422,9 +439,14 @@ struct PfRope {
     int8_t *qq;                  /* Q8 cache: quantized query heads [T][q_dim] */
     float *qd;                   /* their scales [T][n_heads] */
     int pos0, hd, n_heads, n_kv, q_dim, kv_dim, kv_type;
+    const float *q_norm, *k_norm;   /* per-head RMSNorm weights [hd] (qk_norm), or null */
+    float eps;
 };
 
-/* One token per CTA: RoPE on adjacent pairs of every q and k head
+constexpr int PR_MAX_HEADS = 512;   /* query + KV heads a rope CTA normalizes */
+
+/* One token per CTA: with qk_norm the per-head RMSNorm of every q and k head
+ * (model/transformer.c:244-248, before RoPE); RoPE on adjacent pairs of every q and k head
  * (k_scalar.c:79-94) at position pos0 + t, then the K and V rows into the
  * cache in its type (model/transformer.c:188-205: f16 rounding, or the
  * single-scale row quantization per KV head, ops/ops.c:81-96) and, for a Q8
@@ -434,11 +456,29 @@ __global__ void __launch_bounds__(256) pf_rope_kernel(const PfRope a) {
     float *q = a.qkv + (size_t)t * a.ldq, *k = q + a.q_dim, *v = k + a.kv_dim;
     const float *cs = a.rcos + (size_t)p * h2, *sn = a.rsin + (size_t)p * h2;
     const int nq = a.n_heads * h2, nk = a.n_kv * h2;
+    __shared__ float hinv[PR_MAX_HEADS];
+    if (a.q_norm) {
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        for (int h = warp; h < a.n_heads + a.n_kv; h += 8) {
+            const float *x = h < a.n_heads ? q + h * a.hd : k + (h - a.n_heads) * a.hd;
+            float t = 0.0f;
+            for (int i = lane; i < a.hd; i += 32) t = __fadd_rn(t, __fmul_rn(x[i], x[i]));
+            t = warp_sum(t);
+            if (lane == 0) hinv[h] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(t, (float)a.hd), a.eps)));
+        }
+        __syncthreads();
+    }
     for (int idx = threadIdx.x; idx < nq + nk; idx += 256) {
         const bool isq = idx < nq;
         const int r = isq ? idx : idx - nq, h = r / h2, i = r - h * h2;
         float *e = (isq ? q : k) + h * a.hd + 2 * i;
-        const float xa = e[0], xb = e[1], c = cs[i], s = sn[i];
+        float xa = e[0], xb = e[1];
+        const float c = cs[i], s = sn[i];
+        if (a.q_norm) {
+            const float inv = hinv[isq ? h : a.n_heads + h], *w = isq ? a.q_norm : a.k_norm;
+            xa = __fmul_rn(__fmul_rn(xa, inv), w[2 * i]);
+            xb = __fmul_rn(__fmul_rn(xb, inv), w[2 * i + 1]);
+        }
         e[0] = __fsub_rn(__fmul_rn(xa, c), __fmul_rn(xb, s));
         e[1] = __fadd_rn(__fmul_rn(xa, s), __fmul_rn(xb, c));
     }
@@ -774,7 +814,7 @@ struct PfScratch {
     int tc = 0;                  /* tokens per chunk (a multiple of PF_N) */
     size_t npos = 0;
     void *base = nullptr;
-    float *x = nullptr, *qkv = nullptr, *ao = nullptr, *gu = nullptr, *xd = nullptr, *qd = nullptr;
+    float *x = nullptr, *qkv = nullptr, *ao = nullptr, *gu = nullptr, *xd = nullptr, *qd = nullptr, *y = nullptr;
     int8_t *xq = nullptr, *qq = nullptr;
     int *tok = nullptr;
     ~PfScratch() {
@@ -908,6 +948,7 @@ int ensure_scratch(PfScratch *&S, const kc_config &c, int tc, size_t npos) {
     struct B { void **p; size_t bytes; };
     std::vector<B> bufs = {
         { (void **)&S->x, sizeof(float) * T * c.dim },
+        { (void **)&S->y, sizeof(float) * T * c.dim },
         { (void **)&S->qkv, sizeof(float) * T * (size_t)(c.q_dim + 2 * c.kv_dim) },
         { (void **)&S->ao, sizeof(float) * T * c.q_dim },
         { (void **)&S->gu, sizeof(float) * T * 2 * (size_t)c.hidden_dim },
@@ -967,6 +1008,7 @@ int set_attributes(int attn_smem) {
 bool pf_fits(const kc_config &c, int kv_type, int last_pos) {
     const int group = c.n_heads / c.n_kv_heads;
     if (group > PA_MAXG || group * c.head_dim > ATT_MAX_OUT || c.head_dim % 4) return false;
+    if (c.qk_norm && c.n_heads + c.n_kv_heads > PR_MAX_HEADS) return false;
     if (c.dim % QK || c.q_dim % QK || c.hidden_dim % QK) return false;
     if ((c.head_dim * (int)kv_es(kv_type)) % 16) return false;
     return attn_smem_bytes(c, kv_type, (size_t)last_pos + 1) <= PF_ATTN_SMEM_MAX;
@@ -1015,7 +1057,8 @@ int pf_prefill(const PfRun &r, const int *tokens, int n, int pos0, float *logits
             launch_quant(S, S.x, c.dim, L.attn_norm, c.norm_eps, PQ_NORM, c.act, c.dim, T, st);
             launch_gemm(W.qkv, S, T, S.qkv, ldq, PF_STORE, 0.0f, r.err, st);
             PfRope ro{ S.qkv, ldq, L.rcos, L.rsin, L.kc, L.vc, L.kd, L.vd, S.qq, S.qd,
-                       p0, c.head_dim, c.n_heads, c.n_kv_heads, c.q_dim, c.kv_dim, r.kv_type };
+                       p0, c.head_dim, c.n_heads, c.n_kv_heads, c.q_dim, c.kv_dim, r.kv_type,
+                       L.q_norm, L.k_norm, c.norm_eps };
             pf_rope_kernel<<<T, 256, 0, st>>>(ro);
             PfAttn at{ S.qkv, ldq, S.qq, S.qd, L.kc, L.vc, L.kd, L.vd, S.ao,
                        p0, c.head_dim, c.n_heads, c.n_kv_heads, c.q_dim, c.kv_dim, L.window, pad_npos(npos),
@@ -1025,11 +1068,21 @@ int pf_prefill(const PfRun &r, const int *tokens, int n, int pos0, float *logits
             else if (r.kv_type == KC_F16) pf_attn_kernel<KC_F16><<<ag, PA_THREADS, asmem, st>>>(at);
             else pf_attn_kernel<KC_Q8_0><<<ag, PA_THREADS, asmem, st>>>(at);
             launch_quant(S, S.ao, c.q_dim, nullptr, 0.0f, PQ_PLAIN, c.act, c.q_dim, T, st);
-            launch_gemm(W.wo, S, T, S.x, c.dim, PF_RESID, 0.0f, r.err, st);
+            if (L.post_attn) {
+                launch_gemm(W.wo, S, T, S.y, c.dim, PF_STORE, 0.0f, r.err, st);
+                pf_post_kernel<<<T, 256, 0, st>>>(S.x, S.y, L.post_attn, c.dim, c.norm_eps);
+            } else {
+                launch_gemm(W.wo, S, T, S.x, c.dim, PF_RESID, 0.0f, r.err, st);
+            }
             launch_quant(S, S.x, c.dim, L.ffn_norm, c.norm_eps, PQ_NORM, c.act, c.dim, T, st);
             launch_gemm(W.w13, S, T, S.gu, 2 * c.hidden_dim, PF_STORE, 0.0f, r.err, st);
             launch_quant(S, S.gu, 2 * c.hidden_dim, nullptr, 0.0f, PQ_GATED, c.act, c.hidden_dim, T, st);
-            launch_gemm(W.w2, S, T, S.x, c.dim, PF_RESID, 0.0f, r.err, st);
+            if (L.post_ffn) {
+                launch_gemm(W.w2, S, T, S.y, c.dim, PF_STORE, 0.0f, r.err, st);
+                pf_post_kernel<<<T, 256, 0, st>>>(S.x, S.y, L.post_ffn, c.dim, c.norm_eps);
+            } else {
+                launch_gemm(W.w2, S, T, S.x, c.dim, PF_RESID, 0.0f, r.err, st);
+            }
         }
         (void)group;
         PCK(cudaGetLastError(), "prefill launch");

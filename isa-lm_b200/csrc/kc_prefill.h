@@ -19,6 +19,8 @@ struct PfLayerRun {
     float *kd, *vd;
     const float *rcos, *rsin;
     int window;
+    const float *q_norm, *k_norm;          /* per-head RMSNorm before RoPE, or null */
+    const float *post_attn, *post_ffn;     /* RMSNorm of a block's output before the residual add, or null */
 };
 
 struct PfRun {

@@ -162,6 +162,10 @@ extern "C" int kc_model_shard(kc_model *m, int rank, int world) {
     }
     if (world < 1 || world > KC_TP_MAX || rank < 0 || rank >= world) return KC_E_SHAPE;
     if (world == 1) return KC_OK;
+    if (c.post_norms) {
+        set_error("post-norm models do not run tensor parallel");
+        return KC_E_SHAPE;
+    }
     if (c.n_heads % world || c.n_kv_heads % world || (c.q_dim / world) % KC_QK || c.q_dim % world ||
         (c.hidden_dim / world) % KC_QK || c.hidden_dim % world) {
         set_error("heads, q_dim/32 and hidden_dim/32 must divide by the number of ranks");
@@ -393,6 +397,7 @@ struct kc_state {
     cudaStream_t st = nullptr;
     uint8_t *arena = nullptr;
     float *x = nullptr, *qkv = nullptr, *ao = nullptr, *hb = nullptr, *logits = nullptr, *part = nullptr;
+    float *yb = nullptr;   /* post-norm models: the last block's output */
     uint8_t *kc = nullptr, *vc = nullptr;   /* [L][max_seq][kv_dim] of the KV type */
     float *kd = nullptr, *vd = nullptr;     /* Q8 cache scales [L][max_seq][n_kv_heads] */
     float *rcos = nullptr, *rsin = nullptr, *lcos = nullptr, *lsin = nullptr;
@@ -577,6 +582,8 @@ static int setup_step_kernel(kc_state *s) {
         P.kd = s->kd ? s->kd + (size_t)l * lkd : nullptr; P.vd = s->vd ? s->vd + (size_t)l * lkd : nullptr;
         P.rcos = L.local_rope ? s->lcos : s->rcos; P.rsin = L.local_rope ? s->lsin : s->rsin;
         P.window = L.window;
+        P.q_norm = L.q_norm; P.k_norm = L.k_norm;
+        P.post_attn = L.post_attn_norm; P.post_ffn = L.post_ffn_norm;
     }
     int slot = 0, res = 0;
     for (int j = 0; j < G; j++) {
@@ -631,6 +638,8 @@ static int setup_step_kernel(kc_state *s) {
     a.eps = c.norm_eps; a.attn_scale = c.attn_scale; a.attn_softcap = c.attn_softcap; a.final_softcap = c.final_softcap;
     a.embed_scale = c.embed_scale; a.act = c.act;
     a.cls_row0 = m->cls_row0;
+    a.yb = s->yb;
+    a.post_norms = c.post_norms ? 1 : 0;
     a.tp_rank = 0; a.tp_world = 1; a.tp_step0 = 0;
     for (int r = 0; r < KC_TP_MAX; r++) a.tp_box[r] = nullptr;
     a.nsplit = std::min(MAX_NSPLIT, std::max(1, s->num_sms / c.n_kv_heads));
@@ -720,7 +729,10 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
     clear_error();
     if (kv_type != KC_F32 && kv_type != KC_F16 && kv_type != KC_Q8_0) return KC_E_SHAPE;
     const kc_config &c = m->cfg;
-    if (c.qk_norm || c.post_norms) { set_error("qk_norm / post_norms not supported by this build yet"); return KC_E_SHAPE; }
+    if (c.post_norms && m->tp_world > 1) {
+        set_error("post-norm models do not run tensor parallel");
+        return KC_E_SHAPE;
+    }
     const int group = c.n_heads / c.n_kv_heads;
     const int es = (int)kv_elem_bytes(kv_type);
     if (group * c.head_dim > ATT_MAX_OUT || (c.head_dim * es) % 16 || c.head_dim % 16 ||
@@ -747,6 +759,7 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
     struct Buf { void **p; size_t bytes; };
     std::vector<Buf> bufs = {
         { (void **)&s->x, sizeof(float) * c.dim },
+        { (void **)&s->yb, sizeof(float) * c.dim },
         { (void **)&s->qkv, sizeof(float) * (size_t)(c.q_dim + 2 * c.kv_dim) },
         { (void **)&s->ao, sizeof(float) * c.q_dim },
         { (void **)&s->hb, sizeof(float) * c.hidden_dim },
@@ -945,6 +958,10 @@ static int prefill_batched(kc_state *s, const int *tokens, int n, int pos0, floa
         P.rcos = D.local_rope ? s->lcos : s->rcos;
         P.rsin = D.local_rope ? s->lsin : s->rsin;
         P.window = D.window;
+        P.q_norm = D.q_norm;
+        P.k_norm = D.k_norm;
+        P.post_attn = D.post_attn_norm;
+        P.post_ffn = D.post_ffn_norm;
     }
     PfRun r;
     r.m = m;

@@ -54,6 +54,8 @@ struct LayerPlan {
     float *kd, *vd;                 /* Q8 cache: scales [max_seq][n_kv_heads] */
     const float *rcos, *rsin;       /* RoPE tables of this layer */
     int window;
+    const float *q_norm, *k_norm;   /* per-head RMSNorm of q and k before RoPE (Qwen3), or null */
+    const float *post_attn, *post_ffn;   /* RMSNorm of a block's output before the residual add (Gemma 3), or null */
 };
 
 /* ------------------------------------------------------------ the weight stream */
@@ -206,6 +208,8 @@ struct StepArgs {
      * at 0, best logit keys [world] at tp_off_best and their flags at
      * tp_off_bflag, the logits ring at tp_off_logits. tp_step0: the steps of
      * earlier launches (sequence numbers grow by one per exchange). */
+    float *yb;                      /* post-norm models: the last block's output [dim] */
+    int post_norms;
     int cls_row0;
     int tp_rank, tp_world;
     unsigned long long tp_step0;
@@ -976,6 +980,56 @@ __device__ __noinline__ void act_loop(float eps, const float *x, const float *no
     consumer_sync();
 }
 
+/* Post-norm models (model/transformer.c:238-243): the residual stream after a
+ * block is x + RMSNorm(y) * pw, y the block's output (its sum of squares from
+ * the G per-CTA partials in ssp). Every CTA recomputes it for all cols, adds
+ * up its squares and quantizes RMSNorm(x_new) * nw into the activation; the
+ * CTA's own rows of x_new go to own (and into x one phase later, once every
+ * CTA has read the old x). */
+__device__ __noinline__ void act_postnorm(const StepArgs &a, const float *x, const float *y, const float *pw,
+                                          const float *nw, int cols, ActW o, float *red, float *own, int own0,
+                                          int own1) {
+    const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 7) * 4;
+    float t = 0.0f;
+    for (int g = tid; g < (int)gridDim.x; g += NCT) t += __ldcg(a.ssp + g);
+    const float ssy = block_sum(t, red);
+    const float invy = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ssy, (float)cols), a.eps)));
+    auto xn = [&](int i) { return __fadd_rn(__ldcg(x + i), __fmul_rn(__fmul_rn(__ldcg(y + i), invy), pw[i])); };
+    float s2 = 0.0f;
+    for (int i = tid; i < cols; i += NCT) {
+        const float v = xn(i);
+        s2 += v * v;
+    }
+    const float ssx = block_sum(s2, red);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ssx, (float)cols), a.eps)));
+    for (int r = own0 + tid; r < own1; r += NCT) own[r - own0] = xn(r);
+    for (int b0 = 0; b0 < nb; b0 += NCT / 8) {
+        const int b = b0 + (tid >> 3);
+        float u[4] = { 0.0f, 0.0f, 0.0f, 0.0f };
+        if (b < nb)
+            for (int k = 0; k < 4; k++) {
+                const int i = b * QK + j0 + k;
+                u[k] = __fmul_rn(__fmul_rn(xn(i), inv), nw[i]);
+            }
+        put_quant(o, b, nb, j0, u);
+    }
+    consumer_sync();
+}
+
+/* The finish of a post-norm model's O or down projection: the block output
+ * rows (column slices summed in order) into yb and yown, and the CTA's rows of
+ * the residual stream the last prologue computed (own) into x. */
+__device__ __noinline__ void finish_post(const float *res, int nrows, int row0, int ns, float *x, float *yb,
+                                         const float *own, float *yown) {
+    for (int i = threadIdx.x; i < nrows; i += NCT) {
+        float sum = res[i * ns];
+        for (int k = 1; k < ns; k++) sum = __fadd_rn(sum, res[i * ns + k]);
+        yb[row0 + i] = sum;
+        yown[i] = sum;
+        x[row0 + i] = own[i];
+    }
+}
+
 /* act_float for up to 4 * 2048 columns; wider vectors pass by pass. */
 /* wstaged: norm_w already copied into shared memory by prefetch_norm. */
 __device__ __forceinline__ void load_activation(const StepArgs &a, const float *x, const float *norm_w, const float *ssp,
@@ -1097,10 +1151,30 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
     load_tile(t_begin);
     if (tid == 0) ev(0, 21);
     const float *cs = L.rcos + (size_t)pos * h2, *sn = L.rsin + (size_t)pos * h2;
+    /* qk_norm (model/transformer.c:244-248): 1/rms of each query head first */
+    __shared__ float qinv[NCW];
+    if (L.q_norm) {
+        if (warp < group) {
+            const float *qh = a.qkv + (size_t)(g * group + warp) * hd;
+            float t = 0.0f;
+            for (int i = lane; i < hd; i += 32) {
+                const float v = __ldcg(qh + i);
+                t += v * v;
+            }
+            t = warp_sum(t);
+            if (lane == 0) qinv[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)hd), a.eps)));
+        }
+        consumer_sync();
+    }
     for (int idx = tid; idx < group * h2; idx += NCT) {
         const int h = idx / h2, i = idx % h2;
         const float *qh = a.qkv + (size_t)(g * group + h) * hd;
-        const float qa = __ldcg(qh + 2 * i), qb = __ldcg(qh + 2 * i + 1), c = cs[i], s = sn[i];
+        float qa = __ldcg(qh + 2 * i), qb = __ldcg(qh + 2 * i + 1);
+        const float c = cs[i], s = sn[i];
+        if (L.q_norm) {
+            qa = __fmul_rn(__fmul_rn(qa, qinv[h]), L.q_norm[2 * i]);
+            qb = __fmul_rn(__fmul_rn(qb, qinv[h]), L.q_norm[2 * i + 1]);
+        }
         S.sq[h * hd + 2 * i] = __fsub_rn(__fmul_rn(qa, c), __fmul_rn(qb, s));
         S.sq[h * hd + 2 * i + 1] = __fadd_rn(__fmul_rn(qa, s), __fmul_rn(qb, c));
     }
@@ -1109,8 +1183,22 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
     if (t_end == pos + 1 && warp < 2) {
         const float *src = a.qkv + a.q_dim + (warp ? a.kv_dim : 0) + (size_t)g * hd;
         float *row = warp ? S.vnew : S.knew;
+        float kinv = 1.0f;
+        if (warp == 0 && L.k_norm) {
+            float t = 0.0f;
+            for (int i = lane; i < hd; i += 32) {
+                const float v = __ldcg(src + i);
+                t += v * v;
+            }
+            t = warp_sum(t);
+            kinv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)hd), a.eps)));
+        }
         for (int i = lane; i < h2; i += 32) {
-            const float xa = __ldcg(src + 2 * i), xb = __ldcg(src + 2 * i + 1);
+            float xa = __ldcg(src + 2 * i), xb = __ldcg(src + 2 * i + 1);
+            if (warp == 0 && L.k_norm) {
+                xa = __fmul_rn(__fmul_rn(xa, kinv), L.k_norm[2 * i]);
+                xb = __fmul_rn(__fmul_rn(xb, kinv), L.k_norm[2 * i + 1]);
+            }
             if (warp == 0) {
                 row[2 * i] = __fsub_rn(__fmul_rn(xa, cs[i]), __fmul_rn(xb, sn[i]));
                 row[2 * i + 1] = __fadd_rn(__fmul_rn(xa, sn[i]), __fmul_rn(xb, cs[i]));
@@ -1367,6 +1455,7 @@ struct Smem {
     int *flag;
     float *red;
     float *own;
+    float *yown;   /* post-norm models: the CTA's rows of the last block output */
     float *res;
     float *wbuf;   /* the next norm phase's weights, copied in ahead of its barrier */
     unsigned char *act;
@@ -1375,7 +1464,7 @@ struct Smem {
 
 /* res_bytes: a phase's row results (16-byte multiple). */
 __host__ __device__ inline int smem_fixed_bytes(int nstage, int act_bytes, int res_bytes = 0, int wbuf_bytes = 0) {
-    return 16 * nstage + 8 * NCW + 16 + 128 + 4 * OWN_MAX + res_bytes + wbuf_bytes + act_bytes + 128;
+    return 16 * nstage + 8 * NCW + 16 + 128 + 8 * OWN_MAX + res_bytes + wbuf_bytes + act_bytes + 128;
 }
 
 __device__ __forceinline__ Smem carve(unsigned char *smem, int nstage, int act_bytes, int res_bytes = 0,
@@ -1387,7 +1476,8 @@ __device__ __forceinline__ Smem carve(unsigned char *smem, int nstage, int act_b
     s.flag = (int *)(s.cta_best + NCW);
     s.red = (float *)(s.flag + 4);
     s.own = s.red + 32;
-    s.res = s.own + OWN_MAX;
+    s.yown = s.own + OWN_MAX;
+    s.res = s.yown + OWN_MAX;
     s.wbuf = (float *)((unsigned char *)s.res + res_bytes);
     s.act = (unsigned char *)s.wbuf + wbuf_bytes;
     s.ring = (uint8_t *)(((uintptr_t)(s.act + act_bytes) + 127) & ~(uintptr_t)127);
@@ -1457,6 +1547,9 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
                     a.x[r] = e1;
                     sh.own[r - own0] = e1;
                 }
+            } else if (a.post_norms) {
+                act_postnorm(a, a.x, a.yb, a.layers[l - 1].post_ffn, L.attn_norm, a.dim, w_dim, sh.red, sh.own, own0,
+                             own1);
             } else {
                 load_activation(a, a.x, L.attn_norm, a.ssp, a.dim, w_dim, sh.red, sh.wbuf);
             }
@@ -1480,15 +1573,20 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
             trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_C], false, act_view(w_q), sh.res, a.err);
-            if (a.tp_world > 1)
+            if (a.post_norms)
+                finish_post(sh.res, nown, own0, col_slices(a.q_dim / QK, false), a.x, a.yb, sh.own, sh.yown);
+            else if (a.tp_world > 1)
                 tp_resid(a, sh.res, nown, own0, a.x, sh.own, col_slices(a.q_dim / QK, false), 0, tp_seq(a, step, l, 0));
             else
                 finish_phase(FIN_RESID, sh.res, nown, own0, a.x, sh.own, 0, 0.0f, sh.cta_best,
                              col_slices(a.q_dim / QK, false));
             prefetch_norm(sh.wbuf, L.ffn_norm, a.dim);
-            grid_barrier(a, expect, pidx, sh.own, nown);
+            grid_barrier(a, expect, pidx, a.post_norms ? sh.yown : sh.own, nown);
             /* D: gate/up + activation */
-            load_activation(a, a.x, L.ffn_norm, a.ssp, a.dim, w_dim, sh.red, sh.wbuf);
+            if (a.post_norms)
+                act_postnorm(a, a.x, a.yb, L.post_attn, L.ffn_norm, a.dim, w_dim, sh.red, sh.own, own0, own1);
+            else
+                load_activation(a, a.x, L.ffn_norm, a.ssp, a.dim, w_dim, sh.red, sh.wbuf);
             trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_D], true, act_view(w_dim), sh.res, a.err);
@@ -1500,17 +1598,23 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
             trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_E], false, act_view(w_h), sh.res, a.err);
-            if (a.tp_world > 1)
+            if (a.post_norms)
+                finish_post(sh.res, nown, own0, col_slices(a.hidden / QK, false), a.x, a.yb, sh.own, sh.yown);
+            else if (a.tp_world > 1)
                 tp_resid(a, sh.res, nown, own0, a.x, sh.own, col_slices(a.hidden / QK, false), 1, tp_seq(a, step, l, 1));
             else
                 finish_phase(FIN_RESID, sh.res, nown, own0, a.x, sh.own, 0, 0.0f, sh.cta_best,
                              col_slices(a.hidden / QK, false));
             prefetch_norm(sh.wbuf, next_norm, a.dim);
-            grid_barrier(a, expect, pidx, sh.own, nown);
+            grid_barrier(a, expect, pidx, a.post_norms ? sh.yown : sh.own, nown);
         }
         /* F: classifier + argmax */
         if (a.run_cls) {
-            load_activation(a, a.x, a.final_norm, a.ssp, a.dim, w_dim, sh.red, sh.wbuf);
+            if (a.post_norms)
+                act_postnorm(a, a.x, a.yb, a.layers[a.n_layers - 1].post_ffn, a.final_norm, a.dim, w_dim, sh.red,
+                             sh.own, own0, own1);
+            else
+                load_activation(a, a.x, a.final_norm, a.ssp, a.dim, w_dim, sh.red, sh.wbuf);
             trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_F], false, act_view(w_dim), sh.res, a.err);

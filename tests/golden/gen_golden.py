@@ -3,7 +3,7 @@
 Run in a container that has the reference tree (default /root/reference) and
 the reference build of oracle/_ref (make -C oracle ref):
 
-    python tests/golden/gen_golden.py [REFERENCE_ROOT]
+    python tests/golden/gen_golden.py [REFERENCE_ROOT [MODEL ...]]
 
 Fixtures (all small; committed):
   models/*.mlb        models written by the reference's tools/gen_random.py
@@ -51,13 +51,26 @@ MODELS = {
     "swa_q8": ["--wtype", "q8", "--sliding-window", "6", "--seed", "4"],
     "ctx_q4": ["--wtype", "q4", "--dim", "128", "--layers", "2", "--heads", "4", "--kv-heads", "2",
                "--hidden", "256", "--vocab", "96", "--max-seq", "160", "--seed", "11"],
+    # the reference's feature models (Makefile:93-128)
+    "qk_q4": ["--wtype", "q4", "--head-dim", "32", "--qk-norm", "--qkv-bias", "--seed", "4"],
+    "lwin_q8": ["--wtype", "q8", "--layers", "4", "--sliding-window", "5", "--layer-pattern", "2",
+                "--rope-local-theta", "100", "--scales", "f16", "--seed", "5"],
+    "gemma_q4": ["--wtype", "q4", "--layers", "4", "--head-dim", "32", "--qk-norm", "--sliding-window", "5",
+                 "--layer-pattern", "2", "--rope-local-theta", "100", "--gelu", "--post-norms", "--embed-scale", "8",
+                 "--attn-scale", "0.2", "--scales", "f16", "--seed", "4"],
+    "g2_q8": ["--wtype", "q8", "--layers", "4", "--sliding-window", "5", "--layer-pattern", "2", "--gelu",
+              "--post-norms", "--embed-scale", "8", "--attn-scale", "0.25", "--attn-softcap", "2",
+              "--final-softcap", "3", "--scales", "f16", "--seed", "4"],
+    "yarn_q4": ["--wtype", "q4", "--rope-yarn", "4,8", "--seed", "4"],
 }
 
 
-def gen_models():
+def gen_models(only=None):
     os.makedirs(os.path.join(HERE, "models"), exist_ok=True)
     ref = oracle.RefBuild("scalar")
     for name, args in MODELS.items():
+        if only and name not in only:
+            continue
         path = os.path.join(HERE, "models", f"{name}.mlb")
         subprocess.run([sys.executable, os.path.join(REF, "tools", "gen_random.py"), "--out", path, *args], check=True)
         h = ref.open(path, 1, 0, False)
@@ -135,6 +148,8 @@ def gen_writer():
 
 
 if __name__ == "__main__":
-    gen_models()
-    gen_quant()
-    gen_writer()
+    only = sys.argv[2:]   # model names: regenerate just those
+    gen_models(only)
+    if not only:
+        gen_quant()
+        gen_writer()
