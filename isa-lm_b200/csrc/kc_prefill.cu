@@ -516,9 +516,8 @@ __global__ void __launch_bounds__(256) pf_rope_kernel(const PfRope a) {
 /* ------------------------------------------------------------ attention */
 
 constexpr int PA_THREADS = 256;
-constexpr int PA_TILE = 64;                          /* cache positions per shared-memory tile */
+constexpr int PA_ROWS = 32;                          /* query rows (tokens x heads of one KV group) per CTA */
 constexpr int PA_MAXG = 16;                          /* query heads per KV head */
-constexpr int PA_MAXO = ATT_MAX_OUT / PA_THREADS;    /* outputs per thread */
 
 struct PfAttn {
     const float *qkv;            /* rotated query heads at qkv[t * ldq + h * hd] */
@@ -528,190 +527,251 @@ struct PfAttn {
     const void *kc, *vc;
     const float *kd, *vd;
     float *out;                  /* [T][q_dim] */
-    int pos0, hd, n_heads, n_kv, q_dim, kv_dim, window, npos;
+    int T, pos0, hd, n_heads, n_kv, q_dim, kv_dim, window, tq;   /* tq: tokens per CTA */
     float scale, softcap;
 };
 
-/* Shared memory of pf_attn_kernel: query heads, the score rows (npos per
- * head, a multiple of 4), two cache tiles of PA_TILE rows at a pitch of the
- * row's bytes + 16 (16-byte reads of different rows hit different banks),
- * and the Q8 row scales of the two tiles. */
+/* Shared memory of pf_attn_kernel: the CTA's query rows, K and V tiles of pt
+ * positions (double-buffered, rows at a pitch of the row's bytes + 16 so that
+ * 16-byte reads of different rows hit different banks), the tile's scores /
+ * probabilities per row, the rows' running max, sum and rescale, and the Q8
+ * row scales of the tiles. */
 __host__ __device__ inline int pa_pitch(int hd, int es) { return hd * es + 16; }
-__host__ __device__ inline size_t pa_smem_bytes(int group, int hd, int es, int npos) {
-    return sizeof(float) * ((size_t)group * hd + (size_t)group * npos) + 2 * (size_t)PA_TILE * pa_pitch(hd, es) +
-           sizeof(float) * 2 * PA_TILE;
+__host__ __device__ inline size_t pa_smem_bytes(int hd, int es, int pt) {
+    return sizeof(float) * (size_t)PA_ROWS * hd + 4 * (size_t)pt * pa_pitch(hd, es) +
+           sizeof(float) * ((size_t)PA_ROWS * pt + 3 * PA_ROWS + 4 * (size_t)pt);
 }
 
 __device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
-__device__ __forceinline__ float block_reduce(float v, float *red, bool is_max) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    v = is_max ? warp_max(v) : warp_sum(v);
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float r = red[0];
-    for (int w = 1; w < PA_THREADS / 32; w++) r = is_max ? fmaxf(r, red[w]) : __fadd_rn(r, red[w]);
-    return r;
-}
-
-/* Attention of token t (position pos0 + t) for the query heads of KV head g
- * (ops/ops.c:124-180, attend): scores q.k * scale summed over the head
- * dimension in order (Q8 cache: int32 dot of the quantized query and row,
- * (float)s * (qd * scale) * kd), the optional soft-cap, softmax (all -inf:
- * uniform, k_scalar.c:66-77), then out = sum_t p_t * V_t in position order
- * (Q8: (p_t * vd_t) * v). The cache is read in tiles of PA_TILE positions
- * staged through shared memory (cp.async, one tile ahead); the scores of
- * every position stay in shared memory between the passes. */
-template <int KV>
+/* Attention of tq consecutive tokens (positions pos0 + t) for the query heads
+ * of KV head g: ops/ops.c:124-180 (attend) for each of their rows, the cache
+ * read once per CTA for all of them in tiles of PT positions staged through
+ * shared memory (cp.async, one tile ahead). Per row and tile: scores q.k *
+ * scale summed over the head dimension in order (Q8 cache: int32 dot of the
+ * quantized query and row, (float)s * (qd * scale) * kd), the optional
+ * soft-cap, the causal (and sliding-window) mask of the row's position; then
+ * the running softmax (max, exp(s - max), sum) rescales the row's output,
+ * out += sum_t p_t * V_t in position order (Q8: (p_t * vd_t) * v), and the
+ * output is divided by the row's sum at the end. */
+template <int KV, int HD>
 __global__ void __launch_bounds__(PA_THREADS) pf_attn_kernel(const PfAttn a) {
     extern __shared__ __align__(16) unsigned char pa_raw[];
     constexpr int ES = KV == KC_F32 ? 4 : (KV == KC_F16 ? 2 : 1);
-    const int t = blockIdx.x, g = blockIdx.y, tid = threadIdx.x;
-    const int group = a.n_heads / a.n_kv, hd = a.hd, p = a.pos0 + t;
-    const int first = a.window && p >= a.window ? p + 1 - a.window : 0, n = p + 1 - first;
+    constexpr int PT = HD <= 64 ? 64 : 32, hd = HD;
+    const int g = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int group = a.n_heads / a.n_kv;
+    const int t0 = blockIdx.x * a.tq, ntok = min(a.tq, a.T - t0), R = ntok * group;
     const int rowb = hd * ES, pitch = rowb + 16, upr = rowb / 16;
-    float *sq = (float *)pa_raw;                                   /* [group][hd] (Q8: int8 quants) */
-    float *sc = sq + group * hd;                                   /* [group][npos] */
-    unsigned char *tiles = (unsigned char *)(sc + (size_t)group * a.npos);
-    float *srd = (float *)(tiles + 2 * PA_TILE * pitch);           /* [2][PA_TILE] Q8 row scales */
-    __shared__ float red[PA_THREADS / 32];
-    __shared__ float cq[PA_MAXG];
+    float *sq = (float *)pa_raw;                                   /* [PA_ROWS][hd] (Q8: int8 rows) */
+    unsigned char *tiles = (unsigned char *)(sq + PA_ROWS * hd);   /* K0 V0 K1 V1, PT rows each */
+    float *sp = (float *)(tiles + 4 * PT * pitch);                 /* [PA_ROWS][PT] */
+    float *smx = sp + PA_ROWS * PT, *ssum = smx + PA_ROWS, *salpha = ssum + PA_ROWS;
+    float *srd = salpha + PA_ROWS;                                 /* [2 buffers][K, V][PT] Q8 row scales */
+    __shared__ float cq[PA_ROWS];
+    /* row r: token t0 + r / group, query head g * group + r % group */
     if constexpr (KV == KC_Q8_0) {
-        const int8_t *qq = a.qq + (size_t)t * a.q_dim + (size_t)g * group * hd;
-        for (int i = tid; i < group * hd / 4; i += PA_THREADS) ((int *)sq)[i] = ((const int *)qq)[i];
-        if (tid < group) cq[tid] = __fmul_rn(a.qd[(size_t)t * a.n_heads + g * group + tid], a.scale);
+        for (int i = tid; i < R * hd / 4; i += PA_THREADS) {
+            const int r = i / (hd / 4), w = i % (hd / 4);
+            const int8_t *qq = a.qq + (size_t)(t0 + r / group) * a.q_dim + (size_t)(g * group + r % group) * hd;
+            ((int *)sq)[i] = ((const int *)qq)[w];
+        }
+        if (tid < R)
+            cq[tid] = __fmul_rn(a.qd[(size_t)(t0 + tid / group) * a.n_heads + g * group + tid % group], a.scale);
     } else {
-        const float *qsrc = a.qkv + (size_t)t * a.ldq + (size_t)g * group * hd;
-        for (int i = tid; i < group * hd; i += PA_THREADS) sq[i] = qsrc[i];
+        for (int i = tid; i < R * hd; i += PA_THREADS) {
+            const int r = i / hd, d = i % hd;
+            sq[i] = a.qkv[(size_t)(t0 + r / group) * a.ldq + (size_t)(g * group + r % group) * hd + d];
+        }
     }
+    if (tid < PA_ROWS) {
+        smx[tid] = -INFINITY;
+        ssum[tid] = 0.0f;
+    }
+    const int p_first = a.pos0 + t0, p_last = p_first + ntok - 1;
+    const int lo = a.window && p_first >= a.window ? p_first + 1 - a.window : 0;   /* the rows' first position */
+    const int ntiles = (p_last + 1 - lo + PT - 1) / PT;
     const size_t ld = (size_t)a.kv_dim * ES;
     const uint8_t *kbase = (const uint8_t *)a.kc + (size_t)g * rowb, *vbase = (const uint8_t *)a.vc + (size_t)g * rowb;
-    const int ntiles = (n + PA_TILE - 1) / PA_TILE;
-    auto load_tile = [&](const uint8_t *base, const float *rd, int k) {
-        const int t0 = k * PA_TILE, nt = min(PA_TILE, n - t0);
-        unsigned char *dst = tiles + (k & 1) * PA_TILE * pitch;
+    auto load_tile = [&](int k) {
+        const int tp = lo + k * PT, nt = min(PT, p_last + 1 - tp);
+        unsigned char *kd = tiles + (size_t)(2 * (k & 1)) * PT * pitch, *vd = kd + (size_t)PT * pitch;
         for (int u = tid; u < nt * upr; u += PA_THREADS) {
             const int r = u / upr, c = u - r * upr;
-            cp_async16(dst + r * pitch + 16 * c, base + (size_t)(first + t0 + r) * ld + 16 * c);
+            cp_async16(kd + r * pitch + 16 * c, kbase + (size_t)(tp + r) * ld + 16 * c);
+            cp_async16(vd + r * pitch + 16 * c, vbase + (size_t)(tp + r) * ld + 16 * c);
         }
         cp_async_commit();
-        if (KV == KC_Q8_0 && tid < nt) srd[(k & 1) * PA_TILE + tid] = rd[(size_t)(first + t0 + tid) * a.n_kv + g];
+        if (KV == KC_Q8_0 && tid < nt) {
+            srd[(k & 1) * 2 * PT + tid] = a.kd[(size_t)(tp + tid) * a.n_kv + g];
+            srd[(k & 1) * 2 * PT + PT + tid] = a.vd[(size_t)(tp + tid) * a.n_kv + g];
+        }
     };
-    /* scores: thread -> tile position tid % PA_TILE, heads tid / PA_TILE + 4k */
-    load_tile(kbase, a.kd, 0);
+    /* outputs of this thread: dimension tid % hd of rows tid / hd + k * (PA_THREADS / hd) */
+    constexpr int rp = PA_THREADS / HD, NO = PA_ROWS / rp;
+    const int od = tid % hd, or0 = tid / hd;
+    float acc[NO];
+#pragma unroll
+    for (int k = 0; k < NO; k++) acc[k] = 0.0f;
+    load_tile(0);
     for (int k = 0; k < ntiles; k++) {
         if (k + 1 < ntiles) {
-            load_tile(kbase, a.kd, k + 1);
+            load_tile(k + 1);
             cp_async_wait_one();
         } else {
             cp_async_wait_all();
         }
         __syncthreads();
-        const int i = tid & (PA_TILE - 1), nt = min(PA_TILE, n - k * PA_TILE);
-        const unsigned char *row = tiles + (k & 1) * PA_TILE * pitch + i * pitch;
-        if (i < nt) {
-            for (int h = tid / PA_TILE; h < group; h += PA_THREADS / PA_TILE) {
-                float s;
-                if constexpr (KV == KC_Q8_0) {
-                    int isum = 0;
-                    for (int w = 0; w < hd / 4; w++) isum = __dp4a(((const int *)sq)[h * hd / 4 + w], ((const int *)row)[w], isum);
-                    s = __fmul_rn(__fmul_rn((float)isum, cq[h]), srd[(k & 1) * PA_TILE + i]);
-                } else {
-                    float acc = 0.0f;
-                    const float *qh = sq + h * hd;
-                    for (int d0 = 0; d0 < hd; d0 += 4) {
-                        float k4[4];
+        const int tp = lo + k * PT, nt = min(PT, p_last + 1 - tp);
+        const unsigned char *K = tiles + (size_t)(2 * (k & 1)) * PT * pitch, *V = K + (size_t)PT * pitch;
+        const float *rkd = srd + (k & 1) * 2 * PT, *rvd = rkd + PT;
+        /* scores of every (row, position) of the tile, masked by the row's position: thread ->
+         * position tid % PT of rows tid / PT + j * (PA_THREADS / PT), their chains interleaved */
+        {
+            constexpr int RPS = PA_THREADS / PT, NS = PA_ROWS / RPS;
+            const int p = tid % PT, r0 = tid / PT, t = tp + p;
+            const unsigned char *row = K + (size_t)p * pitch;
+            float sc[NS];
+            bool live[NS];
+#pragma unroll
+            for (int j = 0; j < NS; j++) {
+                const int r = r0 + j * RPS, pos = p_first + r / group;
+                const int first = a.window && pos >= a.window ? pos + 1 - a.window : 0;
+                live[j] = r < R && p < nt && t <= pos && t >= first;
+            }
+            if constexpr (KV == KC_Q8_0) {
+                int isum[NS];
+#pragma unroll
+                for (int j = 0; j < NS; j++) isum[j] = 0;
+                for (int w = 0; w < hd / 4; w++) {
+                    const int kw = p < nt ? ((const int *)row)[w] : 0;
+#pragma unroll
+                    for (int j = 0; j < NS; j++)
+                        if (r0 + j * RPS < R) isum[j] = __dp4a(((const int *)sq)[(r0 + j * RPS) * hd / 4 + w], kw, isum[j]);
+                }
+#pragma unroll
+                for (int j = 0; j < NS; j++)
+                    sc[j] = live[j] ? __fmul_rn(__fmul_rn((float)isum[j], cq[r0 + j * RPS]), rkd[p]) : 0.0f;
+            } else {
+#pragma unroll
+                for (int j = 0; j < NS; j++) sc[j] = 0.0f;
+                for (int d0 = 0; d0 < hd; d0 += 4) {
+                    float k4[4] = { 0.0f, 0.0f, 0.0f, 0.0f };
+                    if (p < nt) {
                         if constexpr (KV == KC_F32) {
                             const float4 v = *(const float4 *)(row + 4 * d0);
                             k4[0] = v.x; k4[1] = v.y; k4[2] = v.z; k4[3] = v.w;
                         } else {
                             const uint2 u = *(const uint2 *)(row + 2 * d0);
-                            const float2 lo = __half22float2(*(const __half2 *)&u.x), hi = __half22float2(*(const __half2 *)&u.y);
-                            k4[0] = lo.x; k4[1] = lo.y; k4[2] = hi.x; k4[3] = hi.y;
+                            const float2 l0 = __half22float2(*(const __half2 *)&u.x), h0 = __half22float2(*(const __half2 *)&u.y);
+                            k4[0] = l0.x; k4[1] = l0.y; k4[2] = h0.x; k4[3] = h0.y;
                         }
-                        const float4 q4 = *(const float4 *)(qh + d0);
-                        acc = __fadd_rn(acc, __fmul_rn(q4.x, k4[0]));
-                        acc = __fadd_rn(acc, __fmul_rn(q4.y, k4[1]));
-                        acc = __fadd_rn(acc, __fmul_rn(q4.z, k4[2]));
-                        acc = __fadd_rn(acc, __fmul_rn(q4.w, k4[3]));
                     }
-                    s = __fmul_rn(acc, a.scale);
+#pragma unroll
+                    for (int j = 0; j < NS; j++) {
+                        if (r0 + j * RPS < R) {
+                            const float4 q4 = *(const float4 *)(sq + (r0 + j * RPS) * hd + d0);
+                            sc[j] = __fadd_rn(sc[j], __fmul_rn(q4.x, k4[0]));
+                            sc[j] = __fadd_rn(sc[j], __fmul_rn(q4.y, k4[1]));
+                            sc[j] = __fadd_rn(sc[j], __fmul_rn(q4.z, k4[2]));
+                            sc[j] = __fadd_rn(sc[j], __fmul_rn(q4.w, k4[3]));
+                        }
+                    }
                 }
-                if (a.softcap > 0.0f) s = __fmul_rn(a.softcap, tanhf(__fdiv_rn(s, a.softcap)));
-                sc[(size_t)h * a.npos + k * PA_TILE + i] = s;
+#pragma unroll
+                for (int j = 0; j < NS; j++) sc[j] = __fmul_rn(sc[j], a.scale);
+            }
+#pragma unroll
+            for (int j = 0; j < NS; j++) {
+                const int r = r0 + j * RPS;
+                if (r < R) {
+                    float v = sc[j];
+                    if (live[j] && a.softcap > 0.0f) v = __fmul_rn(a.softcap, tanhf(__fdiv_rn(v, a.softcap)));
+                    sp[r * PT + p] = live[j] ? v : -INFINITY;
+                }
+            }
+        }
+        __syncthreads();
+        /* running softmax: one warp per row */
+        for (int r = warp; r < R; r += PA_THREADS / 32) {
+            float v[PT / 32], mt = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < PT / 32; j++) {
+                v[j] = sp[r * PT + lane + 32 * j];
+                mt = fmaxf(mt, v[j]);
+            }
+            mt = warp_max(mt);
+            const float m_old = smx[r], m_new = fmaxf(m_old, mt);
+            float part = 0.0f;
+#pragma unroll
+            for (int j = 0; j < PT / 32; j++) {
+                const float e = m_new == -INFINITY || v[j] == -INFINITY ? 0.0f : expf(__fsub_rn(v[j], m_new));
+                sp[r * PT + lane + 32 * j] = e;
+                part += e;
+            }
+            part = warp_sum(part);
+            const float alpha = m_new == -INFINITY ? 1.0f : (m_old == -INFINITY ? 0.0f : expf(__fsub_rn(m_old, m_new)));
+            if (lane == 0) {
+                smx[r] = m_new;
+                ssum[r] = __fadd_rn(__fmul_rn(ssum[r], alpha), part);
+                salpha[r] = alpha;
+            }
+        }
+        __syncthreads();
+        /* out = out * alpha + sum_t p_t V_t over the tile, positions in order; the thread's
+         * rows share each V element, their chains interleaved, probabilities read 4 at a time */
+#pragma unroll
+        for (int k2 = 0; k2 < NO; k2++) {
+            const int r = or0 + k2 * rp;
+            if (r < R) acc[k2] = __fmul_rn(acc[k2], salpha[r]);
+        }
+        auto vval = [&](int p) {
+            const unsigned char *row = V + (size_t)p * pitch;
+            if constexpr (KV == KC_F32) return ((const float *)row)[od];
+            else if constexpr (KV == KC_F16) return __half2float(((const __half *)row)[od]);
+            else return (float)((const int8_t *)row)[od];
+        };
+        const int n4 = nt & ~3;
+        for (int p = 0; p < n4; p += 4) {
+            const float v0 = vval(p), v1 = vval(p + 1), v2 = vval(p + 2), v3 = vval(p + 3);
+#pragma unroll
+            for (int k2 = 0; k2 < NO; k2++) {
+                const int r = or0 + k2 * rp;
+                if (r < R) {
+                    float4 w = *(const float4 *)(sp + r * PT + p);
+                    if constexpr (KV == KC_Q8_0) {
+                        w.x = __fmul_rn(w.x, rvd[p]); w.y = __fmul_rn(w.y, rvd[p + 1]);
+                        w.z = __fmul_rn(w.z, rvd[p + 2]); w.w = __fmul_rn(w.w, rvd[p + 3]);
+                    }
+                    float o = acc[k2];
+                    o = __fadd_rn(o, __fmul_rn(w.x, v0));
+                    o = __fadd_rn(o, __fmul_rn(w.y, v1));
+                    o = __fadd_rn(o, __fmul_rn(w.z, v2));
+                    o = __fadd_rn(o, __fmul_rn(w.w, v3));
+                    acc[k2] = o;
+                }
+            }
+        }
+        for (int p = n4; p < nt; p++) {
+            const float vv = vval(p);
+#pragma unroll
+            for (int k2 = 0; k2 < NO; k2++) {
+                const int r = or0 + k2 * rp;
+                if (r < R) {
+                    const float w = KV == KC_Q8_0 ? __fmul_rn(sp[r * PT + p], rvd[p]) : sp[r * PT + p];
+                    acc[k2] = __fadd_rn(acc[k2], __fmul_rn(w, vv));
+                }
             }
         }
         __syncthreads();
     }
-    /* V tile 0 streams in while the softmax runs */
-    load_tile(vbase, a.vd, 0);
-    for (int h = 0; h < group; h++) {
-        float *r = sc + (size_t)h * a.npos;
-        float mx = -INFINITY;
-        for (int i = tid; i < n; i += PA_THREADS) mx = fmaxf(mx, r[i]);
-        mx = block_reduce(mx, red, true);
-        if (mx == -INFINITY) {
-            const float u = __fdiv_rn(1.0f, (float)n);
-            for (int i = tid; i < n; i += PA_THREADS) r[i] = u;
-            continue;
-        }
-        float sum = 0.0f;
-        for (int i = tid; i < n; i += PA_THREADS) {
-            const float e = expf(__fsub_rn(r[i], mx));
-            r[i] = e;
-            sum = __fadd_rn(sum, e);
-        }
-        sum = block_reduce(sum, red, false);
-        const float inv = __fdiv_rn(1.0f, sum);
-        for (int i = tid; i < n; i += PA_THREADS) r[i] = __fmul_rn(r[i], inv);
-    }
-    /* out = sum_t p_t V_t: thread -> outputs tid + k * PA_THREADS, (head, dim) */
-    const int nout = group * hd;
-    float acc[PA_MAXO];
-    int oh[PA_MAXO], od[PA_MAXO];
 #pragma unroll
-    for (int k = 0; k < PA_MAXO; k++) {
-        const int o = tid + k * PA_THREADS;
-        acc[k] = 0.0f;
-        oh[k] = o < nout ? o / hd : 0;
-        od[k] = o < nout ? o % hd : 0;
+    for (int k2 = 0; k2 < NO; k2++) {
+        const int r = or0 + k2 * rp;
+        if (r < R)
+            a.out[(size_t)(t0 + r / group) * a.q_dim + (size_t)(g * group + r % group) * hd + od] =
+                __fdiv_rn(acc[k2], ssum[r]);
     }
-    for (int k = 0; k < ntiles; k++) {
-        if (k + 1 < ntiles) {
-            load_tile(vbase, a.vd, k + 1);
-            cp_async_wait_one();
-        } else {
-            cp_async_wait_all();
-        }
-        __syncthreads();
-        const int nt = min(PA_TILE, n - k * PA_TILE);
-        const unsigned char *T = tiles + (k & 1) * PA_TILE * pitch;
-#pragma unroll
-        for (int kk = 0; kk < PA_MAXO; kk++) {
-            if (tid + kk * PA_THREADS < nout) {
-                const float *pr = sc + (size_t)oh[kk] * a.npos + k * PA_TILE;
-                float s = acc[kk];
-                for (int i = 0; i < nt; i++) {
-                    const unsigned char *row = T + i * pitch;
-                    if constexpr (KV == KC_F32) {
-                        s = __fadd_rn(s, __fmul_rn(pr[i], ((const float *)row)[od[kk]]));
-                    } else if constexpr (KV == KC_F16) {
-                        s = __fadd_rn(s, __fmul_rn(pr[i], __half2float(((const __half *)row)[od[kk]])));
-                    } else {
-                        const float w = __fmul_rn(pr[i], srd[(k & 1) * PA_TILE + i]);
-                        s = __fadd_rn(s, __fmul_rn(w, (float)((const int8_t *)row)[od[kk]]));
-                    }
-                }
-                acc[kk] = s;
-            }
-        }
-        __syncthreads();
-    }
-#pragma unroll
-    for (int k = 0; k < PA_MAXO; k++)
-        if (tid + k * PA_THREADS < nout)
-            a.out[(size_t)t * a.q_dim + (size_t)g * group * hd + oh[k] * hd + od[k]] = acc[k];
 }
 
 /* ------------------------------------------------------------ weight repack */
@@ -934,9 +994,10 @@ int build_cls(kc_model *m, PfModel &P, cudaStream_t st) {
 }
 
 size_t kv_es(int kv_type) { return kv_type == KC_F32 ? 4 : (kv_type == KC_F16 ? 2 : 1); }
-int pad_npos(size_t npos) { return (int)((npos + 3) & ~(size_t)3); }
-int attn_smem_bytes(const kc_config &c, int kv_type, size_t npos) {
-    return (int)pa_smem_bytes(c.n_heads / c.n_kv_heads, c.head_dim, (int)kv_es(kv_type), pad_npos(npos));
+int attn_tile(const kc_config &c) { return c.head_dim <= 64 ? 64 : 32; }
+bool attn_hd_ok(int hd) { return hd == 16 || hd == 32 || hd == 64 || hd == 128; }
+int attn_smem_bytes(const kc_config &c, int kv_type) {
+    return (int)pa_smem_bytes(c.head_dim, (int)kv_es(kv_type), attn_tile(c));
 }
 
 int ensure_scratch(PfScratch *&S, const kc_config &c, int tc, size_t npos) {
@@ -995,10 +1056,20 @@ int set_attributes(int attn_smem) {
         PCK(cudaFuncSetAttribute(pf_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM), "gemm smem");
         done_gemm = 1;
     }
-    PCK(cudaFuncSetAttribute(pf_attn_kernel<KC_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem), "attn");
-    PCK(cudaFuncSetAttribute(pf_attn_kernel<KC_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem), "attn");
-    PCK(cudaFuncSetAttribute(pf_attn_kernel<KC_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem), "attn");
+    const cudaFuncAttribute A = cudaFuncAttributeMaxDynamicSharedMemorySize;
+#define PA_ATTR(KV, HD) PCK(cudaFuncSetAttribute(pf_attn_kernel<KV, HD>, A, attn_smem), "attn")
+    PA_ATTR(KC_F32, 16); PA_ATTR(KC_F32, 32); PA_ATTR(KC_F32, 64); PA_ATTR(KC_F32, 128);
+    PA_ATTR(KC_F16, 16); PA_ATTR(KC_F16, 32); PA_ATTR(KC_F16, 64); PA_ATTR(KC_F16, 128);
+    PA_ATTR(KC_Q8_0, 16); PA_ATTR(KC_Q8_0, 32); PA_ATTR(KC_Q8_0, 64); PA_ATTR(KC_Q8_0, 128);
+#undef PA_ATTR
     return KC_OK;
+}
+
+template <int HD>
+void launch_attn(const PfAttn &at, dim3 grid, int smem, int kv_type, cudaStream_t st) {
+    if (kv_type == KC_F32) pf_attn_kernel<KC_F32, HD><<<grid, PA_THREADS, smem, st>>>(at);
+    else if (kv_type == KC_F16) pf_attn_kernel<KC_F16, HD><<<grid, PA_THREADS, smem, st>>>(at);
+    else pf_attn_kernel<KC_Q8_0, HD><<<grid, PA_THREADS, smem, st>>>(at);
 }
 
 }  // namespace
@@ -1007,11 +1078,12 @@ int set_attributes(int attn_smem) {
  * last_pos; > PF_ATTN_SMEM_MAX means the batched path cannot take it. */
 bool pf_fits(const kc_config &c, int kv_type, int last_pos) {
     const int group = c.n_heads / c.n_kv_heads;
-    if (group > PA_MAXG || group * c.head_dim > ATT_MAX_OUT || c.head_dim % 4) return false;
+    if (group > PA_MAXG || group > PA_ROWS || c.head_dim % 4) return false;
     if (c.qk_norm && c.n_heads + c.n_kv_heads > PR_MAX_HEADS) return false;
     if (c.dim % QK || c.q_dim % QK || c.hidden_dim % QK) return false;
-    if ((c.head_dim * (int)kv_es(kv_type)) % 16) return false;
-    return attn_smem_bytes(c, kv_type, (size_t)last_pos + 1) <= PF_ATTN_SMEM_MAX;
+    (void)last_pos;
+    if ((c.head_dim * (int)kv_es(kv_type)) % 16 || !attn_hd_ok(c.head_dim)) return false;
+    return attn_smem_bytes(c, kv_type) <= PF_ATTN_SMEM_MAX;
 }
 
 void pf_free_model(PfModel *p) { delete p; }
@@ -1041,7 +1113,7 @@ int pf_prefill(const PfRun &r, const int *tokens, int n, int pos0, float *logits
     int rc = ensure_scratch(*r.scratch, c, tc, npos);
     if (rc != KC_OK) return rc;
     PfScratch &S = **r.scratch;
-    const int asmem = attn_smem_bytes(c, r.kv_type, npos);
+    const int asmem = attn_smem_bytes(c, r.kv_type);
     rc = set_attributes(asmem);
     if (rc != KC_OK) return rc;
     const int group = c.n_heads / c.n_kv_heads, ldq = c.q_dim + 2 * c.kv_dim;
@@ -1060,13 +1132,15 @@ int pf_prefill(const PfRun &r, const int *tokens, int n, int pos0, float *logits
                        p0, c.head_dim, c.n_heads, c.n_kv_heads, c.q_dim, c.kv_dim, r.kv_type,
                        L.q_norm, L.k_norm, c.norm_eps };
             pf_rope_kernel<<<T, 256, 0, st>>>(ro);
+            const int tq = std::max(1, PA_ROWS / group);
             PfAttn at{ S.qkv, ldq, S.qq, S.qd, L.kc, L.vc, L.kd, L.vd, S.ao,
-                       p0, c.head_dim, c.n_heads, c.n_kv_heads, c.q_dim, c.kv_dim, L.window, pad_npos(npos),
+                       T, p0, c.head_dim, c.n_heads, c.n_kv_heads, c.q_dim, c.kv_dim, L.window, tq,
                        c.attn_scale, c.attn_softcap };
-            const dim3 ag((unsigned)T, (unsigned)c.n_kv_heads);
-            if (r.kv_type == KC_F32) pf_attn_kernel<KC_F32><<<ag, PA_THREADS, asmem, st>>>(at);
-            else if (r.kv_type == KC_F16) pf_attn_kernel<KC_F16><<<ag, PA_THREADS, asmem, st>>>(at);
-            else pf_attn_kernel<KC_Q8_0><<<ag, PA_THREADS, asmem, st>>>(at);
+            const dim3 ag((unsigned)((T + tq - 1) / tq), (unsigned)c.n_kv_heads);
+            if (c.head_dim == 16) launch_attn<16>(at, ag, asmem, r.kv_type, st);
+            else if (c.head_dim == 32) launch_attn<32>(at, ag, asmem, r.kv_type, st);
+            else if (c.head_dim == 64) launch_attn<64>(at, ag, asmem, r.kv_type, st);
+            else launch_attn<128>(at, ag, asmem, r.kv_type, st);
             launch_quant(S, S.ao, c.q_dim, nullptr, 0.0f, PQ_PLAIN, c.act, c.q_dim, T, st);
             if (L.post_attn) {
                 launch_gemm(W.wo, S, T, S.y, c.dim, PF_STORE, 0.0f, r.err, st);
