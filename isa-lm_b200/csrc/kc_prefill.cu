@@ -653,8 +653,10 @@ __global__ void __launch_bounds__(PA_THREADS) pf_attn_kernel(const PfAttn a) {
                 for (int j = 0; j < NS; j++)
                     sc[j] = live[j] ? __fmul_rn(__fmul_rn((float)isum[j], cq[r0 + j * RPS]), rkd[p]) : 0.0f;
             } else {
+                /* q.k over the head dimension in order, rows in pairs (fma.f32x2) */
+                uint64_t sc2[NS / 2];
 #pragma unroll
-                for (int j = 0; j < NS; j++) sc[j] = 0.0f;
+                for (int j = 0; j < NS / 2; j++) sc2[j] = 0ull;
                 for (int d0 = 0; d0 < hd; d0 += 4) {
                     float k4[4] = { 0.0f, 0.0f, 0.0f, 0.0f };
                     if (p < nt) {
@@ -667,17 +669,20 @@ __global__ void __launch_bounds__(PA_THREADS) pf_attn_kernel(const PfAttn a) {
                             k4[0] = l0.x; k4[1] = l0.y; k4[2] = h0.x; k4[3] = h0.y;
                         }
                     }
+                    const uint64_t kk0 = f2pack(k4[0], k4[0]), kk1 = f2pack(k4[1], k4[1]);
+                    const uint64_t kk2 = f2pack(k4[2], k4[2]), kk3 = f2pack(k4[3], k4[3]);
 #pragma unroll
-                    for (int j = 0; j < NS; j++) {
-                        if (r0 + j * RPS < R) {
-                            const float4 q4 = *(const float4 *)(sq + (r0 + j * RPS) * hd + d0);
-                            sc[j] = __fadd_rn(sc[j], __fmul_rn(q4.x, k4[0]));
-                            sc[j] = __fadd_rn(sc[j], __fmul_rn(q4.y, k4[1]));
-                            sc[j] = __fadd_rn(sc[j], __fmul_rn(q4.z, k4[2]));
-                            sc[j] = __fadd_rn(sc[j], __fmul_rn(q4.w, k4[3]));
-                        }
+                    for (int j = 0; j < NS / 2; j++) {
+                        const float4 qa = *(const float4 *)(sq + (r0 + 2 * j * RPS) * hd + d0);
+                        const float4 qb = *(const float4 *)(sq + (r0 + (2 * j + 1) * RPS) * hd + d0);
+                        sc2[j] = f2fma(f2pack(qa.x, qb.x), kk0, sc2[j]);
+                        sc2[j] = f2fma(f2pack(qa.y, qb.y), kk1, sc2[j]);
+                        sc2[j] = f2fma(f2pack(qa.z, qb.z), kk2, sc2[j]);
+                        sc2[j] = f2fma(f2pack(qa.w, qb.w), kk3, sc2[j]);
                     }
                 }
+#pragma unroll
+                for (int j = 0; j < NS / 2; j++) f2unpack(sc2[j], sc[2 * j], sc[2 * j + 1]);
 #pragma unroll
                 for (int j = 0; j < NS; j++) sc[j] = __fmul_rn(sc[j], a.scale);
             }
@@ -731,38 +736,46 @@ __global__ void __launch_bounds__(PA_THREADS) pf_attn_kernel(const PfAttn a) {
             else if constexpr (KV == KC_F16) return __half2float(((const __half *)row)[od]);
             else return (float)((const int8_t *)row)[od];
         };
+        /* rows in pairs: acc2 = fma((p_r0, p_r1), (v, v), acc2), positions in order */
+        uint64_t acc2[NO / 2];
+#pragma unroll
+        for (int k2 = 0; k2 < NO / 2; k2++) acc2[k2] = f2pack(acc[2 * k2], acc[2 * k2 + 1]);
         const int n4 = nt & ~3;
         for (int p = 0; p < n4; p += 4) {
             const float v0 = vval(p), v1 = vval(p + 1), v2 = vval(p + 2), v3 = vval(p + 3);
+            const uint64_t vv0 = f2pack(v0, v0), vv1 = f2pack(v1, v1), vv2 = f2pack(v2, v2), vv3 = f2pack(v3, v3);
 #pragma unroll
-            for (int k2 = 0; k2 < NO; k2++) {
-                const int r = or0 + k2 * rp;
-                if (r < R) {
-                    float4 w = *(const float4 *)(sp + r * PT + p);
-                    if constexpr (KV == KC_Q8_0) {
-                        w.x = __fmul_rn(w.x, rvd[p]); w.y = __fmul_rn(w.y, rvd[p + 1]);
-                        w.z = __fmul_rn(w.z, rvd[p + 2]); w.w = __fmul_rn(w.w, rvd[p + 3]);
-                    }
-                    float o = acc[k2];
-                    o = __fadd_rn(o, __fmul_rn(w.x, v0));
-                    o = __fadd_rn(o, __fmul_rn(w.y, v1));
-                    o = __fadd_rn(o, __fmul_rn(w.z, v2));
-                    o = __fadd_rn(o, __fmul_rn(w.w, v3));
-                    acc[k2] = o;
+            for (int k2 = 0; k2 < NO / 2; k2++) {
+                const int ra = min(or0 + 2 * k2 * rp, R - 1), rb = min(or0 + (2 * k2 + 1) * rp, R - 1);
+                float4 wa = *(const float4 *)(sp + ra * PT + p), wb = *(const float4 *)(sp + rb * PT + p);
+                if constexpr (KV == KC_Q8_0) {
+                    wa.x = __fmul_rn(wa.x, rvd[p]); wa.y = __fmul_rn(wa.y, rvd[p + 1]);
+                    wa.z = __fmul_rn(wa.z, rvd[p + 2]); wa.w = __fmul_rn(wa.w, rvd[p + 3]);
+                    wb.x = __fmul_rn(wb.x, rvd[p]); wb.y = __fmul_rn(wb.y, rvd[p + 1]);
+                    wb.z = __fmul_rn(wb.z, rvd[p + 2]); wb.w = __fmul_rn(wb.w, rvd[p + 3]);
                 }
+                acc2[k2] = f2fma(f2pack(wa.x, wb.x), vv0, acc2[k2]);
+                acc2[k2] = f2fma(f2pack(wa.y, wb.y), vv1, acc2[k2]);
+                acc2[k2] = f2fma(f2pack(wa.z, wb.z), vv2, acc2[k2]);
+                acc2[k2] = f2fma(f2pack(wa.w, wb.w), vv3, acc2[k2]);
             }
         }
         for (int p = n4; p < nt; p++) {
             const float vv = vval(p);
+            const uint64_t v2 = f2pack(vv, vv);
 #pragma unroll
-            for (int k2 = 0; k2 < NO; k2++) {
-                const int r = or0 + k2 * rp;
-                if (r < R) {
-                    const float w = KV == KC_Q8_0 ? __fmul_rn(sp[r * PT + p], rvd[p]) : sp[r * PT + p];
-                    acc[k2] = __fadd_rn(acc[k2], __fmul_rn(w, vv));
+            for (int k2 = 0; k2 < NO / 2; k2++) {
+                const int ra = min(or0 + 2 * k2 * rp, R - 1), rb = min(or0 + (2 * k2 + 1) * rp, R - 1);
+                float wa = sp[ra * PT + p], wb = sp[rb * PT + p];
+                if constexpr (KV == KC_Q8_0) {
+                    wa = __fmul_rn(wa, rvd[p]);
+                    wb = __fmul_rn(wb, rvd[p]);
                 }
+                acc2[k2] = f2fma(f2pack(wa, wb), v2, acc2[k2]);
             }
         }
+#pragma unroll
+        for (int k2 = 0; k2 < NO / 2; k2++) f2unpack(acc2[k2], acc[2 * k2], acc[2 * k2 + 1]);
         __syncthreads();
     }
 #pragma unroll
