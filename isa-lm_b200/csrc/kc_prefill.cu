@@ -104,6 +104,14 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
         : "r"(taddr));
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tc_st16(uint32_t taddr, uint32_t v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(
+            taddr),
+        "r"(v)
+        : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 /* Pairs of floats in one 64-bit register for the paired FP32 instructions
  * (add/sub/mul/fma .f32x2): each lane of the pair rounds as the scalar
@@ -134,10 +142,10 @@ __device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
 /* An int32 with |s| < 2^22 as a float, exactly, without the conversion unit:
  * the bits 0x4B400000 + s are the float 1.5 * 2^23 + s (the mantissa of
  * 1.5 * 2^23 has ulp 1 and room for s on either side), and subtracting
- * 1.5 * 2^23 leaves s. A 32-element int8 block dot is at most 32 * 127 * 127. */
+ * 1.5 * 2^23 leaves s. A 32-element int8 block dot is at most 32 * 127 * 127.
+ * The GEMM's TMEM accumulators start at these bits, so the MMA itself adds s. */
 constexpr int PF_MAGIC_BITS = 0x4B400000;
 constexpr float PF_MAGIC = 12582912.0f;
-__device__ __forceinline__ float magic_float(uint32_t s) { return __int_as_float((int)s + PF_MAGIC_BITS); }
 
 /* Error bit of the prefill kernels: a pipeline wait gave up. */
 constexpr unsigned PF_ERR_WAIT = 4u;
@@ -220,7 +228,8 @@ __global__ void __launch_bounds__(PF_THREADS, 2) pf_gemm_kernel(const __grid_con
                     atomicOr(g.err, PF_ERR_WAIT);
                     break;
                 }
-                if (!mbar_wait(&tempty[buf], ((ks / PF_NBUF) & 1) ^ 1, g.err)) {
+                /* the epilogue fills each buffer with the bias before its every use */
+                if (!mbar_wait(&tempty[buf], (ks / PF_NBUF) & 1, g.err)) {
                     atomicOr(g.err, PF_ERR_WAIT);
                     break;
                 }
@@ -228,8 +237,8 @@ __global__ void __launch_bounds__(PF_THREADS, 2) pf_gemm_kernel(const __grid_con
                 const uint32_t a = smem_u32(sm + s * PF_STAGE) + j * PF_A_BLK;
                 const uint32_t b = smem_u32(sm + s * PF_STAGE + OFF_B) + j * PF_B_BLK;
                 const uint32_t d = tmem + (uint32_t)(buf * 2 * PF_N);
-                tc_mma_i8(d, umma_desc(a), umma_desc(b), PF_IDESC, 0u);
-                if (kb + 1 < nbk) tc_mma_i8(d + PF_N, umma_desc(a + PF_A_BLK), umma_desc(b + PF_B_BLK), PF_IDESC, 0u);
+                tc_mma_i8(d, umma_desc(a), umma_desc(b), PF_IDESC, 1u);
+                if (kb + 1 < nbk) tc_mma_i8(d + PF_N, umma_desc(a + PF_A_BLK), umma_desc(b + PF_B_BLK), PF_IDESC, 1u);
                 tc_commit(&tfull[buf]);
                 if (j + 2 == PF_KB || kb + 2 >= nbk) tc_commit(&empty[s]);
             }
@@ -247,6 +256,17 @@ __global__ void __launch_bounds__(PF_THREADS, 2) pf_gemm_kernel(const __grid_con
         const uint64_t magic2 = f2pack(PF_MAGIC, PF_MAGIC);
         const int nks = (nbk + 1) / 2;
         bool ok = true;
+        /* every TMEM buffer starts as the int32 bits of 1.5 * 2^23: the MMAs add
+         * their block dots to it, so each word read back is the float 1.5 * 2^23 + s */
+        for (int b = 0; b < PF_NBUF; b++) {
+            tc_st16(tq + (uint32_t)(b * 2 * PF_N), (uint32_t)PF_MAGIC_BITS);
+            tc_st16(tq + (uint32_t)(b * 2 * PF_N + PF_N), (uint32_t)PF_MAGIC_BITS);
+        }
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0)
+            for (int b = 0; b < PF_NBUF; b++) mbar_arrive(&tempty[b]);
         /* acc = fma((float)s, d_w * d_x, acc) for K block j of the stage, two columns per instruction */
         auto accumulate = [&](const uint32_t (&v)[PF_COLS], const unsigned char *stage, int j) {
             const float dw = ((const float *)(stage + OFF_DW))[j * PF_M + q * 32 + lane];
@@ -256,8 +276,8 @@ __global__ void __launch_bounds__(PF_THREADS, 2) pf_gemm_kernel(const __grid_con
             for (int i = 0; i < PF_COLS / 4; i++) {
                 const float4 x = dx4[i];
                 const uint64_t m01 = f2mul(dw2, f2pack(x.x, x.y)), m23 = f2mul(dw2, f2pack(x.z, x.w));
-                const uint64_t s01 = f2sub(f2pack(magic_float(v[4 * i]), magic_float(v[4 * i + 1])), magic2);
-                const uint64_t s23 = f2sub(f2pack(magic_float(v[4 * i + 2]), magic_float(v[4 * i + 3])), magic2);
+                const uint64_t s01 = f2sub(f2pack(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1])), magic2);
+                const uint64_t s23 = f2sub(f2pack(__uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3])), magic2);
                 acc[2 * i] = f2fma(s01, m01, acc[2 * i]);
                 acc[2 * i + 1] = f2fma(s23, m23, acc[2 * i + 1]);
             }
@@ -277,6 +297,9 @@ __global__ void __launch_bounds__(PF_THREADS, 2) pf_gemm_kernel(const __grid_con
             tc_ld16(tq + (uint32_t)(buf * 2 * PF_N), va);
             tc_ld16(tq + (uint32_t)(buf * 2 * PF_N + PF_N), vb);
             tc_wait_ld();
+            tc_st16(tq + (uint32_t)(buf * 2 * PF_N), (uint32_t)PF_MAGIC_BITS);
+            tc_st16(tq + (uint32_t)(buf * 2 * PF_N + PF_N), (uint32_t)PF_MAGIC_BITS);
+            tc_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[buf]);
