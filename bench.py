@@ -297,18 +297,25 @@ def main():
     value = WORLD * K / (ms_max / 1000.0)
     bpt, gemv_bytes = model_bytes_per_token(cfg, ctx + W + K // 2)
 
-    # --- e2e: the drop-in API with host buffers (kc_forward + host argmax, ml_bench's loop)
+    # --- e2e: the drop-in C ABI with host buffers, ml_bench's loop (app/ml_bench.c:125-131):
+    # kc_forward returns the state's host logits buffer, the host takes the argmax over it
     st.prefill(toks[:-1], 0)
+    fwd, vocab = kb.lib().kc_forward, cfg["vocab"]
+
+    def step(tok, pos):
+        ptr = fwd(st._h, tok, pos)
+        if not ptr:
+            raise RuntimeError("kc_forward failed: " + kb.what_detail())
+        return int(np.argmax(np.ctypeslib.as_array(ptr, shape=(vocab,))))
+
     tok, pos = start_tok, start_pos
     for _ in range(W):
-        lg = st.forward(tok, pos)
-        tok, pos = int(np.argmax(lg)), pos + 1
+        tok, pos = step(tok, pos), pos + 1
     if dist is not None:
         dist.barrier()
     t0 = time.perf_counter()
     for _ in range(K):
-        lg = st.forward(tok, pos)
-        tok, pos = int(np.argmax(lg)), pos + 1
+        tok, pos = step(tok, pos), pos + 1
     e2e_s = dist_max(dist, time.perf_counter() - t0)
     e2e = WORLD * K / e2e_s
     # device-resident greedy loop through the C ABI (host tokens in and out)

@@ -408,6 +408,7 @@ struct kc_state {
     int *feed = nullptr, *out_tokens = nullptr;
     float *h_logits = nullptr;
     LoopState *h_ls = nullptr;
+    unsigned *h_err = nullptr;   /* pinned copy of the device error word */
     int num_sms = 148;
     /* the persistent step kernel */
     LayerPlan *d_plan = nullptr;
@@ -714,6 +715,7 @@ extern "C" void kc_state_free(kc_state *s) {
     if (s->arena) cudaFree(s->arena);
     if (s->h_logits) cudaFreeHost(s->h_logits);
     if (s->h_ls) cudaFreeHost(s->h_ls);
+    if (s->h_err) cudaFreeHost(s->h_err);
     if (s->d_plan) cudaFree(s->d_plan);
     for (int r = 0; r < KC_TP_MAX; r++)
         if (s->tp_peer[r]) cudaIpcCloseMemHandle(s->tp_peer[r]);
@@ -804,6 +806,7 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
     if (e != cudaSuccess) return fail(cuda_status(e, "memset"));
     e = cudaMallocHost(&s->h_logits, sizeof(float) * c.vocab);
     if (e == cudaSuccess) e = cudaMallocHost(&s->h_ls, sizeof(LoopState));
+    if (e == cudaSuccess) e = cudaMallocHost(&s->h_err, sizeof(unsigned));
     if (e != cudaSuccess) return fail(cuda_status(e, "pinned host buffers"));
 
     /* RoPE tables: double, stored as float (model/transformer.c:146-162) */
@@ -888,10 +891,11 @@ static int set_loop(kc_state *s, int token, int pos, int feed_mode) {
 }
 
 static int finish(kc_state *s) {
-    unsigned err = 0;
+    /* both words into pinned memory: the copies stay asynchronous, one wait */
     CK(cudaMemcpyAsync(s->h_ls, s->ls, sizeof(LoopState), cudaMemcpyDeviceToHost, s->st));
-    CK(cudaMemcpyAsync(&err, s->err, sizeof err, cudaMemcpyDeviceToHost, s->st));
+    CK(cudaMemcpyAsync(s->h_err, s->err, sizeof(unsigned), cudaMemcpyDeviceToHost, s->st));
     CK(cudaStreamSynchronize(s->st));
+    const unsigned err = *s->h_err;
     if (s->h_ls->err) {
         set_error("a kernel saw a token or position out of range");
         return KC_E_SHAPE;
