@@ -1302,8 +1302,10 @@ extern "C" int kc_sampler_init(kc_sampler **out, kc_state *s, const kc_sampler_o
     p->o = *o;
     if (p->o.repeat_last_n < 0) p->o.repeat_last_n = 0;
     const size_t V = (size_t)s->c.vocab, RL = (size_t)(p->o.repeat_last_n > 0 ? p->o.repeat_last_n : 1);
+    /* the spare key buffer also holds the selection's candidates (SM_TOPK_MAX 64-bit words) */
+    const size_t KB = std::max(sizeof(unsigned) * V, sizeof(unsigned long long) * SM_TOPK_MAX);
     const size_t sz[] = { sizeof(SamplerDev), sizeof(int) * RL, sizeof(float) * V, sizeof(unsigned) * V,
-                          sizeof(unsigned) * V, sizeof(int) * V, sizeof(int) * V, sizeof(int) };
+                          KB, sizeof(int) * V, sizeof(int) * V, sizeof(int) };
     size_t total = 0;
     for (size_t b : sz) total += align256(b);
     cudaError_t e = cudaMalloc(&p->arena, total);

@@ -10,9 +10,12 @@
  *                 (kernels/scalar/k_scalar.c:66-77, all -inf -> uniform);
  *   coin          xorshift64* (:44-49), the same integer stream as the host;
  *   top-k / top-p the tokens ordered by probability, ties by lower id
- *                 (cmp_desc, :73-78): a stable LSD radix sort of all tokens on
- *                 the probability's bits, then the reference's sample_sorted /
- *                 sample_topp on the ordered prefix by one thread, in order;
+ *                 (cmp_desc, :73-78): the k best (top-k), or the tokens at
+ *                 or above the top-p cutoff (top-p alone), by a radix select
+ *                 of the k-th key and a bitonic sort of the k; past 2048 of
+ *                 them, a stable LSD radix sort of all tokens on the
+ *                 probability's bits; then the reference's sample_sorted by
+ *                 one thread, or sample_topp's running sums in blocks;
  *   multinomial   neither: the first token whose cumulative probability
  *                 exceeds the coin (:63-70).
  * The sums over all tokens (softmax, the multinomial prefix) are block
@@ -133,6 +136,90 @@ __device__ void sm_radix_sort(unsigned *ka, int *va, unsigned *kb, int *vb, int 
     /* four passes: the result is back in the caller's (ka, va) */
 }
 
+constexpr int SM_TOPK_MAX = 2048;   /* top-k by selection up to this k; the full sort beyond */
+
+/* The k smallest keys (ties by lower id) of ka[0, n), ascending by (key, id),
+ * into cand[0, k) as key << 32 | id: an MSB-first radix select of the k-th key
+ * (4 histogram passes), every key below it and the lowest ids equal to it, then
+ * a bitonic sort in shared memory. k <= SM_TOPK_MAX. */
+__device__ void sm_topk_select(const unsigned *ka, int n, int k, unsigned long long *cand, int *hist, int *s_cnt) {
+    const int tid = threadIdx.x;
+    __shared__ unsigned s_prefix, s_mask;
+    __shared__ int s_k;
+    if (tid == 0) {
+        s_prefix = 0u;
+        s_mask = 0u;
+        s_k = k;
+    }
+    __syncthreads();
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = tid; i < 256; i += SM_THREADS) hist[i] = 0;
+        __syncthreads();
+        const unsigned prefix = s_prefix, mask = s_mask;
+        for (int i = tid; i < n; i += SM_THREADS) {
+            const unsigned key = ka[i];
+            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            int kk = s_k, d = 0;
+            for (; d < 255 && hist[d] < kk; d++) kk -= hist[d];
+            s_k = kk;
+            s_prefix = prefix | ((unsigned)d << shift);
+            s_mask = mask | (255u << shift);
+        }
+        __syncthreads();
+    }
+    const unsigned T = s_prefix;
+    const int kk = s_k;   /* ids with key == T to take, the lowest first */
+    /* keys below T: any order (sorted below); keys equal to T: the first kk by id */
+    if (tid == 0) *s_cnt = 0;
+    const int chunk = (n + SM_THREADS - 1) / SM_THREADS, lo = tid * chunk, hi = min(n, lo + chunk);
+    int eq = 0;
+    for (int i = lo; i < hi; i++) eq += ka[i] == T;
+    __syncthreads();
+    int *eqs = hist;   /* per-thread counts of keys equal to T, then their exclusive prefix */
+    eqs[tid] = eq;
+    __syncthreads();
+    if (tid == 0) {
+        int s = 0;
+        for (int t = 0; t < SM_THREADS; t++) {
+            const int c = eqs[t];
+            eqs[t] = s;
+            s += c;
+        }
+    }
+    __syncthreads();
+    int rank = eqs[tid];
+    for (int i = lo; i < hi; i++) {
+        const unsigned key = ka[i];
+        if (key < T || (key == T && rank++ < kk)) {
+            const int at = atomicAdd(s_cnt, 1);
+            if (at < SM_TOPK_MAX) cand[at] = ((unsigned long long)key << 32) | (unsigned)i;
+        }
+    }
+    __syncthreads();
+    int m = 1;
+    while (m < k) m <<= 1;
+    for (int i = k + tid; i < m; i += SM_THREADS) cand[i] = ~0ull;
+    __syncthreads();
+    for (int size = 2; size <= m; size <<= 1)
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = tid; i < m; i += SM_THREADS) {
+                const int j = i ^ stride;
+                if (j > i) {
+                    const bool up = (i & size) == 0;
+                    const unsigned long long x = cand[i], y = cand[j];
+                    if ((x > y) == up) {
+                        cand[i] = y;
+                        cand[j] = x;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+}
+
 /* xorshift64*, uniform in [0, 1): model/sampler.c:44-49 */
 __device__ __forceinline__ float sm_random_f32(unsigned long long *st) {
     unsigned long long x = *st;
@@ -212,18 +299,42 @@ __global__ void __launch_bounds__(SM_THREADS, 1) sample_kernel(const SampleArgs 
         const float coin = s_coin;
         const bool use_k = a.topk > 0 && a.topk < n, use_p = a.topp > 0.0f && a.topp < 1.0f;
         if (use_k || use_p) {
-            /* every token by probability descending, ties by lower id */
-            for (int i = tid; i < n; i += SM_THREADS) {
-                a.ka[i] = ~__float_as_uint(p[i]);
-                a.va[i] = i;
-            }
+            /* the tokens by probability descending, ties by lower id: the k best by selection,
+             * or every token by a full sort. Without top-k only the tokens at or above the
+             * top-p cutoff (sample_topp, :133-155) are candidates, counted first. */
+            const float cutoff = n > 1 ? __fdiv_rn(__fsub_rn(1.0f, a.topp), (float)(n - 1)) : 0.0f;
+            __shared__ int s_m;
+            if (tid == 0) s_m = 0;
             __syncthreads();
-            sm_radix_sort(a.ka, a.va, a.kb, a.vb, n, hist, tot);
-            if (tid == 0) {
-                const unsigned *k = a.ka;
-                const int *v = a.va;
-                auto pr = [&](int i) { return __uint_as_float(~k[i]); };
-                if (use_k) {
+            int c = 0;
+            for (int i = tid; i < n; i += SM_THREADS) {
+                const float q = p[i];
+                a.ka[i] = ~__float_as_uint(q);
+                a.va[i] = i;
+                c += q >= cutoff;
+            }
+            if (!use_k) atomicAdd(&s_m, c);
+            __syncthreads();
+            const int m_p = s_m;                               /* top-p candidates (top-p only) */
+            const int ksel = use_k ? a.topk : max(m_p, 1);     /* one: the argmax when none pass */
+            const bool select = ksel <= SM_TOPK_MAX;
+            __shared__ int s_cnt;
+            if (select) {
+                unsigned long long *cand = (unsigned long long *)a.kb;   /* [SM_TOPK_MAX] in the spare key buffer */
+                sm_topk_select(a.ka, n, ksel, cand, hist, &s_cnt);
+                for (int i = tid; i < ksel; i += SM_THREADS) {
+                    a.ka[i] = (unsigned)(cand[i] >> 32);
+                    a.va[i] = (int)(unsigned)cand[i];
+                }
+                __syncthreads();
+            } else {
+                sm_radix_sort(a.ka, a.va, a.kb, a.vb, n, hist, tot);
+            }
+            const unsigned *k = a.ka;
+            const int *v = a.va;
+            auto pr = [&](int i) { return __uint_as_float(~k[i]); };
+            if (use_k) {
+                if (tid == 0) {
                     /* sample_sorted (:108-131) over the k best */
                     const int m = a.topk;
                     float total = 0.0f;
@@ -246,24 +357,44 @@ __global__ void __launch_bounds__(SM_THREADS, 1) sample_kernel(const SampleArgs 
                         if (r < cdf) { tok = v[i]; break; }
                     }
                     s_tok = tok;
+                }
+            } else {
+                /* sample_topp (:133-155): the m tokens at or above the cutoff lead the
+                 * order; their running sums in blocks (per-thread ranges in order) */
+                const int m = m_p;
+                if (m == 0) {
+                    if (tid == 0) s_tok = v[0];   /* argmax: the first in this order is the first index of the maximum */
                 } else {
-                    /* sample_topp (:133-155): the tokens at or above the cutoff */
-                    const float cutoff = n > 1 ? __fdiv_rn(__fsub_rn(1.0f, a.topp), (float)(n - 1)) : 0.0f;
-                    int m = 0;
-                    while (m < n && pr(m) >= cutoff) m++;
-                    if (m == 0) {
-                        s_tok = v[0];   /* argmax: the first in this order is the first index of the maximum */
-                    } else {
+                    const int chunk = (m + SM_THREADS - 1) / SM_THREADS, lo = tid * chunk, hi = min(m, lo + chunk);
+                    float cs = 0.0f;
+                    for (int i = lo; i < hi; i++) cs = __fadd_rn(cs, pr(i));
+                    float *csum = (float *)hist;
+                    csum[tid] = cs;
+                    __syncthreads();
+                    if (tid == 0) {
                         float cum = 0.0f;
-                        int last = m - 1;
-                        for (int i = 0; i < m; i++) {
-                            cum = __fadd_rn(cum, pr(i));
-                            if (cum > a.topp) { last = i; break; }
+                        int last = m - 1, t = 0;
+                        for (; t < SM_THREADS; t++) {
+                            const float nx = __fadd_rn(cum, csum[t]);
+                            if (nx > a.topp) break;
+                            cum = nx;
                         }
+                        if (t < SM_THREADS)
+                            for (int i = t * chunk; i < min(m, (t + 1) * chunk); i++) {
+                                cum = __fadd_rn(cum, pr(i));
+                                if (cum > a.topp) { last = i; break; }
+                            }
                         const float r = __fmul_rn(coin, cum);
+                        const int tl = last / chunk;
                         float cdf = 0.0f;
-                        int tok = v[last];
-                        for (int i = 0; i <= last; i++) {
+                        int u = 0, tok = v[last];
+                        for (; u < tl; u++) {
+                            const float nx = __fadd_rn(cdf, csum[u]);
+                            if (r < nx) break;
+                            cdf = nx;
+                        }
+                        const int l1 = u < tl ? min(m, (u + 1) * chunk) - 1 : last;
+                        for (int i = u * chunk; i <= l1; i++) {
                             cdf = __fadd_rn(cdf, pr(i));
                             if (r < cdf) { tok = v[i]; break; }
                         }

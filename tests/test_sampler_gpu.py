@@ -27,6 +27,9 @@ OPTS = [
     dict(temperature=0.7, topp=0.9, seed=13),
     dict(temperature=0.9, topk=50, topp=0.8, repeat_penalty=1.1, repeat_last_n=16, seed=17),
     dict(temperature=0.6, topp=0.6, topk=200, seed=29),
+    # top-p alone with a few hundred tokens above its cutoff: the selection path
+    # (the flat cases above have tens of thousands: the full sort)
+    dict(temperature=0.05, topp=0.9, seed=19),
 ]
 # Not held: a nucleus of thousands of near-equal probabilities (a flat
 # distribution at a high temperature with top-p near 1), where tokens whose
