@@ -48,7 +48,7 @@ struct PMat {
     int rows, type, d16;
 };
 
-struct LayerPlan {
+struct alignas(16) LayerPlan {
     const float *attn_norm, *ffn_norm;
     void *kc, *vc;                  /* this layer's cache [max_seq][kv_dim] of the state's KV type */
     float *kd, *vd;                 /* Q8 cache: scales [max_seq][n_kv_heads] */
@@ -1499,6 +1499,16 @@ __device__ __forceinline__ void init_ring(const Smem &s, int nstage) {
 
 __shared__ PhasePlan s_plan[NPHASE];
 
+/* The layer plans in shared memory, double-buffered by the running layer
+ * index gl: layer gl + 1's plan is copied (cp.async, LP_UNITS threads) while
+ * layer gl runs, so no phase waits on a global load of its layer's pointers. */
+__shared__ LayerPlan s_lp[2];
+constexpr int LP_UNITS = sizeof(LayerPlan) / 16;
+static_assert(sizeof(LayerPlan) % 16 == 0, "LayerPlan copies in 16-byte units");
+__device__ __forceinline__ void fetch_plan(const LayerPlan *src, LayerPlan *dst) {
+    if (threadIdx.x < LP_UNITS) cp_async16((char *)dst + 16 * threadIdx.x, (const char *)src + 16 * threadIdx.x);
+}
+
 /* Producer: this CTA's stream once per step (the classifier only when the
  * step computes logits). */
 __device__ __forceinline__ void producer(const StepArgs &a, Ring rg) {
@@ -1529,14 +1539,18 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
     unsigned expect = 0, pidx = 0;   /* barrier arrivals due so far, trace index */
     const ActW w_dim = act_layout(sh.act, a.dim), w_q = act_layout(sh.act, a.q_dim), w_h = act_layout(sh.act, a.hidden);
     if (threadIdx.x == 0) timeline_mark(a);
+    fetch_plan(a.layers, &s_lp[0]);
+    cp_async_wait_all();
+    consumer_sync();
+    unsigned gl = 0;   /* running layer index over the launch's steps */
     for (int step = 0; step < a.nsteps; step++) {
         const int tok = __ldcg(&a.ls->token), pos = __ldcg(&a.ls->pos);
         const bool ok = tok >= 0 && tok < a.vocab && pos >= 0 && pos < a.max_seq;
         if (!ok && threadIdx.x == 0) atomicOr(&a.ls->err, 1u);
         const int tk = ok ? tok : 0, ps = ok ? pos : 0;
         const int logit_row0 = (__ldcg(&a.ls->step) % LOGITS_RING) * a.vocab;
-        for (int l = 0; l < a.n_layers; l++) {
-            const LayerPlan L = a.layers[l];
+        for (int l = 0; l < a.n_layers; l++, gl++) {
+            const LayerPlan &L = s_lp[gl & 1];
             const float *next_norm = l + 1 < a.n_layers ? a.layers[l + 1].attn_norm : (a.run_cls ? a.final_norm : nullptr);
             /* A: Q/K/V */
             if (l == 0) {
@@ -1548,8 +1562,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
                     sh.own[r - own0] = e1;
                 }
             } else if (a.post_norms) {
-                act_postnorm(a, a.x, a.yb, a.layers[l - 1].post_ffn, L.attn_norm, a.dim, w_dim, sh.red, sh.own, own0,
-                             own1);
+                act_postnorm(a, a.x, a.yb, s_lp[(gl - 1) & 1].post_ffn, L.attn_norm, a.dim, w_dim, sh.red, sh.own,
+                             own0, own1);
             } else {
                 load_activation(a, a.x, L.attn_norm, a.ssp, a.dim, w_dim, sh.red, sh.wbuf);
             }
@@ -1562,7 +1576,9 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
                              sh.cta_best, col_slices(a.dim / QK, false));
             }
             grid_barrier(a, expect, pidx);
-            /* B: attention */
+            /* B: attention; the next layer's plan is fetched meanwhile (the
+             * buffer's last reader, the previous layer's A prologue, is done) */
+            fetch_plan(a.layers + (l + 1 < a.n_layers ? l + 1 : 0), &s_lp[(gl + 1) & 1]);
             trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             for (int it = j; it < a.n_kv_heads * a.nsplit; it += G)
@@ -1605,14 +1621,15 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
             else
                 finish_phase(FIN_RESID, sh.res, nown, own0, a.x, sh.own, 0, 0.0f, sh.cta_best,
                              col_slices(a.hidden / QK, false));
+            if (threadIdx.x < LP_UNITS) cp_async_wait_all();   /* the next plan (long landed); the barrier publishes it */
             prefetch_norm(sh.wbuf, next_norm, a.dim);
             grid_barrier(a, expect, pidx, a.post_norms ? sh.yown : sh.own, nown);
         }
         /* F: classifier + argmax */
         if (a.run_cls) {
             if (a.post_norms)
-                act_postnorm(a, a.x, a.yb, a.layers[a.n_layers - 1].post_ffn, a.final_norm, a.dim, w_dim, sh.red,
-                             sh.own, own0, own1);
+                act_postnorm(a, a.x, a.yb, s_lp[(gl - 1) & 1].post_ffn, a.final_norm, a.dim, w_dim, sh.red, sh.own,
+                             own0, own1);
             else
                 load_activation(a, a.x, a.final_norm, a.ssp, a.dim, w_dim, sh.red, sh.wbuf);
             trace_mark(a, pidx, 0);
