@@ -403,7 +403,7 @@ struct kc_state {
     float *rcos = nullptr, *rsin = nullptr, *lcos = nullptr, *lsin = nullptr;
     float *inv0 = nullptr;   /* [vocab]: 1/rms of each embedding row (layer 0's RMSNorm) */
     float *ssp = nullptr;    /* [grid]: per-CTA sums of squares of the residual rows it wrote */
-    unsigned *counter = nullptr, *err = nullptr;
+    unsigned *err = nullptr;
     LoopState *ls = nullptr;
     int *feed = nullptr, *out_tokens = nullptr;
     float *h_logits = nullptr;
@@ -478,6 +478,9 @@ static int set_smem_attributes() {
 }
 
 /* Ring depth that fits beside the fixed part of a streaming CTA's shared memory. */
+/* Words of the grid barrier's arrival counter line; the attention counters follow. */
+constexpr size_t BAR_WORDS = 32;
+
 static int ring_stages(int slot, int act_bytes, int static_bytes, int res_bytes = 0, int wbuf_bytes = 0) {
     int nst = 16;
     while (nst >= 2 && smem_fixed_bytes(nst, act_bytes, res_bytes, wbuf_bytes) + nst * slot > KC_MAX_SMEM - static_bytes)
@@ -631,7 +634,7 @@ static int setup_step_kernel(kc_state *s) {
     a.final_norm = m->d_final_norm;
     a.inv0 = s->inv0;
     a.x = s->x; a.qkv = s->qkv; a.ao = s->ao; a.hb = s->hb; a.logits = s->logits; a.part = s->part; a.ssp = s->ssp;
-    a.att_counter = s->counter; a.bar = s->bar; a.err = s->err; a.ls = s->ls; a.feed = s->feed;
+    a.att_counter = s->bar + BAR_WORDS; a.bar = s->bar; a.err = s->err; a.ls = s->ls; a.feed = s->feed;
     a.out_tokens = s->out_tokens;
     a.kv_type = s->kv_type;
     a.n_layers = c.n_layers; a.dim = c.dim; a.q_dim = c.q_dim; a.kv_dim = c.kv_dim; a.hidden = c.hidden_dim;
@@ -656,7 +659,7 @@ static int launch_steps(kc_state *s, int nsteps, int logits, bool timeline = fal
         return KC_E_SHAPE;
     }
     s->last_row = -1;   /* the caller names the row when its last token's logits are kept */
-    CK(cudaMemsetAsync(s->bar, 0, sizeof(unsigned), s->st));
+    CK(cudaMemsetAsync(s->bar, 0, sizeof(unsigned) * (BAR_WORDS + (size_t)s->c.n_kv_heads), s->st));
     StepArgs a = s->sa;
     a.tp_step0 = s->tp_steps;
     s->tp_steps += (unsigned long long)nsteps;
@@ -768,9 +771,10 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
         { (void **)&s->logits, sizeof(float) * (size_t)LOGITS_RING * c.vocab },
         { (void **)&s->part, sizeof(float) * (size_t)c.n_heads * MAX_NSPLIT * (c.head_dim + 2) },
         { (void **)&s->ssp, sizeof(float) * (size_t)s->num_sms },
-        { (void **)&s->counter, sizeof(unsigned) * 2 * (size_t)c.n_kv_heads },
         { (void **)&s->err, sizeof(unsigned) * 4 },
-        { (void **)&s->bar, sizeof(unsigned) * 4 },
+        /* the grid barrier's arrival counter, then (a line further) the attention
+         * splits' arrival counters per KV head: zeroed together before each launch */
+        { (void **)&s->bar, sizeof(unsigned) * (BAR_WORDS + (size_t)c.n_kv_heads) },
         { (void **)&s->timeline_n, sizeof(unsigned) * 4 },
         { (void **)&s->timeline, sizeof(unsigned long long) * 4096 },
         { (void **)&s->ls, sizeof(LoopState) },

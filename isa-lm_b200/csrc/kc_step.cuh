@@ -16,8 +16,8 @@
  *   A  RMSNorm + quantize x (layer 0: the embedding row, its 1/rms from the
  *      host table) -> Q/K/V rows (+ biases)            model/transformer.c:270-277
  *   B  attention work items (KV head, position range): RoPE, this position's
- *      K/V row into the cache, split flash decode; the last CTA per KV head
- *      combines the splits                             transformer.c:280-283, ops/ops.c:124-180
+ *      K/V row into the cache, split flash decode; the splits of a KV
+ *      head combine their output slices                            transformer.c:280-283, ops/ops.c:124-180
  *   C  quantize the attention output -> O rows, x += o  transformer.c:284-287
  *   D  RMSNorm + quantize x -> gate/up row pairs -> act(g) * u   :288-293
  *   E  quantize h -> down rows, x += y                 :294-297
@@ -1071,12 +1071,11 @@ __host__ __device__ inline int attention_scratch_floats(int group, int hd) {
            + att_pad4(ATT_TILE * (hd + 1)) + ATT_TILE                               /* K tile, K scales */
            + ATT_TILE * hd + ATT_TILE                                               /* V tile, V scales */
            + att_pad4(group * ATT_TILE) + 3 * att_pad4(group)                       /* p, m, l, alpha */
-           + att_pad4(hd) * 2 + 4                                                   /* this position's K, V, scales */
-           + group * 32;                                                            /* combine weights */
+           + att_pad4(hd) * 2 + 4;                                                  /* this position's K, V, scales */
 }
 
 struct AttSmem {
-    float *sq, *sqd, *sk, *skd, *sv, *svd, *sp, *sm, *sl, *sa, *knew, *vnew, *knd, *wts;
+    float *sq, *sqd, *sk, *skd, *sv, *svd, *sp, *sm, *sl, *sa, *knew, *vnew, *knd;
     int8_t *sqq;
 };
 
@@ -1095,9 +1094,19 @@ __device__ __forceinline__ AttSmem att_smem(float *f, int group, int hd) {
     s.sa = f; f += att_pad4(group);
     s.knew = f; f += att_pad4(hd);
     s.vnew = f; f += att_pad4(hd);
-    s.knd = f; f += 4;
-    s.wts = f;
+    s.knd = f;
     return s;
+}
+
+/* The splits of a KV head's positions at pos: first = the first position in
+ * the window, C = positions per split (a multiple of ATT_TILE); returns how
+ * many splits hold positions (the rest of the nsplit items are idle). */
+__device__ __forceinline__ int att_splits(const StepArgs &a, const LayerPlan &L, int pos, int &first, int &C) {
+    first = L.window && pos >= L.window ? pos + 1 - L.window : 0;
+    const int n = pos + 1 - first;
+    C = (n + a.nsplit - 1) / a.nsplit;
+    C = C < ATT_TILE ? ATT_TILE : (C + ATT_TILE - 1) / ATT_TILE * ATT_TILE;
+    return (n + C - 1) / C;
 }
 
 /* Attention work item (KV head g, split y) of layer L at position pos, on the
@@ -1112,15 +1121,13 @@ __device__ __forceinline__ AttSmem att_smem(float *f, int group, int hd) {
  * * v). The splits of a KV head then wait for each other and each combines
  * its slice of the head group's outputs into a.ao. */
 template <int KV, int UNITS>
-__device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan &L, int g, int y, int pos, float *fsm) {
+__device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan &L, int g, int y, int pos, float *fsm,
+                                              unsigned att_base) {
     constexpr int ES = KV == KC_F32 ? 4 : (KV == KC_F16 ? 2 : 1);
     const int hd = a.hd, group = a.n_heads / a.n_kv_heads, h2 = hd / 2, tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
-    const int first = L.window && pos >= L.window ? pos + 1 - L.window : 0;
-    const int n = pos + 1 - first;
-    int C = (n + a.nsplit - 1) / a.nsplit;
-    C = C < ATT_TILE ? ATT_TILE : (C + ATT_TILE - 1) / ATT_TILE * ATT_TILE;
-    const int active = (n + C - 1) / C;
+    int first, C;
+    const int active = att_splits(a, L, pos, first, C);
     if (y >= active) return;
     const int t_begin = first + y * C, t_end = min(t_begin + C, pos + 1);
     const AttSmem S = att_smem(fsm, group, hd);
@@ -1148,7 +1155,23 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
         }
     };
     if (tid == 0) ev(0, 20);
-    load_tile(t_begin);
+    /* F32: the first tile goes straight into its shared-memory layout (cp.async;
+     * no registers held across the query's RoPE) */
+    if constexpr (KV == KC_F32) {
+        const int nt = min(ATT_TILE, t_end - t_begin);
+        for (int idx = tid; idx < nt * hd; idx += NCT) {
+            const int t = idx / hd, i = idx - t * hd;
+            if (t_begin + t != pos)
+                cp_async4(S.sk + t * (hd + 1) + i, (const float *)(kb + (size_t)(t_begin + t) * rowb) + i);
+        }
+        for (int idx = tid; idx < nt * upr; idx += NCT) {
+            const int t = idx / upr, u = idx - t * upr;
+            if (t_begin + t != pos) cp_async16(S.sv + t * hd + 4 * u, vb + (size_t)(t_begin + t) * rowb + 16 * u);
+        }
+        cp_async_commit();
+    } else {
+        load_tile(t_begin);
+    }
     if (tid == 0) ev(0, 21);
     const float *cs = L.rcos + (size_t)pos * h2, *sn = L.rsin + (size_t)pos * h2;
     /* qk_norm (model/transformer.c:244-248): 1/rms of each query head first */
@@ -1270,6 +1293,8 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
                             kf[k] = S.knew[PER * u + k];
                             vf[k] = S.vnew[PER * u + k];
                         }
+                    } else if (KV == KC_F32 && t0 == t_begin) {
+                        continue;   /* landed by cp.async */
                     } else if constexpr (KV == KC_F32) {
                         const float *ka = (const float *)&rk[e], *va = (const float *)&rv[e];
 #pragma unroll
@@ -1293,6 +1318,7 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
             S.svd[tid] = own ? S.knd[1] : rvd;
         }
         if (tid == 0) ev(0, 23);
+        if (KV == KC_F32 && t0 == t_begin) cp_async_wait_all();
         if (t0 + ATT_TILE < t_end) load_tile(t0 + ATT_TILE);
         consumer_sync();
         if (tid == 0) ev(0, 24);
@@ -1362,6 +1388,18 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
         consumer_sync();
         if (tid == 0) ev(0, EV_ATT_TILE);
     }
+    if (active == 1) {
+        /* one split: its outputs are the head's (the combine below with one
+         * weight, 1 / l, gives the same bits) */
+#pragma unroll
+        for (int k = 0; k < MAXO; k++) {
+            const int o = (tid + k * NCT) / tpo;
+            if (k * NCT < nout * tpo && o < nout && tid % tpo == 0)
+                a.ao[(size_t)g * nout + o] = __fmul_rn(acc[k], __fdiv_rn(1.0f, S.sl[o / hd]));
+        }
+        if (tid == 0) ev(0, EV_ATT_DONE);
+        return;
+    }
     /* this split's partial: unnormalized outputs, running max and sum */
     const int stride = hd + 2;
 #pragma unroll
@@ -1377,17 +1415,21 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
         ph[hd] = S.sm[tid];
         ph[hd + 1] = S.sl[tid];
     }
-    __threadfence();
     consumer_sync();
     if (tid == 0) ev(0, 27);
     /* the head's splits wait for each other (all resident: a bounded spin),
-     * then each combines its slice of the group's outputs */
-    unsigned *arrived = a.att_counter + g, *done = a.att_counter + a.n_kv_heads + g;
+     * then each combines its slice of the group's outputs. The head's arrival
+     * counter grows over the launch: this round is complete at att_base +
+     * active. One thread fences the CTA's partial (ordered before it by the
+     * consumer barrier) and arrives; its acquire, then the barrier, order the
+     * loads of the other splits' partials. */
+    unsigned *arrived = a.att_counter + g;
     if (tid == 0) {
+        __threadfence();
         atomicAdd(arrived, 1u);
         ev(0, 28);
         unsigned it = 0;
-        while (ld_acquire(arrived) < (unsigned)active) {
+        while (ld_acquire(arrived) < att_base + (unsigned)active) {
             if (++it > (1u << 24)) {
                 atomicOr(a.err, 8u);
                 break;
@@ -1397,49 +1439,55 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
         ev(0, EV_ATT_PART);
     }
     consumer_sync();
-    __threadfence();
     const int chunk = (nout + active - 1) / active, o0 = y * chunk, o1 = min(nout, o0 + chunk);
-    for (int h = warp; h < group; h += NCW) {
-        if (h * hd >= o1 || (h + 1) * hd <= o0) continue;
-        const float *ph = a.part + (size_t)(g * group + h) * a.nsplit * stride;
-        const float m = lane < active ? __ldcg(ph + (size_t)lane * stride + hd) : -INFINITY;
-        const float l = lane < active ? __ldcg(ph + (size_t)lane * stride + hd + 1) : 0.0f;
-        const float M = warp_max(m);
-        const float e = lane < active ? expf(m - M) : 0.0f;
-        const float Ls = warp_sum(l * e);
-        S.wts[h * 32 + lane] = e / Ls;
-    }
-    consumer_sync();
     if (tid == 0) ev(0, EV_ATT_COMBINE);
-    for (int o = o0 + tid; o < o1; o += NCT) {
-        const int h = o / hd, i = o % hd;
-        const float *base = a.part + (size_t)(g * group + h) * a.nsplit * stride + i;
-        const float *w = S.wts + h * 32;
-        float num = 0.0f;
-#pragma unroll 8
-        for (int s2 = 0; s2 < active; s2++) num = fmaf(__ldcg(base + (size_t)s2 * stride), w[s2], num);
-        a.ao[(size_t)(g * group + h) * hd + i] = num;
-    }
-    if (tid == 0) {
-        /* the last split through resets both counters for the next layer */
-        if (atomicAdd(done, 1u) == (unsigned)active - 1) {
-            *arrived = 0u;
-            *done = 0u;
+    /* a warp per output and a lane per split, OPW outputs per warp at a time:
+     * the splits' running maxima, sums and partial outputs arrive in one round
+     * trip; weight e_s / sum_s l_s e_s, e_s = exp(m_s - M), and the weighted
+     * partials summed in split order */
+    constexpr int OPW = 4;
+    for (int ob = o0 + warp; ob < o1; ob += OPW * NCW) {
+        float m[OPW], l[OPW], p[OPW];
+#pragma unroll
+        for (int k = 0; k < OPW; k++) {
+            const int o = ob + k * NCW;
+            m[k] = -INFINITY;
+            l[k] = p[k] = 0.0f;
+            if (o < o1 && lane < active) {
+                const int h = o / hd, i = o - h * hd;
+                const float *ps = a.part + ((size_t)(g * group + h) * a.nsplit + lane) * stride;
+                m[k] = __ldcg(ps + hd);
+                l[k] = __ldcg(ps + hd + 1);
+                p[k] = __ldcg(ps + i);
+            }
         }
-        ev(0, EV_ATT_DONE);
+#pragma unroll
+        for (int k = 0; k < OPW; k++) {
+            const int o = ob + k * NCW;
+            if (o >= o1) break;
+            const float M = warp_max(m[k]);
+            const float e = lane < active ? expf(m[k] - M) : 0.0f;
+            const float w = e / warp_sum(l[k] * e);
+            float num = 0.0f;
+            for (int s2 = 0; s2 < active; s2++)
+                num = fmaf(__shfl_sync(0xffffffffu, p[k], s2), __shfl_sync(0xffffffffu, w, s2), num);
+            if (lane == 0) a.ao[(size_t)g * nout + o] = num;
+        }
     }
+    if (tid == 0) ev(0, EV_ATT_DONE);
 }
 
 /* UNITS: the 16-byte units of K a thread loads per tile, head_dim * bytes / 128. */
-__device__ __forceinline__ void attention_item(const StepArgs &a, const LayerPlan &L, int g, int y, int pos, float *fsm) {
+__device__ __forceinline__ void attention_item(const StepArgs &a, const LayerPlan &L, int g, int y, int pos, float *fsm,
+                                               unsigned att_base) {
     if (a.kv_type == KC_F16) {
-        if (a.hd <= 64) attention_item_t<KC_F16, 1>(a, L, g, y, pos, fsm);
-        else attention_item_t<KC_F16, 2>(a, L, g, y, pos, fsm);
+        if (a.hd <= 64) attention_item_t<KC_F16, 1>(a, L, g, y, pos, fsm, att_base);
+        else attention_item_t<KC_F16, 2>(a, L, g, y, pos, fsm, att_base);
     } else if (a.kv_type == KC_Q8_0) {
-        attention_item_t<KC_Q8_0, 1>(a, L, g, y, pos, fsm);
+        attention_item_t<KC_Q8_0, 1>(a, L, g, y, pos, fsm, att_base);
     } else {
-        if (a.hd <= 64) attention_item_t<KC_F32, 2>(a, L, g, y, pos, fsm);
-        else attention_item_t<KC_F32, 4>(a, L, g, y, pos, fsm);
+        if (a.hd <= 64) attention_item_t<KC_F32, 2>(a, L, g, y, pos, fsm, att_base);
+        else attention_item_t<KC_F32, 4>(a, L, g, y, pos, fsm, att_base);
     }
 }
 
@@ -1542,7 +1590,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
     fetch_plan(a.layers, &s_lp[0]);
     cp_async_wait_all();
     consumer_sync();
-    unsigned gl = 0;   /* running layer index over the launch's steps */
+    unsigned gl = 0;         /* running layer index over the launch's steps */
+    unsigned att_base = 0;   /* arrivals on each KV head's attention counter so far in this launch */
     for (int step = 0; step < a.nsteps; step++) {
         const int tok = __ldcg(&a.ls->token), pos = __ldcg(&a.ls->pos);
         const bool ok = tok >= 0 && tok < a.vocab && pos >= 0 && pos < a.max_seq;
@@ -1582,7 +1631,12 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
             trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             for (int it = j; it < a.n_kv_heads * a.nsplit; it += G)
-                attention_item(a, L, it / a.nsplit, it % a.nsplit, ps, (float *)sh.act);
+                attention_item(a, L, it / a.nsplit, it % a.nsplit, ps, (float *)sh.act, att_base);
+            {
+                int first, C;
+                const int na = att_splits(a, L, ps, first, C);
+                if (na > 1) att_base += (unsigned)na;   /* a single split arrives nowhere */
+            }
             grid_barrier(a, expect, pidx);
             /* C: O projection + residual */
             load_activation(a, a.ao, nullptr, nullptr, a.q_dim, w_q, sh.red);
