@@ -1068,7 +1068,7 @@ constexpr int KVU_MAX = 4;   /* 16-byte units of K (and of V) a thread loads per
 __host__ __device__ inline int att_pad4(int n) { return (n + 3) & ~3; }
 __host__ __device__ inline int attention_scratch_floats(int group, int hd) {
     return att_pad4(group * hd) + att_pad4((group * hd + 3) / 4) + att_pad4(group)   /* q, int8 q, its scales */
-           + att_pad4(ATT_TILE * (hd + 1)) + ATT_TILE                               /* K tile, K scales */
+           + ATT_TILE * (hd + 4) + ATT_TILE                                         /* K tile, K scales */
            + ATT_TILE * hd + ATT_TILE                                               /* V tile, V scales */
            + att_pad4(group * ATT_TILE) + 3 * att_pad4(group)                       /* p, m, l, alpha */
            + att_pad4(hd) * 2 + 4;                                                  /* this position's K, V, scales */
@@ -1084,7 +1084,7 @@ __device__ __forceinline__ AttSmem att_smem(float *f, int group, int hd) {
     s.sq = f; f += att_pad4(group * hd);
     s.sqq = (int8_t *)f; f += att_pad4((group * hd + 3) / 4);
     s.sqd = f; f += att_pad4(group);
-    s.sk = f; f += att_pad4(ATT_TILE * (hd + 1));
+    s.sk = f; f += ATT_TILE * (hd + 4);   /* float K rows hd + 4 apart: 16-byte aligned, float4 reads conflict-free */
     s.skd = f; f += ATT_TILE;
     s.sv = f; f += ATT_TILE * hd;
     s.svd = f; f += ATT_TILE;
@@ -1159,14 +1159,13 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
      * no registers held across the query's RoPE) */
     if constexpr (KV == KC_F32) {
         const int nt = min(ATT_TILE, t_end - t_begin);
-        for (int idx = tid; idx < nt * hd; idx += NCT) {
-            const int t = idx / hd, i = idx - t * hd;
-            if (t_begin + t != pos)
-                cp_async4(S.sk + t * (hd + 1) + i, (const float *)(kb + (size_t)(t_begin + t) * rowb) + i);
-        }
         for (int idx = tid; idx < nt * upr; idx += NCT) {
             const int t = idx / upr, u = idx - t * upr;
-            if (t_begin + t != pos) cp_async16(S.sv + t * hd + 4 * u, vb + (size_t)(t_begin + t) * rowb + 16 * u);
+            if (t_begin + t != pos) {
+                const size_t src = (size_t)(t_begin + t) * rowb + 16 * u;
+                cp_async16(S.sk + t * (hd + 4) + 4 * u, kb + src);
+                cp_async16(S.sv + t * hd + 4 * u, vb + src);
+            }
         }
         cp_async_commit();
     } else {
@@ -1306,7 +1305,7 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
                     }
 #pragma unroll
                     for (int k = 0; k < PER; k++) {
-                        S.sk[t * (hd + 1) + PER * u + k] = kf[k];
+                        S.sk[t * (hd + 4) + PER * u + k] = kf[k];
                         S.sv[t * hd + PER * u + k] = vf[k];
                     }
                 }
@@ -1339,8 +1338,17 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
             } else {
                 float dot = 0.0f;
                 if (t < nt) {
-                    const float *qh = S.sq + h * hd + part * span, *kt = S.sk + t * (hd + 1) + part * span;
-                    for (int i = 0; i < span; i++) dot = fmaf(qh[i], kt[i], dot);
+                    /* float4 reads of q (broadcast) and of the K row, the sum in order */
+                    const float4 *q4 = (const float4 *)(S.sq + h * hd + part * span),
+                                 *k4 = (const float4 *)(S.sk + t * (hd + 4) + part * span);
+#pragma unroll 4
+                    for (int i = 0; i < span / 4; i++) {
+                        const float4 qv = q4[i], kv = k4[i];
+                        dot = fmaf(qv.x, kv.x, dot);
+                        dot = fmaf(qv.y, kv.y, dot);
+                        dot = fmaf(qv.z, kv.z, dot);
+                        dot = fmaf(qv.w, kv.w, dot);
+                    }
                 }
                 for (int o = tpd / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
                 if (t < nt) s = __fmul_rn(dot, a.attn_scale);
@@ -1376,7 +1384,23 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
                     const int h = o / hd, i = o % hd;
                     v = acc[k] * S.sa[h];
                     const float *ph = S.sp + h * ATT_TILE;
-                    for (int t = part; t < nt; t += tpo) {
+                    static_assert(tpo == 1, "one thread per output: positions in order");
+                    int t = 0;
+                    /* the weights four at a time (broadcast float4 reads) */
+                    for (; t + 4 <= nt; t += 4) {
+                        float4 w4 = *(const float4 *)(ph + t);
+                        if constexpr (KV == KC_Q8_0) {
+                            const float4 d4 = *(const float4 *)(S.svd + t);
+                            w4 = make_float4(__fmul_rn(w4.x, d4.x), __fmul_rn(w4.y, d4.y), __fmul_rn(w4.z, d4.z),
+                                             __fmul_rn(w4.w, d4.w));
+                        }
+                        const float *vc = S.sv + t * hd + i;
+                        v = fmaf(w4.x, vc[0], v);
+                        v = fmaf(w4.y, vc[hd], v);
+                        v = fmaf(w4.z, vc[2 * hd], v);
+                        v = fmaf(w4.w, vc[3 * hd], v);
+                    }
+                    for (; t < nt; t++) {
                         const float w = KV == KC_Q8_0 ? __fmul_rn(ph[t], S.svd[t]) : ph[t];
                         v = fmaf(w, S.sv[t * hd + i], v);
                     }
