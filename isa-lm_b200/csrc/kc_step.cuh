@@ -866,14 +866,15 @@ __device__ __noinline__ void act_float(float eps, const float *x, const float *n
     const int passes = (nb + NCT / 8 - 1) / (NCT / 8);
     const bool norm = norm_w != nullptr;
     if (tid == 0) ev(0, EV_ACT_ENTRY);
-    /* every warp loads the G per-CTA sums of squares itself (no block
-     * reduction, no extra barrier), in the same order as every other warp */
-    const int lane = tid & 31;
+    /* one warp per CTA loads the G per-CTA sums of squares (the same few
+     * lines read by every warp of every CTA would queue at their L2 slice) */
+    const int lane = tid & 31, warp = tid >> 5;
+    const bool ssw = norm && ssp && warp == 0;
     float part[SSP_LOADS];
 #pragma unroll
     for (int k = 0; k < SSP_LOADS; k++) {
         const int idx = k * 32 + lane;
-        part[k] = (norm && ssp && idx < (int)gridDim.x) ? __ldcg(ssp + idx) : 0.0f;
+        part[k] = (ssw && idx < (int)gridDim.x) ? __ldcg(ssp + idx) : 0.0f;
     }
     float4 v[ACT_PASSES], w[ACT_PASSES];
 #pragma unroll
@@ -892,19 +893,23 @@ __device__ __noinline__ void act_float(float eps, const float *x, const float *n
     }
     float inv = 1.0f;
     if (norm) {
-        float ss;
         if (ssp) {
-            float t = 0.0f;
+            if (warp == 0) {
+                float t = 0.0f;
 #pragma unroll
-            for (int k = 0; k < SSP_LOADS; k++) t += part[k];
-            ss = warp_sum(t);
+                for (int k = 0; k < SSP_LOADS; k++) t += part[k];
+                const float ss = warp_sum(t);
+                if (lane == 0) red[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
+            }
+            consumer_sync();
+            inv = red[0];
         } else {
             float t = 0.0f;
 #pragma unroll
             for (int p = 0; p < ACT_PASSES; p++) t += v[p].x * v[p].x + v[p].y * v[p].y + v[p].z * v[p].z + v[p].w * v[p].w;
-            ss = block_sum(t, red);
+            const float ss = block_sum(t, red);
+            inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
         }
-        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
     }
     if (tid == 0) ev(0, EV_ACT_INV);
 #pragma unroll 1
@@ -1155,6 +1160,18 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
         }
     };
     if (tid == 0) ev(0, 20);
+    /* this thread's first query pair and its RoPE angle, loaded before the tile
+     * so that both round trips overlap */
+    const float *cs = L.rcos + (size_t)pos * h2, *sn = L.rsin + (size_t)pos * h2;
+    const int nq = group * h2;
+    float2 q0 = make_float2(0.0f, 0.0f);
+    float c0 = 0.0f, s0 = 0.0f;
+    if (tid < nq) {
+        const int h = tid / h2, i = tid - h * h2;
+        q0 = __ldcg((const float2 *)(a.qkv + (size_t)(g * group + h) * hd + 2 * i));
+        c0 = cs[i];
+        s0 = sn[i];
+    }
     /* F32: the first tile goes straight into its shared-memory layout (cp.async;
      * no registers held across the query's RoPE) */
     if constexpr (KV == KC_F32) {
@@ -1172,7 +1189,6 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
         load_tile(t_begin);
     }
     if (tid == 0) ev(0, 21);
-    const float *cs = L.rcos + (size_t)pos * h2, *sn = L.rsin + (size_t)pos * h2;
     /* qk_norm (model/transformer.c:244-248): 1/rms of each query head first */
     __shared__ float qinv[NCW];
     if (L.q_norm) {
@@ -1188,11 +1204,12 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
         }
         consumer_sync();
     }
-    for (int idx = tid; idx < group * h2; idx += NCT) {
+    for (int idx = tid; idx < nq; idx += NCT) {
         const int h = idx / h2, i = idx % h2;
         const float *qh = a.qkv + (size_t)(g * group + h) * hd;
-        float qa = __ldcg(qh + 2 * i), qb = __ldcg(qh + 2 * i + 1);
-        const float c = cs[i], s = sn[i];
+        const bool first_pair = idx == tid;
+        float qa = first_pair ? q0.x : __ldcg(qh + 2 * i), qb = first_pair ? q0.y : __ldcg(qh + 2 * i + 1);
+        const float c = first_pair ? c0 : cs[i], s = first_pair ? s0 : sn[i];
         if (L.q_norm) {
             qa = __fmul_rn(__fmul_rn(qa, qinv[h]), L.q_norm[2 * i]);
             qb = __fmul_rn(__fmul_rn(qb, qinv[h]), L.q_norm[2 * i + 1]);
@@ -1387,6 +1404,7 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
                     static_assert(tpo == 1, "one thread per output: positions in order");
                     int t = 0;
                     /* the weights four at a time (broadcast float4 reads) */
+#pragma unroll 4
                     for (; t + 4 <= nt; t += 4) {
                         float4 w4 = *(const float4 *)(ph + t);
                         if constexpr (KV == KC_Q8_0) {
