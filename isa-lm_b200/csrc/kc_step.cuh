@@ -1635,17 +1635,27 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
     unsigned gl = 0;         /* running layer index over the launch's steps */
     unsigned att_base = 0;   /* arrivals on each KV head's attention counter so far in this launch */
     for (int step = 0; step < a.nsteps; step++) {
-        const int tok = __ldcg(&a.ls->token), pos = __ldcg(&a.ls->pos);
-        const bool ok = tok >= 0 && tok < a.vocab && pos >= 0 && pos < a.max_seq;
-        if (!ok && threadIdx.x == 0) atomicOr(&a.ls->err, 1u);
-        const int tk = ok ? tok : 0, ps = ok ? pos : 0;
-        const int logit_row0 = (__ldcg(&a.ls->step) % LOGITS_RING) * a.vocab;
+        /* the loop state, read by one thread and shared (every thread of every
+         * CTA on the same line would queue at its L2 slice) */
+        __shared__ int s_ls[4];
+        __shared__ float s_inv0;
+        if (threadIdx.x == 0) {
+            const int tok = __ldcg(&a.ls->token), pos = __ldcg(&a.ls->pos);
+            const bool ok = tok >= 0 && tok < a.vocab && pos >= 0 && pos < a.max_seq;
+            if (!ok) atomicOr(&a.ls->err, 1u);
+            s_ls[0] = ok ? tok : 0;
+            s_ls[1] = ok ? pos : 0;
+            s_ls[2] = (__ldcg(&a.ls->step) % LOGITS_RING) * a.vocab;
+            s_inv0 = a.inv0[s_ls[0]];
+        }
+        consumer_sync();
+        const int tk = s_ls[0], ps = s_ls[1], logit_row0 = s_ls[2];
+        const float inv0 = s_inv0;
         for (int l = 0; l < a.n_layers; l++, gl++) {
             const LayerPlan &L = s_lp[gl & 1];
-            const float *next_norm = l + 1 < a.n_layers ? a.layers[l + 1].attn_norm : (a.run_cls ? a.final_norm : nullptr);
             /* A: Q/K/V */
             if (l == 0) {
-                act_embed(a.emb, a.embed_scale, tk, L.attn_norm, a.inv0[tk], a.dim, w_dim);
+                act_embed(a.emb, a.embed_scale, tk, L.attn_norm, inv0, a.dim, w_dim);
                 /* the residual stream starts as the embedding row: this CTA's rows of x */
                 for (int r = own0 + (int)threadIdx.x; r < own1; r += NCT) {
                     const float e1 = embed1(a, tk, a.dim, r);
@@ -1717,8 +1727,12 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
             else
                 finish_phase(FIN_RESID, sh.res, nown, own0, a.x, sh.own, 0, 0.0f, sh.cta_best,
                              col_slices(a.hidden / QK, false));
-            if (threadIdx.x < LP_UNITS) cp_async_wait_all();   /* the next plan (long landed); the barrier publishes it */
-            prefetch_norm(sh.wbuf, next_norm, a.dim);
+            /* the next layer's plan (landed long ago) to every thread, then its
+             * norm weights on their way during the barrier */
+            if (threadIdx.x < LP_UNITS) cp_async_wait_all();
+            consumer_sync();
+            prefetch_norm(sh.wbuf, l + 1 < a.n_layers ? s_lp[(gl + 1) & 1].attn_norm : (a.run_cls ? a.final_norm : nullptr),
+                          a.dim);
             grid_barrier(a, expect, pidx, a.post_norms ? sh.yown : sh.own, nown);
         }
         /* F: classifier + argmax */
