@@ -711,7 +711,7 @@ enum { FIN_STORE = 0, FIN_RESID = 1, FIN_PAIR = 2, FIN_LOGITS = 3 };
  * store, residual add (on the CTA's rows of x in `own` and in out), act(g)*u,
  * or logits with the first-index argmax key of the CTA's rows (returned on
  * thread 0; 0 otherwise). */
-__device__ __noinline__ unsigned long long finish_phase(int kind, const float *res, int nrows, int row0, float *out,
+__device__ __forceinline__ unsigned long long finish_phase(int kind, const float *res, int nrows, int row0, float *out,
                                                         float *own, int act, float softcap, unsigned long long *cta_best,
                                                         int ns) {
     unsigned long long best = 0;
