@@ -858,8 +858,7 @@ __device__ __forceinline__ void put_quant(const ActW &o, int b, int nb, int j0, 
  * memory written by other CTAs (read through L2). 1/rms: from ss = the sum of
  * the G per-CTA partial sums ssp, else reduced here. Every thread issues all
  * its loads (up to 4 passes of 64 blocks, 8 lanes per block) before it uses
- * any, so the prologue costs one round trip to L2; the quantize loop is not
- * unrolled (one copy of its code). */
+ * any, so the prologue costs one round trip to L2. */
 __device__ __noinline__ void act_float(float eps, const float *x, const float *norm_w, const float *ssp, int cols, ActW o,
                                        float *red, const float *wstaged) {
     const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 7) * 4;
@@ -912,12 +911,11 @@ __device__ __noinline__ void act_float(float eps, const float *x, const float *n
         }
     }
     if (tid == 0) ev(0, EV_ACT_INV);
-#pragma unroll 1
-    for (int p = 0; p < passes; p++) {
-        float4 c = v[0], cw = w[0];
-        if (p == 1) { c = v[1]; cw = w[1]; }
-        else if (p == 2) { c = v[2]; cw = w[2]; }
-        else if (p == 3) { c = v[3]; cw = w[3]; }
+    /* the passes unrolled: their block maxima, divisions and stores overlap */
+#pragma unroll
+    for (int p = 0; p < ACT_PASSES; p++) {
+        if (p >= passes) break;
+        const float4 c = v[p], cw = w[p];
         float u[4] = { c.x, c.y, c.z, c.w };
         if (norm) {
             u[0] = __fmul_rn(__fmul_rn(u[0], inv), cw.x);
