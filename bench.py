@@ -213,10 +213,12 @@ def tp_decode(dist, K, W, hbm_peak):
     if dist is not None:
         dist.barrier()
         path = kb.ensure_model(name, MODEL_DIR)
+    t_load = time.perf_counter()
     model = kb.Model(path, upload=False)
     if WORLD > 1:
         model.shard(RANK, WORLD)
-    st = kb.State(model)
+    st = kb.State(model)   # uploads this rank's share, then the state arena
+    load_s = dist_max(dist, (time.perf_counter() - t_load) * 1000.0) / 1000.0
     if WORLD > 1:
         st.tp_connect(kb.exchange_handles(st.tp_handle(), dist))
     cfg = model.config
@@ -238,6 +240,7 @@ def tp_decode(dist, K, W, hbm_peak):
     return {"config": name, "workload": f"{name} batch-1 greedy decode at KV context {ctx}, tensor parallel",
             "parallelism": f"tp{WORLD}", "n_gpus": WORLD, "scaling": "strong", "tok_s": round(tok_s, 2),
             "ms_per_token": round(ms / K, 4), "steps": K, "warmup": W, "bytes_per_token": int(bpt),
+            "load_s": round(load_s, 3),
             "hbm_frac_per_gpu": round(bpt / WORLD * tok_s / 1e9 / hbm_peak, 4),
             "exchange": "O and down partials as tagged 64-bit NVLink peer stores inside the step kernel (no NCCL on the token path)"}
 
@@ -277,7 +280,10 @@ def main():
         print(json.dumps(line), flush=True)
         return
 
-    model = kb.Model(path)
+    t_load = time.perf_counter()
+    model = kb.Model(path)   # map + validate the .mlb, upload (file -> pinned -> HBM)
+    load_s = time.perf_counter() - t_load
+    load_bytes = int(model.device_bytes)
     cfg = model.config
     cfg["shared"] = model_cfg.get("shared", 0)
     ctx = min(ARGS.ctx, cfg["max_seq"] - K - W - 1)
@@ -447,6 +453,8 @@ def main():
                                     "prefill_tok_s": round(cpu["prefill_tok_s"], 1)}
         elif cpu:
             line["cpu_baseline"] = cpu
+        line["model_load"] = {"config": ARGS.config, "seconds": round(load_s, 3), "device_bytes": load_bytes,
+                              "path": "kc_model_load + kc_model_upload (8 threads gather per CTA and layer into pinned slots, async copies)"}
         for k in ("decode_by_context", "decode_by_kv_cache", "e2e_sampled_device", "prefill_tok_s", "prefill_roofline"):
             if k in extras:
                 line[k] = extras[k]

@@ -8,6 +8,9 @@
 #include <algorithm>
 #include <cstdlib>
 #include <new>
+#include <atomic>
+#include <functional>
+#include <mutex>
 #include <thread>
 #include <string>
 #include <vector>
@@ -266,12 +269,14 @@ static uint8_t *put_rec(uint8_t *dst, const HostMat &M, int r, const float *bias
     return dst + rec;
 }
 
-/* CTA j's stream: per layer the A, C, D, E phases of make_plan, then the classifier. */
-static size_t fill_stream(const kc_model *m, const PhasePlan *P, uint8_t *dst) {
+/* Part `part` of CTA j's stream: layer `part`'s A, C, D, E phases of
+ * make_plan, or (part == n_layers) the classifier. */
+static size_t fill_stream_part(const kc_model *m, const PhasePlan *P, int part, uint8_t *dst) {
     const kc_config &c = m->cfg;
     uint8_t *p = dst;
     const HostMat &cls = m->shared ? m->tok_emb : m->wcls;
-    for (const HostLayer &H : m->layers) {
+    if (part < c.n_layers) {
+        const HostLayer &H = m->layers[(size_t)part];
         for (int s = 0; s < P[PH_A].nseg; s++) {
             const Seg &S = P[PH_A].seg[s];
             const bool isq = S.row0 < c.q_dim, isk = !isq && S.row0 < c.q_dim + c.kv_dim;
@@ -289,19 +294,105 @@ static size_t fill_stream(const kc_model *m, const PhasePlan *P, uint8_t *dst) {
         }
         const Seg &E = P[PH_E].seg[0];
         for (int r = 0; r < E.rows; r++) p = put_rec(p, H.w2, E.row0 + r, nullptr, E.rec);
+    } else {
+        const Seg &F = P[PH_F].seg[0];
+        for (int r = 0; r < F.rows; r++) p = put_rec(p, cls, F.row0 + r, nullptr, F.rec);
     }
-    const Seg &F = P[PH_F].seg[0];
-    for (int r = 0; r < F.rows; r++) p = put_rec(p, cls, F.row0 + r, nullptr, F.rec);
     return (size_t)(p - dst);
 }
 
+static size_t stream_layer_bytes(const PhasePlan *P) {
+    return (size_t)(P[PH_A].bytes + P[PH_C].bytes + P[PH_D].bytes + P[PH_E].bytes);
+}
 static size_t stream_cta_bytes(const kc_model *m, const PhasePlan *P) {
-    return (size_t)m->cfg.n_layers * (size_t)(P[PH_A].bytes + P[PH_C].bytes + P[PH_D].bytes + P[PH_E].bytes) +
-           (size_t)P[PH_F].bytes;
+    return (size_t)m->cfg.n_layers * stream_layer_bytes(P) + (size_t)P[PH_F].bytes;
+}
+
+/* Host -> device upload through pinned staging (the load path): W worker
+ * threads, each with two pinned slots and its own stream; a worker fills one
+ * slot on the CPU (a gather from the mapped file) while the copy of its other
+ * slot runs, so the gathers of all workers and the copies overlap. A job is
+ * `bytes` (<= the slot size) written by fill(slot) and copied to dst. */
+struct UploadJob {
+    uint8_t *dst;
+    size_t bytes;
+    std::function<size_t(uint8_t *)> fill;   /* returns the bytes written (checked) */
+};
+
+static int upload_jobs(const std::vector<UploadJob> &jobs, size_t slot) {
+    if (jobs.empty()) return KC_OK;
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    const int W = (int)std::min<size_t>({ (size_t)8, (size_t)hw, jobs.size() });
+    std::vector<uint8_t *> buf((size_t)2 * W, nullptr);
+    std::vector<cudaStream_t> st((size_t)W, nullptr);
+    std::vector<cudaEvent_t> ev((size_t)2 * W, nullptr);
+    cudaError_t e = cudaSuccess;
+    for (int i = 0; i < 2 * W && e == cudaSuccess; i++) {
+        e = cudaHostAlloc((void **)&buf[(size_t)i], slot, cudaHostAllocDefault);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev[(size_t)i], cudaEventDisableTiming);
+    }
+    for (int w = 0; w < W && e == cudaSuccess; w++) e = cudaStreamCreateWithFlags(&st[(size_t)w], cudaStreamNonBlocking);
+    std::atomic<size_t> next{ 0 };
+    std::atomic<int> status{ e == cudaSuccess ? KC_OK : cuda_status(e, "upload staging") };
+    std::mutex mu;
+    std::string msg;   /* the first worker's error message (messages are per thread) */
+    auto fail = [&](int code) {
+        std::lock_guard<std::mutex> lk(mu);
+        if (status == KC_OK) {
+            msg = g_err;
+            status = code;
+        }
+    };
+    auto worker = [&](int w) {
+        const cudaError_t de = cudaSetDevice(dev);
+        if (de != cudaSuccess) {
+            fail(cuda_status(de, "upload worker"));
+            return;
+        }
+        int k = 0;
+        for (size_t i; status == KC_OK && (i = next++) < jobs.size(); k ^= 1) {
+            const UploadJob &J = jobs[i];
+            uint8_t *slot_buf = buf[(size_t)(2 * w + k)];
+            cudaEvent_t done = ev[(size_t)(2 * w + k)];
+            cudaError_t ce = cudaEventSynchronize(done);   /* this slot's previous copy has left */
+            if (ce == cudaSuccess && J.fill(slot_buf) != J.bytes) {
+                set_error("upload: gathered size mismatch");
+                fail(KC_E_IO);
+                return;
+            }
+            if (ce == cudaSuccess) ce = cudaMemcpyAsync(J.dst, slot_buf, J.bytes, cudaMemcpyHostToDevice, st[(size_t)w]);
+            if (ce == cudaSuccess) ce = cudaEventRecord(done, st[(size_t)w]);
+            if (ce != cudaSuccess) {
+                fail(cuda_status(ce, "upload copy"));
+                return;
+            }
+        }
+    };
+    if (status == KC_OK) {
+        std::vector<std::thread> th;
+        for (int w = 0; w < W; w++) th.emplace_back(worker, w);
+        for (std::thread &t : th) t.join();
+    }
+    for (int w = 0; w < W; w++)
+        if (st[(size_t)w]) {
+            const cudaError_t ce = cudaStreamSynchronize(st[(size_t)w]);
+            if (ce != cudaSuccess && status == KC_OK) status = cuda_status(ce, "upload copy");
+            cudaStreamDestroy(st[(size_t)w]);
+        }
+    for (int i = 0; i < 2 * W; i++) {
+        if (ev[(size_t)i]) cudaEventDestroy(ev[(size_t)i]);
+        if (buf[(size_t)i]) cudaFreeHost(buf[(size_t)i]);
+    }
+    if (status != KC_OK && !msg.empty()) set_error(msg);
+    return status;
 }
 
 /* The weight stream for a device of G SMs: every CTA's rows of every matrix,
- * contiguous in the order the step kernel consumes them. */
+ * contiguous in the order the step kernel consumes them (one upload job per
+ * CTA and layer, and one for its classifier rows: gathered from the mapped
+ * file into a pinned slot). */
 static int upload_stream(kc_model *m, int G) {
     StreamGeom g;
     int st = stream_geom(m, g);
@@ -314,22 +405,29 @@ static int upload_stream(kc_model *m, int G) {
         const size_t b = stream_cta_bytes(m, P);
         base[(size_t)j] = total;
         total += align256(b);
-        maxc = std::max(maxc, b);
+        maxc = std::max(maxc, std::max(stream_layer_bytes(P), (size_t)P[PH_F].bytes));
     }
     CK(cudaMalloc(&m->d_stream, total ? total : 256));
     CK(cudaMalloc(&m->d_cta_base, sizeof(unsigned long long) * (size_t)G));
     CK(cudaMemcpy(m->d_cta_base, base.data(), sizeof(unsigned long long) * (size_t)G, cudaMemcpyHostToDevice));
-    std::vector<uint8_t> host(maxc ? maxc : 16);
+    std::vector<UploadJob> jobs;
+    const int L = m->cfg.n_layers;
     for (int j = 0; j < G; j++) {
         PhasePlan P[NPHASE];
         make_plan(g, j, G, P);
-        const size_t b = fill_stream(m, P, host.data());
-        if (b != stream_cta_bytes(m, P)) {
-            set_error("weight stream size mismatch");
-            return KC_E_IO;
+        const size_t lb = stream_layer_bytes(P);
+        for (int part = 0; part <= L; part++) {
+            const size_t b = part < L ? lb : (size_t)P[PH_F].bytes;
+            if (b == 0) continue;
+            jobs.push_back({ m->d_stream + base[(size_t)j] + (size_t)part * lb, b, [m, g, j, G, part](uint8_t *dst) {
+                                 PhasePlan Q[NPHASE];
+                                 make_plan(g, j, G, Q);
+                                 return fill_stream_part(m, Q, part, dst);
+                             } });
         }
-        CK(cudaMemcpy(m->d_stream + base[(size_t)j], host.data(), b, cudaMemcpyHostToDevice));
     }
+    st = upload_jobs(jobs, std::max<size_t>(maxc, 16));
+    if (st != KC_OK) return st;
     m->stream_bytes = total;
     m->stream_G = G;
     return KC_OK;
@@ -367,15 +465,26 @@ extern "C" int kc_model_upload(kc_model *m) {
     for (const Item &it : items) total += align256(it.bytes);
     uint8_t *base = nullptr;
     CK(cudaMalloc(&base, total ? total : 256));
+    /* the file-layout arrays through the pinned pipeline, in pieces of PIECE bytes */
+    constexpr size_t PIECE = (size_t)4 << 20;
+    std::vector<UploadJob> jobs;
     size_t off = 0;
     for (const Item &it : items) {
-        cudaError_t e = cudaMemcpy(base + off, it.src, it.bytes, cudaMemcpyHostToDevice);
-        if (e != cudaSuccess) {
-            cudaFree(base);
-            return cuda_status(e, "upload");
+        for (size_t o = 0; o < it.bytes; o += PIECE) {
+            const size_t n = std::min(PIECE, it.bytes - o);
+            const uint8_t *src = (const uint8_t *)it.src + o;
+            jobs.push_back({ base + off + o, n, [src, n](uint8_t *dst) {
+                                 memcpy(dst, src, n);
+                                 return n;
+                             } });
         }
         *it.dst = base + off;
         off += align256(it.bytes);
+    }
+    st = upload_jobs(jobs, PIECE);
+    if (st != KC_OK) {
+        cudaFree(base);
+        return st;
     }
     m->dev_base = base;
     int dev = 0, sms = 0;
