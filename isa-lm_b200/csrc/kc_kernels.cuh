@@ -108,6 +108,39 @@ __device__ __forceinline__ int dot_q8(uint4 w, int4 x) {
  * nearest without contraction, as the reference builds with -ffp-contract=off.
  * Returns the 4 quants packed in a word; *d and *sum (sum of the 32 quants)
  * are valid on every lane of the group. */
+/* quant4's rule with 4 lanes per block, 8 values per lane (lane groups of 4
+ * consecutive lanes): the same block maximum, d, 127/amax and rounding, so
+ * the bits are the same; half the shuffles and divisions per value. Returns
+ * the 8 int8 values packed in a uint2. */
+__device__ __forceinline__ uint2 quant8(const float v[8], float *d, int *sum) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    uint2 word = make_uint2(0u, 0u);
+    int s = 0;
+    if (amax < 1e-30f) {
+        *d = 0.0f;
+    } else {
+        const float id = __fdiv_rn(127.0f, amax);
+        *d = __fdiv_rn(amax, 127.0f);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            float t = truncf(__fadd_rn(__fmul_rn(v[i], id), copysignf(0.5f, v[i])));
+            t = fminf(fmaxf(t, -127.0f), 127.0f);
+            const int qi = (int)t;
+            s += qi;
+            if (i < 4) word.x |= ((unsigned)qi & 0xffu) << (8 * i);
+            else word.y |= ((unsigned)qi & 0xffu) << (8 * (i - 4));
+        }
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    *sum = s;
+    return word;
+}
+
 __device__ __forceinline__ unsigned quant4(const float v[4], float *d, int *sum) {
     float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));

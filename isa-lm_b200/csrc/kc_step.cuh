@@ -818,21 +818,23 @@ __device__ __forceinline__ float embed1(const StepArgs &a, int tok, int cols, in
  * 1 / sqrt(ss / n + eps)) when norm_w is set. Source: a float vector in global
  * memory written by other CTAs (read through L2) or the embedding row of tok.
  * 1/rms: inv_given when > 0, else from ss = the sum of the G per-CTA partial
- * sums ssp, else reduced here. Every thread issues all its loads (P passes of
- * 64 blocks, 8 lanes per block) before it uses any, so a prologue costs one
- * round trip to L2. */
-constexpr int ACT_PASSES = 4;   /* passes of 64 blocks a thread holds in registers */
+ * sums ssp, else reduced here. Every thread issues all its loads before it
+ * uses any, so a prologue costs one round trip to L2. */
+constexpr int ACT_PASSES = 4;   /* float4 loads a thread holds in registers: 8192 columns at most */
 
 /* Starts copying the norm weights that this thread's act_float slots read
  * into wbuf (asynchronous, no wait): issued before a grid barrier, the copy
  * overlaps the wait instead of adding a round trip after it. */
 __device__ __forceinline__ void prefetch_norm(float *wbuf, const float *nw, int cols) {
-    const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 7) * 4;
+    const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 3) * 8;
     if (!nw) return;
 #pragma unroll
-    for (int p = 0; p < ACT_PASSES; p++) {
-        const int b = p * (NCT / 8) + (tid >> 3);
-        if (b < nb) cp_async16(wbuf + b * QK + j0, nw + b * QK + j0);
+    for (int p = 0; p < ACT_PASSES / 2; p++) {
+        const int b = p * (NCT / 4) + (tid >> 2);
+        if (b < nb) {
+            cp_async16(wbuf + b * QK + j0, nw + b * QK + j0);
+            cp_async16(wbuf + b * QK + j0 + 4, nw + b * QK + j0 + 4);
+        }
     }
     cp_async_commit();
 }
@@ -857,12 +859,13 @@ __device__ __forceinline__ void put_quant(const ActW &o, int b, int nb, int j0, 
  * 1 / sqrt(ss / n + eps)) when norm_w is set; x is a float vector in global
  * memory written by other CTAs (read through L2). 1/rms: from ss = the sum of
  * the G per-CTA partial sums ssp, else reduced here. Every thread issues all
- * its loads (up to 4 passes of 64 blocks, 8 lanes per block) before it uses
- * any, so the prologue costs one round trip to L2. */
+ * its loads (up to 2 passes of 128 blocks, 4 lanes per block, 8 values per
+ * lane) before it uses any, so the prologue costs one round trip to L2. */
 __device__ __noinline__ void act_float(float eps, const float *x, const float *norm_w, const float *ssp, int cols, ActW o,
                                        float *red, const float *wstaged) {
-    const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 7) * 4;
-    const int passes = (nb + NCT / 8 - 1) / (NCT / 8);
+    /* 4 lanes per block, 8 values per lane (two float4), passes of NCT / 4 blocks */
+    const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 3) * 8;
+    const int passes = (nb + NCT / 4 - 1) / (NCT / 4);
     const bool norm = norm_w != nullptr;
     if (tid == 0) ev(0, EV_ACT_ENTRY);
     /* one warp per CTA loads the G per-CTA sums of squares (the same few
@@ -875,20 +878,26 @@ __device__ __noinline__ void act_float(float eps, const float *x, const float *n
         const int idx = k * 32 + lane;
         part[k] = (ssw && idx < (int)gridDim.x) ? __ldcg(ssp + idx) : 0.0f;
     }
-    float4 v[ACT_PASSES], w[ACT_PASSES];
+    constexpr int NP = ACT_PASSES / 2;   /* passes of NCT / 4 blocks */
+    float4 v[2 * NP], w[2 * NP];
 #pragma unroll
-    for (int p = 0; p < ACT_PASSES; p++) {
-        const int b = p * (NCT / 8) + (tid >> 3);
-        v[p] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        w[p] = v[p];
-        if (p < passes && b < nb) v[p] = __ldcg((const float4 *)(x + b * QK + j0));
+    for (int p = 0; p < NP; p++) {
+        const int b = p * (NCT / 4) + (tid >> 2);
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            v[2 * p + h] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            w[2 * p + h] = v[2 * p + h];
+            if (p < passes && b < nb) v[2 * p + h] = __ldcg((const float4 *)(x + b * QK + j0 + 4 * h));
+        }
     }
     if (norm && wstaged) cp_async_wait_all();
 #pragma unroll
-    for (int p = 0; p < ACT_PASSES; p++) {
-        const int b = p * (NCT / 8) + (tid >> 3);
-        if (norm && p < passes && b < nb)
-            w[p] = *(const float4 *)((wstaged ? wstaged : norm_w) + b * QK + j0);
+    for (int p = 0; p < NP; p++) {
+        const int b = p * (NCT / 4) + (tid >> 2);
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+            if (norm && p < passes && b < nb)
+                w[2 * p + h] = *(const float4 *)((wstaged ? wstaged : norm_w) + b * QK + j0 + 4 * h);
     }
     float inv = 1.0f;
     if (norm) {
@@ -905,7 +914,7 @@ __device__ __noinline__ void act_float(float eps, const float *x, const float *n
         } else {
             float t = 0.0f;
 #pragma unroll
-            for (int p = 0; p < ACT_PASSES; p++) t += v[p].x * v[p].x + v[p].y * v[p].y + v[p].z * v[p].z + v[p].w * v[p].w;
+            for (int k = 0; k < 2 * NP; k++) t += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
             const float ss = block_sum(t, red);
             inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
         }
@@ -913,17 +922,26 @@ __device__ __noinline__ void act_float(float eps, const float *x, const float *n
     if (tid == 0) ev(0, EV_ACT_INV);
     /* the passes unrolled: their block maxima, divisions and stores overlap */
 #pragma unroll
-    for (int p = 0; p < ACT_PASSES; p++) {
+    for (int p = 0; p < NP; p++) {
         if (p >= passes) break;
-        const float4 c = v[p], cw = w[p];
-        float u[4] = { c.x, c.y, c.z, c.w };
+        const int b = p * (NCT / 4) + (tid >> 2);
+        const float4 c0 = v[2 * p], c1 = v[2 * p + 1], w0 = w[2 * p], w1 = w[2 * p + 1];
+        float u[8] = { c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w };
         if (norm) {
-            u[0] = __fmul_rn(__fmul_rn(u[0], inv), cw.x);
-            u[1] = __fmul_rn(__fmul_rn(u[1], inv), cw.y);
-            u[2] = __fmul_rn(__fmul_rn(u[2], inv), cw.z);
-            u[3] = __fmul_rn(__fmul_rn(u[3], inv), cw.w);
+            const float wv[8] = { w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w };
+#pragma unroll
+            for (int i = 0; i < 8; i++) u[i] = __fmul_rn(__fmul_rn(u[i], inv), wv[i]);
         }
-        put_quant(o, p * (NCT / 8) + (tid >> 3), nb, j0, u);
+        float d;
+        int sum;
+        const uint2 word = quant8(u, &d, &sum);
+        if (b < nb) {
+            *(uint2 *)((j0 < 16 ? o.xlo : o.xhi) + b * 16 + (j0 & 15)) = word;
+            if ((tid & 3) == 0) {
+                o.xd[b] = d;
+                o.xs[b] = 8 * sum;
+            }
+        }
     }
     if (tid == 0) ev(0, EV_ACT_QUANT);
     consumer_sync();
