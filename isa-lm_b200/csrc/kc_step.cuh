@@ -237,7 +237,10 @@ __device__ __forceinline__ void ev_init(bool enabled) {
 
 enum { EV_PRO_DONE = 2, EV_STAGE_READY = 3, EV_STAGE_DONE = 4, EV_ARRIVE = 5, EV_RELEASE = 6, EV_EMPTY_WAIT = 7,
        EV_ISSUE = 8, EV_ACT_ENTRY = 9, EV_ACT_LOADED = 10, EV_ACT_INV = 11, EV_ACT_QUANT = 12, EV_ATT_PRE = 13,
-       EV_ATT_TILE = 14, EV_ATT_PART = 15, EV_ATT_COMBINE = 16, EV_ATT_DONE = 17 };
+       EV_ATT_TILE = 14, EV_ATT_PART = 15, EV_ATT_COMBINE = 16, EV_ATT_DONE = 17,
+       /* checkpoints inside an attention item */
+       EV_ATT_ENTRY = 20, EV_ATT_ISSUED = 21, EV_ATT_QROPE = 22, EV_ATT_STORED = 23, EV_ATT_SYNCED = 24,
+       EV_ATT_SCORES = 25, EV_ATT_SOFTMAX = 26, EV_ATT_PARTIAL = 27, EV_ATT_ARRIVED = 28 };
 
 __device__ __forceinline__ void ev(int who, unsigned code) {
     unsigned long long *log = s_evp;
@@ -1175,7 +1178,7 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
             rvd = __ldcg(L.vd + (size_t)(t0 + tid) * a.n_kv_heads + g);
         }
     };
-    if (tid == 0) ev(0, 20);
+    if (tid == 0) ev(0, EV_ATT_ENTRY);
     /* this thread's first query pair and its RoPE angle, loaded before the tile
      * so that both round trips overlap */
     const float *cs = L.rcos + (size_t)pos * h2, *sn = L.rsin + (size_t)pos * h2;
@@ -1204,7 +1207,7 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
     } else {
         load_tile(t_begin);
     }
-    if (tid == 0) ev(0, 21);
+    if (tid == 0) ev(0, EV_ATT_ISSUED);
     /* qk_norm (model/transformer.c:244-248): 1/rms of each query head first */
     __shared__ float qinv[NCW];
     if (L.q_norm) {
@@ -1233,7 +1236,7 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
         S.sq[h * hd + 2 * i] = __fsub_rn(__fmul_rn(qa, c), __fmul_rn(qb, s));
         S.sq[h * hd + 2 * i + 1] = __fadd_rn(__fmul_rn(qa, s), __fmul_rn(qb, c));
     }
-    if (tid == 0) ev(0, 22);
+    if (tid == 0) ev(0, EV_ATT_QROPE);
     /* the split holding pos stores that position's K (after RoPE) and V */
     if (t_end == pos + 1 && warp < 2) {
         const float *src = a.qkv + a.q_dim + (warp ? a.kv_dim : 0) + (size_t)g * hd;
@@ -1349,11 +1352,11 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
             S.skd[tid] = own ? S.knd[0] : rkd;
             S.svd[tid] = own ? S.knd[1] : rvd;
         }
-        if (tid == 0) ev(0, 23);
+        if (tid == 0) ev(0, EV_ATT_STORED);
         if (KV == KC_F32 && t0 == t_begin) cp_async_wait_all();
         if (t0 + ATT_TILE < t_end) load_tile(t0 + ATT_TILE);
         consumer_sync();
-        if (tid == 0) ev(0, 24);
+        if (tid == 0) ev(0, EV_ATT_SYNCED);
         /* scores: tpd threads per (head, position); every lane takes part in
          * the shuffles, those past the tile with zero */
         for (int pi = tid / tpd; pi < group * ATT_TILE; pi += NCT / tpd) {
@@ -1390,7 +1393,7 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
             if (part == 0) S.sp[h * ATT_TILE + t] = s;
         }
         consumer_sync();
-        if (tid == 0) ev(0, 25);
+        if (tid == 0) ev(0, EV_ATT_SCORES);
         for (int h = warp; h < group; h += NCW) {
             const float s0 = S.sp[h * ATT_TILE + lane], s1 = S.sp[h * ATT_TILE + 32 + lane];
             const float m_old = S.sm[h], m_new = fmaxf(m_old, warp_max(fmaxf(s0, s1)));
@@ -1406,7 +1409,7 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
             }
         }
         consumer_sync();
-        if (tid == 0) ev(0, 26);
+        if (tid == 0) ev(0, EV_ATT_SOFTMAX);
         /* outputs: tpo threads per (head, dimension), positions interleaved */
 #pragma unroll
         for (int k = 0; k < MAXO; k++) {
@@ -1474,7 +1477,7 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
         ph[hd + 1] = S.sl[tid];
     }
     consumer_sync();
-    if (tid == 0) ev(0, 27);
+    if (tid == 0) ev(0, EV_ATT_PARTIAL);
     /* the head's splits wait for each other (all resident: a bounded spin),
      * then each combines its slice of the group's outputs. The head's arrival
      * counter grows over the launch: this round is complete at att_base +
@@ -1485,7 +1488,7 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
     if (tid == 0) {
         __threadfence();
         atomicAdd(arrived, 1u);
-        ev(0, 28);
+        ev(0, EV_ATT_ARRIVED);
         unsigned it = 0;
         while (ld_acquire(arrived) < att_base + (unsigned)active) {
             if (++it > (1u << 24)) {
