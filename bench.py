@@ -245,11 +245,18 @@ def tp_decode(dist, K, W, hbm_peak):
             "exchange": "O and down partials as tagged 64-bit NVLink peer stores inside the step kernel (no NCCL on the token path)"}
 
 
+def arm_config(ctx):
+    """The workload both arms measure (the `config` of their JSON lines)."""
+    return {"workload": f"{ARGS.config} batch-1 greedy decode at KV context {ctx}", "model": ARGS.config,
+            "ctx": ctx, "batch": 1, "kv_cache": "f32"}
+
+
 def main():
     import numpy as np
     import krafla_b200 as kb
     dist = dist_init()
-    kb.set_device(LOCAL)
+    if ARGS.impl != "reference":   # the reference arm runs on the host cores only
+        kb.set_device(LOCAL)
     hbm_peak, peak_kind = peaks()
     if RANK == 0:
         path = kb.ensure_model(ARGS.config, MODEL_DIR)
@@ -263,15 +270,14 @@ def main():
         if RANK != 0:
             return
         cfg = kb.Model(path, upload=False).config
-        ctx = min(ARGS.ctx, cfg["max_seq"] - K - W)
+        ctx = min(ARGS.ctx, cfg["max_seq"] - K - W - 1)
         cfg["shared"] = model_cfg.get("shared", 0)
         r = cpu_reference(path, cfg, ctx, K, W)
         line = {"metric": "batch-1 decode tok/s", "value": round(r["decode_tok_s"], 3), "unit": "tok/s",
                 "impl": "reference", "n_gpus": ARGS.gpus, "steps": K, "warmup": W,
                 "ms_per_step": round(1000.0 / r["decode_tok_s"], 3), "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot, f32 accumulate", "data": "synthetic",
-                "config": {"workload": f"{ARGS.config} decode at KV context {ctx}", "model": ARGS.config,
-                           "ctx": ctx, "batch": 1},
+                "config": dict(arm_config(ctx), parallelism="host cores (oracle/_ref)"),
                 "cpu_baseline": {"value": round(r["decode_tok_s"], 3), "unit": "tok/s", "cores": r["cores"],
                                  "kind": "reference", "isa": r["isa"], "sample": r["sample"]},
                 "e2e": {"value": round(r["decode_tok_s"], 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
@@ -429,9 +435,8 @@ def main():
             "steps": K, "warmup": W, "ms_per_step": round(ms_max / K, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot (dp4a), f32 accumulate",
             "data": "synthetic (seeded N(0,0.02) weights, uniform prompt ids)",
-            "config": {"workload": f"{ARGS.config} batch-1 greedy decode at KV context {ctx}",
-                       "model": ARGS.config, "ctx": ctx, "batch": 1, "kv_cache": "f32",
-                       "parallelism": f"replicas x{WORLD}", "l2": "weights 871 MB > 126 MB L2: streamed each step"},
+            "config": dict(arm_config(ctx), parallelism=f"replicas x{WORLD}",
+                           l2="weights 871 MB > 126 MB L2: streamed each step"),
             "hbm_roofline_frac": round(bpt * value / WORLD / 1e9 / hbm_peak, 4),
             "bytes_per_token": int(bpt),
             "roofline": {"bound": "hbm", "kernel": "step_kernel (whole decode step, one launch for K steps)",
