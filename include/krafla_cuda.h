@@ -223,8 +223,9 @@ int kc_matvec_dev(float *y, int type, int d_f16, const void *wq, const void *wd,
  * y = W . quantize_q8(x) for a float activation x on the device: the
  * quantized x lives in a file-scope device scratch of the library, so the call
  * allocates nothing, for callers that cannot allocate device memory per call
- * (inside a captured CUDA graph, or a serving loop whose memory is fixed after
- * set-up). cols <= KC_NOALLOC_MAX_COLS, else KC_E_SHAPE with no launch. The
+ * (a serving loop whose device memory is all reserved at set-up, or a host
+ * framework that owns the device allocator and lets no library allocate on
+ * its own). cols <= KC_NOALLOC_MAX_COLS, else KC_E_SHAPE with no launch. The
  * first call on each device looks up the scratch's address with that device
  * current, so it should come before any stream capture. The scratch is one
  * per device: calls that overlap in time (different streams or threads) race

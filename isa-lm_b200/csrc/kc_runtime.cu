@@ -1,7 +1,7 @@
 /* Runtime of libkrafla_cuda: HBM upload of the model, the decode state with
- * its device arena and KV cache, one CUDA graph per token step (replayed for
- * every token: token and position live in device memory), and the C ABI of
- * include/krafla_cuda.h. */
+ * its device arena and KV cache, the launches of the persistent step kernel
+ * (one cooperative launch for many token steps: token and position live in
+ * device memory), and the C ABI of include/krafla_cuda.h. */
 #include <cmath>
 #include <cstdio>
 #include <cstring>
