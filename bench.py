@@ -11,7 +11,8 @@ W untimed and K timed decode steps). Weights (871 MB) are larger than L2, so
 every step streams them from HBM.
 
   value  decode tok/s of all ranks: K tokens per rank / max over ranks of the
-         CUDA-event time of the K graph-replayed steps (inputs in HBM)
+         CUDA-event time of the K steps (one launch of the persistent step
+         kernel; inputs in HBM)
   e2e    the same through the drop-in API with host buffers: K kc_forward calls
          (token and position in, the [vocab] float logits out to the host, the
          reference's ml_bench loop with its host argmax), wall clock
@@ -298,7 +299,7 @@ def main():
     st.prefill(toks[:-1], 0)
     start_tok, start_pos = int(toks[-1]), ctx - 1
 
-    # --- value: device time of K graph replays (CUDA events on the launching stream)
+    # --- value: device time of K steps in one launch (CUDA events on the launching stream)
     with Clocks() as clk:
         if dist is not None:
             dist.barrier()
