@@ -255,8 +255,10 @@ def arm_config(ctx):
 def main():
     import numpy as np
     import krafla_b200 as kb
-    dist = dist_init()
-    if ARGS.impl != "reference":   # the reference arm runs on the host cores only
+    if ARGS.impl == "reference" and RANK != 0:
+        return   # the reference arm: rank 0 alone, on the host cores (no process group, no GPU)
+    dist = dist_init() if ARGS.impl != "reference" else None
+    if ARGS.impl != "reference":
         kb.set_device(LOCAL)
     hbm_peak, peak_kind = peaks()
     if RANK == 0:
@@ -268,8 +270,6 @@ def main():
     model_cfg = dict(kb.CONFIGS[ARGS.config])
 
     if ARGS.impl == "reference":
-        if RANK != 0:
-            return
         cfg = kb.Model(path, upload=False).config
         ctx = min(ARGS.ctx, cfg["max_seq"] - K - W - 1)
         cfg["shared"] = model_cfg.get("shared", 0)

@@ -32,3 +32,21 @@ def test_reference_arm_json_line(tmp_path):
     cb = d["cpu_baseline"]
     assert cb["kind"] == "reference" and cb["value"] == d["value"] and cb["cores"] >= 1 and cb["sample"]
     assert d["e2e"] == {"value": d["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_under_torchrun(tmp_path):
+    """Two ranks (as the driver's scaling runs launch it): rank 0 alone prints the
+    line, the other rank exits 0 without work; no process group is needed."""
+    ref = os.path.join(ROOT, "oracle", "_ref")
+    if not os.path.isdir(ref) or not any(f.endswith(".so") for f in os.listdir(ref)):
+        pytest.skip("oracle/_ref not built")
+    env = dict(os.environ, KRAFLA_MODEL_DIR=str(tmp_path))
+    out = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                          "--master-addr", "127.0.0.1", "--master-port", "29631", os.path.join(ROOT, "bench.py"),
+                          "--impl", "reference", "--gpus", "2", "--config", "cfg0", "--ctx", "32", "--steps", "2",
+                          "--warmup", "1"], capture_output=True, text=True, env=env, timeout=600, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["n_gpus"] == 2 and d["value"] > 0
