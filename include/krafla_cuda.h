@@ -23,6 +23,8 @@ extern "C" {
 enum { KC_OK = 0, KC_E_IO = 1, KC_E_FORMAT = 2, KC_E_SHAPE = 3, KC_E_NOMEM = 4, KC_E_ISA = 5 };
 /* tensor and KV cache types (core/ml.h:67) */
 enum { KC_F32 = 0, KC_Q8_0 = 1, KC_Q4_0 = 2, KC_F16 = 3 };
+/* RoPE scaling kinds of the header's rope_type (model/mlb.h:34) */
+enum { KC_ROPE_NONE = 0, KC_ROPE_LLAMA3 = 1, KC_ROPE_LINEAR = 2, KC_ROPE_YARN = 3 };
 
 /* The model header, field for field in the order of ml_config
  * (model/mlb.h:9-32), so that a reference build can pass &m->cfg. */
@@ -216,7 +218,8 @@ int kc_rmsnorm_quantize_dev(int8_t *q, float *d, float *xn, const float *x, cons
                             void *stream);
 /* Replaces ml_k_matvec_q8 / ml_k_matvec_q4 (k_scalar.c:4-37) over all rows:
  * y[r] = sum_b int32(w.x over block b) * d_w[r,b] * d_x[b]. wd holds f16
- * scales when d_f16 is set. Uses the decode GEMV kernel. */
+ * scales when d_f16 is set. Uses the decode GEMV kernel. Asynchronous on
+ * `stream`: a device wait that gave up is reported by the next kc_dev_sync. */
 int kc_matvec_dev(float *y, int type, int d_f16, const void *wq, const void *wd, int rows, int cols,
                   const int8_t *xq, const float *xd, void *stream);
 /* No counterpart in the reference (its CPU kernels need no device memory).
@@ -230,7 +233,8 @@ int kc_matvec_dev(float *y, int type, int d_f16, const void *wq, const void *wd,
  * current, so it should come before any stream capture. The scratch is one
  * per device: calls that overlap in time (different streams or threads) race
  * on it; calls on one stream are ordered. Same results as kc_quantize_q8_dev
- * then kc_matvec_dev. */
+ * then kc_matvec_dev. A device wait that gave up is reported by the next
+ * kc_dev_sync. */
 #define KC_NOALLOC_MAX_COLS 16384
 int kc_matvec_f32_noalloc(float *y, int type, int d_f16, const void *wq, const void *wd, int rows, int cols,
                           const float *x, void *stream);
@@ -252,7 +256,17 @@ void *kc_dev_alloc(size_t bytes);
 void kc_dev_free(void *p);
 int kc_memcpy_htod(void *dst, const void *src, size_t bytes);
 int kc_memcpy_dtoh(void *dst, const void *src, size_t bytes);
+/* Waits for the current device. KC_E_IO when a kernel-level matvec call
+ * (kc_matvec_dev, kc_matvec_f32_noalloc) on it had a device wait give up
+ * since the last kc_dev_sync (its error word is then cleared). */
 int kc_dev_sync(void);
+/* Diagnostics for tests of the error path: the polls of the kernel-level
+ * matvec's first wait on each chunk of weights (0 restores the default of
+ * about a second). A wait that runs out flags the device error word and then
+ * waits for the chunk, so the results stay correct and the next kc_dev_sync
+ * returns KC_E_IO. No counterpart in the reference (its CPU kernels do not
+ * wait on copies). */
+int kc_debug_wait_limit(unsigned polls);
 
 #ifdef __cplusplus
 }

@@ -203,12 +203,16 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *b, unsigned bytes) {
 __device__ __forceinline__ void mbar_arrive(uint64_t *b) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
 }
+/* Polls of an mbarrier wait before it gives up (about a second under load). */
+constexpr unsigned WAIT_POLLS = 1u << 22;
+
 /* Waits for the phase with the given parity to complete; gives up (false)
- * after a bounded number of polls so that no wait can hang the GPU, or as soon
- * as the error word (when given) is non-zero. */
-__device__ __forceinline__ bool mbar_wait(uint64_t *b, unsigned parity, const unsigned *err = nullptr) {
+ * after `limit` polls so that no wait can hang the GPU, or as soon as the
+ * error word (when given) is non-zero. */
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, unsigned parity, const unsigned *err = nullptr,
+                                          unsigned limit = WAIT_POLLS) {
     const uint32_t a = smem_u32(b);
-    for (unsigned it = 0; it < (1u << 22); it++) {
+    for (unsigned it = 0; it < limit; it++) {
         if (err && (it & 255) == 255 && *(volatile const unsigned *)err) return false;
         unsigned ok;
         asm volatile(

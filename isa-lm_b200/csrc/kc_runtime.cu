@@ -544,8 +544,8 @@ struct kc_state {
  * formulas of transformers: linear, yarn, llama3), in double. */
 static double rope_inv_freq(const kc_config &c, int i) {
     const double inv = std::pow((double)c.rope_theta, -2.0 * i / c.head_dim);
-    if (c.rope_type == 2) return inv / c.rope_factor;
-    if (c.rope_type == 3) {
+    if (c.rope_type == KC_ROPE_LINEAR) return inv / c.rope_factor;
+    if (c.rope_type == KC_ROPE_YARN) {
         const double hd = c.head_dim, orig = c.rope_orig_max_seq, lb = 2.0 * std::log((double)c.rope_theta);
         const double pi2 = 2.0 * 3.14159265358979323846;
         double lo = std::floor(hd * std::log(orig / ((double)c.rope_low_freq_factor * pi2)) / lb);
@@ -557,7 +557,7 @@ static double rope_inv_freq(const kc_config &c, int i) {
         ramp = ramp < 0.0 ? 0.0 : (ramp > 1.0 ? 1.0 : ramp);
         return inv / c.rope_factor * ramp + inv * (1.0 - ramp);
     }
-    if (c.rope_type != 1) return inv;
+    if (c.rope_type != KC_ROPE_LLAMA3) return inv;
     const double f = c.rope_factor, lo = c.rope_low_freq_factor, hi = c.rope_high_freq_factor;
     const double orig = c.rope_orig_max_seq, wavelen = 2.0 * 3.14159265358979323846 / inv;
     if (wavelen < orig / hi) return inv;
@@ -569,20 +569,53 @@ static double rope_inv_freq(const kc_config &c, int i) {
 /* Bytes per cache element of a KV type. */
 static size_t kv_elem_bytes(int kv_type) { return kv_type == KC_F32 ? 4 : (kv_type == KC_F16 ? 2 : 1); }
 
-static unsigned *g_err_word = nullptr;   /* device error word of the kernel-level entry points */
 static const int KC_MAX_SMEM = 227 * 1024;
+constexpr int KC_MAX_DEVICES = 64;
 
-/* Opt-in to the full shared memory of an sm_100 CTA (outside any stream capture). */
+/* The calling thread's current device, checked against the per-device tables. */
+static int current_device(int &dev) {
+    CK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= KC_MAX_DEVICES) {
+        set_error("device index " + std::to_string(dev) + " beyond this library's table of " +
+                  std::to_string(KC_MAX_DEVICES));
+        return KC_E_SHAPE;
+    }
+    return KC_OK;
+}
+
+/* Opt-in to the full shared memory of an sm_100 CTA, once per device (the
+ * attribute belongs to the current device; outside any stream capture). */
 static int set_smem_attributes() {
-    static bool done = false;
-    if (done) return KC_OK;
+    static bool done[KC_MAX_DEVICES];
+    int dev = 0;
+    const int rc = current_device(dev);
+    if (rc != KC_OK) return rc;
+    if (done[dev]) return KC_OK;
     const void *fns[] = { (const void *)step_kernel, (const void *)matvec_kernel, (const void *)activation_kernel };
     for (const void *f : fns) {
         cudaFuncAttributes fa;
         CK(cudaFuncGetAttributes(&fa, f));
         CK(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, KC_MAX_SMEM - (int)fa.sharedSizeBytes));
     }
-    done = true;
+    done[dev] = true;
+    return KC_OK;
+}
+
+/* The kernel-level matvec's error word: one per device (a __device__ variable
+ * lives in every device's copy of this module), sticky until kc_dev_sync
+ * reports it. Its address on each device, looked up on first use. */
+static __device__ unsigned g_kl_err;
+static unsigned *g_kl_err_ptr[KC_MAX_DEVICES];
+/* Polls of the kernel-level consumers' first wait on a chunk (kc_debug_wait_limit). */
+static unsigned g_wait_limit = WAIT_POLLS;
+
+static int kl_err_word(int dev, unsigned *&w) {
+    if (!g_kl_err_ptr[dev]) {
+        void *p = nullptr;
+        CK(cudaGetSymbolAddress(&p, g_kl_err));
+        g_kl_err_ptr[dev] = (unsigned *)p;
+    }
+    w = g_kl_err_ptr[dev];
     return KC_OK;
 }
 
@@ -925,7 +958,7 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
     /* RoPE tables: double, stored as float (model/transformer.c:146-162) */
     {
         std::vector<float> cs(T * h2), sn(T * h2), lc, ls_;
-        const double af = c.rope_type == 3 ? c.rope_attn_factor : 1.0;
+        const double af = c.rope_type == KC_ROPE_YARN ? c.rope_attn_factor : 1.0;
         if (s->lcos) { lc.resize(T * h2); ls_.resize(T * h2); }
         for (size_t i = 0; i < h2; i++) {
             const double freq = rope_inv_freq(c, (int)i);
@@ -1279,15 +1312,16 @@ extern "C" int kc_rmsnorm_quantize_dev(int8_t *q, float *d, float *xn, const flo
 
 extern "C" int kc_matvec_dev(float *y, int type, int d_f16, const void *wq, const void *wd, int rows, int cols,
                              const int8_t *xq, const float *xd, void *stream) {
+    clear_error();
     if (rows <= 0 || cols <= 0 || cols % QK || (type != KC_Q8_0 && type != KC_Q4_0)) return KC_E_SHAPE;
-    if (set_smem_attributes() != KC_OK) return KC_E_IO;
-    if (!g_err_word) {
-        CK(cudaMalloc(&g_err_word, sizeof(unsigned)));
-        CK(cudaMemset(g_err_word, 0, sizeof(unsigned)));
-    }
+    int dev = 0, rc = current_device(dev);
+    if (rc == KC_OK) rc = set_smem_attributes();
+    unsigned *err = nullptr;
+    if (rc == KC_OK) rc = kl_err_word(dev, err);
+    if (rc != KC_OK) return rc;
     MatvecArgs p{};
     p.m = PMat{ (const uint8_t *)wq, wd, rows, type, d_f16 };
-    p.cols = cols; p.xq = xq; p.xd = xd; p.y = y; p.err = g_err_word;
+    p.cols = cols; p.xq = xq; p.xd = xd; p.y = y; p.err = err; p.wait_limit = g_wait_limit;
     p.slot_bytes = stage_slot_bytes(type, d_f16, cols, 0);
     p.act_bytes = (cols + 8 * (cols / QK) + 15) & ~15;
     cudaFuncAttributes fa;
@@ -1295,9 +1329,8 @@ extern "C" int kc_matvec_dev(float *y, int type, int d_f16, const void *wq, cons
     p.nstage = ring_stages(p.slot_bytes, p.act_bytes, (int)fa.sharedSizeBytes);
     if (p.nstage < 2) return KC_E_SHAPE;
     const int smem = smem_fixed_bytes(p.nstage, p.act_bytes) + p.nstage * p.slot_bytes;
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int sms = 148;
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int grid = rows < sms ? rows : sms;
     matvec_kernel<<<grid, STEP_THREADS, smem, (cudaStream_t)stream>>>(p);
     CK(cudaGetLastError());
@@ -1308,15 +1341,16 @@ extern "C" int kc_matvec_dev(float *y, int type, int d_f16, const void *wq, cons
 
 /* Device scratch of kc_matvec_f32_noalloc: the quantized activation
  * (KC_NOALLOC_MAX_COLS int8 quants, then their block scales) and the ring's
- * error word. Zero at module load; the error word is cleared on the call's
- * stream at the start of every call. One copy per device, shared by all
- * callers: calls that overlap in time (different streams or threads) race on
- * it. */
+ * error word. Zero at module load; the quants and scales are rewritten by
+ * every call before they are read, and the error word is sticky: a wait that
+ * gave up stays flagged until kc_dev_sync reports and clears it. One copy per
+ * device, shared by all callers: calls that overlap in time (different
+ * streams or threads) race on it. */
 constexpr int NOALLOC_XD_OFF = KC_NOALLOC_MAX_COLS;
 constexpr int NOALLOC_ERR_OFF = NOALLOC_XD_OFF + (KC_NOALLOC_MAX_COLS / QK) * 4;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_ERR_OFF + 256];
 
-static unsigned char *g_noalloc_ptr[64];   /* the scratch's address on each device, set on first use */
+static unsigned char *g_noalloc_ptr[KC_MAX_DEVICES];   /* the scratch's address on each device, set on first use */
 
 extern "C" int kc_matvec_f32_noalloc(float *y, int type, int d_f16, const void *wq, const void *wd, int rows, int cols,
                                      const float *x, void *stream) {
@@ -1328,8 +1362,8 @@ extern "C" int kc_matvec_f32_noalloc(float *y, int type, int d_f16, const void *
         return KC_E_SHAPE;
     }
     int dev = 0;
-    CK(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return KC_E_SHAPE;
+    const int rc = current_device(dev);
+    if (rc != KC_OK) return rc;
     if (!g_noalloc_ptr[dev]) {
         /* once per device, with that device current (the first call should come before any stream capture) */
         void *ptr = nullptr;
@@ -1342,13 +1376,12 @@ extern "C" int kc_matvec_f32_noalloc(float *y, int type, int d_f16, const void *
     float *xd = (float *)(scr + NOALLOC_XD_OFF);
     unsigned *err = (unsigned *)(scr + NOALLOC_ERR_OFF);
     const cudaStream_t st = (cudaStream_t)stream;
-    CK(cudaMemsetAsync(err, 0, sizeof(unsigned), st));
     const int asmem = 128 + cols + 8 * (cols / QK) + 16;
     activation_kernel<<<1, NCT, asmem, st>>>(x, nullptr, 0.0f, cols, xq, xd, nullptr);
     CK(cudaGetLastError());
     MatvecArgs p{};
     p.m = PMat{ (const uint8_t *)wq, wd, rows, type, d_f16 };
-    p.cols = cols; p.xq = xq; p.xd = xd; p.y = y; p.err = err;
+    p.cols = cols; p.xq = xq; p.xd = xd; p.y = y; p.err = err; p.wait_limit = g_wait_limit;
     p.slot_bytes = stage_slot_bytes(type, d_f16, cols, 0);
     p.act_bytes = (cols + 8 * (cols / QK) + 15) & ~15;
     cudaFuncAttributes fa;
@@ -1386,7 +1419,35 @@ extern "C" void *kc_dev_alloc(size_t bytes) {
 extern "C" void kc_dev_free(void *p) { if (p) cudaFree(p); }
 extern "C" int kc_memcpy_htod(void *dst, const void *src, size_t n) { CK(cudaMemcpy(dst, src, n, cudaMemcpyHostToDevice)); return KC_OK; }
 extern "C" int kc_memcpy_dtoh(void *dst, const void *src, size_t n) { CK(cudaMemcpy(dst, src, n, cudaMemcpyDeviceToHost)); return KC_OK; }
-extern "C" int kc_dev_sync(void) { CK(cudaDeviceSynchronize()); return KC_OK; }
+/* Waits for the current device, then reads (and clears) the sticky error
+ * words of the kernel-level matvec entry points on it. */
+extern "C" int kc_dev_sync(void) {
+    clear_error();
+    CK(cudaDeviceSynchronize());
+    int dev = 0;
+    const int rc = current_device(dev);
+    if (rc != KC_OK) return rc;
+    unsigned *words[2] = { g_kl_err_ptr[dev], g_noalloc_ptr[dev] ? (unsigned *)(g_noalloc_ptr[dev] + NOALLOC_ERR_OFF) : nullptr };
+    const char *names[2] = { "kc_matvec_dev", "kc_matvec_f32_noalloc" };
+    std::string msg;
+    for (int i = 0; i < 2; i++) {
+        if (!words[i]) continue;
+        unsigned w = 0;
+        CK(cudaMemcpy(&w, words[i], sizeof w, cudaMemcpyDeviceToHost));
+        if (!w) continue;
+        CK(cudaMemset(words[i], 0, sizeof w));
+        msg += std::string(msg.empty() ? "" : "; ") + names[i] + ": a device wait gave up (error word " +
+               std::to_string(w) + ")";
+    }
+    if (msg.empty()) return KC_OK;
+    set_error(msg);
+    return KC_E_IO;
+}
+
+extern "C" int kc_debug_wait_limit(unsigned polls) {
+    g_wait_limit = polls ? polls : WAIT_POLLS;
+    return KC_OK;
+}
 
 /* ------------------------------------------------------------------ sampler */
 

@@ -458,9 +458,15 @@ __device__ __forceinline__ void ring_next(Ring &rg) {
     }
 }
 
-/* Consumer: waits until the current slot's chunk has landed. */
-__device__ __forceinline__ const uint8_t *ring_wait_full(const Ring &rg, unsigned *err) {
-    if (!mbar_wait(&rg.full[rg.slot], rg.round & 1u, err) && (threadIdx.x & 31) == 0) atomicOr(err, 2u);
+/* Consumer: waits until the current slot's chunk has landed. A wait that
+ * runs out of its `limit` polls flags error bit 2, then waits once more
+ * (bounded) for the copy: no slot is handed back to the producer, and no CTA
+ * leaves, while a bulk copy into it may still be in flight. */
+__device__ __forceinline__ const uint8_t *ring_wait_full(const Ring &rg, unsigned *err, unsigned limit = WAIT_POLLS) {
+    if (!mbar_wait(&rg.full[rg.slot], rg.round & 1u, nullptr, limit)) {
+        if ((threadIdx.x & 31) == 0) atomicOr(err, 2u);
+        mbar_wait(&rg.full[rg.slot], rg.round & 1u);
+    }
     return rg.base + (size_t)rg.slot * rg.slot_bytes;
 }
 
@@ -471,10 +477,13 @@ __device__ __forceinline__ void ring_release(Ring &rg) {
     ring_next(rg);
 }
 
-/* Producer: waits for the chunk's slot to be free and issues its bulk copy. */
+/* Producer: waits for the chunk's slot to be free and issues its bulk copy.
+ * The wait does not leave early on another CTA's error: every consumer warp
+ * hands back every slot (its own waits drain), so the slot is re-armed only
+ * after its last chunk was read. */
 __device__ __forceinline__ uint8_t *ring_issue(Ring &rg, unsigned bytes, unsigned *err) {
     ev(1, EV_EMPTY_WAIT);
-    if (rg.round > 0 && !mbar_wait(&rg.empty[rg.slot], (rg.round - 1) & 1u, err)) atomicOr(err, 2u);
+    if (rg.round > 0 && !mbar_wait(&rg.empty[rg.slot], (rg.round - 1) & 1u)) atomicOr(err, 2u);
     mbar_expect_tx(&rg.full[rg.slot], bytes);
     return rg.base + (size_t)rg.slot * rg.slot_bytes;
 }
@@ -758,7 +767,8 @@ __device__ __forceinline__ unsigned long long finish_phase(int kind, const float
 
 /* Consumer of the kernel-level matvec (rows [r0, r1) as produce_rows staged them). */
 template <int TYPE, bool D16>
-__device__ void consume_rows(Ring &rg, int cols, int r0, int r1, float *y, const Act &x, unsigned *err) {
+__device__ void consume_rows(Ring &rg, int cols, int r0, int r1, float *y, const Act &x, unsigned *err,
+                             unsigned limit) {
     if (r0 >= r1) return;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nb = cols / QK;
     const int qrow = TYPE == T_Q4 ? cols / 2 : cols, drow = nb * (D16 ? 2 : 4);
@@ -766,7 +776,7 @@ __device__ void consume_rows(Ring &rg, int cols, int r0, int r1, float *y, const
     stage_geom(TYPE, D16, cols, 0, R, qbytes, dbytes);
     for (int ra = r0; ra < r1; ra += R) {
         const int nr = min(R, r1 - ra);
-        const uint8_t *slot = ring_wait_full(rg, err);
+        const uint8_t *slot = ring_wait_full(rg, err, limit);
         const Lay L{ qrow, qbytes + (int)(((size_t)ra * drow) & 15), drow, 0 };
         consume_chunk<TYPE, D16, false>(slot, L, nr, nb, 1, -1, (ra - r0) / GROUP_ROWS, ra, x, nullptr, y, lane, warp);
         ring_release(rg);
@@ -1827,7 +1837,8 @@ struct MatvecArgs {
     const int8_t *xq;
     const float *xd;
     float *y;
-    unsigned *err;
+    unsigned *err;                 /* sticky device error word of the entry point */
+    unsigned wait_limit;           /* polls of the consumers' first wait on a chunk */
     int nstage, slot_bytes, act_bytes;
 };
 
@@ -1846,11 +1857,11 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) matvec_kernel(const __grid_co
     const ActW w = act_layout(sh.act, p.cols);
     act_prequant(p.xq, p.xd, p.cols, w);
     if (p.m.type == T_Q4) {
-        if (p.m.d16) consume_rows<T_Q4, true>(rg, p.cols, r0, r1, p.y, act_view(w), p.err);
-        else consume_rows<T_Q4, false>(rg, p.cols, r0, r1, p.y, act_view(w), p.err);
+        if (p.m.d16) consume_rows<T_Q4, true>(rg, p.cols, r0, r1, p.y, act_view(w), p.err, p.wait_limit);
+        else consume_rows<T_Q4, false>(rg, p.cols, r0, r1, p.y, act_view(w), p.err, p.wait_limit);
     } else {
-        if (p.m.d16) consume_rows<T_Q8, true>(rg, p.cols, r0, r1, p.y, act_view(w), p.err);
-        else consume_rows<T_Q8, false>(rg, p.cols, r0, r1, p.y, act_view(w), p.err);
+        if (p.m.d16) consume_rows<T_Q8, true>(rg, p.cols, r0, r1, p.y, act_view(w), p.err, p.wait_limit);
+        else consume_rows<T_Q8, false>(rg, p.cols, r0, r1, p.y, act_view(w), p.err, p.wait_limit);
     }
 }
 

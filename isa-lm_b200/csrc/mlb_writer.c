@@ -24,6 +24,8 @@
 #include <string.h>
 #include <unistd.h>
 
+#include "mlb_writer.h"
+
 #define QK 32
 #define TINY 1e-30f    /* tools/mlb.py:15 */
 #define SMALL 1e-6f    /* tools/mlb.py:152 */
@@ -202,24 +204,6 @@ void kw_normal(uint64_t seed, uint64_t tid, uint64_t i0, long n, double sigma, f
 }
 
 /* ------------------------------------------------------------ writer */
-
-typedef struct {
-    int dim, n_layers, n_heads, n_kv_heads, hidden_dim, vocab, max_seq;
-    float rope_theta, norm_eps;
-    int wtype;           /* 1 = Q8_0, 2 = Q4_0 */
-    int shared;          /* tied embedding / classifier */
-    int rope_type;       /* 0 none, 1 llama3, 2 linear, 3 yarn */
-    float rope_factor, rope_lo, rope_hi;
-    int rope_orig;
-    int q8_mask;         /* Q4 models: classes kept in Q8 (tools/mlb.py:54) */
-    int qkv_bias;
-    int head_dim;        /* 0: dim / n_heads */
-    int scale_f16;
-    double sigma;        /* weight standard deviation */
-    double bias_sigma;
-    uint64_t seed;
-    int nthreads;
-} kw_config;
 
 typedef struct {
     FILE *f;

@@ -19,8 +19,16 @@ Status codes and their meaning are the reference's ml_status (core/ml.h:7-14).
 """
 import ctypes as C
 import os
+import sys
 
 import numpy as np
+
+_PARENT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if _PARENT not in sys.path:
+    sys.path.insert(0, _PARENT)
+# the synthetic models (configs, files, headers) live in a module of their own
+# that loads no library: bench.py's CPU arm uses it without this package
+from krafla_models import CONFIGS, Q8M, ensure_model, model_path, read_header, write_model  # noqa: E402,F401
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libkrafla_cuda.so")
@@ -93,7 +101,7 @@ def lib():
             "kc_matvec_f32_noalloc": (I, [P, I, I, P, P, I, I, P, P]),
             "kc_matmul_dev": (I, [P, I, I, P, P, I, I, P, P, I, P]), "kc_block_sums_dev": (I, [P, I, P, I, I, P, P]),
             "kc_dev_alloc": (P, [S]), "kc_dev_free": (None, [P]), "kc_memcpy_htod": (I, [P, P, S]),
-            "kc_memcpy_dtoh": (I, [P, P, S]), "kc_dev_sync": (I, []),
+            "kc_memcpy_dtoh": (I, [P, P, S]), "kc_dev_sync": (I, []), "kc_debug_wait_limit": (I, [C.c_uint]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -403,82 +411,16 @@ def block_sums(wtype, wq, rows, cols, xq):
 
 # ---------------------------------------------------------------- model writer
 
-class _GenConfig(C.Structure):
-    _fields_ = [(n, C.c_int) for n in ("dim", "n_layers", "n_heads", "n_kv_heads", "hidden_dim", "vocab",
-                                       "max_seq")] + [
-        ("rope_theta", C.c_float), ("norm_eps", C.c_float), ("wtype", C.c_int), ("shared", C.c_int),
-        ("rope_type", C.c_int), ("rope_factor", C.c_float), ("rope_lo", C.c_float), ("rope_hi", C.c_float),
-        ("rope_orig", C.c_int), ("q8_mask", C.c_int), ("qkv_bias", C.c_int), ("head_dim", C.c_int),
-        ("scale_f16", C.c_int), ("sigma", C.c_double), ("bias_sigma", C.c_double), ("seed", C.c_uint64),
-        ("nthreads", C.c_int)]
-
-
 def gen():
+    """The model writer's library (its quantizers and generator, for tests)."""
     global _gen
     if _gen is None:
         if not os.path.exists(GEN_PATH):
             raise RuntimeError(f"{GEN_PATH} missing: build it first")
         g = C.CDLL(GEN_PATH)
-        g.kw_write_model.restype, g.kw_write_model.argtypes = C.c_int, [C.c_char_p, C.POINTER(_GenConfig)]
         g.kw_quantize.restype = C.c_int
         g.kw_quantize.argtypes = [C.c_int, C.c_int, C.c_void_p, C.c_long, C.c_void_p, C.c_void_p]
         g.kw_normal.restype = None
         g.kw_normal.argtypes = [C.c_uint64, C.c_uint64, C.c_uint64, C.c_long, C.c_double, C.c_void_p]
-        g.kw_config_size.restype = C.c_size_t
-        assert g.kw_config_size() == C.sizeof(_GenConfig), "kw_config layout mismatch"
         _gen = g
     return _gen
-
-
-Q8M = {"emb": 1, "cls": 2, "qk": 4, "v": 8, "o": 16, "up": 32, "down": 64}
-
-# synthetic N(0, 0.02) weights, norms 1.0, f16 block scales.
-CONFIGS = {
-    "cfg0": dict(dim=288, n_layers=6, n_heads=6, n_kv_heads=6, hidden_dim=768, vocab=32000, max_seq=256,
-                 rope_theta=10000.0, wtype="q8"),
-    "cfg1": dict(dim=896, n_layers=24, n_heads=14, n_kv_heads=2, hidden_dim=4864, vocab=151936, max_seq=512,
-                 rope_theta=1e6, wtype="q4", q8=("v", "o", "down"), shared=1, qkv_bias=1),
-    "cfg2": dict(dim=2048, n_layers=16, n_heads=32, n_kv_heads=8, hidden_dim=8192, vocab=128256, max_seq=4096,
-                 rope_theta=5e5, wtype="q4", q8=("v", "o", "down"), shared=1,
-                 rope_scaling=("llama3", 32.0, 1.0, 4.0, 8192)),
-    "cfg4": dict(dim=4096, n_layers=32, n_heads=32, n_kv_heads=8, hidden_dim=14336, vocab=128256, max_seq=8192,
-                 rope_theta=5e5, wtype="q8"),
-}
-
-
-def write_model(path, dim, n_layers, n_heads, n_kv_heads, hidden_dim, vocab, max_seq, rope_theta=10000.0,
-                norm_eps=1e-5, wtype="q8", q8=(), shared=0, qkv_bias=0, head_dim=0, rope_scaling=None,
-                scale_f16=1, sigma=0.02, bias_sigma=0.02, seed=0, nthreads=None):
-    """Writes a synthetic .mlb (seeded N(0, sigma) weights, the reference's
-    quantization rules and file layout)."""
-    c = _GenConfig()
-    c.dim, c.n_layers, c.n_heads, c.n_kv_heads = dim, n_layers, n_heads, n_kv_heads
-    c.hidden_dim, c.vocab, c.max_seq = hidden_dim, vocab, max_seq
-    c.rope_theta, c.norm_eps = rope_theta, norm_eps
-    c.wtype = 1 if wtype == "q8" else 2
-    c.shared, c.qkv_bias, c.head_dim, c.scale_f16 = int(shared), int(qkv_bias), head_dim, int(scale_f16)
-    c.q8_mask = sum(Q8M[k] for k in q8)
-    if rope_scaling:
-        kind = rope_scaling[0]
-        c.rope_type = {"llama3": 1, "linear": 2}[kind]
-        c.rope_factor = rope_scaling[1]
-        if kind == "llama3":
-            c.rope_lo, c.rope_hi, c.rope_orig = rope_scaling[2], rope_scaling[3], rope_scaling[4]
-    c.sigma, c.bias_sigma, c.seed = sigma, bias_sigma, seed
-    c.nthreads = nthreads or os.cpu_count() or 1
-    st = gen().kw_write_model(os.fsencode(path), C.byref(c))
-    if st:
-        raise OSError(st, f"writing {path}")
-
-
-def ensure_model(name, directory, seed=0, **overrides):
-    """Path of BASELINE config `name` (CONFIGS) in `directory`, written once."""
-    cfg = dict(CONFIGS[name], **overrides)
-    tag = "" if not overrides else "_" + "_".join(f"{k}{v}" for k, v in sorted(overrides.items()))
-    path = os.path.join(directory, f"{name}{tag}_s{seed}.mlb")
-    if not os.path.exists(path):
-        os.makedirs(directory, exist_ok=True)
-        tmp = path + f".tmp{os.getpid()}"
-        write_model(tmp, seed=seed, **cfg)
-        os.replace(tmp, path)
-    return path

@@ -20,10 +20,26 @@ P, I, F = C.c_void_p, C.c_int, C.c_float
 _orc = None
 
 
-def build(ref_root="/root/reference"):
+def reference_root():
+    """The reference source tree: $KRAFLA_REF, else the `reference_path` of the
+    repository's BASELINE.json; None when neither names a directory here (as
+    on a machine without the reference, where the prebuilt oracle/_ref is used)."""
+    root = os.environ.get("KRAFLA_REF")
+    if not root:
+        try:
+            import json
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+                root = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            root = None
+    return root if root and os.path.isdir(root) else None
+
+
+def build(ref_root=None):
     """Builds liboracle.so, and oracle/_ref when the reference tree is present."""
     subprocess.run(["make", "-s", "-C", HERE, "liboracle.so"], check=True)
-    if os.path.isdir(ref_root):
+    ref_root = ref_root or reference_root()
+    if ref_root:
         subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={ref_root}"], check=True)
 
 

@@ -1,6 +1,7 @@
 """Writes the golden fixtures of tests/golden from the reference itself.
 
-Run in a container that has the reference tree (default /root/reference) and
+Run in a container that has the reference tree (the argument, else $KRAFLA_REF,
+else BASELINE.json's reference_path) and
 the reference build of oracle/_ref (make -C oracle ref):
 
     python tests/golden/gen_golden.py [REFERENCE_ROOT [MODEL ...]]
@@ -29,7 +30,11 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+import oracle as _oracle  # noqa: E402
+REF = sys.argv[1] if len(sys.argv) > 1 else _oracle.reference_root()
+if not REF:
+    sys.exit("gen_golden: the reference tree is not here (pass it, or set KRAFLA_REF)")
 sys.path.insert(0, os.path.join(REF, "tools"))
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 sys.path.insert(0, os.path.join(ROOT, "isa-lm_b200"))

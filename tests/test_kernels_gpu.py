@@ -171,3 +171,32 @@ def test_matmul_scaled(wtype, rows, cols, n, f16):
 def test_matmul_rejects_bad_shapes():
     assert kb.lib().kc_matmul_dev(None, kb.Q8_0, 0, None, None, 4, 33, None, None, 1, None) == kb.E_SHAPE
     assert kb.lib().kc_matmul_dev(None, kb.Q8_0, 0, None, None, 4, 32, None, None, 0, None) == kb.E_SHAPE
+
+
+def test_matvec_wait_timeout_is_reported():
+    """A kernel-level matvec whose first wait on each chunk of weights may poll
+    only once (kc_debug_wait_limit) runs out of it: the device error word is
+    flagged, the wait then drains the chunk (the result stays right), the next
+    kc_dev_sync returns KC_E_IO with the reason and clears the word, and a call
+    with the default limit afterwards syncs clean. No fault is involved."""
+    rows, cols = 2048, 8192
+    rng = np.random.default_rng(11)
+    wq, wd = make_w(rng, kb.Q4_0, rows, cols, f16=True)
+    xq = rng.integers(-127, 128, cols).astype(np.int8)
+    xd = rng.uniform(0.001, 0.05, cols // 32).astype(np.float32)
+    want = kb.matvec(kb.Q4_0, wq, wd, rows, cols, xq, xd)
+    bw, bd = kb.DevBuf.of(wq), kb.DevBuf.of(wd, pad=16)
+    bxq, bxd, by = kb.DevBuf.of(xq), kb.DevBuf.of(xd), kb.DevBuf(4 * rows)
+    L = kb.lib()
+    try:
+        assert L.kc_debug_wait_limit(1) == kb.OK
+        assert L.kc_matvec_dev(by.ptr, kb.Q4_0, 1, bw.ptr, bd.ptr, rows, cols, bxq.ptr, bxd.ptr, None) == kb.OK
+        assert L.kc_dev_sync() == kb.E_IO
+        assert "gave up" in kb.what_detail()
+    finally:
+        L.kc_debug_wait_limit(0)
+    assert np.array_equal(by.get(np.float32, rows), want)
+    assert L.kc_dev_sync() == kb.OK   # the word was cleared by the report
+    assert L.kc_matvec_dev(by.ptr, kb.Q4_0, 1, bw.ptr, bd.ptr, rows, cols, bxq.ptr, bxd.ptr, None) == kb.OK
+    assert L.kc_dev_sync() == kb.OK
+    assert np.array_equal(by.get(np.float32, rows), want)
