@@ -261,12 +261,12 @@ int kc_memcpy_dtoh(void *dst, const void *src, size_t bytes);
  * since the last kc_dev_sync (its error word is then cleared). */
 int kc_dev_sync(void);
 /* Diagnostics for tests of the error path: the polls of the kernel-level
- * matvec's first wait on each chunk of weights (0 restores the default of
- * about a second). A wait that runs out flags the device error word and then
- * waits for the chunk, so the results stay correct and the next kc_dev_sync
- * returns KC_E_IO. No counterpart in the reference (its CPU kernels do not
- * wait on copies). */
-int kc_debug_wait_limit(unsigned polls);
+ * matvec's first wait on each chunk of weights (0: it gives up at once;
+ * negative: the default of about a second). A wait that runs out flags the
+ * device error word and then waits for the chunk, so the results stay
+ * correct and the next kc_dev_sync returns KC_E_IO. No counterpart in the
+ * reference (its CPU kernels do not wait on copies). */
+int kc_debug_wait_limit(int polls);
 
 #ifdef __cplusplus
 }

@@ -1444,8 +1444,8 @@ extern "C" int kc_dev_sync(void) {
     return KC_E_IO;
 }
 
-extern "C" int kc_debug_wait_limit(unsigned polls) {
-    g_wait_limit = polls ? polls : WAIT_POLLS;
+extern "C" int kc_debug_wait_limit(int polls) {
+    g_wait_limit = polls < 0 ? WAIT_POLLS : (unsigned)polls;
     return KC_OK;
 }
 

@@ -174,8 +174,8 @@ def test_matmul_rejects_bad_shapes():
 
 
 def test_matvec_wait_timeout_is_reported():
-    """A kernel-level matvec whose first wait on each chunk of weights may poll
-    only once (kc_debug_wait_limit) runs out of it: the device error word is
+    """A kernel-level matvec whose first wait on each chunk of weights gives up
+    at once (kc_debug_wait_limit 0) runs out of it: the device error word is
     flagged, the wait then drains the chunk (the result stays right), the next
     kc_dev_sync returns KC_E_IO with the reason and clears the word, and a call
     with the default limit afterwards syncs clean. No fault is involved."""
@@ -189,12 +189,12 @@ def test_matvec_wait_timeout_is_reported():
     bxq, bxd, by = kb.DevBuf.of(xq), kb.DevBuf.of(xd), kb.DevBuf(4 * rows)
     L = kb.lib()
     try:
-        assert L.kc_debug_wait_limit(1) == kb.OK
+        assert L.kc_debug_wait_limit(0) == kb.OK
         assert L.kc_matvec_dev(by.ptr, kb.Q4_0, 1, bw.ptr, bd.ptr, rows, cols, bxq.ptr, bxd.ptr, None) == kb.OK
         assert L.kc_dev_sync() == kb.E_IO
         assert "gave up" in kb.what_detail()
     finally:
-        L.kc_debug_wait_limit(0)
+        L.kc_debug_wait_limit(-1)
     assert np.array_equal(by.get(np.float32, rows), want)
     assert L.kc_dev_sync() == kb.OK   # the word was cleared by the report
     assert L.kc_matvec_dev(by.ptr, kb.Q4_0, 1, bw.ptr, bd.ptr, rows, cols, bxq.ptr, bxd.ptr, None) == kb.OK
