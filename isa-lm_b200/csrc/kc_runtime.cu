@@ -505,13 +505,18 @@ struct kc_state {
     int kv_type = KC_F32;
     cudaStream_t st = nullptr;
     uint8_t *arena = nullptr;
-    float *x = nullptr, *qkv = nullptr, *ao = nullptr, *hb = nullptr, *logits = nullptr, *part = nullptr;
-    float *yb = nullptr;   /* post-norm models: the last block's output */
+    /* the step kernel's tagged words (tag << 32 | float bits): x after the O
+     * and after the down phase [2][dim], the CTAs' sums of squares [2][grid],
+     * post-norm block outputs [2][dim], q|k|v, attention partials, attention
+     * output, FFN hidden */
+    unsigned long long *xw = nullptr, *sspw = nullptr, *yw = nullptr, *qkvw = nullptr, *partw = nullptr;
+    unsigned long long *aow = nullptr, *hbw = nullptr;
+    unsigned tag_next = 1;   /* tag of the next launch's first output (0: the zeroed buffers' tag) */
+    float *logits = nullptr;
     uint8_t *kc = nullptr, *vc = nullptr;   /* [L][max_seq][kv_dim] of the KV type */
     float *kd = nullptr, *vd = nullptr;     /* Q8 cache scales [L][max_seq][n_kv_heads] */
     float *rcos = nullptr, *rsin = nullptr, *lcos = nullptr, *lsin = nullptr;
     float *inv0 = nullptr;   /* [vocab]: 1/rms of each embedding row (layer 0's RMSNorm) */
-    float *ssp = nullptr;    /* [grid]: per-CTA sums of squares of the residual rows it wrote */
     unsigned *err = nullptr;
     LoopState *ls = nullptr;
     int *feed = nullptr, *out_tokens = nullptr;
@@ -775,8 +780,9 @@ static int setup_step_kernel(kc_state *s) {
     a.geom = g;
     a.final_norm = m->d_final_norm;
     a.inv0 = s->inv0;
-    a.x = s->x; a.qkv = s->qkv; a.ao = s->ao; a.hb = s->hb; a.logits = s->logits; a.part = s->part; a.ssp = s->ssp;
-    a.att_counter = s->bar + BAR_WORDS; a.bar = s->bar; a.err = s->err; a.ls = s->ls; a.feed = s->feed;
+    a.xw = s->xw; a.sspw = s->sspw; a.yw = s->yw; a.qkvw = s->qkvw; a.partw = s->partw; a.aow = s->aow;
+    a.hbw = s->hbw; a.logits = s->logits;
+    a.bar = s->bar; a.err = s->err; a.ls = s->ls; a.feed = s->feed;
     a.out_tokens = s->out_tokens;
     a.kv_type = s->kv_type;
     a.n_layers = c.n_layers; a.dim = c.dim; a.q_dim = c.q_dim; a.kv_dim = c.kv_dim; a.hidden = c.hidden_dim;
@@ -784,7 +790,6 @@ static int setup_step_kernel(kc_state *s) {
     a.eps = c.norm_eps; a.attn_scale = c.attn_scale; a.attn_softcap = c.attn_softcap; a.final_softcap = c.final_softcap;
     a.embed_scale = c.embed_scale; a.act = c.act;
     a.cls_row0 = m->cls_row0;
-    a.yb = s->yb;
     a.post_norms = c.post_norms ? 1 : 0;
     a.tp_rank = 0; a.tp_world = 1; a.tp_step0 = 0;
     for (int r = 0; r < KC_TP_MAX; r++) a.tp_box[r] = nullptr;
@@ -801,8 +806,11 @@ static int launch_steps(kc_state *s, int nsteps, int logits, bool timeline = fal
         return KC_E_SHAPE;
     }
     s->last_row = -1;   /* the caller names the row when its last token's logits are kept */
-    CK(cudaMemsetAsync(s->bar, 0, sizeof(unsigned) * (BAR_WORDS + (size_t)s->c.n_kv_heads), s->st));
+    CK(cudaMemsetAsync(s->bar, 0, sizeof(unsigned) * BAR_WORDS, s->st));
     StepArgs a = s->sa;
+    /* this launch's tags: NTAG per layer and step, after the last launch's */
+    a.tag0 = s->tag_next;
+    s->tag_next += (unsigned)((unsigned long long)nsteps * s->c.n_layers * NTAG);
     a.tp_step0 = s->tp_steps;
     s->tp_steps += (unsigned long long)nsteps;
     a.nsteps = nsteps;
@@ -905,18 +913,17 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
     const size_t lkv = (size_t)c.n_layers * T * c.kv_dim * kv_elem_bytes(kv_type);
     struct Buf { void **p; size_t bytes; };
     std::vector<Buf> bufs = {
-        { (void **)&s->x, sizeof(float) * c.dim },
-        { (void **)&s->yb, sizeof(float) * c.dim },
-        { (void **)&s->qkv, sizeof(float) * (size_t)(c.q_dim + 2 * c.kv_dim) },
-        { (void **)&s->ao, sizeof(float) * c.q_dim },
-        { (void **)&s->hb, sizeof(float) * c.hidden_dim },
+        { (void **)&s->xw, sizeof(unsigned long long) * 2 * c.dim },
+        { (void **)&s->yw, sizeof(unsigned long long) * 2 * c.dim },
+        { (void **)&s->sspw, sizeof(unsigned long long) * 2 * (size_t)s->num_sms },
+        { (void **)&s->qkvw, sizeof(unsigned long long) * (size_t)(c.q_dim + 2 * c.kv_dim) },
+        { (void **)&s->aow, sizeof(unsigned long long) * c.q_dim },
+        { (void **)&s->hbw, sizeof(unsigned long long) * c.hidden_dim },
+        { (void **)&s->partw, sizeof(unsigned long long) * (size_t)c.n_heads * MAX_NSPLIT * (c.head_dim + 2) },
         { (void **)&s->logits, sizeof(float) * (size_t)LOGITS_RING * c.vocab },
-        { (void **)&s->part, sizeof(float) * (size_t)c.n_heads * MAX_NSPLIT * (c.head_dim + 2) },
-        { (void **)&s->ssp, sizeof(float) * (size_t)s->num_sms },
         { (void **)&s->err, sizeof(unsigned) * 4 },
-        /* the grid barrier's arrival counter, then (a line further) the attention
-         * splits' arrival counters per KV head: zeroed together before each launch */
-        { (void **)&s->bar, sizeof(unsigned) * (BAR_WORDS + (size_t)c.n_kv_heads) },
+        /* the step-end barrier's arrival counter, zeroed before each launch */
+        { (void **)&s->bar, sizeof(unsigned) * BAR_WORDS },
         { (void **)&s->timeline_n, sizeof(unsigned) * 4 },
         { (void **)&s->timeline, sizeof(unsigned long long) * 4096 },
         { (void **)&s->ls, sizeof(LoopState) },
@@ -1200,19 +1207,30 @@ extern "C" int kc_debug_copy(kc_state *s, int which, void *dst, size_t bytes) {
     const kc_config &c = s->c;
     const void *src = nullptr;
     size_t n = 0;
+    const unsigned long long *words = nullptr;   /* tagged words: the floats are their low halves */
     switch (which) {
-    case 0: src = s->x; n = sizeof(float) * c.dim; break;
-    case 1: src = s->qkv; n = sizeof(float) * (size_t)(c.q_dim + 2 * c.kv_dim); break;
-    case 2: src = s->ao; n = sizeof(float) * c.q_dim; break;
-    case 3: src = s->hb; n = sizeof(float) * c.hidden_dim; break;
+    case 0: words = s->xw + c.dim; n = (size_t)c.dim; break;
+    case 1: words = s->qkvw; n = (size_t)(c.q_dim + 2 * c.kv_dim); break;
+    case 2: words = s->aow; n = (size_t)c.q_dim; break;
+    case 3: words = s->hbw; n = (size_t)c.hidden_dim; break;
     case 4: src = s->kc; n = kv_elem_bytes(s->kv_type) * (size_t)c.n_layers * c.max_seq * c.kv_dim; break;
     case 5: src = s->vc; n = kv_elem_bytes(s->kv_type) * (size_t)c.n_layers * c.max_seq * c.kv_dim; break;
     case 6: src = s->kd; n = s->kd ? sizeof(float) * (size_t)c.n_layers * c.max_seq * c.n_kv_heads : 0; break;
     case 7: src = s->vd; n = s->vd ? sizeof(float) * (size_t)c.n_layers * c.max_seq * c.n_kv_heads : 0; break;
     default: return KC_E_SHAPE;
     }
-    if (bytes < n || !src) return KC_E_SHAPE;
     CK(cudaStreamSynchronize(s->st));
+    if (words) {
+        if (bytes < n * sizeof(float)) return KC_E_SHAPE;
+        std::vector<unsigned long long> h(n);
+        CK(cudaMemcpy(h.data(), words, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
+        for (size_t i = 0; i < n; i++) {
+            const unsigned u = (unsigned)h[i];
+            std::memcpy((char *)dst + i * sizeof(float), &u, sizeof(float));
+        }
+        return KC_OK;
+    }
+    if (bytes < n || !src) return KC_E_SHAPE;
     CK(cudaMemcpy(dst, src, n, cudaMemcpyDeviceToHost));
     return KC_OK;
 }

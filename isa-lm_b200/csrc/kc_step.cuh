@@ -186,9 +186,15 @@ struct StepArgs {
     const unsigned long long *cta_base;   /* [G] byte offset of each CTA's stream */
     StreamGeom geom;
     const float *final_norm, *inv0;
-    float *x, *qkv, *ao, *hb, *logits, *part;
-    float *ssp;                     /* [G] per-CTA sum of squares of the x rows it owns */
-    unsigned *att_counter, *bar, *err;
+    /* the vectors between phases as tagged words (see "tagged words"): x rows
+     * after the O and after the down phase [2][dim], the CTAs' sums of squares
+     * of their residual rows [2][G], post-norm models' block outputs [2][dim],
+     * q|k|v [q_dim + 2 kv_dim], attention split partials
+     * [n_heads][nsplit][hd + 2], attention output [q_dim], FFN hidden [hidden] */
+    unsigned long long *xw, *sspw, *yw, *qkvw, *partw, *aow, *hbw;
+    unsigned tag0;                  /* tag of the launch's first output (tag_of) */
+    float *logits;
+    unsigned *bar, *err;
     LoopState *ls;
     const int *feed;
     int *out_tokens;
@@ -208,7 +214,6 @@ struct StepArgs {
      * at 0, best logit keys [world] at tp_off_best and their flags at
      * tp_off_bflag, the logits ring at tp_off_logits. tp_step0: the steps of
      * earlier launches (sequence numbers grow by one per exchange). */
-    float *yb;                      /* post-norm models: the last block's output [dim] */
     int post_norms;
     int cls_row0;
     int tp_rank, tp_world;
@@ -313,36 +318,88 @@ __device__ __forceinline__ void wait_count(const StepArgs &a, unsigned target) {
     timeline_mark(a);
 }
 
-/* Grid barrier of the phases: every CTA arrives once on the arrival counter;
- * `expect` (the same in every CTA) counts the arrivals due so far in this
- * launch (the host zeroes the counter before each launch). A counter with
- * one atomic per CTA measured faster on B200 than per-CTA flags polled by
- * every CTA (which floods L2 with polls) or a two-level counter. With own
- * set, warp 0 first stores the sum of squares of the CTA's nown rows of x
- * into ssp[blockIdx.x], ordered before the arrival by thread 0's fence. */
-__device__ __forceinline__ void grid_barrier(const StepArgs &a, unsigned &expect, unsigned &pidx,
-                                             const float *own = nullptr, int nown = 0) {
-    consumer_sync();
+/* The end of a phase as this CTA sees it (diagnostics): its trace marks and,
+ * on CTA 0, a timeline entry. No barrier: the next phase's prologue waits on
+ * the tagged words it reads. */
+__device__ __forceinline__ void phase_end(const StepArgs &a, unsigned &pidx) {
     const unsigned p = pidx++;
-    expect += gridDim.x;
-    if (threadIdx.x < 32) {
-        if (own) {
-            float t = 0.0f;
-            for (int i = threadIdx.x; i < nown; i += 32) t += own[i] * own[i];
-            t = warp_sum(t);
-            if (threadIdx.x == 0) a.ssp[blockIdx.x] = t;
-        }
-        if (threadIdx.x == 0) {
-            trace_mark(a, p, 1);
-            ev(0, EV_ARRIVE);
-            __threadfence();
-            atomicAdd(a.bar, 1u);
-            wait_count(a, expect);
-            trace_mark(a, p, 2);
-            ev(0, EV_RELEASE);
-        }
+    if (threadIdx.x == 0) {
+        trace_mark(a, p, 1);
+        trace_mark(a, p, 2);
+        timeline_mark(a);
+        ev(0, EV_ARRIVE);
     }
-    consumer_sync();
+}
+
+/* ------------------------------------------------------------ tagged words */
+
+/* Within a step, the vectors between phases travel as 64-bit words: a 32-bit
+ * tag in the high half (the number of the phase output: launch step, layer and
+ * kind, see tag_of) and the float in the low half. An aligned 8-byte store is
+ * seen whole or not at all, so each word is its own ready flag: a reader loads
+ * the words it needs, then loads again those whose tag is not yet the
+ * expected one. No fence, counter or grid barrier sits between the phases of
+ * a layer; each CTA waits for exactly the words it reads, the moment they
+ * land. Words are compared for equality, so tags may wrap.
+ *
+ * A word is rewritten only after every reader of its previous value is done:
+ * every CTA runs every phase's prologue (it reads the whole input vector,
+ * rows of its own or not) and publishes its sum of squares after the O and
+ * after the down phase; x and those sums have one buffer for each of the two
+ * phases. The next write of a word then lies behind, in the data flow, a
+ * prologue in which every CTA has read every other CTA's sum of the phase
+ * after that CTA's last read of the word. */
+typedef unsigned long long word_t;
+enum { TAG_QKV = 0, TAG_PART = 1, TAG_AO = 2, TAG_XC = 3, TAG_HB = 4, TAG_XE = 5, NTAG = 6 };
+constexpr unsigned POLL_LIMIT = 1u << 22;   /* loads of one word before a reader gives up (seconds) */
+constexpr unsigned ERR_POLL = 32u;          /* error bit: a tagged input never came */
+
+__device__ __forceinline__ unsigned tag_of(const StepArgs &a, int step, int l, int kind) {
+    return a.tag0 + (unsigned)((step * a.n_layers + l) * NTAG + kind);
+}
+__device__ __forceinline__ word_t mkword(unsigned tag, float v) {
+    return ((word_t)tag << 32) | (word_t)__float_as_uint(v);
+}
+__device__ __forceinline__ float wval(word_t w) { return __uint_as_float((unsigned)w); }
+__device__ __forceinline__ bool wok(word_t w, unsigned tag) { return (unsigned)(w >> 32) == tag; }
+__device__ __forceinline__ void st_word(word_t *p, word_t w) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ word_t ld_word(const word_t *p) {
+    word_t v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+/* Two words (16-byte aligned); each element is a single-copy atomic 8 bytes. */
+__device__ __forceinline__ void ld_words2(const word_t *p, word_t &a, word_t &b) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+/* Loads p again until the word carries tag (bounded; gives up at once when
+ * another CTA has flagged the error word). */
+__device__ __forceinline__ float wait_word(const word_t *p, unsigned tag, word_t w, unsigned *err) {
+    for (unsigned it = 0; !wok(w, tag); it++) {
+        if (it >= POLL_LIMIT) {
+            atomicOr(err, ERR_POLL);
+            break;
+        }
+        if ((it & 63) == 63 && *(volatile const unsigned *)err) break;
+        w = ld_word(p);
+    }
+    return wval(w);
+}
+__device__ __forceinline__ void wait_words2(const word_t *p, unsigned tag, word_t &a, word_t &b, unsigned *err) {
+    for (unsigned it = 0; !(wok(a, tag) && wok(b, tag)); it++) {
+        if (it >= POLL_LIMIT) {
+            atomicOr(err, ERR_POLL);
+            break;
+        }
+        if ((it & 63) == 63 && *(volatile const unsigned *)err) break;
+        ld_words2(p, a, b);
+    }
+}
+/* Waits for one tagged word and returns its float (one load when it has landed). */
+__device__ __forceinline__ float get_word(const word_t *p, unsigned tag, unsigned *err) {
+    return wait_word(p, tag, ld_word(p), err);
 }
 
 /* ------------------------------------------------------------ tensor parallelism */
@@ -388,11 +445,11 @@ __device__ __forceinline__ unsigned long long ld_sys_u64(const unsigned long lon
  * (the row's column slices summed in order) into slot [ph][rank][row] of every
  * rank's exchange buffer, then waits in its own buffer for every rank's word
  * of that row carrying this exchange's number and adds them in rank order:
- * x[row] += y_0 + y_1 + ... Every rank runs the same grid, so CTA j of every
+ * own[row] += y_0 + y_1 + ... Every rank runs the same grid, so CTA j of every
  * rank owns the same rows of x; a rank can store the next exchange's words
  * into a slot only after this rank has passed the exchange in between. */
-__device__ __noinline__ void tp_resid(const StepArgs &a, const float *res, int nrows, int row0, float *out,
-                                      float *own, int ns, int ph, unsigned seq) {
+__device__ __noinline__ void tp_resid(const StepArgs &a, const float *res, int nrows, int row0, float *own, int ns,
+                                      int ph, unsigned seq) {
     const int me = a.tp_rank, W = a.tp_world, D = a.dim;
     for (int i = threadIdx.x; i < nrows; i += NCT) {
         float sum = res[i * ns];
@@ -417,9 +474,7 @@ __device__ __noinline__ void tp_resid(const StepArgs &a, const float *res, int n
             const float v = __uint_as_float((unsigned)w);
             tot = r == 0 ? v : __fadd_rn(tot, v);
         }
-        const float v = __fadd_rn(own[i], tot);
-        own[i] = v;
-        out[row0 + i] = v;
+        own[i] = __fadd_rn(own[i], tot);
     }
 }
 
@@ -720,12 +775,13 @@ __device__ __forceinline__ void consume_phase(Ring &rg, const PhasePlan &P, bool
 enum { FIN_STORE = 0, FIN_RESID = 1, FIN_PAIR = 2, FIN_LOGITS = 3 };
 
 /* The rows of a phase after its dot products (res, in row order from row0):
- * store, residual add (on the CTA's rows of x in `own` and in out), act(g)*u,
- * or logits with the first-index argmax key of the CTA's rows (returned on
- * thread 0; 0 otherwise). */
+ * store, residual add (on the CTA's rows of x in `own`), act(g)*u — each
+ * result as a tagged word into wout — or logits into out with the
+ * first-index argmax key of the CTA's rows (returned on thread 0; 0
+ * otherwise). */
 __device__ __forceinline__ unsigned long long finish_phase(int kind, const float *res, int nrows, int row0, float *out,
-                                                        float *own, int act, float softcap, unsigned long long *cta_best,
-                                                        int ns) {
+                                                        word_t *wout, unsigned tag, float *own, int act, float softcap,
+                                                        unsigned long long *cta_best, int ns) {
     unsigned long long best = 0;
     for (int i = threadIdx.x; i < nrows; i += NCT) {
         const int row = row0 + i;
@@ -735,14 +791,14 @@ __device__ __forceinline__ unsigned long long finish_phase(int kind, const float
             for (int k = 1; k < ns; k++) sum = __fadd_rn(sum, res[i * ns + k]);
         }
         if (kind == FIN_STORE) {
-            out[row] = sum;
+            st_word(wout + row, mkword(tag, sum));
         } else if (kind == FIN_RESID) {
             const float v = __fadd_rn(own[i], sum);
             own[i] = v;
-            out[row] = v;
+            st_word(wout + row, mkword(tag, v));
         } else if (kind == FIN_PAIR) {
             const float2 gu = ((const float2 *)res)[i];
-            out[row] = act_mul(act, gu.x, gu.y);
+            st_word(wout + row, mkword(tag, act_mul(act, gu.x, gu.y)));
         } else {
             float v = sum;
             if (softcap > 0.0f) v = __fmul_rn(softcap, tanhf(__fdiv_rn(v, softcap)));
@@ -763,6 +819,25 @@ __device__ __forceinline__ unsigned long long finish_phase(int kind, const float
             for (int w = 0; w < NCW; w++) best = cta_best[w] > best ? cta_best[w] : best;
     }
     return best;
+}
+
+/* This CTA's rows of x (own, from row0) as tagged words (after a residual
+ * phase that wrote own without them: tensor parallelism, post-norms). */
+__device__ __forceinline__ void publish_rows(word_t *w, unsigned tag, const float *own, int nrows, int row0) {
+    for (int i = threadIdx.x; i < nrows; i += NCT) st_word(w + row0 + i, mkword(tag, own[i]));
+}
+
+/* After a residual phase, the CTA's sum of squares of its n rows (of x, or of
+ * a post-norm model's block output) into its tagged word: every CTA
+ * publishes one, rows or none (the next RMSNorm adds all G of them). */
+__device__ __forceinline__ void publish_ssp(word_t *sspw, unsigned tag, const float *rows, int n) {
+    consumer_sync();
+    if (threadIdx.x < 32) {
+        float t = 0.0f;
+        for (int i = threadIdx.x; i < n; i += 32) t += rows[i] * rows[i];
+        t = warp_sum(t);
+        if (threadIdx.x == 0) st_word(sspw + blockIdx.x, mkword(tag, t));
+    }
 }
 
 /* Consumer of the kernel-level matvec (rows [r0, r1) as produce_rows staged them). */
@@ -869,14 +944,16 @@ __device__ __forceinline__ void put_quant(const ActW &o, int b, int nb, int j0, 
 
 /* The activation of a phase into shared memory: quantize_q8 of v, with
  * v = RMSNorm(x) * w (k_scalar.c:59-64: o = (x * inv) * w, inv =
- * 1 / sqrt(ss / n + eps)) when norm_w is set; x is a float vector in global
- * memory written by other CTAs (read through L2). 1/rms: from ss = the sum of
- * the G per-CTA partial sums ssp, else reduced here. Every thread issues all
- * its loads (up to 2 passes of 128 blocks, 4 lanes per block, 8 values per
- * lane) before it uses any, so the prologue costs one round trip to L2. */
-__device__ __noinline__ void act_float(float eps, const float *x, const float *norm_w, const float *ssp, int cols, ActW o,
-                                       float *red, const float *wstaged) {
-    /* 4 lanes per block, 8 values per lane (two float4), passes of NCT / 4 blocks */
+ * 1 / sqrt(ss / n + eps)) when norm_w is set; x arrives as tagged words from
+ * the CTAs that wrote it (tag: the phase output read). 1/rms: from ss = the
+ * sum of the G per-CTA partial sums (tagged words sspw), else reduced here.
+ * Every thread issues all its loads (up to 2 passes of 128 blocks, 4 lanes
+ * per block, 8 values per lane) before it waits on any, so the prologue costs
+ * one round trip to L2 once its input has landed. */
+__device__ __noinline__ void act_float(float eps, const word_t *xw, unsigned tag, const float *norm_w,
+                                       const word_t *sspw, int cols, ActW o, float *red, const float *wstaged,
+                                       unsigned *err) {
+    /* 4 lanes per block, 8 values per lane (four word pairs), passes of NCT / 4 blocks */
     const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 3) * 8;
     const int passes = (nb + NCT / 4 - 1) / (NCT / 4);
     const bool norm = norm_w != nullptr;
@@ -884,25 +961,35 @@ __device__ __noinline__ void act_float(float eps, const float *x, const float *n
     /* one warp per CTA loads the G per-CTA sums of squares (the same few
      * lines read by every warp of every CTA would queue at their L2 slice) */
     const int lane = tid & 31, warp = tid >> 5;
-    const bool ssw = norm && ssp && warp == 0;
-    float part[SSP_LOADS];
+    const bool ssw = norm && sspw && warp == 0;
+    word_t part[SSP_LOADS];
 #pragma unroll
     for (int k = 0; k < SSP_LOADS; k++) {
         const int idx = k * 32 + lane;
-        part[k] = (ssw && idx < (int)gridDim.x) ? __ldcg(ssp + idx) : 0.0f;
+        part[k] = (ssw && idx < (int)gridDim.x) ? ld_word(sspw + idx) : mkword(tag, 0.0f);
     }
     constexpr int NP = ACT_PASSES / 2;   /* passes of NCT / 4 blocks */
-    float4 v[2 * NP], w[2 * NP];
+    word_t v[NP][8];
 #pragma unroll
     for (int p = 0; p < NP; p++) {
         const int b = p * (NCT / 4) + (tid >> 2);
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-            v[2 * p + h] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            w[2 * p + h] = v[2 * p + h];
-            if (p < passes && b < nb) v[2 * p + h] = __ldcg((const float4 *)(x + b * QK + j0 + 4 * h));
+        for (int h = 0; h < 4; h++) {
+            v[p][2 * h] = v[p][2 * h + 1] = mkword(tag, 0.0f);
+            if (p < passes && b < nb) ld_words2(xw + b * QK + j0 + 2 * h, v[p][2 * h], v[p][2 * h + 1]);
         }
     }
+#pragma unroll
+    for (int p = 0; p < NP; p++) {
+        const int b = p * (NCT / 4) + (tid >> 2);
+#pragma unroll
+        for (int h = 0; h < 4; h++)
+            if (p < passes && b < nb) wait_words2(xw + b * QK + j0 + 2 * h, tag, v[p][2 * h], v[p][2 * h + 1], err);
+    }
+    if (tid == 0) ev(0, EV_ACT_LOADED);
+    float4 w[2 * NP];
+#pragma unroll
+    for (int k = 0; k < 2 * NP; k++) w[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     if (norm && wstaged) cp_async_wait_all();
 #pragma unroll
     for (int p = 0; p < NP; p++) {
@@ -914,11 +1001,14 @@ __device__ __noinline__ void act_float(float eps, const float *x, const float *n
     }
     float inv = 1.0f;
     if (norm) {
-        if (ssp) {
+        if (sspw) {
             if (warp == 0) {
                 float t = 0.0f;
 #pragma unroll
-                for (int k = 0; k < SSP_LOADS; k++) t += part[k];
+                for (int k = 0; k < SSP_LOADS; k++) {
+                    const int idx = k * 32 + lane;
+                    if (ssw && idx < (int)gridDim.x) t += wait_word(sspw + idx, tag, part[k], err);
+                }
                 const float ss = warp_sum(t);
                 if (lane == 0) red[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
             }
@@ -927,7 +1017,13 @@ __device__ __noinline__ void act_float(float eps, const float *x, const float *n
         } else {
             float t = 0.0f;
 #pragma unroll
-            for (int k = 0; k < 2 * NP; k++) t += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
+            for (int p = 0; p < NP; p++)
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const float a0 = wval(v[p][4 * h]), a1 = wval(v[p][4 * h + 1]), a2 = wval(v[p][4 * h + 2]),
+                                a3 = wval(v[p][4 * h + 3]);
+                    t += a0 * a0 + a1 * a1 + a2 * a2 + a3 * a3;
+                }
             const float ss = block_sum(t, red);
             inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
         }
@@ -938,9 +1034,11 @@ __device__ __noinline__ void act_float(float eps, const float *x, const float *n
     for (int p = 0; p < NP; p++) {
         if (p >= passes) break;
         const int b = p * (NCT / 4) + (tid >> 2);
-        const float4 c0 = v[2 * p], c1 = v[2 * p + 1], w0 = w[2 * p], w1 = w[2 * p + 1];
-        float u[8] = { c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w };
+        float u[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) u[k] = wval(v[p][k]);
         if (norm) {
+            const float4 w0 = w[2 * p], w1 = w[2 * p + 1];
             const float wv[8] = { w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w };
 #pragma unroll
             for (int i = 0; i < 8; i++) u[i] = __fmul_rn(__fmul_rn(u[i], inv), wv[i]);
@@ -1014,21 +1112,58 @@ __device__ __noinline__ void act_loop(float eps, const float *x, const float *no
     consumer_sync();
 }
 
+/* act_loop over tagged words: wider vectors in the step kernel, pass by pass. */
+__device__ __noinline__ void act_loop_w(float eps, const word_t *xw, unsigned tag, const float *norm_w,
+                                        const word_t *sspw, int cols, ActW o, float *red, unsigned *err) {
+    const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 7) * 4;
+    float inv = 1.0f;
+    if (norm_w) {
+        float t = 0.0f;
+        for (int g = tid; g < (int)gridDim.x; g += NCT) t += get_word(sspw + g, tag, err);
+        const float ss = block_sum(t, red);
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
+    }
+    for (int b0 = 0; b0 < nb; b0 += NCT / 8) {
+        const int b = b0 + (tid >> 3);
+        float u[4] = { 0.0f, 0.0f, 0.0f, 0.0f };
+        if (b < nb) {
+            word_t w0, w1, w2, w3;
+            const word_t *p = xw + b * QK + j0;
+            ld_words2(p, w0, w1);
+            ld_words2(p + 2, w2, w3);
+            wait_words2(p, tag, w0, w1, err);
+            wait_words2(p + 2, tag, w2, w3, err);
+            u[0] = wval(w0); u[1] = wval(w1); u[2] = wval(w2); u[3] = wval(w3);
+            if (norm_w) {
+                const float4 w = *(const float4 *)(norm_w + b * QK + j0);
+                u[0] = __fmul_rn(__fmul_rn(u[0], inv), w.x);
+                u[1] = __fmul_rn(__fmul_rn(u[1], inv), w.y);
+                u[2] = __fmul_rn(__fmul_rn(u[2], inv), w.z);
+                u[3] = __fmul_rn(__fmul_rn(u[3], inv), w.w);
+            }
+        }
+        put_quant(o, b, nb, j0, u);
+    }
+    consumer_sync();
+}
+
 /* Post-norm models (model/transformer.c:238-243): the residual stream after a
  * block is x + RMSNorm(y) * pw, y the block's output (its sum of squares from
- * the G per-CTA partials in ssp). Every CTA recomputes it for all cols, adds
- * up its squares and quantizes RMSNorm(x_new) * nw into the activation; the
- * CTA's own rows of x_new go to own (and into x one phase later, once every
- * CTA has read the old x). */
-__device__ __noinline__ void act_postnorm(const StepArgs &a, const float *x, const float *y, const float *pw,
-                                          const float *nw, int cols, ActW o, float *red, float *own, int own0,
-                                          int own1) {
+ * the G per-CTA partials ssw), all three tagged words of the block's phase.
+ * Every CTA recomputes it for all cols, adds up its squares and quantizes
+ * RMSNorm(x_new) * nw into the activation; the CTA's own rows of x_new go to
+ * own (and out as words one phase later, with the next block's output). */
+__device__ __noinline__ void act_postnorm(const StepArgs &a, const word_t *x, const word_t *y, const word_t *ssw,
+                                          unsigned tag, const float *pw, const float *nw, int cols, ActW o, float *red,
+                                          float *own, int own0, int own1) {
     const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 7) * 4;
     float t = 0.0f;
-    for (int g = tid; g < (int)gridDim.x; g += NCT) t += __ldcg(a.ssp + g);
+    for (int g = tid; g < (int)gridDim.x; g += NCT) t += get_word(ssw + g, tag, a.err);
     const float ssy = block_sum(t, red);
     const float invy = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ssy, (float)cols), a.eps)));
-    auto xn = [&](int i) { return __fadd_rn(__ldcg(x + i), __fmul_rn(__fmul_rn(__ldcg(y + i), invy), pw[i])); };
+    auto xn = [&](int i) {
+        return __fadd_rn(get_word(x + i, tag, a.err), __fmul_rn(__fmul_rn(get_word(y + i, tag, a.err), invy), pw[i]));
+    };
     float s2 = 0.0f;
     for (int i = tid; i < cols; i += NCT) {
         const float v = xn(i);
@@ -1051,25 +1186,28 @@ __device__ __noinline__ void act_postnorm(const StepArgs &a, const float *x, con
 }
 
 /* The finish of a post-norm model's O or down projection: the block output
- * rows (column slices summed in order) into yb and yown, and the CTA's rows of
- * the residual stream the last prologue computed (own) into x. */
-__device__ __noinline__ void finish_post(const float *res, int nrows, int row0, int ns, float *x, float *yb,
-                                         const float *own, float *yown) {
+ * rows (column slices summed in order) into yown and out as words (yw), and
+ * the CTA's rows of the residual stream the last prologue computed (own) as
+ * words (xw), with the same tag. */
+__device__ __noinline__ void finish_post(const float *res, int nrows, int row0, int ns, word_t *xw, word_t *yw,
+                                         unsigned tag, const float *own, float *yown) {
     for (int i = threadIdx.x; i < nrows; i += NCT) {
         float sum = res[i * ns];
         for (int k = 1; k < ns; k++) sum = __fadd_rn(sum, res[i * ns + k]);
-        yb[row0 + i] = sum;
         yown[i] = sum;
-        x[row0 + i] = own[i];
+        st_word(yw + row0 + i, mkword(tag, sum));
+        st_word(xw + row0 + i, mkword(tag, own[i]));
     }
 }
 
-/* act_float for up to 4 * 2048 columns; wider vectors pass by pass. */
-/* wstaged: norm_w already copied into shared memory by prefetch_norm. */
-__device__ __forceinline__ void load_activation(const StepArgs &a, const float *x, const float *norm_w, const float *ssp,
-                                                int cols, const ActW &o, float *red, const float *wstaged = nullptr) {
-    if (cols <= ACT_PASSES * NCT / 8 * QK) act_float(a.eps, x, norm_w, ssp, cols, o, red, wstaged);
-    else act_loop(a.eps, x, norm_w, cols, o, red);
+/* act_float for up to 4 * 2048 columns; wider vectors pass by pass. x: the
+ * phase output's tagged words; wstaged: norm_w already copied into shared
+ * memory by prefetch_norm. */
+__device__ __forceinline__ void load_activation(const StepArgs &a, const word_t *x, unsigned tag, const float *norm_w,
+                                                const word_t *ssp, int cols, const ActW &o, float *red,
+                                                const float *wstaged = nullptr) {
+    if (cols <= ACT_PASSES * NCT / 8 * QK) act_float(a.eps, x, tag, norm_w, ssp, cols, o, red, wstaged, a.err);
+    else act_loop_w(a.eps, x, tag, norm_w, ssp, cols, o, red, a.err);
 }
 
 /* An already quantized activation (kernel-level matvec) into the same layout. */
@@ -1152,11 +1290,12 @@ __device__ __forceinline__ int att_splits(const StepArgs &a, const LayerPlan &L,
  * scores q.k * scale (Q8: the query quantized per head, int32 dot,
  * (float)s * (qd * scale) * kd), soft-capped when set; online softmax over
  * 64-position tiles loaded one tile ahead; the weighted V sum (Q8: (p * vd)
- * * v). The splits of a KV head then wait for each other and each combines
- * its slice of the head group's outputs into a.ao. */
+ * * v). The splits of a KV head then publish their partials as tagged words
+ * (t_part) and each combines its slice of the head group's outputs into the
+ * attention output words (t_ao); q, k and v arrive as tagged words (t_qkv). */
 template <int KV, int UNITS>
 __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan &L, int g, int y, int pos, float *fsm,
-                                              unsigned att_base) {
+                                              unsigned t_qkv, unsigned t_part, unsigned t_ao) {
     constexpr int ES = KV == KC_F32 ? 4 : (KV == KC_F16 ? 2 : 1);
     const int hd = a.hd, group = a.n_heads / a.n_kv_heads, h2 = hd / 2, tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
@@ -1193,11 +1332,11 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
      * so that both round trips overlap */
     const float *cs = L.rcos + (size_t)pos * h2, *sn = L.rsin + (size_t)pos * h2;
     const int nq = group * h2;
-    float2 q0 = make_float2(0.0f, 0.0f);
+    word_t q0a = mkword(t_qkv, 0.0f), q0b = q0a;
     float c0 = 0.0f, s0 = 0.0f;
     if (tid < nq) {
         const int h = tid / h2, i = tid - h * h2;
-        q0 = __ldcg((const float2 *)(a.qkv + (size_t)(g * group + h) * hd + 2 * i));
+        ld_words2(a.qkvw + (size_t)(g * group + h) * hd + 2 * i, q0a, q0b);
         c0 = cs[i];
         s0 = sn[i];
     }
@@ -1217,15 +1356,19 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
     } else {
         load_tile(t_begin);
     }
+    if (tid < nq) {
+        const int h = tid / h2, i = tid - h * h2;
+        wait_words2(a.qkvw + (size_t)(g * group + h) * hd + 2 * i, t_qkv, q0a, q0b, a.err);
+    }
     if (tid == 0) ev(0, EV_ATT_ISSUED);
     /* qk_norm (model/transformer.c:244-248): 1/rms of each query head first */
     __shared__ float qinv[NCW];
     if (L.q_norm) {
         if (warp < group) {
-            const float *qh = a.qkv + (size_t)(g * group + warp) * hd;
+            const word_t *qh = a.qkvw + (size_t)(g * group + warp) * hd;
             float t = 0.0f;
             for (int i = lane; i < hd; i += 32) {
-                const float v = __ldcg(qh + i);
+                const float v = get_word(qh + i, t_qkv, a.err);
                 t += v * v;
             }
             t = warp_sum(t);
@@ -1235,9 +1378,10 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
     }
     for (int idx = tid; idx < nq; idx += NCT) {
         const int h = idx / h2, i = idx % h2;
-        const float *qh = a.qkv + (size_t)(g * group + h) * hd;
+        const word_t *qh = a.qkvw + (size_t)(g * group + h) * hd;
         const bool first_pair = idx == tid;
-        float qa = first_pair ? q0.x : __ldcg(qh + 2 * i), qb = first_pair ? q0.y : __ldcg(qh + 2 * i + 1);
+        float qa = first_pair ? wval(q0a) : get_word(qh + 2 * i, t_qkv, a.err);
+        float qb = first_pair ? wval(q0b) : get_word(qh + 2 * i + 1, t_qkv, a.err);
         const float c = first_pair ? c0 : cs[i], s = first_pair ? s0 : sn[i];
         if (L.q_norm) {
             qa = __fmul_rn(__fmul_rn(qa, qinv[h]), L.q_norm[2 * i]);
@@ -1249,20 +1393,23 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
     if (tid == 0) ev(0, EV_ATT_QROPE);
     /* the split holding pos stores that position's K (after RoPE) and V */
     if (t_end == pos + 1 && warp < 2) {
-        const float *src = a.qkv + a.q_dim + (warp ? a.kv_dim : 0) + (size_t)g * hd;
+        const word_t *src = a.qkvw + a.q_dim + (warp ? a.kv_dim : 0) + (size_t)g * hd;
         float *row = warp ? S.vnew : S.knew;
         float kinv = 1.0f;
         if (warp == 0 && L.k_norm) {
             float t = 0.0f;
             for (int i = lane; i < hd; i += 32) {
-                const float v = __ldcg(src + i);
+                const float v = get_word(src + i, t_qkv, a.err);
                 t += v * v;
             }
             t = warp_sum(t);
             kinv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)hd), a.eps)));
         }
         for (int i = lane; i < h2; i += 32) {
-            float xa = __ldcg(src + 2 * i), xb = __ldcg(src + 2 * i + 1);
+            word_t wa, wb;
+            ld_words2(src + 2 * i, wa, wb);
+            wait_words2(src + 2 * i, t_qkv, wa, wb, a.err);
+            float xa = wval(wa), xb = wval(wb);
             if (warp == 0 && L.k_norm) {
                 xa = __fmul_rn(__fmul_rn(xa, kinv), L.k_norm[2 * i]);
                 xb = __fmul_rn(__fmul_rn(xb, kinv), L.k_norm[2 * i + 1]);
@@ -1466,70 +1613,64 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
         for (int k = 0; k < MAXO; k++) {
             const int o = (tid + k * NCT) / tpo;
             if (k * NCT < nout * tpo && o < nout && tid % tpo == 0)
-                a.ao[(size_t)g * nout + o] = __fmul_rn(acc[k], __fdiv_rn(1.0f, S.sl[o / hd]));
+                st_word(a.aow + (size_t)g * nout + o, mkword(t_ao, __fmul_rn(acc[k], __fdiv_rn(1.0f, S.sl[o / hd]))));
         }
         if (tid == 0) ev(0, EV_ATT_DONE);
         return;
     }
-    /* this split's partial: unnormalized outputs, running max and sum */
+    /* this split's partial as tagged words: unnormalized outputs, running max
+     * and sum (no fence, no counter: the combining splits wait on the words) */
     const int stride = hd + 2;
 #pragma unroll
     for (int k = 0; k < MAXO; k++) {
         const int o = (tid + k * NCT) / tpo;
         if (k * NCT < nout * tpo && o < nout && tid % tpo == 0) {
             const int h = o / hd, i = o % hd;
-            a.part[((size_t)(g * group + h) * a.nsplit + y) * stride + i] = acc[k];
+            st_word(a.partw + ((size_t)(g * group + h) * a.nsplit + y) * stride + i, mkword(t_part, acc[k]));
         }
     }
     if (tid < group) {
-        float *ph = a.part + ((size_t)(g * group + tid) * a.nsplit + y) * stride;
-        ph[hd] = S.sm[tid];
-        ph[hd + 1] = S.sl[tid];
+        word_t *ph = a.partw + ((size_t)(g * group + tid) * a.nsplit + y) * stride;
+        st_word(ph + hd, mkword(t_part, S.sm[tid]));
+        st_word(ph + hd + 1, mkword(t_part, S.sl[tid]));
     }
-    consumer_sync();
     if (tid == 0) ev(0, EV_ATT_PARTIAL);
-    /* the head's splits wait for each other (all resident: a bounded spin),
-     * then each combines its slice of the group's outputs. The head's arrival
-     * counter grows over the launch: this round is complete at att_base +
-     * active. One thread fences the CTA's partial (ordered before it by the
-     * consumer barrier) and arrives; its acquire, then the barrier, order the
-     * loads of the other splits' partials. */
-    unsigned *arrived = a.att_counter + g;
-    if (tid == 0) {
-        __threadfence();
-        atomicAdd(arrived, 1u);
-        ev(0, EV_ATT_ARRIVED);
-        unsigned it = 0;
-        while (ld_acquire(arrived) < att_base + (unsigned)active) {
-            if (++it > (1u << 24)) {
-                atomicOr(a.err, 8u);
-                break;
-            }
-            if ((it & 1023) == 0 && ld_acquire(a.err)) break;
-        }
-        ev(0, EV_ATT_PART);
-    }
-    consumer_sync();
     const int chunk = (nout + active - 1) / active, o0 = y * chunk, o1 = min(nout, o0 + chunk);
     if (tid == 0) ev(0, EV_ATT_COMBINE);
-    /* a warp per output and a lane per split, OPW outputs per warp at a time:
-     * the splits' running maxima, sums and partial outputs arrive in one round
-     * trip; weight e_s / sum_s l_s e_s, e_s = exp(m_s - M), and the weighted
-     * partials summed in split order */
+    /* each split combines its slice of the group's outputs: a warp per output
+     * and a lane per split, OPW outputs per warp at a time; the splits'
+     * running maxima, sums and partial outputs are requested together and
+     * waited for word by word; weight e_s / sum_s l_s e_s, e_s = exp(m_s - M),
+     * and the weighted partials summed in split order */
     constexpr int OPW = 4;
     for (int ob = o0 + warp; ob < o1; ob += OPW * NCW) {
         float m[OPW], l[OPW], p[OPW];
+        word_t wm[OPW], wl[OPW], wp[OPW];
 #pragma unroll
         for (int k = 0; k < OPW; k++) {
             const int o = ob + k * NCW;
-            m[k] = -INFINITY;
-            l[k] = p[k] = 0.0f;
+            wm[k] = mkword(t_part, -INFINITY);
+            wl[k] = wp[k] = mkword(t_part, 0.0f);
             if (o < o1 && lane < active) {
                 const int h = o / hd, i = o - h * hd;
-                const float *ps = a.part + ((size_t)(g * group + h) * a.nsplit + lane) * stride;
-                m[k] = __ldcg(ps + hd);
-                l[k] = __ldcg(ps + hd + 1);
-                p[k] = __ldcg(ps + i);
+                const word_t *ps = a.partw + ((size_t)(g * group + h) * a.nsplit + lane) * stride;
+                wm[k] = ld_word(ps + hd);
+                wl[k] = ld_word(ps + hd + 1);
+                wp[k] = ld_word(ps + i);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < OPW; k++) {
+            const int o = ob + k * NCW;
+            m[k] = wval(wm[k]);
+            l[k] = wval(wl[k]);
+            p[k] = wval(wp[k]);
+            if (o < o1 && lane < active) {
+                const int h = o / hd, i = o - h * hd;
+                const word_t *ps = a.partw + ((size_t)(g * group + h) * a.nsplit + lane) * stride;
+                m[k] = wait_word(ps + hd, t_part, wm[k], a.err);
+                l[k] = wait_word(ps + hd + 1, t_part, wl[k], a.err);
+                p[k] = wait_word(ps + i, t_part, wp[k], a.err);
             }
         }
 #pragma unroll
@@ -1542,7 +1683,7 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
             float num = 0.0f;
             for (int s2 = 0; s2 < active; s2++)
                 num = fmaf(__shfl_sync(0xffffffffu, p[k], s2), __shfl_sync(0xffffffffu, w, s2), num);
-            if (lane == 0) a.ao[(size_t)g * nout + o] = num;
+            if (lane == 0) st_word(a.aow + (size_t)g * nout + o, mkword(t_ao, num));
         }
     }
     if (tid == 0) ev(0, EV_ATT_DONE);
@@ -1550,15 +1691,15 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
 
 /* UNITS: the 16-byte units of K a thread loads per tile, head_dim * bytes / 128. */
 __device__ __forceinline__ void attention_item(const StepArgs &a, const LayerPlan &L, int g, int y, int pos, float *fsm,
-                                               unsigned att_base) {
+                                               unsigned t_qkv, unsigned t_part, unsigned t_ao) {
     if (a.kv_type == KC_F16) {
-        if (a.hd <= 64) attention_item_t<KC_F16, 1>(a, L, g, y, pos, fsm, att_base);
-        else attention_item_t<KC_F16, 2>(a, L, g, y, pos, fsm, att_base);
+        if (a.hd <= 64) attention_item_t<KC_F16, 1>(a, L, g, y, pos, fsm, t_qkv, t_part, t_ao);
+        else attention_item_t<KC_F16, 2>(a, L, g, y, pos, fsm, t_qkv, t_part, t_ao);
     } else if (a.kv_type == KC_Q8_0) {
-        attention_item_t<KC_Q8_0, 1>(a, L, g, y, pos, fsm, att_base);
+        attention_item_t<KC_Q8_0, 1>(a, L, g, y, pos, fsm, t_qkv, t_part, t_ao);
     } else {
-        if (a.hd <= 64) attention_item_t<KC_F32, 2>(a, L, g, y, pos, fsm, att_base);
-        else attention_item_t<KC_F32, 4>(a, L, g, y, pos, fsm, att_base);
+        if (a.hd <= 64) attention_item_t<KC_F32, 2>(a, L, g, y, pos, fsm, t_qkv, t_part, t_ao);
+        else attention_item_t<KC_F32, 4>(a, L, g, y, pos, fsm, t_qkv, t_part, t_ao);
     }
 }
 
@@ -1655,14 +1796,18 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
     int own0, own1;
     share_rows(a.dim, j, G, own0, own1);
     const int nown = own1 - own0;
-    unsigned expect = 0, pidx = 0;   /* barrier arrivals due so far, trace index */
+    unsigned expect = 0, pidx = 0;   /* step-end barrier arrivals due so far, trace index */
     const ActW w_dim = act_layout(sh.act, a.dim), w_q = act_layout(sh.act, a.q_dim), w_h = act_layout(sh.act, a.hidden);
+    /* x words, sums of squares, post-norm block outputs: one buffer for the O
+     * phase (C) and one for the down phase (E) */
+    word_t *const xw_c = a.xw, *const xw_e = a.xw + a.dim;
+    word_t *const ss_c = a.sspw, *const ss_e = a.sspw + G;
+    word_t *const yw_c = a.yw, *const yw_e = a.yw + a.dim;
     if (threadIdx.x == 0) timeline_mark(a);
     fetch_plan(a.layers, &s_lp[0]);
     cp_async_wait_all();
     consumer_sync();
-    unsigned gl = 0;         /* running layer index over the launch's steps */
-    unsigned att_base = 0;   /* arrivals on each KV head's attention counter so far in this launch */
+    unsigned gl = 0;   /* running layer index over the launch's steps */
     for (int step = 0; step < a.nsteps; step++) {
         /* the loop state, read by one thread and shared (every thread of every
          * CTA on the same line would queue at its L2 slice) */
@@ -1682,102 +1827,112 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
         const float inv0 = s_inv0;
         for (int l = 0; l < a.n_layers; l++, gl++) {
             const LayerPlan &L = s_lp[gl & 1];
+            const unsigned t_qkv = tag_of(a, step, l, TAG_QKV), t_part = tag_of(a, step, l, TAG_PART);
+            const unsigned t_ao = tag_of(a, step, l, TAG_AO), t_xc = tag_of(a, step, l, TAG_XC);
+            const unsigned t_hb = tag_of(a, step, l, TAG_HB), t_xe = tag_of(a, step, l, TAG_XE);
             /* A: Q/K/V */
             if (l == 0) {
                 act_embed(a.emb, a.embed_scale, tk, L.attn_norm, inv0, a.dim, w_dim);
                 /* the residual stream starts as the embedding row: this CTA's rows of x */
-                for (int r = own0 + (int)threadIdx.x; r < own1; r += NCT) {
-                    const float e1 = embed1(a, tk, a.dim, r);
-                    a.x[r] = e1;
-                    sh.own[r - own0] = e1;
-                }
+                for (int r = own0 + (int)threadIdx.x; r < own1; r += NCT) sh.own[r - own0] = embed1(a, tk, a.dim, r);
             } else if (a.post_norms) {
-                act_postnorm(a, a.x, a.yb, s_lp[(gl - 1) & 1].post_ffn, L.attn_norm, a.dim, w_dim, sh.red, sh.own,
-                             own0, own1);
+                act_postnorm(a, xw_e, yw_e, ss_e, tag_of(a, step, l - 1, TAG_XE), s_lp[(gl - 1) & 1].post_ffn,
+                             L.attn_norm, a.dim, w_dim, sh.red, sh.own, own0, own1);
             } else {
-                load_activation(a, a.x, L.attn_norm, a.ssp, a.dim, w_dim, sh.red, sh.wbuf);
+                load_activation(a, xw_e, tag_of(a, step, l - 1, TAG_XE), L.attn_norm, ss_e, a.dim, w_dim, sh.red,
+                                sh.wbuf);
             }
             trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_A], false, act_view(w_dim), sh.res, a.err);
             {
                 const PhasePlan &P = s_plan[PH_A];
-                finish_phase(FIN_STORE, sh.res, plan_rows(P), P.nseg ? P.seg[0].row0 : 0, a.qkv, nullptr, 0, 0.0f,
-                             sh.cta_best, col_slices(a.dim / QK, false));
+                finish_phase(FIN_STORE, sh.res, plan_rows(P), P.nseg ? P.seg[0].row0 : 0, nullptr, a.qkvw, t_qkv,
+                             nullptr, 0, 0.0f, sh.cta_best, col_slices(a.dim / QK, false));
             }
-            grid_barrier(a, expect, pidx);
+            phase_end(a, pidx);
             /* B: attention; the next layer's plan is fetched meanwhile (the
              * buffer's last reader, the previous layer's A prologue, is done) */
             fetch_plan(a.layers + (l + 1 < a.n_layers ? l + 1 : 0), &s_lp[(gl + 1) & 1]);
             trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             for (int it = j; it < a.n_kv_heads * a.nsplit; it += G)
-                attention_item(a, L, it / a.nsplit, it % a.nsplit, ps, (float *)sh.act, att_base);
-            {
-                int first, C;
-                const int na = att_splits(a, L, ps, first, C);
-                if (na > 1) att_base += (unsigned)na;   /* a single split arrives nowhere */
-            }
-            grid_barrier(a, expect, pidx);
+                attention_item(a, L, it / a.nsplit, it % a.nsplit, ps, (float *)sh.act, t_qkv, t_part, t_ao);
+            consumer_sync();   /* the attention scratch is the next activation's space */
+            phase_end(a, pidx);
             /* C: O projection + residual */
-            load_activation(a, a.ao, nullptr, nullptr, a.q_dim, w_q, sh.red);
+            load_activation(a, a.aow, t_ao, nullptr, nullptr, a.q_dim, w_q, sh.red);
             trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_C], false, act_view(w_q), sh.res, a.err);
-            if (a.post_norms)
-                finish_post(sh.res, nown, own0, col_slices(a.q_dim / QK, false), a.x, a.yb, sh.own, sh.yown);
-            else if (a.tp_world > 1)
-                tp_resid(a, sh.res, nown, own0, a.x, sh.own, col_slices(a.q_dim / QK, false), 0, tp_seq(a, step, l, 0));
-            else
-                finish_phase(FIN_RESID, sh.res, nown, own0, a.x, sh.own, 0, 0.0f, sh.cta_best,
-                             col_slices(a.q_dim / QK, false));
+            if (a.post_norms) {
+                finish_post(sh.res, nown, own0, col_slices(a.q_dim / QK, false), xw_c, yw_c, t_xc, sh.own, sh.yown);
+                publish_ssp(ss_c, t_xc, sh.yown, nown);
+            } else {
+                if (a.tp_world > 1) {
+                    tp_resid(a, sh.res, nown, own0, sh.own, col_slices(a.q_dim / QK, false), 0, tp_seq(a, step, l, 0));
+                    publish_rows(xw_c, t_xc, sh.own, nown, own0);
+                } else {
+                    finish_phase(FIN_RESID, sh.res, nown, own0, nullptr, xw_c, t_xc, sh.own, 0, 0.0f, sh.cta_best,
+                                 col_slices(a.q_dim / QK, false));
+                }
+                publish_ssp(ss_c, t_xc, sh.own, nown);
+            }
             prefetch_norm(sh.wbuf, L.ffn_norm, a.dim);
-            grid_barrier(a, expect, pidx, a.post_norms ? sh.yown : sh.own, nown);
+            phase_end(a, pidx);
             /* D: gate/up + activation */
             if (a.post_norms)
-                act_postnorm(a, a.x, a.yb, L.post_attn, L.ffn_norm, a.dim, w_dim, sh.red, sh.own, own0, own1);
+                act_postnorm(a, xw_c, yw_c, ss_c, t_xc, L.post_attn, L.ffn_norm, a.dim, w_dim, sh.red, sh.own, own0,
+                             own1);
             else
-                load_activation(a, a.x, L.ffn_norm, a.ssp, a.dim, w_dim, sh.red, sh.wbuf);
+                load_activation(a, xw_c, t_xc, L.ffn_norm, ss_c, a.dim, w_dim, sh.red, sh.wbuf);
             trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_D], true, act_view(w_dim), sh.res, a.err);
-            finish_phase(FIN_PAIR, sh.res, s_plan[PH_D].seg[0].rows, s_plan[PH_D].seg[0].row0, a.hb, nullptr, a.act, 0.0f,
-                         sh.cta_best, 1);
-            grid_barrier(a, expect, pidx);
+            finish_phase(FIN_PAIR, sh.res, s_plan[PH_D].seg[0].rows, s_plan[PH_D].seg[0].row0, nullptr, a.hbw, t_hb,
+                         nullptr, a.act, 0.0f, sh.cta_best, 1);
+            phase_end(a, pidx);
             /* E: down + residual */
-            load_activation(a, a.hb, nullptr, nullptr, a.hidden, w_h, sh.red);
+            load_activation(a, a.hbw, t_hb, nullptr, nullptr, a.hidden, w_h, sh.red);
             trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_E], false, act_view(w_h), sh.res, a.err);
-            if (a.post_norms)
-                finish_post(sh.res, nown, own0, col_slices(a.hidden / QK, false), a.x, a.yb, sh.own, sh.yown);
-            else if (a.tp_world > 1)
-                tp_resid(a, sh.res, nown, own0, a.x, sh.own, col_slices(a.hidden / QK, false), 1, tp_seq(a, step, l, 1));
-            else
-                finish_phase(FIN_RESID, sh.res, nown, own0, a.x, sh.own, 0, 0.0f, sh.cta_best,
-                             col_slices(a.hidden / QK, false));
+            if (a.post_norms) {
+                finish_post(sh.res, nown, own0, col_slices(a.hidden / QK, false), xw_e, yw_e, t_xe, sh.own, sh.yown);
+                publish_ssp(ss_e, t_xe, sh.yown, nown);
+            } else {
+                if (a.tp_world > 1) {
+                    tp_resid(a, sh.res, nown, own0, sh.own, col_slices(a.hidden / QK, false), 1, tp_seq(a, step, l, 1));
+                    publish_rows(xw_e, t_xe, sh.own, nown, own0);
+                } else {
+                    finish_phase(FIN_RESID, sh.res, nown, own0, nullptr, xw_e, t_xe, sh.own, 0, 0.0f, sh.cta_best,
+                                 col_slices(a.hidden / QK, false));
+                }
+                publish_ssp(ss_e, t_xe, sh.own, nown);
+            }
             /* the next layer's plan (landed long ago) to every thread, then its
-             * norm weights on their way during the barrier */
+             * norm weights on their way while the next prologue waits */
             if (threadIdx.x < LP_UNITS) cp_async_wait_all();
             consumer_sync();
             prefetch_norm(sh.wbuf, l + 1 < a.n_layers ? s_lp[(gl + 1) & 1].attn_norm : (a.run_cls ? a.final_norm : nullptr),
                           a.dim);
-            grid_barrier(a, expect, pidx, a.post_norms ? sh.yown : sh.own, nown);
+            phase_end(a, pidx);
         }
         /* F: classifier + argmax */
         if (a.run_cls) {
+            const unsigned t_last = tag_of(a, step, a.n_layers - 1, TAG_XE);
             if (a.post_norms)
-                act_postnorm(a, a.x, a.yb, s_lp[(gl - 1) & 1].post_ffn, a.final_norm, a.dim, w_dim, sh.red, sh.own,
-                             own0, own1);
+                act_postnorm(a, xw_e, yw_e, ss_e, t_last, s_lp[(gl - 1) & 1].post_ffn, a.final_norm, a.dim, w_dim,
+                             sh.red, sh.own, own0, own1);
             else
-                load_activation(a, a.x, a.final_norm, a.ssp, a.dim, w_dim, sh.red, sh.wbuf);
+                load_activation(a, xw_e, t_last, a.final_norm, ss_e, a.dim, w_dim, sh.red, sh.wbuf);
             trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             consume_phase(rg, s_plan[PH_F], false, act_view(w_dim), sh.res, a.err);
             const Seg &F = s_plan[PH_F].seg[0];
             const unsigned long long b =
                 finish_phase(FIN_LOGITS, sh.res, F.rows, a.cls_row0 + F.row0, a.logits + logit_row0, nullptr, 0,
-                             a.final_softcap, sh.cta_best, col_slices(a.dim / QK, false));
+                             nullptr, 0, a.final_softcap, sh.cta_best, col_slices(a.dim / QK, false));
             if (threadIdx.x == 0 && b) atomicMax(&a.ls->best, b);
             if (a.tp_world > 1) {
                 /* this rank's logits rows into every other rank's ring (each thread
@@ -1792,7 +1947,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
             }
         }
         /* every CTA arrives; the last one advances the loop state, then
-         * releases the others with one more arrival */
+         * releases the others with one more arrival (the one grid barrier of a
+         * step: it also orders this step's KV rows before the next step's reads) */
         consumer_sync();
         const unsigned pfin = pidx++;
         expect += gridDim.x;
