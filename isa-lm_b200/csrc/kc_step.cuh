@@ -840,6 +840,29 @@ __device__ __forceinline__ void publish_ssp(word_t *sspw, unsigned tag, const fl
     }
 }
 
+/* The residual add of a phase whose CTA rows fit one warp (n <= 32): lane i
+ * sums row i's column slices in order, adds it to own[i] and publishes the
+ * row, and the warp publishes the rows' sum of squares in the same pass (the
+ * same per-lane squares and warp tree as publish_ssp, so the same bits),
+ * with no CTA barrier in between: the next RMSNorm gets x and its sum
+ * together. */
+__device__ __forceinline__ void finish_resid_warp(const float *res, int n, int row0, word_t *xw, word_t *sspw,
+                                                  unsigned tag, float *own, int ns) {
+    if (threadIdx.x >= 32) return;
+    const int i = threadIdx.x;
+    float t = 0.0f;
+    if (i < n) {
+        float sum = res[i * ns];
+        for (int k = 1; k < ns; k++) sum = __fadd_rn(sum, res[i * ns + k]);
+        const float v = __fadd_rn(own[i], sum);
+        own[i] = v;
+        st_word(xw + row0 + i, mkword(tag, v));
+        t = v * v;
+    }
+    t = warp_sum(t);
+    if (i == 0) st_word(sspw + blockIdx.x, mkword(tag, t));
+}
+
 /* Consumer of the kernel-level matvec (rows [r0, r1) as produce_rows staged them). */
 template <int TYPE, bool D16>
 __device__ void consume_rows(Ring &rg, int cols, int r0, int r1, float *y, const Act &x, unsigned *err,
@@ -1872,11 +1895,14 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
                 if (a.tp_world > 1) {
                     tp_resid(a, sh.res, nown, own0, sh.own, col_slices(a.q_dim / QK, false), 0, tp_seq(a, step, l, 0));
                     publish_rows(xw_c, t_xc, sh.own, nown, own0);
+                    publish_ssp(ss_c, t_xc, sh.own, nown);
+                } else if (nown <= 32) {
+                    finish_resid_warp(sh.res, nown, own0, xw_c, ss_c, t_xc, sh.own, col_slices(a.q_dim / QK, false));
                 } else {
                     finish_phase(FIN_RESID, sh.res, nown, own0, nullptr, xw_c, t_xc, sh.own, 0, 0.0f, sh.cta_best,
                                  col_slices(a.q_dim / QK, false));
+                    publish_ssp(ss_c, t_xc, sh.own, nown);
                 }
-                publish_ssp(ss_c, t_xc, sh.own, nown);
             }
             prefetch_norm(sh.wbuf, L.ffn_norm, a.dim);
             phase_end(a, pidx);
@@ -1904,11 +1930,14 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
                 if (a.tp_world > 1) {
                     tp_resid(a, sh.res, nown, own0, sh.own, col_slices(a.hidden / QK, false), 1, tp_seq(a, step, l, 1));
                     publish_rows(xw_e, t_xe, sh.own, nown, own0);
+                    publish_ssp(ss_e, t_xe, sh.own, nown);
+                } else if (nown <= 32) {
+                    finish_resid_warp(sh.res, nown, own0, xw_e, ss_e, t_xe, sh.own, col_slices(a.hidden / QK, false));
                 } else {
                     finish_phase(FIN_RESID, sh.res, nown, own0, nullptr, xw_e, t_xe, sh.own, 0, 0.0f, sh.cta_best,
                                  col_slices(a.hidden / QK, false));
+                    publish_ssp(ss_e, t_xe, sh.own, nown);
                 }
-                publish_ssp(ss_e, t_xe, sh.own, nown);
             }
             /* the next layer's plan (landed long ago) to every thread, then its
              * norm weights on their way while the next prologue waits */
