@@ -23,7 +23,9 @@
 namespace kc {
 
 constexpr int QK = 32;
-constexpr int NCW = 16;                  /* consumer warps of a streaming CTA */
+constexpr int NCW = 8;                   /* consumer warps of a streaming CTA: 288 threads with the
+                                            producer, so that a thread gets up to 224 registers and the
+                                            decode step runs without spills or call frames */
 constexpr int NCT = NCW * 32;            /* consumer threads */
 constexpr int STEP_THREADS = NCT + 32;   /* + the producer warp */
 constexpr int STAGE_Q = 32 * 1024;       /* bytes of quants per ring stage (at least one row) */

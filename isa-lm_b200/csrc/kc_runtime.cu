@@ -891,7 +891,7 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
     const int group = c.n_heads / c.n_kv_heads;
     const int es = (int)kv_elem_bytes(kv_type);
     if (group * c.head_dim > ATT_MAX_OUT || (c.head_dim * es) % 16 || c.head_dim % 16 ||
-        ATT_TILE * (c.head_dim * es / 16) > KVU_MAX * NCT || group > NCW) {
+        (kv_type != KC_F32 && c.head_dim > 128) || group > NCW) {
         set_error("attention head layout outside this build's kernel limits");
         return KC_E_SHAPE;
     }

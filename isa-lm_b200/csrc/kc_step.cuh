@@ -448,7 +448,7 @@ __device__ __forceinline__ unsigned long long ld_sys_u64(const unsigned long lon
  * own[row] += y_0 + y_1 + ... Every rank runs the same grid, so CTA j of every
  * rank owns the same rows of x; a rank can store the next exchange's words
  * into a slot only after this rank has passed the exchange in between. */
-__device__ __noinline__ void tp_resid(const StepArgs &a, const float *res, int nrows, int row0, float *own, int ns,
+__device__ __forceinline__ void tp_resid(const StepArgs &a, const float *res, int nrows, int row0, float *own, int ns,
                                       int ph, unsigned seq) {
     const int me = a.tp_rank, W = a.tp_world, D = a.dim;
     for (int i = threadIdx.x; i < nrows; i += NCT) {
@@ -931,7 +931,7 @@ __device__ __forceinline__ float embed1(const StepArgs &a, int tok, int cols, in
  * 1/rms: inv_given when > 0, else from ss = the sum of the G per-CTA partial
  * sums ssp, else reduced here. Every thread issues all its loads before it
  * uses any, so a prologue costs one round trip to L2. */
-constexpr int ACT_PASSES = 4;   /* float4 loads a thread holds in registers: 8192 columns at most */
+constexpr int ACT_PASSES = 8;   /* float4 loads a thread holds in registers: 8192 columns at most */
 
 /* Starts copying the norm weights that this thread's act_float slots read
  * into wbuf (asynchronous, no wait): issued before a grid barrier, the copy
@@ -973,7 +973,7 @@ __device__ __forceinline__ void put_quant(const ActW &o, int b, int nb, int j0, 
  * Every thread issues all its loads (up to 2 passes of 128 blocks, 4 lanes
  * per block, 8 values per lane) before it waits on any, so the prologue costs
  * one round trip to L2 once its input has landed. */
-__device__ __noinline__ void act_float(float eps, const word_t *xw, unsigned tag, const float *norm_w,
+__device__ __forceinline__ void act_float(float eps, const word_t *xw, unsigned tag, const float *norm_w,
                                        const word_t *sspw, int cols, ActW o, float *red, const float *wstaged,
                                        unsigned *err) {
     /* 4 lanes per block, 8 values per lane (four word pairs), passes of NCT / 4 blocks */
@@ -984,54 +984,62 @@ __device__ __noinline__ void act_float(float eps, const word_t *xw, unsigned tag
     /* one warp per CTA loads the G per-CTA sums of squares (the same few
      * lines read by every warp of every CTA would queue at their L2 slice) */
     const int lane = tid & 31, warp = tid >> 5;
-    const bool ssw = norm && sspw && warp == 0;
-    word_t part[SSP_LOADS];
-#pragma unroll
-    for (int k = 0; k < SSP_LOADS; k++) {
-        const int idx = k * 32 + lane;
-        part[k] = (ssw && idx < (int)gridDim.x) ? ld_word(sspw + idx) : mkword(tag, 0.0f);
-    }
+    const bool ssw = norm && sspw && tid < (int)gridDim.x;   /* thread t reads CTA t's sum */
     constexpr int NP = ACT_PASSES / 2;   /* passes of NCT / 4 blocks */
-    word_t v[NP][8];
+    bool live[NP];
+    const word_t *src[NP];
 #pragma unroll
     for (int p = 0; p < NP; p++) {
         const int b = p * (NCT / 4) + (tid >> 2);
-#pragma unroll
-        for (int h = 0; h < 4; h++) {
-            v[p][2 * h] = v[p][2 * h + 1] = mkword(tag, 0.0f);
-            if (p < passes && b < nb) ld_words2(xw + b * QK + j0 + 2 * h, v[p][2 * h], v[p][2 * h + 1]);
-        }
+        live[p] = p < passes && b < nb;
+        src[p] = xw + b * QK + j0;
     }
+    /* every word this thread reads, requested together; then, in one loop,
+     * the stale ones again until all carry the tag */
+    word_t v[NP][8], part = mkword(tag, 0.0f);
+    bool fresh = false;
+    for (unsigned it = 0;; it++) {
 #pragma unroll
-    for (int p = 0; p < NP; p++) {
-        const int b = p * (NCT / 4) + (tid >> 2);
+        for (int p = 0; p < NP; p++)
 #pragma unroll
-        for (int h = 0; h < 4; h++)
-            if (p < passes && b < nb) wait_words2(xw + b * QK + j0 + 2 * h, tag, v[p][2 * h], v[p][2 * h + 1], err);
+            for (int h = 0; h < 4; h++) {
+                if (!live[p]) {
+                    v[p][2 * h] = v[p][2 * h + 1] = mkword(tag, 0.0f);
+                } else if (it == 0 || !(wok(v[p][2 * h], tag) && wok(v[p][2 * h + 1], tag))) {
+                    ld_words2(src[p] + 2 * h, v[p][2 * h], v[p][2 * h + 1]);
+                }
+            }
+        if (ssw && (it == 0 || !wok(part, tag))) part = ld_word(sspw + tid);
+        fresh = wok(part, tag);
+#pragma unroll
+        for (int p = 0; p < NP; p++)
+#pragma unroll
+            for (int k = 0; k < 8; k++) fresh = fresh && wok(v[p][k], tag);
+        if (fresh) break;
+        if (it >= POLL_LIMIT) {
+            atomicOr(err, ERR_POLL);
+            break;
+        }
+        if ((it & 63) == 63 && *(volatile const unsigned *)err) break;
     }
     if (tid == 0) ev(0, EV_ACT_LOADED);
-    float4 w[2 * NP];
-#pragma unroll
-    for (int k = 0; k < 2 * NP; k++) w[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    /* the norm weights: staged in shared memory by prefetch_norm (this
+     * thread's own copies), read where they are used */
     if (norm && wstaged) cp_async_wait_all();
-#pragma unroll
-    for (int p = 0; p < NP; p++) {
-        const int b = p * (NCT / 4) + (tid >> 2);
-#pragma unroll
-        for (int h = 0; h < 2; h++)
-            if (norm && p < passes && b < nb)
-                w[2 * p + h] = *(const float4 *)((wstaged ? wstaged : norm_w) + b * QK + j0 + 4 * h);
-    }
+    const float *wsrc = wstaged ? wstaged : norm_w;
     float inv = 1.0f;
     if (norm) {
         if (sspw) {
+            /* the G sums through shared memory, then added by warp 0 as lane l
+             * adds CTAs l, l + 32, ... in order and the warp's tree adds lanes */
+            float *sums = red + 32;
+            if (ssw) sums[tid] = wval(part);
+            consumer_sync();
             if (warp == 0) {
                 float t = 0.0f;
 #pragma unroll
-                for (int k = 0; k < SSP_LOADS; k++) {
-                    const int idx = k * 32 + lane;
-                    if (ssw && idx < (int)gridDim.x) t += wait_word(sspw + idx, tag, part[k], err);
-                }
+                for (int k = 0; k < SSP_LOADS; k++)
+                    if (k * 32 + lane < (int)gridDim.x) t += sums[k * 32 + lane];
                 const float ss = warp_sum(t);
                 if (lane == 0) red[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
             }
@@ -1052,16 +1060,16 @@ __device__ __noinline__ void act_float(float eps, const word_t *xw, unsigned tag
         }
     }
     if (tid == 0) ev(0, EV_ACT_INV);
-    /* the passes unrolled: their block maxima, divisions and stores overlap */
-#pragma unroll
-    for (int p = 0; p < NP; p++) {
-        if (p >= passes) break;
-        const int b = p * (NCT / 4) + (tid >> 2);
+    /* the passes in one copy of the code: the second pass's values move into
+     * the first's registers at the end of each round */
+    int b = tid >> 2;
+#pragma unroll 1
+    for (int p = 0; p < passes; p++, b += NCT / 4) {
         float u[8];
 #pragma unroll
-        for (int k = 0; k < 8; k++) u[k] = wval(v[p][k]);
-        if (norm) {
-            const float4 w0 = w[2 * p], w1 = w[2 * p + 1];
+        for (int k = 0; k < 8; k++) u[k] = wval(v[0][k]);
+        if (norm && b < nb) {
+            const float4 w0 = *(const float4 *)(wsrc + b * QK + j0), w1 = *(const float4 *)(wsrc + b * QK + j0 + 4);
             const float wv[8] = { w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w };
 #pragma unroll
             for (int i = 0; i < 8; i++) u[i] = __fmul_rn(__fmul_rn(u[i], inv), wv[i]);
@@ -1076,6 +1084,10 @@ __device__ __noinline__ void act_float(float eps, const word_t *xw, unsigned tag
                 o.xs[b] = 8 * sum;
             }
         }
+#pragma unroll
+        for (int q = 0; q + 1 < NP; q++)
+#pragma unroll
+            for (int k = 0; k < 8; k++) v[q][k] = v[q + 1][k];
     }
     if (tid == 0) ev(0, EV_ACT_QUANT);
     consumer_sync();
@@ -1083,7 +1095,7 @@ __device__ __noinline__ void act_float(float eps, const word_t *xw, unsigned tag
 
 /* Layer 0's activation: the embedding row of tok, its 1/rms from the host
  * table (inv), times the norm weights. */
-__device__ __noinline__ void act_embed(PMat emb, float embed_scale, int tok, const float *norm_w, float inv, int cols,
+__device__ __forceinline__ void act_embed(PMat emb, float embed_scale, int tok, const float *norm_w, float inv, int cols,
                                        ActW o) {
     const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 7) * 4;
 #pragma unroll 1
@@ -1136,7 +1148,7 @@ __device__ __noinline__ void act_loop(float eps, const float *x, const float *no
 }
 
 /* act_loop over tagged words: wider vectors in the step kernel, pass by pass. */
-__device__ __noinline__ void act_loop_w(float eps, const word_t *xw, unsigned tag, const float *norm_w,
+__device__ __forceinline__ void act_loop_w(float eps, const word_t *xw, unsigned tag, const float *norm_w,
                                         const word_t *sspw, int cols, ActW o, float *red, unsigned *err) {
     const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 7) * 4;
     float inv = 1.0f;
@@ -1176,7 +1188,7 @@ __device__ __noinline__ void act_loop_w(float eps, const word_t *xw, unsigned ta
  * Every CTA recomputes it for all cols, adds up its squares and quantizes
  * RMSNorm(x_new) * nw into the activation; the CTA's own rows of x_new go to
  * own (and out as words one phase later, with the next block's output). */
-__device__ __noinline__ void act_postnorm(const StepArgs &a, const word_t *x, const word_t *y, const word_t *ssw,
+__device__ __forceinline__ void act_postnorm(const StepArgs &a, const word_t *x, const word_t *y, const word_t *ssw,
                                           unsigned tag, const float *pw, const float *nw, int cols, ActW o, float *red,
                                           float *own, int own0, int own1) {
     const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 7) * 4;
@@ -1212,7 +1224,7 @@ __device__ __noinline__ void act_postnorm(const StepArgs &a, const word_t *x, co
  * rows (column slices summed in order) into yown and out as words (yw), and
  * the CTA's rows of the residual stream the last prologue computed (own) as
  * words (xw), with the same tag. */
-__device__ __noinline__ void finish_post(const float *res, int nrows, int row0, int ns, word_t *xw, word_t *yw,
+__device__ __forceinline__ void finish_post(const float *res, int nrows, int row0, int ns, word_t *xw, word_t *yw,
                                          unsigned tag, const float *own, float *yown) {
     for (int i = threadIdx.x; i < nrows; i += NCT) {
         float sum = res[i * ns];
@@ -1256,7 +1268,9 @@ __device__ void act_prequant(const int8_t *pq, const float *pd, int cols, const 
 
 /* ------------------------------------------------------------ attention */
 
-constexpr int KVU_MAX = 4;   /* 16-byte units of K (and of V) a thread loads per tile */
+constexpr int KVU_MAX = 8;   /* 16-byte units of K (and of V) a thread loads per tile */
+/* 16-byte units of a K (or V) tile per consumer thread for head_dim hd at es bytes per element. */
+__host__ __device__ constexpr int att_units(int es, int hd) { return (ATT_TILE * (hd * es / 16) + NCT - 1) / NCT; }
 
 /* Shared scratch of an attention item, in floats (layout in att_smem; every
  * region starts on a 16-byte boundary). */
@@ -1266,11 +1280,12 @@ __host__ __device__ inline int attention_scratch_floats(int group, int hd) {
            + ATT_TILE * (hd + 4) + ATT_TILE                                         /* K tile, K scales */
            + ATT_TILE * hd + ATT_TILE                                               /* V tile, V scales */
            + att_pad4(group * ATT_TILE) + 3 * att_pad4(group)                       /* p, m, l, alpha */
-           + att_pad4(hd) * 2 + 4;                                                  /* this position's K, V, scales */
+           + att_pad4(hd) * 2 + 4                                                   /* this position's K, V, scales */
+           + att_pad4(group * hd);                                                  /* the outputs' running sums */
 }
 
 struct AttSmem {
-    float *sq, *sqd, *sk, *skd, *sv, *svd, *sp, *sm, *sl, *sa, *knew, *vnew, *knd;
+    float *sq, *sqd, *sk, *skd, *sv, *svd, *sp, *sm, *sl, *sa, *knew, *vnew, *knd, *acc;
     int8_t *sqq;
 };
 
@@ -1289,7 +1304,8 @@ __device__ __forceinline__ AttSmem att_smem(float *f, int group, int hd) {
     s.sa = f; f += att_pad4(group);
     s.knew = f; f += att_pad4(hd);
     s.vnew = f; f += att_pad4(hd);
-    s.knd = f;
+    s.knd = f; f += 4;
+    s.acc = f;
     return s;
 }
 
@@ -1316,10 +1332,13 @@ __device__ __forceinline__ int att_splits(const StepArgs &a, const LayerPlan &L,
  * * v). The splits of a KV head then publish their partials as tagged words
  * (t_part) and each combines its slice of the head group's outputs into the
  * attention output words (t_ao); q, k and v arrive as tagged words (t_qkv). */
-template <int KV, int UNITS>
-__device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan &L, int g, int y, int pos, float *fsm,
-                                              unsigned t_qkv, unsigned t_part, unsigned t_ao) {
+template <int KV>
+__device__ __forceinline__ void attention_item_t(const StepArgs &a, const LayerPlan &L, int g, int y, int pos, float *fsm,
+                                                 unsigned t_qkv, unsigned t_part, unsigned t_ao) {
     constexpr int ES = KV == KC_F32 ? 4 : (KV == KC_F16 ? 2 : 1);
+    /* F16 and Q8 tiles pass through registers (converted on their way into
+     * shared memory), up to head_dim 128; F32 tiles are copied by cp.async */
+    constexpr int UNITS = KV == KC_F32 ? 1 : att_units(ES, 128);
     const int hd = a.hd, group = a.n_heads / a.n_kv_heads, h2 = hd / 2, tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
     int first, C;
@@ -1330,9 +1349,9 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
     const int upr = hd * ES / 16;                      /* 16-byte units per cache row */
     const size_t rowb = (size_t)a.kv_dim * ES;
     const uint8_t *kb = (const uint8_t *)L.kc + (size_t)g * hd * ES, *vb = (const uint8_t *)L.vc + (size_t)g * hd * ES;
-    /* the first tile's K and V go into registers before anything else, so
-     * their latency overlaps the query's; each later tile is loaded while the
-     * one before is computed; the split's own position comes from knew/vnew */
+    /* the first tile's K and V are requested before anything else, so their
+     * latency overlaps the query's; each later tile is loaded while the one
+     * before is computed; the split's own position comes from knew/vnew */
     uint4 rk[UNITS], rv[UNITS];
     float rkd = 0.0f, rvd = 0.0f;
     auto load_tile = [&](int t0) {
@@ -1350,6 +1369,16 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
             rvd = __ldcg(L.vd + (size_t)(t0 + tid) * a.n_kv_heads + g);
         }
     };
+    /* F32: K (or V) rows of a tile straight into their shared-memory layout,
+     * one cp.async group (the own position's row is not in the cache yet) */
+    auto copy_rows = [&](int t0, const uint8_t *src, float *dst, int ld) {
+        const int nt = min(ATT_TILE, t_end - t0);
+        for (int idx = tid; idx < nt * upr; idx += NCT) {
+            const int t = idx / upr, u = idx - t * upr;
+            if (t0 + t != pos) cp_async16(dst + t * ld + 4 * u, src + (size_t)(t0 + t) * rowb + 16 * u);
+        }
+        cp_async_commit();
+    };
     if (tid == 0) ev(0, EV_ATT_ENTRY);
     /* this thread's first query pair and its RoPE angle, loaded before the tile
      * so that both round trips overlap */
@@ -1363,19 +1392,9 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
         c0 = cs[i];
         s0 = sn[i];
     }
-    /* F32: the first tile goes straight into its shared-memory layout (cp.async;
-     * no registers held across the query's RoPE) */
     if constexpr (KV == KC_F32) {
-        const int nt = min(ATT_TILE, t_end - t_begin);
-        for (int idx = tid; idx < nt * upr; idx += NCT) {
-            const int t = idx / upr, u = idx - t * upr;
-            if (t_begin + t != pos) {
-                const size_t src = (size_t)(t_begin + t) * rowb + 16 * u;
-                cp_async16(S.sk + t * (hd + 4) + 4 * u, kb + src);
-                cp_async16(S.sv + t * hd + 4 * u, vb + src);
-            }
-        }
-        cp_async_commit();
+        copy_rows(t_begin, kb, S.sk, hd + 4);
+        copy_rows(t_begin, vb, S.sv, hd);
     } else {
         load_tile(t_begin);
     }
@@ -1468,21 +1487,27 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
         S.sl[tid] = 0.0f;
     }
     const int nout = group * hd;
-    constexpr int MAXO = (ATT_MAX_OUT + NCT - 1) / NCT;
     /* one thread per score (a dot over hd) and per output (a sum over the
-     * tile), each summed in the order of the reference's loops */
-    constexpr int tpd = 1, tpo = 1;
-    float acc[MAXO];
-#pragma unroll
-    for (int k = 0; k < MAXO; k++) acc[k] = 0.0f;
+     * tile), each summed in the order of the reference's loops; the outputs'
+     * running sums in shared memory (acc) */
+    constexpr int tpd = 1;
+    for (int o = tid; o < nout; o += NCT) S.acc[o] = 0.0f;
     consumer_sync();
     if (KV == KC_Q8_0 && warp < group)
         S.sqd[warp] = warp_quantize_row(S.sq + warp * hd, hd, S.sqq + warp * hd, nullptr, lane);
     if (tid == 0) ev(0, EV_ATT_PRE);
     for (int t0 = t_begin; t0 < t_end; t0 += ATT_TILE) {
         const int nt = min(ATT_TILE, t_end - t0);
+        if constexpr (KV == KC_F32) {
+            /* the tile came by cp.async, all but the own position's row */
+            if (pos >= t0 && pos < t0 + nt)
+                for (int i = tid; i < hd; i += NCT) {
+                    S.sk[(pos - t0) * (hd + 4) + i] = S.knew[i];
+                    S.sv[(pos - t0) * hd + i] = S.vnew[i];
+                }
+        }
 #pragma unroll
-        for (int e = 0; e < UNITS; e++) {
+        for (int e = 0; e < (KV == KC_F32 ? 0 : UNITS); e++) {
             const int idx = tid + e * NCT, t = idx / upr, u = idx - t * upr;
             if (idx < nt * upr) {
                 const bool own = t0 + t == pos;
@@ -1508,12 +1533,8 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
                             kf[k] = S.knew[PER * u + k];
                             vf[k] = S.vnew[PER * u + k];
                         }
-                    } else if (KV == KC_F32 && t0 == t_begin) {
-                        continue;   /* landed by cp.async */
                     } else if constexpr (KV == KC_F32) {
-                        const float *ka = (const float *)&rk[e], *va = (const float *)&rv[e];
-#pragma unroll
-                        for (int k = 0; k < PER; k++) { kf[k] = ka[k]; vf[k] = va[k]; }
+                        continue;   /* not reached: F32 tiles come by cp.async */
                     } else {
                         const __half *ka = (const __half *)&rk[e], *va = (const __half *)&rv[e];
 #pragma unroll
@@ -1533,8 +1554,11 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
             S.svd[tid] = own ? S.knd[1] : rvd;
         }
         if (tid == 0) ev(0, EV_ATT_STORED);
-        if (KV == KC_F32 && t0 == t_begin) cp_async_wait_all();
-        if (t0 + ATT_TILE < t_end) load_tile(t0 + ATT_TILE);
+        if constexpr (KV == KC_F32) {
+            cp_async_wait_all();   /* this thread's copies of the tile's K and V */
+        } else {
+            if (t0 + ATT_TILE < t_end) load_tile(t0 + ATT_TILE);
+        }
         consumer_sync();
         if (tid == 0) ev(0, EV_ATT_SYNCED);
         /* scores: tpd threads per (head, position); every lane takes part in
@@ -1573,6 +1597,8 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
             if (part == 0) S.sp[h * ATT_TILE + t] = s;
         }
         consumer_sync();
+        /* F32: K is read; the next tile's K lands during the softmax and the V sum */
+        if (KV == KC_F32 && t0 + ATT_TILE < t_end) copy_rows(t0 + ATT_TILE, kb, S.sk, hd + 4);
         if (tid == 0) ev(0, EV_ATT_SCORES);
         for (int h = warp; h < group; h += NCW) {
             const float s0 = S.sp[h * ATT_TILE + lane], s1 = S.sp[h * ATT_TILE + 32 + lane];
@@ -1590,67 +1616,52 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
         }
         consumer_sync();
         if (tid == 0) ev(0, EV_ATT_SOFTMAX);
-        /* outputs: tpo threads per (head, dimension), positions interleaved */
-#pragma unroll
-        for (int k = 0; k < MAXO; k++) {
-            const int o = (tid + k * NCT) / tpo, part = tid % tpo;
-            if (k * NCT < nout * tpo) {
-                float v = 0.0f;
-                if (o < nout) {
-                    const int h = o / hd, i = o % hd;
-                    v = acc[k] * S.sa[h];
-                    const float *ph = S.sp + h * ATT_TILE;
-                    static_assert(tpo == 1, "one thread per output: positions in order");
-                    int t = 0;
-                    /* the weights four at a time (broadcast float4 reads) */
+        /* outputs: a thread per (head, dimension), positions in order */
+        for (int o = tid; o < nout; o += NCT) {
+            const int h = o / hd, i = o % hd;
+            float v = S.acc[o] * S.sa[h];
+            const float *ph = S.sp + h * ATT_TILE;
+            int t = 0;
+            /* the weights four at a time (broadcast float4 reads) */
 #pragma unroll 4
-                    for (; t + 4 <= nt; t += 4) {
-                        float4 w4 = *(const float4 *)(ph + t);
-                        if constexpr (KV == KC_Q8_0) {
-                            const float4 d4 = *(const float4 *)(S.svd + t);
-                            w4 = make_float4(__fmul_rn(w4.x, d4.x), __fmul_rn(w4.y, d4.y), __fmul_rn(w4.z, d4.z),
-                                             __fmul_rn(w4.w, d4.w));
-                        }
-                        const float *vc = S.sv + t * hd + i;
-                        v = fmaf(w4.x, vc[0], v);
-                        v = fmaf(w4.y, vc[hd], v);
-                        v = fmaf(w4.z, vc[2 * hd], v);
-                        v = fmaf(w4.w, vc[3 * hd], v);
-                    }
-                    for (; t < nt; t++) {
-                        const float w = KV == KC_Q8_0 ? __fmul_rn(ph[t], S.svd[t]) : ph[t];
-                        v = fmaf(w, S.sv[t * hd + i], v);
-                    }
+            for (; t + 4 <= nt; t += 4) {
+                float4 w4 = *(const float4 *)(ph + t);
+                if constexpr (KV == KC_Q8_0) {
+                    const float4 d4 = *(const float4 *)(S.svd + t);
+                    w4 = make_float4(__fmul_rn(w4.x, d4.x), __fmul_rn(w4.y, d4.y), __fmul_rn(w4.z, d4.z),
+                                     __fmul_rn(w4.w, d4.w));
                 }
-                for (int sh = tpo / 2; sh > 0; sh >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sh);
-                if (o < nout && part == 0) acc[k] = v;
+                const float *vc = S.sv + t * hd + i;
+                v = fmaf(w4.x, vc[0], v);
+                v = fmaf(w4.y, vc[hd], v);
+                v = fmaf(w4.z, vc[2 * hd], v);
+                v = fmaf(w4.w, vc[3 * hd], v);
             }
+            for (; t < nt; t++) {
+                const float w = KV == KC_Q8_0 ? __fmul_rn(ph[t], S.svd[t]) : ph[t];
+                v = fmaf(w, S.sv[t * hd + i], v);
+            }
+            S.acc[o] = v;
         }
         consumer_sync();
+        /* F32: V is read; the next tile's V lands during the next scores */
+        if (KV == KC_F32 && t0 + ATT_TILE < t_end) copy_rows(t0 + ATT_TILE, vb, S.sv, hd);
         if (tid == 0) ev(0, EV_ATT_TILE);
     }
     if (active == 1) {
         /* one split: its outputs are the head's (the combine below with one
          * weight, 1 / l, gives the same bits) */
-#pragma unroll
-        for (int k = 0; k < MAXO; k++) {
-            const int o = (tid + k * NCT) / tpo;
-            if (k * NCT < nout * tpo && o < nout && tid % tpo == 0)
-                st_word(a.aow + (size_t)g * nout + o, mkword(t_ao, __fmul_rn(acc[k], __fdiv_rn(1.0f, S.sl[o / hd]))));
-        }
+        for (int o = tid; o < nout; o += NCT)
+            st_word(a.aow + (size_t)g * nout + o, mkword(t_ao, __fmul_rn(S.acc[o], __fdiv_rn(1.0f, S.sl[o / hd]))));
         if (tid == 0) ev(0, EV_ATT_DONE);
         return;
     }
     /* this split's partial as tagged words: unnormalized outputs, running max
      * and sum (no fence, no counter: the combining splits wait on the words) */
     const int stride = hd + 2;
-#pragma unroll
-    for (int k = 0; k < MAXO; k++) {
-        const int o = (tid + k * NCT) / tpo;
-        if (k * NCT < nout * tpo && o < nout && tid % tpo == 0) {
-            const int h = o / hd, i = o % hd;
-            st_word(a.partw + ((size_t)(g * group + h) * a.nsplit + y) * stride + i, mkword(t_part, acc[k]));
-        }
+    for (int o = tid; o < nout; o += NCT) {
+        const int h = o / hd, i = o % hd;
+        st_word(a.partw + ((size_t)(g * group + h) * a.nsplit + y) * stride + i, mkword(t_part, S.acc[o]));
     }
     if (tid < group) {
         word_t *ph = a.partw + ((size_t)(g * group + tid) * a.nsplit + y) * stride;
@@ -1660,76 +1671,80 @@ __device__ __noinline__ void attention_item_t(const StepArgs &a, const LayerPlan
     if (tid == 0) ev(0, EV_ATT_PARTIAL);
     const int chunk = (nout + active - 1) / active, o0 = y * chunk, o1 = min(nout, o0 + chunk);
     if (tid == 0) ev(0, EV_ATT_COMBINE);
-    /* each split combines its slice of the group's outputs: a warp per output
-     * and a lane per split, OPW outputs per warp at a time; the splits'
-     * running maxima, sums and partial outputs are requested together and
-     * waited for word by word; weight e_s / sum_s l_s e_s, e_s = exp(m_s - M),
-     * and the weighted partials summed in split order */
-    constexpr int OPW = 4;
-    for (int ob = o0 + warp; ob < o1; ob += OPW * NCW) {
-        float m[OPW], l[OPW], p[OPW];
-        word_t wm[OPW], wl[OPW], wp[OPW];
-#pragma unroll
-        for (int k = 0; k < OPW; k++) {
-            const int o = ob + k * NCW;
-            wm[k] = mkword(t_part, -INFINITY);
-            wl[k] = wp[k] = mkword(t_part, 0.0f);
-            if (o < o1 && lane < active) {
-                const int h = o / hd, i = o - h * hd;
-                const word_t *ps = a.partw + ((size_t)(g * group + h) * a.nsplit + lane) * stride;
-                wm[k] = ld_word(ps + hd);
-                wl[k] = ld_word(ps + hd + 1);
-                wp[k] = ld_word(ps + i);
-            }
+    /* each split combines its slice [o0, o1) of the group's outputs. First a
+     * warp per query head of the slice, a lane per split: the splits' running
+     * maxima and sums (tagged words), M = max m_s, e_s = exp(m_s - M), weight
+     * w_s = e_s / sum_s l_s e_s into shared memory. Then a thread per output:
+     * the splits' partials, requested together, summed in split order with
+     * those weights. */
+    const int h0 = o0 / hd, nh = o1 > o0 ? (o1 - 1) / hd - h0 + 1 : 0;
+    float *sw = S.sp;   /* [nh][MAX_NSPLIT]: the scores' space, free after the last tile */
+    if (warp < nh) {
+        const word_t *ps = a.partw + ((size_t)(g * group + h0 + warp) * a.nsplit + lane) * stride;
+        float m = -INFINITY, lsum = 0.0f;
+        if (lane < active) {
+            word_t wm = ld_word(ps + hd), wl = ld_word(ps + hd + 1);
+            m = wait_word(ps + hd, t_part, wm, a.err);
+            lsum = wait_word(ps + hd + 1, t_part, wl, a.err);
         }
+        const float M = warp_max(m);
+        const float e = lane < active ? expf(m - M) : 0.0f;
+        const float w = e / warp_sum(lsum * e);
+        sw[warp * MAX_NSPLIT + lane] = w;
+    }
+    consumer_sync();
+#pragma unroll 1
+    for (int o = o0 + tid; o < o1; o += NCT) {
+        const int h = o / hd, i = o - h * hd;
+        const word_t *ps = a.partw + (size_t)(g * group + h) * a.nsplit * stride + i;
+        const float *wh = sw + (h - h0) * MAX_NSPLIT;
+        float num = 0.0f;
+        /* the splits' words 16 at a time (one round trip for up to 16 splits),
+         * again (all 16) until every tag is this layer's; the sum in split order */
+        constexpr int CB = 16;
+#pragma unroll 1
+        for (int s0 = 0; s0 < active; s0 += CB) {
+            float pv[CB];
+            for (unsigned it = 0;; it++) {
+                bool ok = true;
 #pragma unroll
-        for (int k = 0; k < OPW; k++) {
-            const int o = ob + k * NCW;
-            m[k] = wval(wm[k]);
-            l[k] = wval(wl[k]);
-            p[k] = wval(wp[k]);
-            if (o < o1 && lane < active) {
-                const int h = o / hd, i = o - h * hd;
-                const word_t *ps = a.partw + ((size_t)(g * group + h) * a.nsplit + lane) * stride;
-                m[k] = wait_word(ps + hd, t_part, wm[k], a.err);
-                l[k] = wait_word(ps + hd + 1, t_part, wl[k], a.err);
-                p[k] = wait_word(ps + i, t_part, wp[k], a.err);
-            }
-        }
+                for (int k = 0; k < CB; k++) {
+                    pv[k] = 0.0f;
+                    if (s0 + k < active) {
+                        const word_t wv = ld_word(ps + (size_t)(s0 + k) * stride);
+                        ok = ok && wok(wv, t_part);
+                        pv[k] = wval(wv);
+                    }
+                }
+                if (ok) break;
+                if (it >= POLL_LIMIT) {
+                    atomicOr(a.err, ERR_POLL);
+                    break;
+                }
+                if ((it & 63) == 63 && *(volatile const unsigned *)a.err) break;
+                    }
 #pragma unroll
-        for (int k = 0; k < OPW; k++) {
-            const int o = ob + k * NCW;
-            if (o >= o1) break;
-            const float M = warp_max(m[k]);
-            const float e = lane < active ? expf(m[k] - M) : 0.0f;
-            const float w = e / warp_sum(l[k] * e);
-            float num = 0.0f;
-            for (int s2 = 0; s2 < active; s2++)
-                num = fmaf(__shfl_sync(0xffffffffu, p[k], s2), __shfl_sync(0xffffffffu, w, s2), num);
-            if (lane == 0) st_word(a.aow + (size_t)g * nout + o, mkword(t_ao, num));
+            for (int k = 0; k < CB; k++)
+                if (s0 + k < active) num = fmaf(pv[k], wh[s0 + k], num);
         }
+        st_word(a.aow + (size_t)g * nout + o, mkword(t_ao, num));
     }
     if (tid == 0) ev(0, EV_ATT_DONE);
 }
 
-/* UNITS: the 16-byte units of K a thread loads per tile, head_dim * bytes / 128. */
+/* The attention item in the state's KV type (one inlined copy per type). */
 __device__ __forceinline__ void attention_item(const StepArgs &a, const LayerPlan &L, int g, int y, int pos, float *fsm,
                                                unsigned t_qkv, unsigned t_part, unsigned t_ao) {
-    if (a.kv_type == KC_F16) {
-        if (a.hd <= 64) attention_item_t<KC_F16, 1>(a, L, g, y, pos, fsm, t_qkv, t_part, t_ao);
-        else attention_item_t<KC_F16, 2>(a, L, g, y, pos, fsm, t_qkv, t_part, t_ao);
-    } else if (a.kv_type == KC_Q8_0) {
-        attention_item_t<KC_Q8_0, 1>(a, L, g, y, pos, fsm, t_qkv, t_part, t_ao);
-    } else {
-        if (a.hd <= 64) attention_item_t<KC_F32, 2>(a, L, g, y, pos, fsm, t_qkv, t_part, t_ao);
-        else attention_item_t<KC_F32, 4>(a, L, g, y, pos, fsm, t_qkv, t_part, t_ao);
-    }
+    if (a.kv_type == KC_F16) attention_item_t<KC_F16>(a, L, g, y, pos, fsm, t_qkv, t_part, t_ao);
+    else if (a.kv_type == KC_Q8_0) attention_item_t<KC_Q8_0>(a, L, g, y, pos, fsm, t_qkv, t_part, t_ao);
+    else attention_item_t<KC_F32>(a, L, g, y, pos, fsm, t_qkv, t_part, t_ao);
 }
 
 /* ------------------------------------------------------------ shared layout */
 
 /* Dynamic shared memory of a streaming CTA: mbarriers [2][nstage], per-warp
- * argmax [NCW], flag, reduction scratch [32], the owned rows of x [OWN_MAX],
+ * argmax [NCW], flag, reduction scratch [32] and the per-CTA sums of squares
+ * [32 * SSP_LOADS], the owned rows of x [OWN_MAX],
  * activation (or attention scratch) of act_bytes, then the ring (128 B
  * aligned). */
 struct Smem {
@@ -1747,7 +1762,8 @@ struct Smem {
 
 /* res_bytes: a phase's row results (16-byte multiple). */
 __host__ __device__ inline int smem_fixed_bytes(int nstage, int act_bytes, int res_bytes = 0, int wbuf_bytes = 0) {
-    return 16 * nstage + 8 * NCW + 16 + 128 + 8 * OWN_MAX + res_bytes + wbuf_bytes + act_bytes + 128;
+    return 16 * nstage + 8 * NCW + 16 + 4 * (32 + 32 * SSP_LOADS) + 8 * OWN_MAX + res_bytes + wbuf_bytes + act_bytes +
+           128;
 }
 
 __device__ __forceinline__ Smem carve(unsigned char *smem, int nstage, int act_bytes, int res_bytes = 0,
@@ -1758,7 +1774,7 @@ __device__ __forceinline__ Smem carve(unsigned char *smem, int nstage, int act_b
     s.cta_best = (unsigned long long *)(s.empty + nstage);
     s.flag = (int *)(s.cta_best + NCW);
     s.red = (float *)(s.flag + 4);
-    s.own = s.red + 32;
+    s.own = s.red + 32 + 32 * SSP_LOADS;
     s.yown = s.own + OWN_MAX;
     s.res = s.yown + OWN_MAX;
     s.wbuf = (float *)((unsigned char *)s.res + res_bytes);
@@ -1820,7 +1836,6 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
     share_rows(a.dim, j, G, own0, own1);
     const int nown = own1 - own0;
     unsigned expect = 0, pidx = 0;   /* step-end barrier arrivals due so far, trace index */
-    const ActW w_dim = act_layout(sh.act, a.dim), w_q = act_layout(sh.act, a.q_dim), w_h = act_layout(sh.act, a.hidden);
     /* x words, sums of squares, post-norm block outputs: one buffer for the O
      * phase (C) and one for the down phase (E) */
     word_t *const xw_c = a.xw, *const xw_e = a.xw + a.dim;
@@ -1848,132 +1863,125 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
         consumer_sync();
         const int tk = s_ls[0], ps = s_ls[1], logit_row0 = s_ls[2];
         const float inv0 = s_inv0;
-        for (int l = 0; l < a.n_layers; l++, gl++) {
+        /* the step as one loop over its stages: per layer A (Q/K/V), B
+         * (attention), C (O + residual), D (gate/up), E (down + residual),
+         * then F (classifier). Every matrix phase runs through the same code
+         * (one copy of the prologue call, of the consumer loops and of the
+         * finish): the instructions a layer executes stay few enough to be
+         * cached instead of fetched again from L2 in every phase. */
+        const int nstages = 5 * a.n_layers + (a.run_cls ? 1 : 0);
+        for (int sg = 0; sg < nstages; sg++) {
+            const int l = sg / 5, k = sg - 5 * l;
+            const bool cls = l == a.n_layers;   /* F */
             const LayerPlan &L = s_lp[gl & 1];
-            const unsigned t_qkv = tag_of(a, step, l, TAG_QKV), t_part = tag_of(a, step, l, TAG_PART);
-            const unsigned t_ao = tag_of(a, step, l, TAG_AO), t_xc = tag_of(a, step, l, TAG_XC);
-            const unsigned t_hb = tag_of(a, step, l, TAG_HB), t_xe = tag_of(a, step, l, TAG_XE);
-            /* A: Q/K/V */
-            if (l == 0) {
-                act_embed(a.emb, a.embed_scale, tk, L.attn_norm, inv0, a.dim, w_dim);
+            if (k == 1) {
+                /* B: attention; the next layer's plan is fetched meanwhile (the
+                 * buffer's last reader, the previous layer's A prologue, is done) */
+                fetch_plan(a.layers + (l + 1 < a.n_layers ? l + 1 : 0), &s_lp[(gl + 1) & 1]);
+                trace_mark(a, pidx, 0);
+                if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
+                const unsigned t_qkv = tag_of(a, step, l, TAG_QKV);
+                for (int it = j; it < a.n_kv_heads * a.nsplit; it += G)
+                    attention_item(a, L, it / a.nsplit, it % a.nsplit, ps, (float *)sh.act, t_qkv, t_qkv + 1,
+                                   t_qkv + 2);
+                consumer_sync();   /* the attention scratch is the next activation's space */
+                phase_end(a, pidx);
+                continue;
+            }
+            /* the stage's matrix phase: its plan, input words and their tag, norm */
+            const int ph = cls ? PH_F : (k == 0 ? PH_A : (k == 2 ? PH_C : (k == 3 ? PH_D : PH_E)));
+            const int cols = ph == PH_C ? a.q_dim : (ph == PH_E ? a.hidden : a.dim);
+            const ActW w = act_layout(sh.act, cols);
+            const unsigned tg = tag_of(a, step, cls ? a.n_layers - 1 : l, 0);   /* the layer's first tag */
+            if (ph == PH_A && l == 0) {
+                act_embed(a.emb, a.embed_scale, tk, L.attn_norm, inv0, a.dim, w);
                 /* the residual stream starts as the embedding row: this CTA's rows of x */
                 for (int r = own0 + (int)threadIdx.x; r < own1; r += NCT) sh.own[r - own0] = embed1(a, tk, a.dim, r);
-            } else if (a.post_norms) {
-                act_postnorm(a, xw_e, yw_e, ss_e, tag_of(a, step, l - 1, TAG_XE), s_lp[(gl - 1) & 1].post_ffn,
-                             L.attn_norm, a.dim, w_dim, sh.red, sh.own, own0, own1);
             } else {
-                load_activation(a, xw_e, tag_of(a, step, l - 1, TAG_XE), L.attn_norm, ss_e, a.dim, w_dim, sh.red,
-                                sh.wbuf);
+                const word_t *in;
+                const word_t *ssw = nullptr, *yin = nullptr;
+                const float *nw = nullptr, *pw = nullptr;
+                unsigned tin;
+                if (ph == PH_A || ph == PH_F) {   /* x after the previous layer's down phase */
+                    tin = ph == PH_F ? tg + TAG_XE : tg - NTAG + TAG_XE;
+                    in = xw_e, ssw = ss_e, yin = yw_e;
+                    nw = ph == PH_F ? a.final_norm : L.attn_norm;
+                    pw = s_lp[(gl - 1) & 1].post_ffn;
+                } else if (ph == PH_D) {          /* x after this layer's O phase */
+                    tin = tg + TAG_XC;
+                    in = xw_c, ssw = ss_c, yin = yw_c;
+                    nw = L.ffn_norm;
+                    pw = L.post_attn;
+                } else {                          /* attention output, FFN hidden */
+                    tin = tg + (ph == PH_C ? TAG_AO : TAG_HB);
+                    in = ph == PH_C ? a.aow : a.hbw;
+                }
+                if (a.post_norms && nw)
+                    act_postnorm(a, in, yin, ssw, tin, pw, nw, a.dim, w, sh.red, sh.own, own0, own1);
+                else
+                    load_activation(a, in, tin, nw, ssw, cols, w, sh.red, nw ? sh.wbuf : nullptr);
             }
             trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
-            consume_phase(rg, s_plan[PH_A], false, act_view(w_dim), sh.res, a.err);
-            {
-                const PhasePlan &P = s_plan[PH_A];
-                finish_phase(FIN_STORE, sh.res, plan_rows(P), P.nseg ? P.seg[0].row0 : 0, nullptr, a.qkvw, t_qkv,
-                             nullptr, 0, 0.0f, sh.cta_best, col_slices(a.dim / QK, false));
-            }
-            phase_end(a, pidx);
-            /* B: attention; the next layer's plan is fetched meanwhile (the
-             * buffer's last reader, the previous layer's A prologue, is done) */
-            fetch_plan(a.layers + (l + 1 < a.n_layers ? l + 1 : 0), &s_lp[(gl + 1) & 1]);
-            trace_mark(a, pidx, 0);
-            if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
-            for (int it = j; it < a.n_kv_heads * a.nsplit; it += G)
-                attention_item(a, L, it / a.nsplit, it % a.nsplit, ps, (float *)sh.act, t_qkv, t_part, t_ao);
-            consumer_sync();   /* the attention scratch is the next activation's space */
-            phase_end(a, pidx);
-            /* C: O projection + residual */
-            load_activation(a, a.aow, t_ao, nullptr, nullptr, a.q_dim, w_q, sh.red);
-            trace_mark(a, pidx, 0);
-            if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
-            consume_phase(rg, s_plan[PH_C], false, act_view(w_q), sh.res, a.err);
-            if (a.post_norms) {
-                finish_post(sh.res, nown, own0, col_slices(a.q_dim / QK, false), xw_c, yw_c, t_xc, sh.own, sh.yown);
-                publish_ssp(ss_c, t_xc, sh.yown, nown);
-            } else {
+            const PhasePlan &P = s_plan[ph];
+            consume_phase(rg, P, ph == PH_D, act_view(w), sh.res, a.err);
+            const int ns = col_slices(cols / QK, false);
+            if (ph == PH_A) {
+                finish_phase(FIN_STORE, sh.res, plan_rows(P), P.nseg ? P.seg[0].row0 : 0, nullptr, a.qkvw,
+                             tg + TAG_QKV, nullptr, 0, 0.0f, sh.cta_best, ns);
+            } else if (ph == PH_D) {
+                finish_phase(FIN_PAIR, sh.res, P.seg[0].rows, P.seg[0].row0, nullptr, a.hbw, tg + TAG_HB, nullptr,
+                             a.act, 0.0f, sh.cta_best, 1);
+            } else if (ph == PH_F) {
+                const Seg &F = P.seg[0];
+                const unsigned long long b =
+                    finish_phase(FIN_LOGITS, sh.res, F.rows, a.cls_row0 + F.row0, a.logits + logit_row0, nullptr, 0,
+                                 nullptr, 0, a.final_softcap, sh.cta_best, ns);
+                if (threadIdx.x == 0 && b) atomicMax(&a.ls->best, b);
                 if (a.tp_world > 1) {
-                    tp_resid(a, sh.res, nown, own0, sh.own, col_slices(a.q_dim / QK, false), 0, tp_seq(a, step, l, 0));
-                    publish_rows(xw_c, t_xc, sh.own, nown, own0);
-                    publish_ssp(ss_c, t_xc, sh.own, nown);
-                } else if (nown <= 32) {
-                    finish_resid_warp(sh.res, nown, own0, xw_c, ss_c, t_xc, sh.own, col_slices(a.q_dim / QK, false));
-                } else {
-                    finish_phase(FIN_RESID, sh.res, nown, own0, nullptr, xw_c, t_xc, sh.own, 0, 0.0f, sh.cta_best,
-                                 col_slices(a.q_dim / QK, false));
-                    publish_ssp(ss_c, t_xc, sh.own, nown);
+                    /* this rank's logits rows into every other rank's ring (each thread
+                     * re-reads the rows it wrote itself) */
+                    for (int i = threadIdx.x; i < F.rows; i += NCT) {
+                        const size_t o = (size_t)logit_row0 + a.cls_row0 + F.row0 + i;
+                        const float v = a.logits[o];
+                        for (int r = 0; r < a.tp_world; r++)
+                            if (r != a.tp_rank) ((float *)(a.tp_box[r] + a.tp_off_logits))[o] = v;
+                    }
+                    __threadfence_system();
                 }
-            }
-            prefetch_norm(sh.wbuf, L.ffn_norm, a.dim);
-            phase_end(a, pidx);
-            /* D: gate/up + activation */
-            if (a.post_norms)
-                act_postnorm(a, xw_c, yw_c, ss_c, t_xc, L.post_attn, L.ffn_norm, a.dim, w_dim, sh.red, sh.own, own0,
-                             own1);
-            else
-                load_activation(a, xw_c, t_xc, L.ffn_norm, ss_c, a.dim, w_dim, sh.red, sh.wbuf);
-            trace_mark(a, pidx, 0);
-            if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
-            consume_phase(rg, s_plan[PH_D], true, act_view(w_dim), sh.res, a.err);
-            finish_phase(FIN_PAIR, sh.res, s_plan[PH_D].seg[0].rows, s_plan[PH_D].seg[0].row0, nullptr, a.hbw, t_hb,
-                         nullptr, a.act, 0.0f, sh.cta_best, 1);
-            phase_end(a, pidx);
-            /* E: down + residual */
-            load_activation(a, a.hbw, t_hb, nullptr, nullptr, a.hidden, w_h, sh.red);
-            trace_mark(a, pidx, 0);
-            if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
-            consume_phase(rg, s_plan[PH_E], false, act_view(w_h), sh.res, a.err);
-            if (a.post_norms) {
-                finish_post(sh.res, nown, own0, col_slices(a.hidden / QK, false), xw_e, yw_e, t_xe, sh.own, sh.yown);
-                publish_ssp(ss_e, t_xe, sh.yown, nown);
+                break;   /* F is the step's last stage */
             } else {
-                if (a.tp_world > 1) {
-                    tp_resid(a, sh.res, nown, own0, sh.own, col_slices(a.hidden / QK, false), 1, tp_seq(a, step, l, 1));
-                    publish_rows(xw_e, t_xe, sh.own, nown, own0);
-                    publish_ssp(ss_e, t_xe, sh.own, nown);
+                /* C and E: the residual add on the CTA's rows of x */
+                const bool c = ph == PH_C;
+                const unsigned tx = tg + (c ? TAG_XC : TAG_XE);
+                word_t *const xo = c ? xw_c : xw_e, *const so = c ? ss_c : ss_e;
+                if (a.post_norms) {
+                    finish_post(sh.res, nown, own0, ns, xo, c ? yw_c : yw_e, tx, sh.own, sh.yown);
+                    publish_ssp(so, tx, sh.yown, nown);
+                } else if (a.tp_world > 1) {
+                    tp_resid(a, sh.res, nown, own0, sh.own, ns, c ? 0 : 1, tp_seq(a, step, l, c ? 0 : 1));
+                    publish_rows(xo, tx, sh.own, nown, own0);
+                    publish_ssp(so, tx, sh.own, nown);
                 } else if (nown <= 32) {
-                    finish_resid_warp(sh.res, nown, own0, xw_e, ss_e, t_xe, sh.own, col_slices(a.hidden / QK, false));
+                    finish_resid_warp(sh.res, nown, own0, xo, so, tx, sh.own, ns);
                 } else {
-                    finish_phase(FIN_RESID, sh.res, nown, own0, nullptr, xw_e, t_xe, sh.own, 0, 0.0f, sh.cta_best,
-                                 col_slices(a.hidden / QK, false));
-                    publish_ssp(ss_e, t_xe, sh.own, nown);
+                    finish_phase(FIN_RESID, sh.res, nown, own0, nullptr, xo, tx, sh.own, 0, 0.0f, sh.cta_best, ns);
+                    publish_ssp(so, tx, sh.own, nown);
+                }
+                if (c) {
+                    prefetch_norm(sh.wbuf, L.ffn_norm, a.dim);
+                } else {
+                    /* the next layer's plan (landed long ago) to every thread, then its
+                     * norm weights on their way while the next prologue waits */
+                    if (threadIdx.x < LP_UNITS) cp_async_wait_all();
+                    consumer_sync();
+                    prefetch_norm(sh.wbuf,
+                                  l + 1 < a.n_layers ? s_lp[(gl + 1) & 1].attn_norm : (a.run_cls ? a.final_norm : nullptr),
+                                  a.dim);
+                    gl++;
                 }
             }
-            /* the next layer's plan (landed long ago) to every thread, then its
-             * norm weights on their way while the next prologue waits */
-            if (threadIdx.x < LP_UNITS) cp_async_wait_all();
-            consumer_sync();
-            prefetch_norm(sh.wbuf, l + 1 < a.n_layers ? s_lp[(gl + 1) & 1].attn_norm : (a.run_cls ? a.final_norm : nullptr),
-                          a.dim);
             phase_end(a, pidx);
-        }
-        /* F: classifier + argmax */
-        if (a.run_cls) {
-            const unsigned t_last = tag_of(a, step, a.n_layers - 1, TAG_XE);
-            if (a.post_norms)
-                act_postnorm(a, xw_e, yw_e, ss_e, t_last, s_lp[(gl - 1) & 1].post_ffn, a.final_norm, a.dim, w_dim,
-                             sh.red, sh.own, own0, own1);
-            else
-                load_activation(a, xw_e, t_last, a.final_norm, ss_e, a.dim, w_dim, sh.red, sh.wbuf);
-            trace_mark(a, pidx, 0);
-            if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
-            consume_phase(rg, s_plan[PH_F], false, act_view(w_dim), sh.res, a.err);
-            const Seg &F = s_plan[PH_F].seg[0];
-            const unsigned long long b =
-                finish_phase(FIN_LOGITS, sh.res, F.rows, a.cls_row0 + F.row0, a.logits + logit_row0, nullptr, 0,
-                             nullptr, 0, a.final_softcap, sh.cta_best, col_slices(a.dim / QK, false));
-            if (threadIdx.x == 0 && b) atomicMax(&a.ls->best, b);
-            if (a.tp_world > 1) {
-                /* this rank's logits rows into every other rank's ring (each thread
-                 * re-reads the rows it wrote itself) */
-                for (int i = threadIdx.x; i < F.rows; i += NCT) {
-                    const size_t o = (size_t)logit_row0 + a.cls_row0 + F.row0 + i;
-                    const float v = a.logits[o];
-                    for (int r = 0; r < a.tp_world; r++)
-                        if (r != a.tp_rank) ((float *)(a.tp_box[r] + a.tp_off_logits))[o] = v;
-                }
-                __threadfence_system();
-            }
         }
         /* every CTA arrives; the last one advances the loop state, then
          * releases the others with one more arrival (the one grid barrier of a
