@@ -170,7 +170,8 @@ void kc_sampler_free(kc_sampler *p);
 
 /* Debug view of the state after the last step: copies a device buffer to the
  * host (which: 0 x [dim], 1 q|k|v before RoPE [q_dim + 2 kv_dim], 2 attention
- * output [q_dim], 3 FFN hidden [hidden_dim], 4 / 5 the K / V cache
+ * output [q_dim], 3 FFN hidden [hidden_dim] (2 and 3 as the quantized
+ * activation of the next matrix, dequantized: q * d), 4 / 5 the K / V cache
  * [n_layers][max_seq][kv_dim]). KC_E_SHAPE when bytes is too small. */
 int kc_debug_copy(kc_state *s, int which, void *dst, size_t bytes);
 /* A sharded state's exchange buffer handle (CUDA IPC, KC_TP_HANDLE_BYTES

@@ -389,6 +389,11 @@ static int upload_jobs(const std::vector<UploadJob> &jobs, size_t slot) {
     return status;
 }
 
+/* CTAs of the step kernel on a device of `sms` SMs: one per SM, at most one
+ * per row of x (every CTA owns rows of x, so that each one's reads of a
+ * phase's words lie, in the data flow, before the next write of those words). */
+static int step_grid(const kc_config &c, int sms) { return std::min(sms, c.dim); }
+
 /* The weight stream for a device of G SMs: every CTA's rows of every matrix,
  * contiguous in the order the step kernel consumes them (one upload job per
  * CTA and layer, and one for its classifier rows: gathered from the mapped
@@ -490,7 +495,7 @@ extern "C" int kc_model_upload(kc_model *m) {
     int dev = 0, sms = 0;
     CK(cudaGetDevice(&dev));
     CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    st = upload_stream(m, sms);
+    st = upload_stream(m, step_grid(m->cfg, sms));
     if (st != KC_OK) return st;
     m->dev_bytes = total + m->stream_bytes;
     m->uploaded = 1;
@@ -596,7 +601,9 @@ static int set_smem_attributes() {
     const int rc = current_device(dev);
     if (rc != KC_OK) return rc;
     if (done[dev]) return KC_OK;
-    const void *fns[] = { (const void *)step_kernel, (const void *)matvec_kernel, (const void *)activation_kernel };
+    const void *fns[] = { (const void *)step_kernel<KC_F32>, (const void *)step_kernel<KC_F16>,
+                          (const void *)step_kernel<KC_Q8_0>, (const void *)matvec_kernel,
+                          (const void *)activation_kernel };
     for (const void *f : fns) {
         cudaFuncAttributes fa;
         CK(cudaFuncGetAttributes(&fa, f));
@@ -701,6 +708,12 @@ static void embed_inv_table(const kc_model *m, std::vector<float> &out) {
 
 static PMat pmat(const DevMat &m) { return PMat{ m.q, m.d, m.rows, m.type, m.d16 }; }
 
+/* The step kernel's instance for a KV cache type. */
+typedef void (*StepFn)(StepArgs);
+static StepFn step_fn(int kv_type) {
+    return kv_type == KC_F16 ? step_kernel<KC_F16> : (kv_type == KC_Q8_0 ? step_kernel<KC_Q8_0> : step_kernel<KC_F32>);
+}
+
 /* The persistent step kernel's plan: per-layer pointers in device memory, the
  * ring geometry from the shared-memory budget, the attention split. */
 static int setup_step_kernel(kc_state *s) {
@@ -758,7 +771,7 @@ static int setup_step_kernel(kc_state *s) {
         return KC_E_SHAPE;
     }
     cudaFuncAttributes fa;
-    CK(cudaFuncGetAttributes(&fa, step_kernel));
+    CK(cudaFuncGetAttributes(&fa, (const void *)step_fn(s->kv_type)));
     const int wbuf = 4 * c.dim;
     const int nst = ring_stages(slot, act, (int)fa.sharedSizeBytes, res, wbuf);
     if (nst < 2) {
@@ -767,7 +780,7 @@ static int setup_step_kernel(kc_state *s) {
     }
     s->step_smem = smem_fixed_bytes(nst, act, res, wbuf) + nst * slot;
     int per_sm = 0;
-    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, step_kernel, STEP_THREADS, s->step_smem));
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, step_fn(s->kv_type), STEP_THREADS, s->step_smem));
     if (per_sm < 1) {
         set_error("the step kernel does not fit on an SM");
         return KC_E_SHAPE;
@@ -829,7 +842,7 @@ static int launch_steps(kc_state *s, int nsteps, int logits, bool timeline = fal
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    CK(cudaLaunchKernelEx(&cfg, step_kernel, a));
+    CK(cudaLaunchKernelEx(&cfg, step_fn(s->kv_type), a));
     return KC_OK;
 }
 
@@ -905,6 +918,7 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
     int dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&s->num_sms, cudaDevAttrMultiProcessorCount, dev);
+    s->num_sms = step_grid(c, s->num_sms);
     auto fail = [&](int code) { kc_state_free(s); return code; };
     cudaError_t e = cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking);
     if (e != cudaSuccess) return fail(cuda_status(e, "stream"));
@@ -917,8 +931,9 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
         { (void **)&s->yw, sizeof(unsigned long long) * 2 * c.dim },
         { (void **)&s->sspw, sizeof(unsigned long long) * 2 * (size_t)s->num_sms },
         { (void **)&s->qkvw, sizeof(unsigned long long) * (size_t)(c.q_dim + 2 * c.kv_dim) },
-        { (void **)&s->aow, sizeof(unsigned long long) * c.q_dim },
-        { (void **)&s->hbw, sizeof(unsigned long long) * c.hidden_dim },
+        /* quantized vectors: n / 4 quant words, then n / 32 scale words */
+        { (void **)&s->aow, sizeof(unsigned long long) * (size_t)(c.q_dim / 4 + c.q_dim / QK) },
+        { (void **)&s->hbw, sizeof(unsigned long long) * (size_t)(c.hidden_dim / 4 + c.hidden_dim / QK) },
         { (void **)&s->partw, sizeof(unsigned long long) * (size_t)c.n_heads * MAX_NSPLIT * (c.head_dim + 2) },
         { (void **)&s->logits, sizeof(float) * (size_t)LOGITS_RING * c.vocab },
         { (void **)&s->err, sizeof(unsigned) * 4 },
@@ -1211,8 +1226,23 @@ extern "C" int kc_debug_copy(kc_state *s, int which, void *dst, size_t bytes) {
     switch (which) {
     case 0: words = s->xw + c.dim; n = (size_t)c.dim; break;
     case 1: words = s->qkvw; n = (size_t)(c.q_dim + 2 * c.kv_dim); break;
-    case 2: words = s->aow; n = (size_t)c.q_dim; break;
-    case 3: words = s->hbw; n = (size_t)c.hidden_dim; break;
+    case 2: case 3: {
+        /* quantized words: the dequantized values q * d */
+        n = (size_t)(which == 2 ? c.q_dim : c.hidden_dim);
+        if (bytes < n * sizeof(float)) return KC_E_SHAPE;
+        CK(cudaStreamSynchronize(s->st));
+        const size_t nw = n / 4 + n / QK;
+        std::vector<unsigned long long> h(nw);
+        CK(cudaMemcpy(h.data(), which == 2 ? s->aow : s->hbw, nw * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
+        for (size_t i = 0; i < n; i++) {
+            const unsigned qw = (unsigned)h[i / 4], dw = (unsigned)h[n / 4 + i / QK];
+            float d;
+            std::memcpy(&d, &dw, sizeof d);
+            const float v = (float)(int8_t)(qw >> (8 * (i % 4))) * d;
+            std::memcpy((char *)dst + i * sizeof(float), &v, sizeof(float));
+        }
+        return KC_OK;
+    }
     case 4: src = s->kc; n = kv_elem_bytes(s->kv_type) * (size_t)c.n_layers * c.max_seq * c.kv_dim; break;
     case 5: src = s->vc; n = kv_elem_bytes(s->kv_type) * (size_t)c.n_layers * c.max_seq * c.kv_dim; break;
     case 6: src = s->kd; n = s->kd ? sizeof(float) * (size_t)c.n_layers * c.max_seq * c.n_kv_heads : 0; break;

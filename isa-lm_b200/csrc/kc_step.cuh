@@ -145,7 +145,9 @@ __host__ __device__ inline void make_plan(const StreamGeom &g, int j, int G, Pha
     P[PH_E].nseg = 1;
     P[PH_E].cols = g.hidden;
     P[PH_E].seg[0] = make_seg(r1 - r0, r0, g.t_down, g.d16_down, g.hidden, 0, 0);
-    share_rows(g.hidden, j, G, r0, r1);
+    share_rows(g.hidden / QK, j, G, r0, r1);   /* whole blocks: the finish quantizes them */
+    r0 *= QK;
+    r1 *= QK;
     P[PH_D].nseg = 1;
     P[PH_D].cols = g.dim;
     P[PH_D].seg[0] = make_seg(r1 - r0, r0, g.t_up, g.d16_up, g.dim, 0, 1);
@@ -374,6 +376,14 @@ __device__ __forceinline__ word_t ld_word(const word_t *p) {
 __device__ __forceinline__ void ld_words2(const word_t *p, word_t &a, word_t &b) {
     asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
+/* Four words in one 256-bit load (32-byte aligned): half the requests of two
+ * v2 loads at the L2 slices that every CTA polls at once. */
+__device__ __forceinline__ void ld_words4(const word_t *p, word_t &a, word_t &b, word_t &c, word_t &d) {
+    asm volatile("ld.relaxed.gpu.global.v4.u64 {%0, %1, %2, %3}, [%4];"
+                 : "=l"(a), "=l"(b), "=l"(c), "=l"(d)
+                 : "l"(p)
+                 : "memory");
+}
 /* Loads p again until the word carries tag (bounded; gives up at once when
  * another CTA has flagged the error word). */
 __device__ __forceinline__ float wait_word(const word_t *p, unsigned tag, word_t w, unsigned *err) {
@@ -400,6 +410,37 @@ __device__ __forceinline__ void wait_words2(const word_t *p, unsigned tag, word_
 /* Waits for one tagged word and returns its float (one load when it has landed). */
 __device__ __forceinline__ float get_word(const word_t *p, unsigned tag, unsigned *err) {
     return wait_word(p, tag, ld_word(p), err);
+}
+
+/* Quantized vectors between phases (the attention output, the FFN hidden):
+ * n values travel as n / 4 words of four int8 quants (elements 4k..4k+3 in
+ * word k, in the low half) and then n / 32 words of block scales, all tagged.
+ * The producer owns whole 32-value blocks and quantizes them itself, so the
+ * consumers' prologue only copies, and reads 2.25 bytes per value instead
+ * of 8. */
+
+/* One block of 32 values, one per lane, quantized by the warp with quant4's
+ * rule (the same maximum, d, 127 / amax and rounding, so the same bits as
+ * quantizing the floats in the consumer) and published as block b of aw
+ * (an n-value vector): lane 4k writes quant word k, lane 0 the scale. */
+__device__ __forceinline__ void publish_qblock(word_t *aw, int n, int b, unsigned tag, float v) {
+    const int lane = threadIdx.x & 31;
+    float amax = fabsf(v);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    unsigned q = 0;
+    float d = 0.0f;
+    if (!(amax < 1e-30f)) {
+        const float id = __fdiv_rn(127.0f, amax);
+        d = __fdiv_rn(amax, 127.0f);
+        float t = truncf(__fadd_rn(__fmul_rn(v, id), copysignf(0.5f, v)));
+        t = fminf(fmaxf(t, -127.0f), 127.0f);
+        q = ((unsigned)(int)t & 0xffu) << (8 * (lane & 3));
+    }
+    q |= __shfl_xor_sync(0xffffffffu, q, 1);
+    q |= __shfl_xor_sync(0xffffffffu, q, 2);
+    if ((lane & 3) == 0) st_word(aw + (size_t)b * 8 + (lane >> 2), mkword(tag, __uint_as_float(q)));
+    if (lane == 0) st_word(aw + n / 4 + b, mkword(tag, d));
 }
 
 /* ------------------------------------------------------------ tensor parallelism */
@@ -772,33 +813,26 @@ __device__ __forceinline__ void consume_phase(Ring &rg, const PhasePlan &P, bool
     consumer_sync();
 }
 
-enum { FIN_STORE = 0, FIN_RESID = 1, FIN_PAIR = 2, FIN_LOGITS = 3 };
+enum { FIN_STORE = 0, FIN_RESID = 1, FIN_LOGITS = 3 };
 
 /* The rows of a phase after its dot products (res, in row order from row0):
- * store, residual add (on the CTA's rows of x in `own`), act(g)*u — each
- * result as a tagged word into wout — or logits into out with the
- * first-index argmax key of the CTA's rows (returned on thread 0; 0
- * otherwise). */
+ * store or residual add (on the CTA's rows of x in `own`), each result as a
+ * tagged word into wout, or logits into out with the first-index argmax key
+ * of the CTA's rows (returned on thread 0; 0 otherwise). */
 __device__ __forceinline__ unsigned long long finish_phase(int kind, const float *res, int nrows, int row0, float *out,
                                                         word_t *wout, unsigned tag, float *own, int act, float softcap,
                                                         unsigned long long *cta_best, int ns) {
     unsigned long long best = 0;
     for (int i = threadIdx.x; i < nrows; i += NCT) {
         const int row = row0 + i;
-        float sum = 0.0f;
-        if (kind != FIN_PAIR) {
-            sum = res[i * ns];
-            for (int k = 1; k < ns; k++) sum = __fadd_rn(sum, res[i * ns + k]);
-        }
+        float sum = res[i * ns];
+        for (int k = 1; k < ns; k++) sum = __fadd_rn(sum, res[i * ns + k]);
         if (kind == FIN_STORE) {
             st_word(wout + row, mkword(tag, sum));
         } else if (kind == FIN_RESID) {
             const float v = __fadd_rn(own[i], sum);
             own[i] = v;
             st_word(wout + row, mkword(tag, v));
-        } else if (kind == FIN_PAIR) {
-            const float2 gu = ((const float2 *)res)[i];
-            st_word(wout + row, mkword(tag, act_mul(act, gu.x, gu.y)));
         } else {
             float v = sum;
             if (softcap > 0.0f) v = __fmul_rn(softcap, tanhf(__fdiv_rn(v, softcap)));
@@ -819,6 +853,18 @@ __device__ __forceinline__ unsigned long long finish_phase(int kind, const float
             for (int w = 0; w < NCW; w++) best = cta_best[w] > best ? cta_best[w] : best;
     }
     return best;
+}
+
+/* The gate|up phase's finish: h = act(g) * u on the CTA's rows (whole blocks
+ * from row0), a block per warp quantized and published into hw (an n-value
+ * vector, publish_qblock). */
+__device__ __forceinline__ void finish_pair_q(const float *res, int nrows, int row0, word_t *hw, int n, unsigned tag,
+                                              int act) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int b = warp; b < nrows / QK; b += NCW) {
+        const float2 gu = ((const float2 *)res)[b * QK + lane];
+        publish_qblock(hw, n, row0 / QK + b, tag, act_mul(act, gu.x, gu.y));
+    }
 }
 
 /* This CTA's rows of x (own, from row0) as tagged words (after a residual
@@ -842,25 +888,17 @@ __device__ __forceinline__ void publish_ssp(word_t *sspw, unsigned tag, const fl
 
 /* The residual add of a phase whose CTA rows fit one warp (n <= 32): lane i
  * sums row i's column slices in order, adds it to own[i] and publishes the
- * row, and the warp publishes the rows' sum of squares in the same pass (the
- * same per-lane squares and warp tree as publish_ssp, so the same bits),
- * with no CTA barrier in between: the next RMSNorm gets x and its sum
- * together. */
-__device__ __forceinline__ void finish_resid_warp(const float *res, int n, int row0, word_t *xw, word_t *sspw,
-                                                  unsigned tag, float *own, int ns) {
-    if (threadIdx.x >= 32) return;
+ * row, with no CTA barrier in between. */
+__device__ __forceinline__ void finish_resid_warp(const float *res, int n, int row0, word_t *xw, unsigned tag,
+                                                  float *own, int ns) {
     const int i = threadIdx.x;
-    float t = 0.0f;
     if (i < n) {
         float sum = res[i * ns];
         for (int k = 1; k < ns; k++) sum = __fadd_rn(sum, res[i * ns + k]);
         const float v = __fadd_rn(own[i], sum);
         own[i] = v;
         st_word(xw + row0 + i, mkword(tag, v));
-        t = v * v;
     }
-    t = warp_sum(t);
-    if (i == 0) st_word(sspw + blockIdx.x, mkword(tag, t));
 }
 
 /* Consumer of the kernel-level matvec (rows [r0, r1) as produce_rows staged them). */
@@ -931,7 +969,7 @@ __device__ __forceinline__ float embed1(const StepArgs &a, int tok, int cols, in
  * 1/rms: inv_given when > 0, else from ss = the sum of the G per-CTA partial
  * sums ssp, else reduced here. Every thread issues all its loads before it
  * uses any, so a prologue costs one round trip to L2. */
-constexpr int ACT_PASSES = 8;   /* float4 loads a thread holds in registers: 8192 columns at most */
+constexpr int ACT_PASSES = 4;   /* float4 loads a thread holds in registers: 4096 columns at most */
 
 /* Starts copying the norm weights that this thread's act_float slots read
  * into wbuf (asynchronous, no wait): issued before a grid barrier, the copy
@@ -1002,11 +1040,12 @@ __device__ __forceinline__ void act_float(float eps, const word_t *xw, unsigned 
 #pragma unroll
         for (int p = 0; p < NP; p++)
 #pragma unroll
-            for (int h = 0; h < 4; h++) {
+            for (int h = 0; h < 2; h++) {
+                word_t *q = &v[p][4 * h];
                 if (!live[p]) {
-                    v[p][2 * h] = v[p][2 * h + 1] = mkword(tag, 0.0f);
-                } else if (it == 0 || !(wok(v[p][2 * h], tag) && wok(v[p][2 * h + 1], tag))) {
-                    ld_words2(src[p] + 2 * h, v[p][2 * h], v[p][2 * h + 1]);
+                    q[0] = q[1] = q[2] = q[3] = mkword(tag, 0.0f);
+                } else if (it == 0 || !(wok(q[0], tag) && wok(q[1], tag) && wok(q[2], tag) && wok(q[3], tag))) {
+                    ld_words4(src[p] + 4 * h, q[0], q[1], q[2], q[3]);
                 }
             }
         if (ssw && (it == 0 || !wok(part, tag))) part = ld_word(sspw + tid);
@@ -1153,8 +1192,16 @@ __device__ __forceinline__ void act_loop_w(float eps, const word_t *xw, unsigned
     const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 7) * 4;
     float inv = 1.0f;
     if (norm_w) {
+        /* the sum of squares from the G per-CTA sums, else from x itself */
         float t = 0.0f;
-        for (int g = tid; g < (int)gridDim.x; g += NCT) t += get_word(sspw + g, tag, err);
+        if (sspw) {
+            for (int g = tid; g < (int)gridDim.x; g += NCT) t += get_word(sspw + g, tag, err);
+        } else {
+            for (int i = tid; i < cols; i += NCT) {
+                const float v = get_word(xw + i, tag, err);
+                t += v * v;
+            }
+        }
         const float ss = block_sum(t, red);
         inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
     }
@@ -1235,7 +1282,7 @@ __device__ __forceinline__ void finish_post(const float *res, int nrows, int row
     }
 }
 
-/* act_float for up to 4 * 2048 columns; wider vectors pass by pass. x: the
+/* act_float for up to 2 * 2048 columns; wider vectors pass by pass. x: the
  * phase output's tagged words; wstaged: norm_w already copied into shared
  * memory by prefetch_norm. */
 __device__ __forceinline__ void load_activation(const StepArgs &a, const word_t *x, unsigned tag, const float *norm_w,
@@ -1243,6 +1290,51 @@ __device__ __forceinline__ void load_activation(const StepArgs &a, const word_t 
                                                 const float *wstaged = nullptr) {
     if (cols <= ACT_PASSES * NCT / 8 * QK) act_float(a.eps, x, tag, norm_w, ssp, cols, o, red, wstaged, a.err);
     else act_loop_w(a.eps, x, tag, norm_w, ssp, cols, o, red, a.err);
+}
+
+/* The activation of a phase whose input arrives quantized (publish_qblock
+ * words of a cols-value vector): quants and scales into the split layout and
+ * 8 * each block's quant sum (the Q4 offset term). Thread t takes blocks t,
+ * t + NCT, ...: a block's nine words are requested together, then the stale
+ * ones again until all carry the tag. */
+__device__ __forceinline__ void act_qwords(const word_t *aw, unsigned tag, int cols, const ActW &o, unsigned *err) {
+    const int nb = cols / QK, tid = threadIdx.x;
+    if (tid == 0) ev(0, EV_ACT_ENTRY);
+#pragma unroll 1
+    for (int b = tid; b < nb; b += NCT) {
+        word_t w[9];
+        const word_t *q = aw + (size_t)b * 8;
+        for (unsigned it = 0;; it++) {
+#pragma unroll
+            for (int h = 0; h < 2; h++)
+                if (it == 0 || !(wok(w[4 * h], tag) && wok(w[4 * h + 1], tag) && wok(w[4 * h + 2], tag) &&
+                                 wok(w[4 * h + 3], tag)))
+                    ld_words4(q + 4 * h, w[4 * h], w[4 * h + 1], w[4 * h + 2], w[4 * h + 3]);
+            if (it == 0 || !wok(w[8], tag)) w[8] = ld_word(aw + cols / 4 + b);
+            bool fresh = true;
+#pragma unroll
+            for (int i = 0; i < 9; i++) fresh = fresh && wok(w[i], tag);
+            if (fresh) break;
+            if (it >= POLL_LIMIT) {
+                atomicOr(err, ERR_POLL);
+                break;
+            }
+            if ((it & 63) == 63 && *(volatile const unsigned *)err) break;
+        }
+        int sum = 0;
+        unsigned u[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            u[i] = (unsigned)w[i];
+            sum = __dp4a((int)u[i], 0x01010101, sum);
+        }
+        *(uint4 *)(o.xlo + b * 16) = make_uint4(u[0], u[1], u[2], u[3]);
+        *(uint4 *)(o.xhi + b * 16) = make_uint4(u[4], u[5], u[6], u[7]);
+        o.xd[b] = wval(w[8]);
+        o.xs[b] = 8 * sum;
+    }
+    if (tid == 0) ev(0, EV_ACT_QUANT);
+    consumer_sync();
 }
 
 /* An already quantized activation (kernel-level matvec) into the same layout. */
@@ -1329,9 +1421,9 @@ __device__ __forceinline__ int att_splits(const StepArgs &a, const LayerPlan &L,
  * scores q.k * scale (Q8: the query quantized per head, int32 dot,
  * (float)s * (qd * scale) * kd), soft-capped when set; online softmax over
  * 64-position tiles loaded one tile ahead; the weighted V sum (Q8: (p * vd)
- * * v). The splits of a KV head then publish their partials as tagged words
- * (t_part) and each combines its slice of the head group's outputs into the
- * attention output words (t_ao); q, k and v arrive as tagged words (t_qkv). */
+ * * v). With one split the item publishes the head group's outputs,
+ * quantized (t_ao); else the splits publish their partials as tagged words
+ * (t_part) for attention_combine. q, k and v arrive as tagged words (t_qkv). */
 template <int KV>
 __device__ __forceinline__ void attention_item_t(const StepArgs &a, const LayerPlan &L, int g, int y, int pos, float *fsm,
                                                  unsigned t_qkv, unsigned t_part, unsigned t_ao) {
@@ -1648,16 +1740,19 @@ __device__ __forceinline__ void attention_item_t(const StepArgs &a, const LayerP
         if (KV == KC_F32 && t0 + ATT_TILE < t_end) copy_rows(t0 + ATT_TILE, vb, S.sv, hd);
         if (tid == 0) ev(0, EV_ATT_TILE);
     }
-    if (active == 1) {
-        /* one split: its outputs are the head's (the combine below with one
-         * weight, 1 / l, gives the same bits) */
-        for (int o = tid; o < nout; o += NCT)
-            st_word(a.aow + (size_t)g * nout + o, mkword(t_ao, __fmul_rn(S.acc[o], __fdiv_rn(1.0f, S.sl[o / hd]))));
+    if (active == 1 && nout % QK == 0) {
+        /* one split: its outputs are the head group's (the combine with one
+         * weight, 1 / l, gives the same bits), quantized a block per warp */
+        for (int b = warp; b < nout / QK; b += NCW) {
+            const int o = b * QK + lane;
+            publish_qblock(a.aow, a.q_dim, g * (nout / QK) + b, t_ao,
+                           __fmul_rn(S.acc[o], __fdiv_rn(1.0f, S.sl[o / hd])));
+        }
         if (tid == 0) ev(0, EV_ATT_DONE);
         return;
     }
     /* this split's partial as tagged words: unnormalized outputs, running max
-     * and sum (no fence, no counter: the combining splits wait on the words) */
+     * and sum (no fence, no counter: the combine waits on the words) */
     const int stride = hd + 2;
     for (int o = tid; o < nout; o += NCT) {
         const int h = o / hd, i = o % hd;
@@ -1669,39 +1764,43 @@ __device__ __forceinline__ void attention_item_t(const StepArgs &a, const LayerP
         st_word(ph + hd + 1, mkword(t_part, S.sl[tid]));
     }
     if (tid == 0) ev(0, EV_ATT_PARTIAL);
-    const int chunk = (nout + active - 1) / active, o0 = y * chunk, o1 = min(nout, o0 + chunk);
+}
+
+/* Block B (attention output values 32B .. 32B + 31, of one or a few query
+ * heads) from the `active` splits' partials of layer tag t_part, quantized
+ * and published (t_ao). First a warp per query head of the block, a lane per
+ * split: the splits' running maxima and sums, M = max m_s, e_s = exp(m_s - M),
+ * weight w_s = e_s / sum_s l_s e_s into shared memory (sw). Then warp 0, a
+ * lane per output: the splits' partials, requested together, summed in split
+ * order with those weights. Runs after the CTA's own attention items (a
+ * combine waits on other CTAs' items, never an item on a combine). */
+__device__ __forceinline__ void attention_combine(const StepArgs &a, int B, int active, float *sw, unsigned t_part,
+                                                  unsigned t_ao) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, hd = a.hd, stride = hd + 2;
+    const int o0 = B * QK, h0 = o0 / hd, nh = (o0 + QK - 1) / hd - h0 + 1;
     if (tid == 0) ev(0, EV_ATT_COMBINE);
-    /* each split combines its slice [o0, o1) of the group's outputs. First a
-     * warp per query head of the slice, a lane per split: the splits' running
-     * maxima and sums (tagged words), M = max m_s, e_s = exp(m_s - M), weight
-     * w_s = e_s / sum_s l_s e_s into shared memory. Then a thread per output:
-     * the splits' partials, requested together, summed in split order with
-     * those weights. */
-    const int h0 = o0 / hd, nh = o1 > o0 ? (o1 - 1) / hd - h0 + 1 : 0;
-    float *sw = S.sp;   /* [nh][MAX_NSPLIT]: the scores' space, free after the last tile */
-    if (warp < nh) {
-        const word_t *ps = a.partw + ((size_t)(g * group + h0 + warp) * a.nsplit + lane) * stride;
+    for (int w = warp; w < nh; w += NCW) {
+        const word_t *ps = a.partw + ((size_t)(h0 + w) * a.nsplit + lane) * stride;
         float m = -INFINITY, lsum = 0.0f;
         if (lane < active) {
-            word_t wm = ld_word(ps + hd), wl = ld_word(ps + hd + 1);
-            m = wait_word(ps + hd, t_part, wm, a.err);
-            lsum = wait_word(ps + hd + 1, t_part, wl, a.err);
+            word_t wm, wl;
+            ld_words2(ps + hd, wm, wl);
+            wait_words2(ps + hd, t_part, wm, wl, a.err);
+            m = wval(wm);
+            lsum = wval(wl);
         }
         const float M = warp_max(m);
         const float e = lane < active ? expf(m - M) : 0.0f;
-        const float w = e / warp_sum(lsum * e);
-        sw[warp * MAX_NSPLIT + lane] = w;
+        const float wt = e / warp_sum(lsum * e);
+        sw[w * MAX_NSPLIT + lane] = wt;
     }
     consumer_sync();
-#pragma unroll 1
-    for (int o = o0 + tid; o < o1; o += NCT) {
-        const int h = o / hd, i = o - h * hd;
-        const word_t *ps = a.partw + (size_t)(g * group + h) * a.nsplit * stride + i;
+    if (warp == 0) {
+        const int o = o0 + lane, h = o / hd, i = o - h * hd;
+        const word_t *ps = a.partw + (size_t)h * a.nsplit * stride + i;
         const float *wh = sw + (h - h0) * MAX_NSPLIT;
+        constexpr int CB = 16;   /* splits requested together */
         float num = 0.0f;
-        /* the splits' words 16 at a time (one round trip for up to 16 splits),
-         * again (all 16) until every tag is this layer's; the sum in split order */
-        constexpr int CB = 16;
 #pragma unroll 1
         for (int s0 = 0; s0 < active; s0 += CB) {
             float pv[CB];
@@ -1722,22 +1821,15 @@ __device__ __forceinline__ void attention_item_t(const StepArgs &a, const LayerP
                     break;
                 }
                 if ((it & 63) == 63 && *(volatile const unsigned *)a.err) break;
-                    }
+            }
 #pragma unroll
             for (int k = 0; k < CB; k++)
                 if (s0 + k < active) num = fmaf(pv[k], wh[s0 + k], num);
         }
-        st_word(a.aow + (size_t)g * nout + o, mkword(t_ao, num));
+        publish_qblock(a.aow, a.q_dim, B, t_ao, num);
     }
+    consumer_sync();   /* sw is the next block's (and the next activation's) space */
     if (tid == 0) ev(0, EV_ATT_DONE);
-}
-
-/* The attention item in the state's KV type (one inlined copy per type). */
-__device__ __forceinline__ void attention_item(const StepArgs &a, const LayerPlan &L, int g, int y, int pos, float *fsm,
-                                               unsigned t_qkv, unsigned t_part, unsigned t_ao) {
-    if (a.kv_type == KC_F16) attention_item_t<KC_F16>(a, L, g, y, pos, fsm, t_qkv, t_part, t_ao);
-    else if (a.kv_type == KC_Q8_0) attention_item_t<KC_Q8_0>(a, L, g, y, pos, fsm, t_qkv, t_part, t_ao);
-    else attention_item_t<KC_F32>(a, L, g, y, pos, fsm, t_qkv, t_part, t_ao);
 }
 
 /* ------------------------------------------------------------ shared layout */
@@ -1820,6 +1912,10 @@ __device__ __forceinline__ void producer(const StepArgs &a, Ring rg) {
     }
 }
 
+/* One instance per KV cache type (KV: KC_F32, KC_F16, KC_Q8_0; the host
+ * launches the state's): each carries only its own attention code, so the
+ * instructions a layer runs through stay fewer and closer together. */
+template <int KV>
 __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_constant__ StepArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     const Smem sh = carve(smem, a.nstage, a.act_bytes, a.res_bytes, a.wbuf_bytes);
@@ -1882,9 +1978,14 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
                 if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
                 const unsigned t_qkv = tag_of(a, step, l, TAG_QKV);
                 for (int it = j; it < a.n_kv_heads * a.nsplit; it += G)
-                    attention_item(a, L, it / a.nsplit, it % a.nsplit, ps, (float *)sh.act, t_qkv, t_qkv + 1,
-                                   t_qkv + 2);
-                consumer_sync();   /* the attention scratch is the next activation's space */
+                    attention_item_t<KV>(a, L, it / a.nsplit, it % a.nsplit, ps, (float *)sh.act, t_qkv, t_qkv + 1,
+                                         t_qkv + 2);
+                consumer_sync();   /* the attention scratch is the combine's (and the next activation's) space */
+                int first, span;
+                const int active = att_splits(a, L, ps, first, span);
+                if (active > 1 || (a.n_heads / a.n_kv_heads * a.hd) % QK != 0)
+                    for (int B = j; B < a.q_dim / QK; B += G)
+                        attention_combine(a, B, active, (float *)sh.act, t_qkv + 1, t_qkv + 2);
                 phase_end(a, pidx);
                 continue;
             }
@@ -1898,28 +1999,20 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
                 /* the residual stream starts as the embedding row: this CTA's rows of x */
                 for (int r = own0 + (int)threadIdx.x; r < own1; r += NCT) sh.own[r - own0] = embed1(a, tk, a.dim, r);
             } else {
-                const word_t *in;
-                const word_t *ssw = nullptr, *yin = nullptr;
-                const float *nw = nullptr, *pw = nullptr;
-                unsigned tin;
-                if (ph == PH_A || ph == PH_F) {   /* x after the previous layer's down phase */
-                    tin = ph == PH_F ? tg + TAG_XE : tg - NTAG + TAG_XE;
-                    in = xw_e, ssw = ss_e, yin = yw_e;
-                    nw = ph == PH_F ? a.final_norm : L.attn_norm;
-                    pw = s_lp[(gl - 1) & 1].post_ffn;
-                } else if (ph == PH_D) {          /* x after this layer's O phase */
-                    tin = tg + TAG_XC;
-                    in = xw_c, ssw = ss_c, yin = yw_c;
-                    nw = L.ffn_norm;
-                    pw = L.post_attn;
-                } else {                          /* attention output, FFN hidden */
-                    tin = tg + (ph == PH_C ? TAG_AO : TAG_HB);
-                    in = ph == PH_C ? a.aow : a.hbw;
+                if (ph == PH_C || ph == PH_E) {   /* attention output, FFN hidden: quantized words */
+                    act_qwords(ph == PH_C ? a.aow : a.hbw, tg + (ph == PH_C ? TAG_AO : TAG_HB), cols, w, a.err);
+                } else {
+                    /* x after the previous layer's down phase (A, F) or this layer's O phase (D) */
+                    const bool e = ph != PH_D;
+                    const unsigned tin = ph == PH_D ? tg + TAG_XC : (ph == PH_F ? tg + TAG_XE : tg - NTAG + TAG_XE);
+                    const float *nw = ph == PH_D ? L.ffn_norm : (ph == PH_F ? a.final_norm : L.attn_norm);
+                    if (a.post_norms)
+                        act_postnorm(a, e ? xw_e : xw_c, e ? yw_e : yw_c, e ? ss_e : ss_c, tin,
+                                     e ? s_lp[(gl - 1) & 1].post_ffn : L.post_attn, nw, a.dim, w, sh.red, sh.own, own0,
+                                     own1);
+                    else
+                        load_activation(a, e ? xw_e : xw_c, tin, nw, nullptr, cols, w, sh.red, nw ? sh.wbuf : nullptr);
                 }
-                if (a.post_norms && nw)
-                    act_postnorm(a, in, yin, ssw, tin, pw, nw, a.dim, w, sh.red, sh.own, own0, own1);
-                else
-                    load_activation(a, in, tin, nw, ssw, cols, w, sh.red, nw ? sh.wbuf : nullptr);
             }
             trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
@@ -1930,8 +2023,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
                 finish_phase(FIN_STORE, sh.res, plan_rows(P), P.nseg ? P.seg[0].row0 : 0, nullptr, a.qkvw,
                              tg + TAG_QKV, nullptr, 0, 0.0f, sh.cta_best, ns);
             } else if (ph == PH_D) {
-                finish_phase(FIN_PAIR, sh.res, P.seg[0].rows, P.seg[0].row0, nullptr, a.hbw, tg + TAG_HB, nullptr,
-                             a.act, 0.0f, sh.cta_best, 1);
+                finish_pair_q(sh.res, P.seg[0].rows, P.seg[0].row0, a.hbw, a.hidden, tg + TAG_HB, a.act);
             } else if (ph == PH_F) {
                 const Seg &F = P.seg[0];
                 const unsigned long long b =
@@ -1961,12 +2053,10 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
                 } else if (a.tp_world > 1) {
                     tp_resid(a, sh.res, nown, own0, sh.own, ns, c ? 0 : 1, tp_seq(a, step, l, c ? 0 : 1));
                     publish_rows(xo, tx, sh.own, nown, own0);
-                    publish_ssp(so, tx, sh.own, nown);
                 } else if (nown <= 32) {
-                    finish_resid_warp(sh.res, nown, own0, xo, so, tx, sh.own, ns);
+                    finish_resid_warp(sh.res, nown, own0, xo, tx, sh.own, ns);
                 } else {
                     finish_phase(FIN_RESID, sh.res, nown, own0, nullptr, xo, tx, sh.own, 0, 0.0f, sh.cta_best, ns);
-                    publish_ssp(so, tx, sh.own, nown);
                 }
                 if (c) {
                     prefetch_norm(sh.wbuf, L.ffn_norm, a.dim);
