@@ -13,6 +13,7 @@
 #include <mutex>
 #include <thread>
 #include <string>
+#include <numeric>
 #include <vector>
 #include <sys/mman.h>
 
@@ -633,7 +634,8 @@ static int kl_err_word(int dev, unsigned *&w) {
 
 /* Ring depth that fits beside the fixed part of a streaming CTA's shared memory. */
 /* Words of the grid barrier's arrival counter line; the attention counters follow. */
-constexpr size_t BAR_WORDS = 32;
+constexpr int ATT_UNITS_MAX = 64;   /* attention unit counters after the step-end barrier's words */
+constexpr size_t BAR_WORDS = 32 + (size_t)ATT_CNT_STRIDE * ATT_UNITS_MAX;
 
 static int ring_stages(int slot, int act_bytes, int static_bytes, int res_bytes = 0, int wbuf_bytes = 0) {
     int nst = 16;
@@ -763,6 +765,13 @@ static int setup_step_kernel(kc_state *s) {
     CK(cudaMemcpy(s->d_plan, plan.data(), sizeof(LayerPlan) * plan.size(), cudaMemcpyHostToDevice));
     const int group = c.n_heads / c.n_kv_heads;
     const int att_bytes = (int)sizeof(float) * attention_scratch_floats(group, c.head_dim);
+    /* attention units: the fewest KV heads whose outputs fill whole 32-value blocks */
+    const int att_unit = QK / std::gcd(group * c.head_dim, QK);
+    if (c.n_kv_heads % att_unit || c.n_kv_heads / att_unit > ATT_UNITS_MAX ||
+        att_unit * group * (MAX_NSPLIT + c.head_dim) > attention_scratch_floats(group, c.head_dim)) {
+        set_error("attention head layout outside the step kernel's combine limits");
+        return KC_E_SHAPE;
+    }
     int act = 0;
     for (int cols : { c.dim, c.q_dim, c.hidden_dim }) act = std::max(act, cols + 8 * (cols / QK));
     act = (std::max(act, att_bytes) + 15) & ~15;
@@ -796,6 +805,8 @@ static int setup_step_kernel(kc_state *s) {
     a.xw = s->xw; a.sspw = s->sspw; a.yw = s->yw; a.qkvw = s->qkvw; a.partw = s->partw; a.aow = s->aow;
     a.hbw = s->hbw; a.logits = s->logits;
     a.bar = s->bar; a.err = s->err; a.ls = s->ls; a.feed = s->feed;
+    a.attc = s->bar + 32;
+    a.att_unit = att_unit;
     a.out_tokens = s->out_tokens;
     a.kv_type = s->kv_type;
     a.n_layers = c.n_layers; a.dim = c.dim; a.q_dim = c.q_dim; a.kv_dim = c.kv_dim; a.hidden = c.hidden_dim;

@@ -89,6 +89,7 @@ constexpr int CHUNK_BYTES = 48 * 1024;   /* bytes per bulk copy (at least one re
 constexpr int GROUP_ROWS = 4;            /* rows per warp task (two gate|up pairs) */
 constexpr int OWN_MAX = 128;             /* rows of x a CTA may own */
 static_assert((NCW & (NCW - 1)) == 0, "warp round-robin uses a mask");
+constexpr int ATT_CNT_STRIDE = 32;       /* words between attention unit counters (one 128-byte line each) */
 constexpr int SSP_LOADS = 8;             /* per-lane loads of per-CTA values (sums, flags): grids of up to 256 CTAs */
 
 /* Record bytes: quants, scales, the bias when present, padded to 16. */
@@ -195,6 +196,11 @@ struct StepArgs {
      * [n_heads][nsplit][hd + 2], attention output [q_dim], FFN hidden [hidden] */
     unsigned long long *xw, *sspw, *yw, *qkvw, *partw, *aow, *hbw;
     unsigned tag0;                  /* tag of the launch's first output (tag_of) */
+    /* attention split arrivals: a counter per unit of att_unit KV heads (the
+     * fewest whose outputs fill whole 32-value blocks), ATT_CNT_STRIDE words
+     * apart, zeroed before each launch */
+    unsigned *attc;
+    int att_unit;
     float *logits;
     unsigned *bar, *err;
     LoopState *ls;
@@ -1412,6 +1418,9 @@ __device__ __forceinline__ int att_splits(const StepArgs &a, const LayerPlan &L,
     return (n + C - 1) / C;
 }
 
+__device__ __forceinline__ void attention_combine(const StepArgs &a, int U, int active, float *fsm, unsigned t_part,
+                                                  unsigned t_ao);
+
 /* Attention work item (KV head g, split y) of layer L at position pos, on the
  * consumer threads; fsm: shared scratch. ops/ops.c:124-180 with the cache
  * types of model/transformer.c:188-205 (KV: KC_F32, KC_F16 or KC_Q8_0):
@@ -1421,12 +1430,14 @@ __device__ __forceinline__ int att_splits(const StepArgs &a, const LayerPlan &L,
  * scores q.k * scale (Q8: the query quantized per head, int32 dot,
  * (float)s * (qd * scale) * kd), soft-capped when set; online softmax over
  * 64-position tiles loaded one tile ahead; the weighted V sum (Q8: (p * vd)
- * * v). With one split the item publishes the head group's outputs,
- * quantized (t_ao); else the splits publish their partials as tagged words
- * (t_part) for attention_combine. q, k and v arrive as tagged words (t_qkv). */
+ * * v). With one split (and a head group of whole blocks) the item
+ * publishes the group's outputs, quantized (t_ao); else the splits publish
+ * their partials as tagged words (t_part) and count themselves on their
+ * unit's counter, and the one whose arrival brings it to `last` combines the
+ * unit (attention_combine). q, k and v arrive as tagged words (t_qkv). */
 template <int KV>
 __device__ __forceinline__ void attention_item_t(const StepArgs &a, const LayerPlan &L, int g, int y, int pos, float *fsm,
-                                                 unsigned t_qkv, unsigned t_part, unsigned t_ao) {
+                                                 unsigned t_qkv, unsigned t_part, unsigned t_ao, unsigned last) {
     constexpr int ES = KV == KC_F32 ? 4 : (KV == KC_F16 ? 2 : 1);
     /* F16 and Q8 tiles pass through registers (converted on their way into
      * shared memory), up to head_dim 128; F32 tiles are copied by cp.async */
@@ -1740,7 +1751,7 @@ __device__ __forceinline__ void attention_item_t(const StepArgs &a, const LayerP
         if (KV == KC_F32 && t0 + ATT_TILE < t_end) copy_rows(t0 + ATT_TILE, vb, S.sv, hd);
         if (tid == 0) ev(0, EV_ATT_TILE);
     }
-    if (active == 1 && nout % QK == 0) {
+    if (active == 1 && a.att_unit == 1) {
         /* one split: its outputs are the head group's (the combine with one
          * weight, 1 / l, gives the same bits), quantized a block per warp */
         for (int b = warp; b < nout / QK; b += NCW) {
@@ -1764,71 +1775,79 @@ __device__ __forceinline__ void attention_item_t(const StepArgs &a, const LayerP
         st_word(ph + hd + 1, mkword(t_part, S.sl[tid]));
     }
     if (tid == 0) ev(0, EV_ATT_PARTIAL);
+    /* arrival on the unit's counter (released after every thread's partial
+     * words); the split that brings it to `last` has every partial visible
+     * (acquired) and combines the unit at once */
+    __shared__ int s_last;
+    consumer_sync();
+    if (tid == 0) {
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        const unsigned prev = atomicAdd(a.attc + (size_t)(g / a.att_unit) * ATT_CNT_STRIDE, 1u);
+        s_last = prev == last;
+        if (prev == last) asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    }
+    consumer_sync();
+    if (s_last) attention_combine(a, g / a.att_unit, active, fsm, t_part, t_ao);
 }
 
-/* Block B (attention output values 32B .. 32B + 31, of one or a few query
- * heads) from the `active` splits' partials of layer tag t_part, quantized
- * and published (t_ao). First a warp per query head of the block, a lane per
- * split: the splits' running maxima and sums, M = max m_s, e_s = exp(m_s - M),
- * weight w_s = e_s / sum_s l_s e_s into shared memory (sw). Then warp 0, a
- * lane per output: the splits' partials, requested together, summed in split
- * order with those weights. Runs after the CTA's own attention items (a
- * combine waits on other CTAs' items, never an item on a combine). */
-__device__ __forceinline__ void attention_combine(const StepArgs &a, int B, int active, float *sw, unsigned t_part,
+/* The combine of attention unit U (a.att_unit KV heads whose outputs are
+ * whole 32-value blocks: outputs [U * n, U * n + n), n = att_unit * group *
+ * hd) by the split that arrived last, once every split's partial is visible:
+ * first a warp per query head, a lane per split: the splits' running maxima
+ * and sums, M = max m_s, e_s = exp(m_s - M), weight w_s = e_s / sum_s l_s e_s
+ * into shared memory; then a thread per output sums the splits' partials in
+ * split order with those weights; then a warp per block quantizes and
+ * publishes the unit's blocks of the attention output (t_ao). */
+__device__ __forceinline__ void attention_combine(const StepArgs &a, int U, int active, float *fsm, unsigned t_part,
                                                   unsigned t_ao) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, hd = a.hd, stride = hd + 2;
-    const int o0 = B * QK, h0 = o0 / hd, nh = (o0 + QK - 1) / hd - h0 + 1;
+    const int heads = a.att_unit * (a.n_heads / a.n_kv_heads), h0 = U * heads, n = heads * hd;
+    float *sw = fsm, *out = fsm + heads * MAX_NSPLIT;   /* [heads][MAX_NSPLIT] weights, [n] outputs */
     if (tid == 0) ev(0, EV_ATT_COMBINE);
-    for (int w = warp; w < nh; w += NCW) {
+    for (int w = warp; w < heads; w += NCW) {
         const word_t *ps = a.partw + ((size_t)(h0 + w) * a.nsplit + lane) * stride;
         float m = -INFINITY, lsum = 0.0f;
         if (lane < active) {
             word_t wm, wl;
             ld_words2(ps + hd, wm, wl);
-            wait_words2(ps + hd, t_part, wm, wl, a.err);
+            if (!wok(wm, t_part) || !wok(wl, t_part)) atomicOr(a.err, ERR_POLL);
             m = wval(wm);
             lsum = wval(wl);
         }
         const float M = warp_max(m);
         const float e = lane < active ? expf(m - M) : 0.0f;
-        const float wt = e / warp_sum(lsum * e);
-        sw[w * MAX_NSPLIT + lane] = wt;
+        sw[w * MAX_NSPLIT + lane] = e / warp_sum(lsum * e);
     }
     consumer_sync();
-    if (warp == 0) {
-        const int o = o0 + lane, h = o / hd, i = o - h * hd;
-        const word_t *ps = a.partw + (size_t)h * a.nsplit * stride + i;
-        const float *wh = sw + (h - h0) * MAX_NSPLIT;
+#pragma unroll 1
+    for (int o = tid; o < n; o += NCT) {
+        const int h = o / hd, i = o - h * hd;
+        const word_t *ps = a.partw + (size_t)(h0 + h) * a.nsplit * stride + i;
+        const float *wh = sw + h * MAX_NSPLIT;
         constexpr int CB = 16;   /* splits requested together */
         float num = 0.0f;
+        bool ok = true;
 #pragma unroll 1
         for (int s0 = 0; s0 < active; s0 += CB) {
             float pv[CB];
-            for (unsigned it = 0;; it++) {
-                bool ok = true;
 #pragma unroll
-                for (int k = 0; k < CB; k++) {
-                    pv[k] = 0.0f;
-                    if (s0 + k < active) {
-                        const word_t wv = ld_word(ps + (size_t)(s0 + k) * stride);
-                        ok = ok && wok(wv, t_part);
-                        pv[k] = wval(wv);
-                    }
+            for (int k = 0; k < CB; k++) {
+                pv[k] = 0.0f;
+                if (s0 + k < active) {
+                    const word_t wv = ld_word(ps + (size_t)(s0 + k) * stride);
+                    ok = ok && wok(wv, t_part);
+                    pv[k] = wval(wv);
                 }
-                if (ok) break;
-                if (it >= POLL_LIMIT) {
-                    atomicOr(a.err, ERR_POLL);
-                    break;
-                }
-                if ((it & 63) == 63 && *(volatile const unsigned *)a.err) break;
             }
 #pragma unroll
             for (int k = 0; k < CB; k++)
                 if (s0 + k < active) num = fmaf(pv[k], wh[s0 + k], num);
         }
-        publish_qblock(a.aow, a.q_dim, B, t_ao, num);
+        if (!ok) atomicOr(a.err, ERR_POLL);
+        out[o] = num;
     }
-    consumer_sync();   /* sw is the next block's (and the next activation's) space */
+    consumer_sync();
+    for (int b = warp; b < n / QK; b += NCW) publish_qblock(a.aow, a.q_dim, U * (n / QK) + b, t_ao, out[b * QK + lane]);
     if (tid == 0) ev(0, EV_ATT_DONE);
 }
 
@@ -1932,6 +1951,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
     share_rows(a.dim, j, G, own0, own1);
     const int nown = own1 - own0;
     unsigned expect = 0, pidx = 0;   /* step-end barrier arrivals due so far, trace index */
+    unsigned att_seen = 0;           /* arrivals on each attention unit counter so far in this launch */
     /* x words, sums of squares, post-norm block outputs: one buffer for the O
      * phase (C) and one for the down phase (E) */
     word_t *const xw_c = a.xw, *const xw_e = a.xw + a.dim;
@@ -1977,15 +1997,17 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
                 trace_mark(a, pidx, 0);
                 if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
                 const unsigned t_qkv = tag_of(a, step, l, TAG_QKV);
-                for (int it = j; it < a.n_kv_heads * a.nsplit; it += G)
-                    attention_item_t<KV>(a, L, it / a.nsplit, it % a.nsplit, ps, (float *)sh.act, t_qkv, t_qkv + 1,
-                                         t_qkv + 2);
-                consumer_sync();   /* the attention scratch is the combine's (and the next activation's) space */
+                /* arrivals on each unit counter before this layer's: every CTA
+                 * keeps the count (the counters only grow within a launch) */
                 int first, span;
                 const int active = att_splits(a, L, ps, first, span);
-                if (active > 1 || (a.n_heads / a.n_kv_heads * a.hd) % QK != 0)
-                    for (int B = j; B < a.q_dim / QK; B += G)
-                        attention_combine(a, B, active, (float *)sh.act, t_qkv + 1, t_qkv + 2);
+                const bool direct = active == 1 && a.att_unit == 1;
+                const unsigned last = att_seen + (unsigned)(a.att_unit * active) - 1u;
+                for (int it = j; it < a.n_kv_heads * a.nsplit; it += G)
+                    attention_item_t<KV>(a, L, it / a.nsplit, it % a.nsplit, ps, (float *)sh.act, t_qkv, t_qkv + 1,
+                                         t_qkv + 2, last);
+                if (!direct) att_seen += (unsigned)(a.att_unit * active);
+                consumer_sync();   /* the attention scratch is the next activation's space */
                 phase_end(a, pidx);
                 continue;
             }
