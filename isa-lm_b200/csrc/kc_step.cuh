@@ -1781,8 +1781,11 @@ __device__ __forceinline__ void attention_item_t(const StepArgs &a, const LayerP
     __shared__ int s_last;
     consumer_sync();
     if (tid == 0) {
-        asm volatile("fence.acq_rel.gpu;" ::: "memory");
-        const unsigned prev = atomicAdd(a.attc + (size_t)(g / a.att_unit) * ATT_CNT_STRIDE, 1u);
+        unsigned prev;
+        asm volatile("atom.release.gpu.global.add.u32 %0, [%1], 1;"
+                     : "=r"(prev)
+                     : "l"(a.attc + (size_t)(g / a.att_unit) * ATT_CNT_STRIDE)
+                     : "memory");
         s_last = prev == last;
         if (prev == last) asm volatile("fence.acq_rel.gpu;" ::: "memory");
     }
