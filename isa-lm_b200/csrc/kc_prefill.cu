@@ -812,24 +812,29 @@ __global__ void __launch_bounds__(PA_THREADS) pf_attn_kernel(const PfAttn a) {
 
 /* ------------------------------------------------------------ weight repack */
 
-/* Row r, block b of a file matrix (Q8: int8 rows; Q4: 16 bytes per block,
- * byte j = element j low nibble and j+16 high nibble, value nibble - 8) into
- * row row0 + r of the packed matrix: int8 quants in the MMA tile layout and
- * the block scale as float. */
-__global__ void pf_pack_kernel(const uint8_t *q, const void *d, int type, int d16, int rows, int cols, int row0,
+/* Row r, block b of a matrix (Q8: int8 rows; Q4: 16 bytes per block, byte j =
+ * element j low nibble and j+16 high nibble, value nibble - 8) into row
+ * row0 + r of the packed matrix: int8 quants in the MMA tile layout and the
+ * block scale as float. Row r's quants start at q + r * qstride and its
+ * scales at d + r * dstride, or, with row_off, both at row_off[r] bytes into
+ * q and d (the weight stream's records: quants, then scales). */
+__global__ void pf_pack_kernel(const uint8_t *q, size_t qstride, const uint8_t *d, size_t dstride,
+                               const unsigned long long *row_off, int type, int d16, int rows, int cols, int row0,
                                int nbk, int8_t *wq, float *wd) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int nb = cols / QK;
     if (i >= (size_t)rows * nb) return;
     const int r = (int)(i / nb), b = (int)(i - (size_t)r * nb);
     const int R = row0 + r, m = R / PF_M, rr = R - m * PF_M;
+    const uint8_t *qr = q + (row_off ? row_off[r] : (size_t)r * qstride);
+    const uint8_t *dr = d + (row_off ? row_off[r] : (size_t)r * dstride);
     alignas(16) int8_t v[QK];
     if (type == T_Q8) {
-        const uint4 *src = (const uint4 *)(q + (size_t)r * cols + (size_t)b * QK);
+        const uint4 *src = (const uint4 *)(qr + (size_t)b * QK);
         *(uint4 *)v = src[0];
         *(uint4 *)(v + 16) = src[1];
     } else {
-        const uint8_t *src = q + ((size_t)r * nb + b) * (QK / 2);
+        const uint8_t *src = qr + (size_t)b * (QK / 2);
         for (int j = 0; j < 16; j++) {
             v[j] = (int8_t)((src[j] & 15) - 8);
             v[j + 16] = (int8_t)((src[j] >> 4) - 8);
@@ -838,8 +843,7 @@ __global__ void pf_pack_kernel(const uint8_t *q, const void *d, int type, int d1
     int8_t *dst = wq + ((size_t)m * nbk + b) * PF_A_BLK;
     *(uint4 *)(dst + tile_off(rr, 0)) = *(const uint4 *)v;
     *(uint4 *)(dst + tile_off(rr, 16)) = *(const uint4 *)(v + 16);
-    wd[((size_t)m * nbk + b) * PF_M + rr] =
-        d16 ? __half2float(((const __half *)d)[(size_t)r * nb + b]) : ((const float *)d)[(size_t)r * nb + b];
+    wd[((size_t)m * nbk + b) * PF_M + rr] = d16 ? __half2float(((const __half *)dr)[b]) : ((const float *)dr)[b];
 }
 
 /* Token t's quantized activation row (int8 [cols], scales [cols/32]) into
@@ -939,41 +943,18 @@ int alloc_mat(PfModel &P, PfMat &M, int rows, int cols, cudaStream_t st) {
     return KC_OK;
 }
 
-/* Staging buffers for one file matrix on its way to the pack kernel. */
-struct Staging {
-    uint8_t *q = nullptr;
-    void *d = nullptr;
-    size_t qcap = 0, dcap = 0;
-    ~Staging() {
-        if (q) cudaFree(q);
-        if (d) cudaFree(d);
-    }
-};
-
-int pack_part(const HostMat &H, int row0, PfMat &M, Staging &sg, cudaStream_t st) {
-    if (H.cols != M.cols || row0 + H.rows > M.rows || (H.type != KC_Q8_0 && H.type != KC_Q4_0)) {
+/* Packs rows [0, rows) of one weight-stream matrix (records at the offsets
+ * row_off, in the stream's types) into rows row0.. of M. */
+int pack_rows(const uint8_t *stream, const unsigned long long *row_off, int rows, int type, int d16, int row0, PfMat &M,
+              cudaStream_t st) {
+    if (row0 + rows > M.rows || (type != T_Q8 && type != T_Q4)) {
         set_error("prefill: a matrix does not fit its packed operand");
         return KC_E_SHAPE;
     }
-    const size_t qb = H.qbytes(), db = H.dbytes();
-    PCK(cudaStreamSynchronize(st), "staging");
-    if (qb > sg.qcap) {
-        if (sg.q) cudaFree(sg.q);
-        sg.q = nullptr;
-        PCK(cudaMalloc(&sg.q, qb), "staging");
-        sg.qcap = qb;
-    }
-    if (db > sg.dcap) {
-        if (sg.d) cudaFree(sg.d);
-        sg.d = nullptr;
-        PCK(cudaMalloc(&sg.d, db), "staging");
-        sg.dcap = db;
-    }
-    PCK(cudaMemcpyAsync(sg.q, H.q, qb, cudaMemcpyHostToDevice, st), "weights upload");
-    PCK(cudaMemcpyAsync(sg.d, H.d, db, cudaMemcpyHostToDevice, st), "scales upload");
-    const size_t items = (size_t)H.rows * (H.cols / QK);
-    pf_pack_kernel<<<(unsigned)((items + 255) / 256), 256, 0, st>>>(sg.q, sg.d, H.type == KC_Q4_0 ? T_Q4 : T_Q8,
-                                                                     H.d16, H.rows, H.cols, row0, M.nbk, M.q, M.d);
+    const int qrow = type == T_Q4 ? M.cols / 2 : M.cols;
+    const size_t items = (size_t)rows * (M.cols / QK);
+    pf_pack_kernel<<<(unsigned)((items + 255) / 256), 256, 0, st>>>(stream, 0, stream + qrow, 0, row_off, type, d16,
+                                                                     rows, M.cols, row0, M.nbk, M.q, M.d);
     PCK(cudaGetLastError(), "pack kernel");
     return KC_OK;
 }
@@ -993,38 +974,35 @@ int stack_bias(PfModel &P, PfMat &M, const std::vector<std::pair<const float *, 
     return KC_OK;
 }
 
-int build_layers(kc_model *m, PfModel &P, cudaStream_t st) {
+int pack_all(kc_model *m, const uint8_t *stream, const PfRowTable &t, PfModel &P, cudaStream_t st) {
     const kc_config &c = m->cfg;
-    Staging sg;
+    const HostLayer &H0 = m->layers[0];
+    const HostMat &cls = m->shared ? m->tok_emb : m->wcls;
+    auto ty = [](const HostMat &h) { return h.type == KC_Q4_0 ? T_Q4 : T_Q8; };
+    const size_t nq = (size_t)c.q_dim + 2 * (size_t)c.kv_dim, nd = (size_t)c.dim, nh = 2 * (size_t)c.hidden_dim;
     P.layers.resize((size_t)c.n_layers);
+    int r;
     for (int l = 0; l < c.n_layers; l++) {
         const HostLayer &H = m->layers[(size_t)l];
         PfLayerW &W = P.layers[(size_t)l];
-        int r;
-        if ((r = alloc_mat(P, W.qkv, c.q_dim + 2 * c.kv_dim, c.dim, st)) != KC_OK) return r;
-        if ((r = pack_part(H.wq, 0, W.qkv, sg, st)) != KC_OK) return r;
-        if ((r = pack_part(H.wk, c.q_dim, W.qkv, sg, st)) != KC_OK) return r;
-        if ((r = pack_part(H.wv, c.q_dim + c.kv_dim, W.qkv, sg, st)) != KC_OK) return r;
+        const unsigned long long *q = t.qkv + l * nq;
+        if ((r = alloc_mat(P, W.qkv, (int)nq, c.dim, st)) != KC_OK) return r;
+        if ((r = pack_rows(stream, q, c.q_dim, ty(H0.wq), H0.wq.d16, 0, W.qkv, st)) != KC_OK) return r;
+        if ((r = pack_rows(stream, q + c.q_dim, c.kv_dim, ty(H0.wk), H0.wk.d16, c.q_dim, W.qkv, st)) != KC_OK) return r;
+        if ((r = pack_rows(stream, q + c.q_dim + c.kv_dim, c.kv_dim, ty(H0.wv), H0.wv.d16, c.q_dim + c.kv_dim, W.qkv,
+                           st)) != KC_OK)
+            return r;
         if (H.bq && (r = stack_bias(P, W.qkv, { { H.bq, c.q_dim }, { H.bk, c.kv_dim }, { H.bv, c.kv_dim } }, st)) != KC_OK)
             return r;
         if ((r = alloc_mat(P, W.wo, c.dim, c.q_dim, st)) != KC_OK) return r;
-        if ((r = pack_part(H.wo, 0, W.wo, sg, st)) != KC_OK) return r;
-        if ((r = alloc_mat(P, W.w13, 2 * c.hidden_dim, c.dim, st)) != KC_OK) return r;
-        if ((r = pack_part(H.w1, 0, W.w13, sg, st)) != KC_OK) return r;
-        if ((r = pack_part(H.w3, c.hidden_dim, W.w13, sg, st)) != KC_OK) return r;
+        if ((r = pack_rows(stream, t.wo + l * nd, c.dim, ty(H0.wo), H0.wo.d16, 0, W.wo, st)) != KC_OK) return r;
+        if ((r = alloc_mat(P, W.w13, (int)nh, c.dim, st)) != KC_OK) return r;
+        if ((r = pack_rows(stream, t.w13 + l * nh, (int)nh, ty(H0.w1), H0.w1.d16, 0, W.w13, st)) != KC_OK) return r;
         if ((r = alloc_mat(P, W.w2, c.dim, c.hidden_dim, st)) != KC_OK) return r;
-        if ((r = pack_part(H.w2, 0, W.w2, sg, st)) != KC_OK) return r;
+        if ((r = pack_rows(stream, t.w2 + l * nd, c.dim, ty(H0.w2), H0.w2.d16, 0, W.w2, st)) != KC_OK) return r;
     }
-    PCK(cudaStreamSynchronize(st), "weight repack");
-    return KC_OK;
-}
-
-int build_cls(kc_model *m, PfModel &P, cudaStream_t st) {
-    Staging sg;
-    int r = alloc_mat(P, P.cls, m->cfg.vocab, m->cfg.dim, st);
-    if (r == KC_OK) r = pack_part(m->wcls, 0, P.cls, sg, st);
-    if (r != KC_OK) return r;
-    PCK(cudaStreamSynchronize(st), "classifier repack");
+    if ((r = alloc_mat(P, P.cls, c.vocab, c.dim, st)) != KC_OK) return r;
+    if ((r = pack_rows(stream, t.cls, c.vocab, ty(cls), cls.d16, 0, P.cls, st)) != KC_OK) return r;
     P.have_cls = true;
     return KC_OK;
 }
@@ -1122,6 +1100,23 @@ bool pf_fits(const kc_config &c, int kv_type, int last_pos) {
     return attn_smem_bytes(c, kv_type) <= PF_ATTN_SMEM_MAX;
 }
 
+int pf_pack_model(kc_model *m, const uint8_t *stream, const PfRowTable &t, cudaStream_t st) {
+    PfModel *P = new (std::nothrow) PfModel();
+    if (!P) return KC_E_NOMEM;
+    int rc = pack_all(m, stream, t, *P, st);
+    if (rc == KC_OK) {
+        const cudaError_t e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) rc = cuda_err(e, "weight repack");
+    }
+    if (rc != KC_OK) {
+        delete P;
+        return rc;
+    }
+    pf_free_model(m->pf);
+    m->pf = P;
+    return KC_OK;
+}
+
 void pf_free_model(PfModel *p) { delete p; }
 void pf_free_scratch(PfScratch *p) { delete p; }
 size_t pf_model_bytes(const PfModel *p) { return p ? p->bytes : 0; }
@@ -1129,21 +1124,11 @@ size_t pf_model_bytes(const PfModel *p) { return p ? p->bytes : 0; }
 int pf_prefill(const PfRun &r, const int *tokens, int n, int pos0, float *logits) {
     const kc_config &c = r.m->cfg;
     cudaStream_t st = r.st;
-    if (!r.m->pf) {
-        PfModel *P = new (std::nothrow) PfModel();
-        if (!P) return KC_E_NOMEM;
-        const int rc = build_layers(r.m, *P, st);
-        if (rc != KC_OK) {
-            delete P;
-            return rc;
-        }
-        r.m->pf = P;
+    if (!r.m->pf || !r.m->pf->have_cls) {
+        set_error("prefill: the model's GEMM operands were not packed at upload");
+        return KC_E_SHAPE;
     }
     PfModel &P = *r.m->pf;
-    if (logits && !P.have_cls) {
-        const int rc = build_cls(r.m, P, st);
-        if (rc != KC_OK) return rc;
-    }
     const int tc = std::max(PF_N, std::min(r.batch, n) + PF_N - 1) / PF_N * PF_N;
     const size_t npos = (size_t)pos0 + n;
     int rc = ensure_scratch(*r.scratch, c, tc, npos);
@@ -1235,8 +1220,10 @@ extern "C" int kc_matmul_dev(float *y, int type, int d_f16, const void *wq, cons
     int rc = alloc_mat(P, W, rows, cols, st);
     if (rc != KC_OK) return rc;
     const size_t items = (size_t)rows * (cols / QK);
-    pf_pack_kernel<<<(unsigned)((items + 255) / 256), 256, 0, st>>>((const uint8_t *)wq, wd, type == KC_Q4_0 ? T_Q4 : T_Q8,
-                                                                     d_f16, rows, cols, 0, W.nbk, W.q, W.d);
+    const size_t qrow = type == KC_Q4_0 ? (size_t)cols / 2 : (size_t)cols, drow = (size_t)(cols / QK) * (d_f16 ? 2 : 4);
+    pf_pack_kernel<<<(unsigned)((items + 255) / 256), 256, 0, st>>>((const uint8_t *)wq, qrow, (const uint8_t *)wd, drow,
+                                                                     nullptr, type == KC_Q4_0 ? T_Q4 : T_Q8, d_f16, rows,
+                                                                     cols, 0, W.nbk, W.q, W.d);
     const int tpad = (n + PF_N - 1) / PF_N * PF_N;
     PfScratch S;
     void *buf = nullptr;

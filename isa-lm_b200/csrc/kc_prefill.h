@@ -39,11 +39,22 @@ struct PfRun {
     int batch;                         /* tokens per chunk */
 };
 
+/* Device byte offsets, into the weight stream, of the row records the
+ * batched prefill's GEMM operands are packed from (a record: quants, then
+ * block scales): Q|K|V [n_layers][q_dim + 2 kv_dim], O [n_layers][dim], gate
+ * then up [n_layers][2 hidden], down [n_layers][dim], classifier [vocab]. */
+struct PfRowTable {
+    const unsigned long long *qkv, *wo, *w13, *w2, *cls;
+};
+/* Packs every GEMM operand of the model from its uploaded weight stream
+ * (device to device; at upload). */
+int pf_pack_model(kc_model *m, const uint8_t *stream, const PfRowTable &t, cudaStream_t st);
+
 /* True when the batched kernels take this model and a chunk reaching
  * position last_pos. */
 bool pf_fits(const kc_config &c, int kv_type, int last_pos);
-/* Runs the n tokens at pos0.. (logits: host [n][vocab] or null); builds the
- * packed weights on first use. */
+/* Runs the n tokens at pos0.. (logits: host [n][vocab] or null) through the
+ * operands pf_pack_model built. */
 int pf_prefill(const PfRun &r, const int *tokens, int n, int pos0, float *logits);
 void pf_free_model(PfModel *p);
 void pf_free_scratch(PfScratch *p);

@@ -395,6 +395,50 @@ static int upload_jobs(const std::vector<UploadJob> &jobs, size_t slot) {
  * phase's words lie, in the data flow, before the next write of those words). */
 static int step_grid(const kc_config &c, int sms) { return std::min(sms, c.dim); }
 
+/* The batched prefill's GEMM operands (unsharded models), packed on the
+ * device from the weight stream just uploaded: a table of where each matrix
+ * row's record lies in the stream (the walk of fill_stream_part), then one
+ * pack launch per matrix; no weight crosses the host link twice. */
+static int pack_prefill(kc_model *m, const StreamGeom &g, int G, const std::vector<unsigned long long> &base) {
+    const kc_config &c = m->cfg;
+    const size_t L = (size_t)c.n_layers, nq = (size_t)c.q_dim + 2 * (size_t)c.kv_dim, nd = (size_t)c.dim;
+    const size_t nh = 2 * (size_t)c.hidden_dim, hid = (size_t)c.hidden_dim;
+    const size_t oo = L * nq, o13 = oo + L * nd, o2 = o13 + L * nh, ocls = o2 + L * nd, n = ocls + (size_t)g.vocab;
+    std::vector<unsigned long long> t(n, 0);
+    for (int j = 0; j < G; j++) {
+        PhasePlan P[NPHASE];
+        make_plan(g, j, G, P);
+        const size_t lb = stream_layer_bytes(P);
+        for (size_t l = 0; l < L; l++) {
+            unsigned long long off = base[(size_t)j] + l * lb;
+            for (int k = 0; k < P[PH_A].nseg; k++) {
+                const Seg &S = P[PH_A].seg[k];
+                for (int r = 0; r < S.rows; r++, off += (unsigned)S.rec) t[l * nq + (size_t)(S.row0 + r)] = off;
+            }
+            const Seg &C = P[PH_C].seg[0], &D = P[PH_D].seg[0], &E = P[PH_E].seg[0];
+            for (int r = 0; r < C.rows; r++, off += (unsigned)C.rec) t[oo + l * nd + (size_t)(C.row0 + r)] = off;
+            for (int r = 0; r < D.rows; r++, off += (unsigned)D.rec) {
+                t[o13 + l * nh + (size_t)(D.row0 + r)] = off;                       /* gate */
+                t[o13 + l * nh + hid + (size_t)(D.row0 + r)] = off + (unsigned)(D.rec / 2);   /* up */
+            }
+            for (int r = 0; r < E.rows; r++, off += (unsigned)E.rec) t[o2 + l * nd + (size_t)(E.row0 + r)] = off;
+        }
+        unsigned long long off = base[(size_t)j] + L * lb;
+        const Seg &F = P[PH_F].seg[0];
+        for (int r = 0; r < F.rows; r++, off += (unsigned)F.rec) t[ocls + (size_t)(F.row0 + r)] = off;
+    }
+    unsigned long long *d = nullptr;
+    cudaStream_t st = nullptr;
+    CK(cudaMalloc(&d, sizeof(unsigned long long) * n));
+    cudaError_t e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d, t.data(), sizeof(unsigned long long) * n, cudaMemcpyHostToDevice, st);
+    int rc = e == cudaSuccess ? KC_OK : cuda_status(e, "prefill row table");
+    if (rc == KC_OK) rc = pf_pack_model(m, m->d_stream, PfRowTable{ d, d + oo, d + o13, d + o2, d + ocls }, st);
+    if (st) cudaStreamDestroy(st);
+    cudaFree(d);
+    return rc;
+}
+
 /* The weight stream for a device of G SMs: every CTA's rows of every matrix,
  * contiguous in the order the step kernel consumes them (one upload job per
  * CTA and layer, and one for its classifier rows: gathered from the mapped
@@ -436,6 +480,7 @@ static int upload_stream(kc_model *m, int G) {
     if (st != KC_OK) return st;
     m->stream_bytes = total;
     m->stream_G = G;
+    if (m->tp_world == 1) return pack_prefill(m, g, G, base);
     return KC_OK;
 }
 
