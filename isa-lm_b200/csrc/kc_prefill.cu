@@ -924,22 +924,34 @@ struct PfScratch {
 
 namespace {
 
-int alloc_mat(PfModel &P, PfMat &M, int rows, int cols, cudaStream_t st) {
+/* Bytes of one packed operand: quants [mt][nbk][PF_A_BLK], scales [mt][nbk][PF_M] (each 256-aligned). */
+size_t mat_bytes(int rows, int cols) {
+    const size_t mt = (size_t)(rows + PF_M - 1) / PF_M, nbk = (size_t)cols / QK;
+    return up256(mt * nbk * PF_A_BLK) + up256(mt * nbk * PF_M * sizeof(float));
+}
+
+/* A packed operand of rows x cols, carved from *arena (advanced) or, without
+ * one, in its own allocation. The padding rows of the last row tile stay
+ * unwritten: they only feed output rows the GEMM never stores. */
+int alloc_mat(PfModel &P, PfMat &M, int rows, int cols, uint8_t **arena = nullptr) {
     M.rows = rows;
     M.cols = cols;
     M.mt = (rows + PF_M - 1) / PF_M;
     M.nbk = cols / QK;
-    const size_t qb = (size_t)M.mt * M.nbk * PF_A_BLK, db = (size_t)M.mt * M.nbk * PF_M * sizeof(float);
-    void *q = nullptr, *d = nullptr;
-    PCK(cudaMalloc(&q, qb), "packed weights");
-    P.allocs.push_back(q);
-    PCK(cudaMalloc(&d, db), "packed scales");
-    P.allocs.push_back(d);
-    P.bytes += qb + db;
-    PCK(cudaMemsetAsync(q, 0, qb, st), "memset");
-    PCK(cudaMemsetAsync(d, 0, db, st), "memset");
-    M.q = (int8_t *)q;
-    M.d = (float *)d;
+    const size_t qb = up256((size_t)M.mt * M.nbk * PF_A_BLK);
+    uint8_t *base = nullptr;
+    if (arena) {
+        base = *arena;
+        *arena += mat_bytes(rows, cols);
+    } else {
+        void *b = nullptr;
+        PCK(cudaMalloc(&b, mat_bytes(rows, cols)), "packed weights");
+        P.allocs.push_back(b);
+        P.bytes += mat_bytes(rows, cols);
+        base = (uint8_t *)b;
+    }
+    M.q = (int8_t *)base;
+    M.d = (float *)(base + qb);
     return KC_OK;
 }
 
@@ -981,12 +993,21 @@ int pack_all(kc_model *m, const uint8_t *stream, const PfRowTable &t, PfModel &P
     auto ty = [](const HostMat &h) { return h.type == KC_Q4_0 ? T_Q4 : T_Q8; };
     const size_t nq = (size_t)c.q_dim + 2 * (size_t)c.kv_dim, nd = (size_t)c.dim, nh = 2 * (size_t)c.hidden_dim;
     P.layers.resize((size_t)c.n_layers);
+    /* one allocation for every operand */
+    const size_t per_layer = mat_bytes((int)nq, c.dim) + mat_bytes(c.dim, c.q_dim) + mat_bytes((int)nh, c.dim) +
+                             mat_bytes(c.dim, c.hidden_dim);
+    const size_t total = per_layer * (size_t)c.n_layers + mat_bytes(c.vocab, c.dim);
+    void *base = nullptr;
+    PCK(cudaMalloc(&base, total), "packed weights");
+    P.allocs.push_back(base);
+    P.bytes += total;
+    uint8_t *arena = (uint8_t *)base;
     int r;
     for (int l = 0; l < c.n_layers; l++) {
         const HostLayer &H = m->layers[(size_t)l];
         PfLayerW &W = P.layers[(size_t)l];
         const unsigned long long *q = t.qkv + l * nq;
-        if ((r = alloc_mat(P, W.qkv, (int)nq, c.dim, st)) != KC_OK) return r;
+        if ((r = alloc_mat(P, W.qkv, (int)nq, c.dim, &arena)) != KC_OK) return r;
         if ((r = pack_rows(stream, q, c.q_dim, ty(H0.wq), H0.wq.d16, 0, W.qkv, st)) != KC_OK) return r;
         if ((r = pack_rows(stream, q + c.q_dim, c.kv_dim, ty(H0.wk), H0.wk.d16, c.q_dim, W.qkv, st)) != KC_OK) return r;
         if ((r = pack_rows(stream, q + c.q_dim + c.kv_dim, c.kv_dim, ty(H0.wv), H0.wv.d16, c.q_dim + c.kv_dim, W.qkv,
@@ -994,14 +1015,14 @@ int pack_all(kc_model *m, const uint8_t *stream, const PfRowTable &t, PfModel &P
             return r;
         if (H.bq && (r = stack_bias(P, W.qkv, { { H.bq, c.q_dim }, { H.bk, c.kv_dim }, { H.bv, c.kv_dim } }, st)) != KC_OK)
             return r;
-        if ((r = alloc_mat(P, W.wo, c.dim, c.q_dim, st)) != KC_OK) return r;
+        if ((r = alloc_mat(P, W.wo, c.dim, c.q_dim, &arena)) != KC_OK) return r;
         if ((r = pack_rows(stream, t.wo + l * nd, c.dim, ty(H0.wo), H0.wo.d16, 0, W.wo, st)) != KC_OK) return r;
-        if ((r = alloc_mat(P, W.w13, (int)nh, c.dim, st)) != KC_OK) return r;
+        if ((r = alloc_mat(P, W.w13, (int)nh, c.dim, &arena)) != KC_OK) return r;
         if ((r = pack_rows(stream, t.w13 + l * nh, (int)nh, ty(H0.w1), H0.w1.d16, 0, W.w13, st)) != KC_OK) return r;
-        if ((r = alloc_mat(P, W.w2, c.dim, c.hidden_dim, st)) != KC_OK) return r;
+        if ((r = alloc_mat(P, W.w2, c.dim, c.hidden_dim, &arena)) != KC_OK) return r;
         if ((r = pack_rows(stream, t.w2 + l * nd, c.dim, ty(H0.w2), H0.w2.d16, 0, W.w2, st)) != KC_OK) return r;
     }
-    if ((r = alloc_mat(P, P.cls, c.vocab, c.dim, st)) != KC_OK) return r;
+    if ((r = alloc_mat(P, P.cls, c.vocab, c.dim, &arena)) != KC_OK) return r;
     if ((r = pack_rows(stream, t.cls, c.vocab, ty(cls), cls.d16, 0, P.cls, st)) != KC_OK) return r;
     P.have_cls = true;
     return KC_OK;
@@ -1217,7 +1238,7 @@ extern "C" int kc_matmul_dev(float *y, int type, int d_f16, const void *wq, cons
     cudaStream_t st = (cudaStream_t)stream;
     PfModel P;
     PfMat W;
-    int rc = alloc_mat(P, W, rows, cols, st);
+    int rc = alloc_mat(P, W, rows, cols);
     if (rc != KC_OK) return rc;
     const size_t items = (size_t)rows * (cols / QK);
     const size_t qrow = type == KC_Q4_0 ? (size_t)cols / 2 : (size_t)cols, drow = (size_t)(cols / QK) * (d_f16 ? 2 : 4);

@@ -6,30 +6,30 @@
  * Q|K|V rows, the O rows, the gate|up row pairs, the down rows; then the
  * classifier rows — each row one record: quants, block scales, bias. The
  * producer warp of a CTA streams its own byte range into a ring of
- * shared-memory slots, one bulk copy per chunk of whole rows (<= 32 KB), the
- * slots handed over with full/empty mbarriers. Copies are few and large, and
- * the ring holds the next ~190 KB of the CTA's weights across phase and layer
- * boundaries, so HBM keeps streaming while the consumers wait at barriers.
+ * shared-memory slots, one bulk copy per chunk of whole rows (<= 48 KB), the
+ * slots handed over with full/empty mbarriers, so HBM keeps streaming while
+ * the consumers wait on their inputs.
  *
- * The 16 consumer warps run the phases of a step, separated by grid barriers
- * (an arrival counter in global memory; every wait is bounded):
+ * The 8 consumer warps run the phases of a step:
  *   A  RMSNorm + quantize x (layer 0: the embedding row, its 1/rms from the
  *      host table) -> Q/K/V rows (+ biases)            model/transformer.c:270-277
  *   B  attention work items (KV head, position range): RoPE, this position's
- *      K/V row into the cache, split flash decode; the splits of a KV
- *      head combine their output slices                            transformer.c:280-283, ops/ops.c:124-180
- *   C  quantize the attention output -> O rows, x += o  transformer.c:284-287
- *   D  RMSNorm + quantize x -> gate/up row pairs -> act(g) * u   :288-293
- *   E  quantize h -> down rows, x += y                 :294-297
+ *      K/V row into the cache, split flash decode; the last split of a KV
+ *      head unit to finish combines the unit's outputs and quantizes them
+ *                                                      transformer.c:280-283, ops/ops.c:124-180
+ *   C  O rows on the quantized attention output, x += o :284-287
+ *   D  RMSNorm + quantize x -> gate/up row pairs -> act(g) * u, quantized by
+ *      the CTA that owns the block                     :288-293
+ *   E  down rows on the quantized hidden vector, x += y :294-297
  *   F  RMSNorm + quantize x -> classifier rows and the first-index argmax;
  *      the last CTA to arrive advances the token loop  :299-305, model/sampler.c:57-61
- * Several steps run in one launch: the token of step s+1 is the argmax of
- * step s (greedy) or the next prompt token (prefill).
+ * Between phases the vectors travel as tagged 64-bit words (see "tagged
+ * words"): each CTA waits for exactly the words it reads; the one grid
+ * barrier of a step is at its end. Several steps run in one launch: the token
+ * of step s+1 is the argmax of step s (greedy) or the next prompt token.
  *
  * Each CTA owns the same rows of x in phases C and E; it keeps them in shared
- * memory (the residual add reads no global memory) and publishes their sum of
- * squares with its barrier arrival, so the next RMSNorm adds G partial sums
- * instead of reading x twice.
+ * memory (the residual add reads no global memory) and publishes them as words.
  *
  * Quantized activations follow the reference's rule bit for bit
  * (kernels/scalar/k_scalar.c:39-57); block dot products are exact int32
@@ -351,12 +351,11 @@ __device__ __forceinline__ void phase_end(const StepArgs &a, unsigned &pidx) {
  * land. Words are compared for equality, so tags may wrap.
  *
  * A word is rewritten only after every reader of its previous value is done:
- * every CTA runs every phase's prologue (it reads the whole input vector,
- * rows of its own or not) and publishes its sum of squares after the O and
- * after the down phase; x and those sums have one buffer for each of the two
- * phases. The next write of a word then lies behind, in the data flow, a
- * prologue in which every CTA has read every other CTA's sum of the phase
- * after that CTA's last read of the word. */
+ * x has one buffer for each of the two phases that write it (after O, after
+ * down), and every CTA owns rows of x (the grid has at most one CTA per row).
+ * A CTA reads a vector in a prologue and writes its own rows of x later in
+ * the same layer; every other vector's next write lies behind, in the data
+ * flow, a phase that reads all of x, so behind every CTA's reads. */
 typedef unsigned long long word_t;
 enum { TAG_QKV = 0, TAG_PART = 1, TAG_AO = 2, TAG_XC = 3, TAG_HB = 4, TAG_XE = 5, NTAG = 6 };
 constexpr unsigned POLL_LIMIT = 1u << 22;   /* loads of one word before a reader gives up (seconds) */
