@@ -343,6 +343,30 @@ def test_kv_cache_types_one_step_away(name, kv):
     assert rel_err(got[:2], ref[:2]).max() <= RTOL
 
 
+@pytest.mark.parametrize("kv", [kb.F32, kb.F16, kb.Q8_0])
+def test_attention_unit_of_two_kv_heads(tmp_path, kv):
+    """Head groups narrower than a quantization block: 4 heads on 4 KV heads of
+    head_dim 16 give 16 attention outputs per KV head, so two KV heads form one
+    unit; their splits count on one counter and the last of them combines both
+    heads and quantizes their shared 32-value block (no golden model takes this
+    path). 96 positions: one split per KV head below position 64, two above.
+    Decode against the oracle: strict while the first split holds the context,
+    the reference's two-implementations criterion over the whole run."""
+    path = str(tmp_path / "unit2.mlb")
+    kb.write_model(path, dim=64, n_layers=2, n_heads=4, n_kv_heads=4, hidden_dim=128, vocab=256, max_seq=128,
+                   wtype="q8", seed=3)
+    toks = [(i * 37) % 255 + 1 for i in range(96)]
+    m = kb.Model(path)
+    st = kb.State(m, kv_type=kv)
+    got = np.stack([st.forward(t, p) for p, t in enumerate(toks)])
+    ref = oracle.OracleModel(path, kv_type=kv).prefill(toks)
+    st.free()
+    m.free()
+    if kv == kb.F32:
+        assert rel_err(got[:16], ref[:16]).max() <= RTOL
+    assert all(valid_pair(got[i], ref[i]) for i in range(len(toks)))
+
+
 @pytest.mark.parametrize("kv", [kb.F16, kb.Q8_0])
 def test_kv_cache_types_long_context(kv):
     # 150 positions across several tiles and splits; the reference's bound for
