@@ -1008,22 +1008,22 @@ int pack_all(kc_model *m, const uint8_t *stream, const PfRowTable &t, PfModel &P
         PfLayerW &W = P.layers[(size_t)l];
         const unsigned long long *q = t.qkv + l * nq;
         if ((r = alloc_mat(P, W.qkv, (int)nq, c.dim, &arena)) != KC_OK) return r;
-        if ((r = pack_rows(stream, q, c.q_dim, ty(H0.wq), H0.wq.d16, 0, W.qkv, st)) != KC_OK) return r;
-        if ((r = pack_rows(stream, q + c.q_dim, c.kv_dim, ty(H0.wk), H0.wk.d16, c.q_dim, W.qkv, st)) != KC_OK) return r;
-        if ((r = pack_rows(stream, q + c.q_dim + c.kv_dim, c.kv_dim, ty(H0.wv), H0.wv.d16, c.q_dim + c.kv_dim, W.qkv,
+        if ((r = pack_rows(stream, q, c.q_dim, ty(H0.wq), t.d16, 0, W.qkv, st)) != KC_OK) return r;
+        if ((r = pack_rows(stream, q + c.q_dim, c.kv_dim, ty(H0.wk), t.d16, c.q_dim, W.qkv, st)) != KC_OK) return r;
+        if ((r = pack_rows(stream, q + c.q_dim + c.kv_dim, c.kv_dim, ty(H0.wv), t.d16, c.q_dim + c.kv_dim, W.qkv,
                            st)) != KC_OK)
             return r;
         if (H.bq && (r = stack_bias(P, W.qkv, { { H.bq, c.q_dim }, { H.bk, c.kv_dim }, { H.bv, c.kv_dim } }, st)) != KC_OK)
             return r;
         if ((r = alloc_mat(P, W.wo, c.dim, c.q_dim, &arena)) != KC_OK) return r;
-        if ((r = pack_rows(stream, t.wo + l * nd, c.dim, ty(H0.wo), H0.wo.d16, 0, W.wo, st)) != KC_OK) return r;
+        if ((r = pack_rows(stream, t.wo + l * nd, c.dim, ty(H0.wo), t.d16, 0, W.wo, st)) != KC_OK) return r;
         if ((r = alloc_mat(P, W.w13, (int)nh, c.dim, &arena)) != KC_OK) return r;
-        if ((r = pack_rows(stream, t.w13 + l * nh, (int)nh, ty(H0.w1), H0.w1.d16, 0, W.w13, st)) != KC_OK) return r;
+        if ((r = pack_rows(stream, t.w13 + l * nh, (int)nh, ty(H0.w1), t.d16, 0, W.w13, st)) != KC_OK) return r;
         if ((r = alloc_mat(P, W.w2, c.dim, c.hidden_dim, &arena)) != KC_OK) return r;
-        if ((r = pack_rows(stream, t.w2 + l * nd, c.dim, ty(H0.w2), H0.w2.d16, 0, W.w2, st)) != KC_OK) return r;
+        if ((r = pack_rows(stream, t.w2 + l * nd, c.dim, ty(H0.w2), t.d16, 0, W.w2, st)) != KC_OK) return r;
     }
     if ((r = alloc_mat(P, P.cls, c.vocab, c.dim, &arena)) != KC_OK) return r;
-    if ((r = pack_rows(stream, t.cls, c.vocab, ty(cls), cls.d16, 0, P.cls, st)) != KC_OK) return r;
+    if ((r = pack_rows(stream, t.cls, c.vocab, ty(cls), t.d16, 0, P.cls, st)) != KC_OK) return r;
     P.have_cls = true;
     return KC_OK;
 }

@@ -41,10 +41,11 @@ struct PfRun {
 
 /* Device byte offsets, into the weight stream, of the row records the
  * batched prefill's GEMM operands are packed from (a record: quants, then
- * block scales): Q|K|V [n_layers][q_dim + 2 kv_dim], O [n_layers][dim], gate
+ * block scales of the stream's type): Q|K|V [n_layers][q_dim + 2 kv_dim], O [n_layers][dim], gate
  * then up [n_layers][2 hidden], down [n_layers][dim], classifier [vocab]. */
 struct PfRowTable {
     const unsigned long long *qkv, *wo, *w13, *w2, *cls;
+    int d16;   /* the stream's block scales are f16 (else f32) */
 };
 /* Packs every GEMM operand of the model from its uploaded weight stream
  * (device to device; at upload). */

@@ -252,16 +252,42 @@ static int stream_geom(const kc_model *m, StreamGeom &g) {
         set_error("classifier is not Q8_0/Q4_0");
         return KC_E_SHAPE;
     }
+    /* one block-scale type for the whole stream (the step kernel is built per
+     * type): f16 when every streamed matrix has f16 scales, else f32 (f16
+     * scales widened, exactly) */
+    if (!(g.d16_q && g.d16_k && g.d16_v && g.d16_o && g.d16_up && g.d16_down && g.d16_cls))
+        g.d16_q = g.d16_k = g.d16_v = g.d16_o = g.d16_up = g.d16_down = g.d16_cls = 0;
     return KC_OK;
 }
 
-/* One row record of the stream: quants, scales, bias, zero padding to rec. */
-static uint8_t *put_rec(uint8_t *dst, const HostMat &M, int r, const float *bias, int rec) {
+/* An IEEE half as float (exact: every half is a float). */
+static float half_to_float(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16, e = (h >> 10) & 0x1fu, mm = h & 0x3ffu;
+    if (e == 0) return (sign ? -1.0f : 1.0f) * (float)mm * (1.0f / 16777216.0f);
+    const uint32_t x = sign | (e == 31 ? 0x7f800000u | (mm << 13) : ((e + 112u) << 23) | (mm << 13));
+    float f;
+    std::memcpy(&f, &x, 4);
+    return f;
+}
+
+/* One row record of the stream: quants, scales (f16 as in the file when the
+ * stream's scales are f16 (s16), else f32), bias, zero padding to rec. */
+static uint8_t *put_rec(uint8_t *dst, const HostMat &M, int r, const float *bias, int rec, bool s16) {
     const size_t qrow = M.type == KC_Q4_0 ? (size_t)M.cols / 2 : (size_t)M.cols, nb = (size_t)M.cols / KC_QK;
     const size_t dsz = M.d16 ? 2 : 4;
     std::memcpy(dst, (const uint8_t *)M.q + (size_t)r * qrow, qrow);
-    std::memcpy(dst + qrow, (const uint8_t *)M.d + (size_t)r * nb * dsz, nb * dsz);
-    size_t off = qrow + nb * dsz;
+    const uint8_t *d = (const uint8_t *)M.d + (size_t)r * nb * dsz;
+    if (M.d16 && !s16) {
+        for (size_t b = 0; b < nb; b++) {
+            uint16_t h;
+            std::memcpy(&h, d + 2 * b, 2);
+            const float f = half_to_float(h);
+            std::memcpy(dst + qrow + 4 * b, &f, 4);
+        }
+    } else {
+        std::memcpy(dst + qrow, d, nb * dsz);
+    }
+    size_t off = qrow + nb * (s16 ? 2 : 4);
     if (bias) {
         std::memcpy(dst + off, bias + r, sizeof(float));
         off += sizeof(float);
@@ -284,20 +310,20 @@ static size_t fill_stream_part(const kc_model *m, const PhasePlan *P, int part, 
             const HostMat &M = isq ? H.wq : isk ? H.wk : H.wv;
             const float *bias = isq ? H.bq : isk ? H.bk : H.bv;
             const int lo = isq ? 0 : isk ? c.q_dim : c.q_dim + c.kv_dim;
-            for (int r = 0; r < S.rows; r++) p = put_rec(p, M, S.row0 + r - lo, bias, S.rec);
+            for (int r = 0; r < S.rows; r++) p = put_rec(p, M, S.row0 + r - lo, bias, S.rec, S.d16);
         }
         const Seg &C = P[PH_C].seg[0];
-        for (int r = 0; r < C.rows; r++) p = put_rec(p, H.wo, C.row0 + r, nullptr, C.rec);
+        for (int r = 0; r < C.rows; r++) p = put_rec(p, H.wo, C.row0 + r, nullptr, C.rec, C.d16);
         const Seg &D = P[PH_D].seg[0];
         for (int r = 0; r < D.rows; r++) {
-            p = put_rec(p, H.w1, D.row0 + r, nullptr, D.rec / 2);
-            p = put_rec(p, H.w3, D.row0 + r, nullptr, D.rec / 2);
+            p = put_rec(p, H.w1, D.row0 + r, nullptr, D.rec / 2, D.d16);
+            p = put_rec(p, H.w3, D.row0 + r, nullptr, D.rec / 2, D.d16);
         }
         const Seg &E = P[PH_E].seg[0];
-        for (int r = 0; r < E.rows; r++) p = put_rec(p, H.w2, E.row0 + r, nullptr, E.rec);
+        for (int r = 0; r < E.rows; r++) p = put_rec(p, H.w2, E.row0 + r, nullptr, E.rec, E.d16);
     } else {
         const Seg &F = P[PH_F].seg[0];
-        for (int r = 0; r < F.rows; r++) p = put_rec(p, cls, F.row0 + r, nullptr, F.rec);
+        for (int r = 0; r < F.rows; r++) p = put_rec(p, cls, F.row0 + r, nullptr, F.rec, F.d16);
     }
     return (size_t)(p - dst);
 }
@@ -433,7 +459,7 @@ static int pack_prefill(kc_model *m, const StreamGeom &g, int G, const std::vect
     cudaError_t e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMemcpyAsync(d, t.data(), sizeof(unsigned long long) * n, cudaMemcpyHostToDevice, st);
     int rc = e == cudaSuccess ? KC_OK : cuda_status(e, "prefill row table");
-    if (rc == KC_OK) rc = pf_pack_model(m, m->d_stream, PfRowTable{ d, d + oo, d + o13, d + o2, d + ocls }, st);
+    if (rc == KC_OK) rc = pf_pack_model(m, m->d_stream, PfRowTable{ d, d + oo, d + o13, d + o2, d + ocls, g.d16_q }, st);
     if (st) cudaStreamDestroy(st);
     cudaFree(d);
     return rc;
@@ -647,9 +673,10 @@ static int set_smem_attributes() {
     const int rc = current_device(dev);
     if (rc != KC_OK) return rc;
     if (done[dev]) return KC_OK;
-    const void *fns[] = { (const void *)step_kernel<KC_F32>, (const void *)step_kernel<KC_F16>,
-                          (const void *)step_kernel<KC_Q8_0>, (const void *)matvec_kernel,
-                          (const void *)activation_kernel };
+    const void *fns[] = { (const void *)step_kernel<KC_F32, true>,  (const void *)step_kernel<KC_F16, true>,
+                          (const void *)step_kernel<KC_Q8_0, true>, (const void *)step_kernel<KC_F32, false>,
+                          (const void *)step_kernel<KC_F16, false>, (const void *)step_kernel<KC_Q8_0, false>,
+                          (const void *)matvec_kernel, (const void *)activation_kernel };
     for (const void *f : fns) {
         cudaFuncAttributes fa;
         CK(cudaFuncGetAttributes(&fa, f));
@@ -703,16 +730,7 @@ static void embed_inv_table(const kc_model *m, std::vector<float> &out) {
     const int dim = c.dim, nb = dim / QK;
     out.assign((size_t)c.vocab, 0.0f);
     auto scale = [&](size_t i) -> float {
-        if (E.d16) {
-            const uint16_t h = ((const uint16_t *)E.d)[i];
-            const uint32_t sign = (uint32_t)(h & 0x8000u) << 16, e = (h >> 10) & 0x1fu, mm = h & 0x3ffu;
-            if (e == 0) return (sign ? -1.0f : 1.0f) * (float)mm * (1.0f / 16777216.0f);
-            const uint32_t x = sign | (e == 31 ? 0x7f800000u | (mm << 13) : ((e + 112u) << 23) | (mm << 13));
-            float f;
-            std::memcpy(&f, &x, 4);
-            return f;
-        }
-        return ((const float *)E.d)[i];
+        return E.d16 ? half_to_float(((const uint16_t *)E.d)[i]) : ((const float *)E.d)[i];
     };
     auto work = [&](int t0, int t1) {
         std::vector<float> x((size_t)dim);
@@ -755,10 +773,11 @@ static void embed_inv_table(const kc_model *m, std::vector<float> &out) {
 
 static PMat pmat(const DevMat &m) { return PMat{ m.q, m.d, m.rows, m.type, m.d16 }; }
 
-/* The step kernel's instance for a KV cache type. */
+/* The step kernel's instance for a KV cache type and the stream's scale type. */
 typedef void (*StepFn)(StepArgs);
-static StepFn step_fn(int kv_type) {
-    return kv_type == KC_F16 ? step_kernel<KC_F16> : (kv_type == KC_Q8_0 ? step_kernel<KC_Q8_0> : step_kernel<KC_F32>);
+static StepFn step_fn(int kv_type, int d16) {
+    if (d16) return kv_type == KC_F16 ? step_kernel<KC_F16, true> : (kv_type == KC_Q8_0 ? step_kernel<KC_Q8_0, true> : step_kernel<KC_F32, true>);
+    return kv_type == KC_F16 ? step_kernel<KC_F16, false> : (kv_type == KC_Q8_0 ? step_kernel<KC_Q8_0, false> : step_kernel<KC_F32, false>);
 }
 
 /* The persistent step kernel's plan: per-layer pointers in device memory, the
@@ -825,7 +844,7 @@ static int setup_step_kernel(kc_state *s) {
         return KC_E_SHAPE;
     }
     cudaFuncAttributes fa;
-    CK(cudaFuncGetAttributes(&fa, (const void *)step_fn(s->kv_type)));
+    CK(cudaFuncGetAttributes(&fa, (const void *)step_fn(s->kv_type, g.d16_q)));
     const int wbuf = 4 * c.dim;
     const int nst = ring_stages(slot, act, (int)fa.sharedSizeBytes, res, wbuf);
     if (nst < 2) {
@@ -834,7 +853,7 @@ static int setup_step_kernel(kc_state *s) {
     }
     s->step_smem = smem_fixed_bytes(nst, act, res, wbuf) + nst * slot;
     int per_sm = 0;
-    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, step_fn(s->kv_type), STEP_THREADS, s->step_smem));
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, step_fn(s->kv_type, g.d16_q), STEP_THREADS, s->step_smem));
     if (per_sm < 1) {
         set_error("the step kernel does not fit on an SM");
         return KC_E_SHAPE;
@@ -898,7 +917,7 @@ static int launch_steps(kc_state *s, int nsteps, int logits, bool timeline = fal
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    CK(cudaLaunchKernelEx(&cfg, step_fn(s->kv_type), a));
+    CK(cudaLaunchKernelEx(&cfg, step_fn(s->kv_type, a.geom.d16_q), a));
     return KC_OK;
 }
 

@@ -494,7 +494,7 @@ __device__ __forceinline__ unsigned long long ld_sys_u64(const unsigned long lon
  * own[row] += y_0 + y_1 + ... Every rank runs the same grid, so CTA j of every
  * rank owns the same rows of x; a rank can store the next exchange's words
  * into a slot only after this rank has passed the exchange in between. */
-__device__ __forceinline__ void tp_resid(const StepArgs &a, const float *res, int nrows, int row0, float *own, int ns,
+__device__ __noinline__ void tp_resid(const StepArgs &a, const float *res, int nrows, int row0, float *own, int ns,
                                       int ph, unsigned seq) {
     const int me = a.tp_rank, W = a.tp_world, D = a.dim;
     for (int i = threadIdx.x; i < nrows; i += NCT) {
@@ -701,7 +701,7 @@ __device__ __forceinline__ float dot_group(const uint8_t *q, const uint8_t *d, c
     for (int i = 0; i < NR; i++)
 #pragma unroll
         for (int k = 0; k < NA; k++) acc[i][k] = 0.0f;
-#pragma unroll 2
+#pragma unroll 1
     for (int b = b_lo + lane; b < b_hi; b += 32) {
         const int4 xl = x.xlo[b], xh = x.xhi[b];
         const float dx = x.xd[b];
@@ -796,22 +796,19 @@ __device__ __forceinline__ void consume_seg(Ring &rg, Seg S, int seg_off, int co
 }
 
 /* All segments of a phase into res (one inlined copy of each consumer loop:
- * Q4/Q8, f16/f32 scales, single rows or gate|up pairs), then a consumer
- * barrier. */
+ * Q4/Q8, single rows or gate|up pairs, in the stream's scale type D16), then
+ * a consumer barrier. */
+template <bool D16>
 __device__ __forceinline__ void consume_phase(Ring &rg, const PhasePlan &P, bool pair, const Act &x, float *res,
                                               unsigned *err) {
     int off = 0;
     for (int s = 0; s < P.nseg; s++) {
         const Seg S = P.seg[s];
-        switch ((S.type == T_Q4 ? 4 : 0) + (S.d16 ? 2 : 0) + (pair ? 1 : 0)) {
-        case 7: consume_seg<T_Q4, true, true>(rg, S, off, P.cols, x, res, err); break;
-        case 6: consume_seg<T_Q4, true, false>(rg, S, off, P.cols, x, res, err); break;
-        case 5: consume_seg<T_Q4, false, true>(rg, S, off, P.cols, x, res, err); break;
-        case 4: consume_seg<T_Q4, false, false>(rg, S, off, P.cols, x, res, err); break;
-        case 3: consume_seg<T_Q8, true, true>(rg, S, off, P.cols, x, res, err); break;
-        case 2: consume_seg<T_Q8, true, false>(rg, S, off, P.cols, x, res, err); break;
-        case 1: consume_seg<T_Q8, false, true>(rg, S, off, P.cols, x, res, err); break;
-        default: consume_seg<T_Q8, false, false>(rg, S, off, P.cols, x, res, err); break;
+        switch ((S.type == T_Q4 ? 2 : 0) + (pair ? 1 : 0)) {
+        case 3: consume_seg<T_Q4, D16, true>(rg, S, off, P.cols, x, res, err); break;
+        case 2: consume_seg<T_Q4, D16, false>(rg, S, off, P.cols, x, res, err); break;
+        case 1: consume_seg<T_Q8, D16, true>(rg, S, off, P.cols, x, res, err); break;
+        default: consume_seg<T_Q8, D16, false>(rg, S, off, P.cols, x, res, err); break;
         }
         off += S.rows;
     }
@@ -1240,7 +1237,7 @@ __device__ __forceinline__ void act_loop_w(float eps, const word_t *xw, unsigned
  * Every CTA recomputes it for all cols, adds up its squares and quantizes
  * RMSNorm(x_new) * nw into the activation; the CTA's own rows of x_new go to
  * own (and out as words one phase later, with the next block's output). */
-__device__ __forceinline__ void act_postnorm(const StepArgs &a, const word_t *x, const word_t *y, const word_t *ssw,
+__device__ __noinline__ void act_postnorm(const StepArgs &a, const word_t *x, const word_t *y, const word_t *ssw,
                                           unsigned tag, const float *pw, const float *nw, int cols, ActW o, float *red,
                                           float *own, int own0, int own1) {
     const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 7) * 4;
@@ -1276,7 +1273,7 @@ __device__ __forceinline__ void act_postnorm(const StepArgs &a, const word_t *x,
  * rows (column slices summed in order) into yown and out as words (yw), and
  * the CTA's rows of the residual stream the last prologue computed (own) as
  * words (xw), with the same tag. */
-__device__ __forceinline__ void finish_post(const float *res, int nrows, int row0, int ns, word_t *xw, word_t *yw,
+__device__ __noinline__ void finish_post(const float *res, int nrows, int row0, int ns, word_t *xw, word_t *yw,
                                          unsigned tag, const float *own, float *yown) {
     for (int i = threadIdx.x; i < nrows; i += NCT) {
         float sum = res[i * ns];
@@ -1933,10 +1930,12 @@ __device__ __forceinline__ void producer(const StepArgs &a, Ring rg) {
     }
 }
 
-/* One instance per KV cache type (KV: KC_F32, KC_F16, KC_Q8_0; the host
- * launches the state's): each carries only its own attention code, so the
- * instructions a layer runs through stay fewer and closer together. */
-template <int KV>
+/* One instance per KV cache type (KV: KC_F32, KC_F16, KC_Q8_0) and block
+ * scale type of the weight stream (D16: f16, else f32); the host launches the
+ * state's. Each carries only its own attention and consumer code, and the
+ * post-norm and tensor-parallel steps are out of line, so the instructions a
+ * layer runs through stay fewer and closer together. */
+template <int KV, bool D16>
 __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_constant__ StepArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     const Smem sh = carve(smem, a.nstage, a.act_bytes, a.res_bytes, a.wbuf_bytes);
@@ -2041,7 +2040,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
             trace_mark(a, pidx, 0);
             if (threadIdx.x == 0) ev(0, EV_PRO_DONE);
             const PhasePlan &P = s_plan[ph];
-            consume_phase(rg, P, ph == PH_D, act_view(w), sh.res, a.err);
+            consume_phase<D16>(rg, P, ph == PH_D, act_view(w), sh.res, a.err);
             const int ns = col_slices(cols / QK, false);
             if (ph == PH_A) {
                 finish_phase(FIN_STORE, sh.res, plan_rows(P), P.nseg ? P.seg[0].row0 : 0, nullptr, a.qkvw,
