@@ -88,10 +88,12 @@ int kc_model_from_host(kc_model **out, const kc_config *cfg, const kc_tensor *to
                        const float *final_norm, const kc_layer_desc *layers);
 /* Replaces ml_model_pack (model/pack_model.h:13-19): the one-time upload of
  * every quantized matrix (Q4/Q8 quants + f16 or f32 block scales), norm and
- * bias to HBM. Idempotent. */
+ * bias to HBM, in the decode kernel's per-SM stream layout; for an unsharded
+ * model also the batched prefill's tensor-core operands (int8 tiles, float
+ * scales), packed on the device from that stream. Idempotent. */
 int kc_model_upload(kc_model *m);
 const kc_config *kc_model_config(const kc_model *m);
-/* Bytes of weights held on the device (quants + scales + float arrays). */
+/* Bytes of weights held on the device (decode stream, prefill operands, float arrays). */
 size_t kc_model_device_bytes(const kc_model *m);
 void kc_model_free(kc_model *m);
 
