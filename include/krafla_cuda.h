@@ -270,6 +270,11 @@ int kc_dev_sync(void);
  * correct and the next kc_dev_sync returns KC_E_IO. No counterpart in the
  * reference (its CPU kernels do not wait on copies). */
 int kc_debug_wait_limit(int polls);
+/* Testing: how the decode kernel shares the gate|up rows of models uploaded
+ * from now on: -1 by the model (default), 0 whole 32-row blocks, 1 4-row units
+ * with blocks split between CTAs. Returns the previous mode. No reference
+ * counterpart. */
+int kc_debug_ffn_split(int mode);
 
 #ifdef __cplusplus
 }

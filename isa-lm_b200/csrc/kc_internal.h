@@ -82,6 +82,7 @@ struct kc_model {
     size_t stream_bytes = 0;
     unsigned long long *d_cta_base = nullptr;   /* [stream_G] */
     int stream_G = 0;
+    int ffn_unit = 0;   /* rows per ownership unit of the gate|up phase in the stream (32 or 4), set at upload */
     /* the batched prefill's packed weights, built on first use */
     kc::PfModel *pf = nullptr;
     /* tensor parallelism (kc_model_shard): after sharding, cfg holds this rank's

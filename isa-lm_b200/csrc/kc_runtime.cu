@@ -224,6 +224,28 @@ struct Item {
 
 /* Types and shapes of the streamed matrices; KC_E_SHAPE when a matrix class
  * changes type between layers or a matrix is not Q8_0/Q4_0. */
+/* Ownership of the gate|up phase's rows (kc_debug_ffn_split): -1 by the
+ * model, 0 whole blocks, 1 split blocks. */
+static int g_ffn_split = -1;
+
+extern "C" int kc_debug_ffn_split(int mode) {
+    const int old = g_ffn_split;
+    g_ffn_split = mode < 0 ? -1 : (mode ? 1 : 0);
+    return old;
+}
+
+/* Rows per unit of the gate|up phase for G CTAs: whole 32-row blocks (each CTA
+ * quantizes its own blocks), unless whole blocks leave the busiest CTA more
+ * than ~2 us of weight bytes (at its share of the HBM rate) above the average,
+ * then 4-row units with split blocks (their CTAs exchange one maximum). */
+static int ffn_unit(const kc_config &c, const StreamGeom &g, int G) {
+    if (g_ffn_split >= 0) return g_ffn_split ? 4 : QK;
+    const int nbk = c.hidden_dim / QK, maxb = (nbk + G - 1) / G;
+    const double block_bytes = 2.0 * QK * rec_bytes(g.t_up, g.d16_up, c.dim, 0);
+    const double gap_us = ((double)maxb - (double)nbk / G) * block_bytes / 44000.0;
+    return gap_us > 2.0 ? 4 : QK;
+}
+
 static int stream_geom(const kc_model *m, StreamGeom &g) {
     const kc_config &c = m->cfg;
     const HostLayer &L0 = m->layers[0];
@@ -257,6 +279,7 @@ static int stream_geom(const kc_model *m, StreamGeom &g) {
      * scales widened, exactly) */
     if (!(g.d16_q && g.d16_k && g.d16_v && g.d16_o && g.d16_up && g.d16_down && g.d16_cls))
         g.d16_q = g.d16_k = g.d16_v = g.d16_o = g.d16_up = g.d16_down = g.d16_cls = 0;
+    g.d_unit = m->ffn_unit ? m->ffn_unit : QK;   /* set by upload_stream */
     return KC_OK;
 }
 
@@ -473,6 +496,8 @@ static int upload_stream(kc_model *m, int G) {
     StreamGeom g;
     int st = stream_geom(m, g);
     if (st != KC_OK) return st;
+    m->ffn_unit = ffn_unit(m->cfg, g, G);
+    g.d_unit = m->ffn_unit;
     std::vector<unsigned long long> base((size_t)G);
     size_t total = 0, maxc = 0;
     for (int j = 0; j < G; j++) {
@@ -587,7 +612,7 @@ struct kc_state {
      * post-norm block outputs [2][dim], q|k|v, attention partials, attention
      * output, FFN hidden */
     unsigned long long *xw = nullptr, *sspw = nullptr, *yw = nullptr, *qkvw = nullptr, *partw = nullptr;
-    unsigned long long *aow = nullptr, *hbw = nullptr;
+    unsigned long long *aow = nullptr, *hbw = nullptr, *amaxw = nullptr;
     unsigned tag_next = 1;   /* tag of the next launch's first output (0: the zeroed buffers' tag) */
     float *logits = nullptr;
     uint8_t *kc = nullptr, *vc = nullptr;   /* [L][max_seq][kv_dim] of the KV type */
@@ -870,6 +895,7 @@ static int setup_step_kernel(kc_state *s) {
     a.hbw = s->hbw; a.logits = s->logits;
     a.bar = s->bar; a.err = s->err; a.ls = s->ls; a.feed = s->feed;
     a.attc = s->bar + 32;
+    a.amaxw = s->amaxw;
     a.att_unit = att_unit;
     a.out_tokens = s->out_tokens;
     a.kv_type = s->kv_type;
@@ -1009,6 +1035,8 @@ extern "C" int kc_state_init(kc_state **out, kc_model *m, int nthreads, int kv_t
         /* quantized vectors: n / 4 quant words, then n / 32 scale words */
         { (void **)&s->aow, sizeof(unsigned long long) * (size_t)(c.q_dim / 4 + c.q_dim / QK) },
         { (void **)&s->hbw, sizeof(unsigned long long) * (size_t)(c.hidden_dim / 4 + c.hidden_dim / QK) },
+        /* split FFN blocks: the covering CTAs' partial maxima [hidden / 32][8] */
+        { (void **)&s->amaxw, sizeof(unsigned long long) * (size_t)(c.hidden_dim / QK) * 8 },
         { (void **)&s->partw, sizeof(unsigned long long) * (size_t)c.n_heads * MAX_NSPLIT * (c.head_dim + 2) },
         { (void **)&s->logits, sizeof(float) * (size_t)LOGITS_RING * c.vocab },
         { (void **)&s->err, sizeof(unsigned) * 4 },

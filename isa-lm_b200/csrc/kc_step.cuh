@@ -67,6 +67,8 @@ struct StreamGeom {
     int t_q, t_k, t_v, t_o, t_up, t_down, t_cls;         /* T_Q8 / T_Q4 */
     int d16_q, d16_k, d16_v, d16_o, d16_up, d16_down, d16_cls;
     int b_q, b_k, b_v;                                     /* rows carry a bias */
+    int d_unit;   /* rows of the gate|up phase are shared in units of d_unit: 32 (whole blocks), or 4 when whole
+                   * blocks would leave some CTAs with a block more (split blocks agree on their maximum) */
 };
 
 /* A run of one matrix's rows in a CTA's stream. */
@@ -146,9 +148,9 @@ __host__ __device__ inline void make_plan(const StreamGeom &g, int j, int G, Pha
     P[PH_E].nseg = 1;
     P[PH_E].cols = g.hidden;
     P[PH_E].seg[0] = make_seg(r1 - r0, r0, g.t_down, g.d16_down, g.hidden, 0, 0);
-    share_rows(g.hidden / QK, j, G, r0, r1);   /* whole blocks: the finish quantizes them */
-    r0 *= QK;
-    r1 *= QK;
+    share_rows(g.hidden / g.d_unit, j, G, r0, r1);   /* whole blocks, or 4-row units of split blocks */
+    r0 *= g.d_unit;
+    r1 *= g.d_unit;
     P[PH_D].nseg = 1;
     P[PH_D].cols = g.dim;
     P[PH_D].seg[0] = make_seg(r1 - r0, r0, g.t_up, g.d16_up, g.dim, 0, 1);
@@ -201,6 +203,9 @@ struct StepArgs {
      * apart, zeroed before each launch */
     unsigned *attc;
     int att_unit;
+    /* split FFN blocks (geom.d_unit 4): the covering CTAs' partial maxima,
+     * tagged words [hidden / 32][8] */
+    unsigned long long *amaxw;
     float *logits;
     unsigned *bar, *err;
     LoopState *ls;
@@ -866,6 +871,73 @@ __device__ __forceinline__ void finish_pair_q(const float *res, int nrows, int r
     for (int b = warp; b < nrows / QK; b += NCW) {
         const float2 gu = ((const float2 *)res)[b * QK + lane];
         publish_qblock(hw, n, row0 / QK + b, tag, act_mul(act, gu.x, gu.y));
+    }
+}
+
+/* Owner of unit u of U units shared by G CTAs (share_rows' inverse). */
+__device__ __forceinline__ int unit_owner(int u, int U, int G) { return (int)(((long long)(u + 1) * G - 1) / U); }
+
+/* The gate|up phase's finish when its rows are shared in 4-row units (U of
+ * them) and blocks of the hidden vector are split between CTAs: every covering
+ * CTA publishes its rows' |max| of each split block (slot: its first unit's
+ * offset in the block), then, with every partial it owns published, waits for
+ * the other covering CTAs' and quantizes its own rows with the block's maximum
+ * (the max of the partials is exact, so the quants and scale are those of the
+ * whole block); the block's first CTA writes the scale. Whole blocks as
+ * finish_pair_q. */
+__device__ __forceinline__ void finish_pair_split(const float *res, int nrows, int row0, word_t *hw, int n, unsigned tag,
+                                                  int act, word_t *amaxw, int U, unsigned *err) {
+    if (nrows <= 0) return;
+    constexpr int UPB = QK / 4;   /* units per block */
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, G = gridDim.x, j = blockIdx.x;
+    const int b0 = row0 / QK, b1 = (row0 + nrows - 1) / QK;
+    auto value = [&](int bi) {
+        const int row = bi * QK + lane;
+        if (row < row0 || row >= row0 + nrows) return 0.0f;
+        const float2 gu = ((const float2 *)res)[row - row0];
+        return act_mul(act, gu.x, gu.y);
+    };
+    auto wmax = [&](float m) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        return m;
+    };
+    const int my_slot_first = (row0 / 4) % UPB;   /* my first unit's offset in block b0 */
+    /* first every partial of a split block */
+    for (int bi = b0 + warp; bi <= b1; bi += NCW) {
+        const bool whole = unit_owner(bi * UPB, U, G) == j && unit_owner(bi * UPB + UPB - 1, U, G) == j;
+        const float m = wmax(fabsf(value(bi)));
+        if (!whole && lane == 0) st_word(amaxw + (size_t)bi * UPB + (bi == b0 ? my_slot_first : 0), mkword(tag, m));
+    }
+    for (int bi = b0 + warp; bi <= b1; bi += NCW) {
+        const float v = value(bi);
+        float amax = wmax(fabsf(v));
+        const int o0 = unit_owner(bi * UPB, U, G);
+        if (!(o0 == j && unit_owner(bi * UPB + UPB - 1, U, G) == j)) {
+            /* lane k < 8: the CTA whose first unit in the block is unit k, when it is another CTA */
+            float other = 0.0f;
+            if (lane < UPB) {
+                const int ok = unit_owner(bi * UPB + lane, U, G);
+                const bool start = lane == 0 || unit_owner(bi * UPB + lane - 1, U, G) != ok;
+                if (start && ok != j) other = get_word(amaxw + (size_t)bi * UPB + lane, tag, err);
+            }
+            amax = fmaxf(amax, wmax(other));
+        }
+        unsigned q = 0;
+        float d = 0.0f;
+        if (!(amax < 1e-30f)) {
+            const float id = __fdiv_rn(127.0f, amax);
+            d = __fdiv_rn(amax, 127.0f);
+            float t = truncf(__fadd_rn(__fmul_rn(v, id), copysignf(0.5f, v)));
+            t = fminf(fmaxf(t, -127.0f), 127.0f);
+            q = ((unsigned)(int)t & 0xffu) << (8 * (lane & 3));
+        }
+        q |= __shfl_xor_sync(0xffffffffu, q, 1);
+        q |= __shfl_xor_sync(0xffffffffu, q, 2);
+        const int row = bi * QK + lane;
+        if ((lane & 3) == 0 && row >= row0 && row < row0 + nrows)
+            st_word(hw + (size_t)bi * 8 + (lane >> 2), mkword(tag, __uint_as_float(q)));
+        if (lane == 0 && o0 == j) st_word(hw + n / 4 + bi, mkword(tag, d));
     }
 }
 
@@ -2046,7 +2118,11 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
                 finish_phase(FIN_STORE, sh.res, plan_rows(P), P.nseg ? P.seg[0].row0 : 0, nullptr, a.qkvw,
                              tg + TAG_QKV, nullptr, 0, 0.0f, sh.cta_best, ns);
             } else if (ph == PH_D) {
-                finish_pair_q(sh.res, P.seg[0].rows, P.seg[0].row0, a.hbw, a.hidden, tg + TAG_HB, a.act);
+                if (a.geom.d_unit == QK)
+                    finish_pair_q(sh.res, P.seg[0].rows, P.seg[0].row0, a.hbw, a.hidden, tg + TAG_HB, a.act);
+                else
+                    finish_pair_split(sh.res, P.seg[0].rows, P.seg[0].row0, a.hbw, a.hidden, tg + TAG_HB, a.act,
+                                      a.amaxw, a.hidden / a.geom.d_unit, a.err);
             } else if (ph == PH_F) {
                 const Seg &F = P.seg[0];
                 const unsigned long long b =

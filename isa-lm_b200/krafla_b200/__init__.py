@@ -102,6 +102,7 @@ def lib():
             "kc_matmul_dev": (I, [P, I, I, P, P, I, I, P, P, I, P]), "kc_block_sums_dev": (I, [P, I, P, I, I, P, P]),
             "kc_dev_alloc": (P, [S]), "kc_dev_free": (None, [P]), "kc_memcpy_htod": (I, [P, P, S]),
             "kc_memcpy_dtoh": (I, [P, P, S]), "kc_dev_sync": (I, []), "kc_debug_wait_limit": (I, [I]),
+            "kc_debug_ffn_split": (I, [I]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)

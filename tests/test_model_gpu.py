@@ -367,6 +367,49 @@ def test_attention_unit_of_two_kv_heads(tmp_path, kv):
     assert all(valid_pair(got[i], ref[i]) for i in range(len(toks)))
 
 
+def _decode_with_ffn_mode(path, mode, toks):
+    L = kb.lib()
+    old = L.kc_debug_ffn_split(mode)
+    try:
+        m = kb.Model(path)
+        st = kb.State(m)
+        got = np.stack([st.forward(t, p) for p, t in enumerate(toks)])
+        st.free()
+        m.free()
+    finally:
+        L.kc_debug_ffn_split(old)
+    return got
+
+
+@pytest.mark.parametrize("name", ["rand_q4", "mixf16_q4", "gemma_q4", "bias_q4"])
+def test_ffn_split_blocks_equal_whole_blocks(name):
+    """The gate|up rows shared in 4-row units (blocks of the hidden vector split
+    between CTAs, which agree on each block's maximum) against whole 32-row
+    blocks per CTA: each hidden value and each block's quantization are the
+    same whichever CTAs own the rows, so the logits are equal bit for bit (the
+    golden models' 4 blocks spread over 8 CTAs each)."""
+    path = os.path.join(GOLDEN, "models", f"{name}.mlb")
+    whole = _decode_with_ffn_mode(path, 0, TOKENS)
+    split = _decode_with_ffn_mode(path, 1, TOKENS)
+    assert np.array_equal(whole.view(np.uint32), split.view(np.uint32))
+
+
+def test_ffn_split_blocks_wide_model(tmp_path):
+    """Split blocks on a model whose hidden blocks each span about three CTAs
+    (1536 hidden rows, 148 CTAs): equal bit for bit to whole blocks, and the
+    reference's strict bar against the oracle over the first steps."""
+    path = str(tmp_path / "ffn.mlb")
+    kb.write_model(path, dim=512, n_layers=2, n_heads=8, n_kv_heads=2, hidden_dim=1536, vocab=512, max_seq=64,
+                   wtype="q4", q8=("v", "o", "down"), seed=5)
+    toks = [(i * 53) % 511 + 1 for i in range(12)]
+    whole = _decode_with_ffn_mode(path, 0, toks)
+    split = _decode_with_ffn_mode(path, 1, toks)
+    assert np.array_equal(whole.view(np.uint32), split.view(np.uint32))
+    ref = oracle.OracleModel(path).prefill(toks)
+    assert rel_err(split[:4], ref[:4]).max() <= RTOL
+    assert all(valid_pair(split[i], ref[i]) for i in range(len(toks)))
+
+
 @pytest.mark.parametrize("kv", [kb.F16, kb.Q8_0])
 def test_kv_cache_types_long_context(kv):
     # 150 positions across several tiles and splits; the reference's bound for

@@ -34,7 +34,7 @@ def _free_port():
         return sk.getsockname()[1]
 
 
-def _worker(rank, world, port, path, kv, out):
+def _worker(rank, world, port, path, kv, out, ffn=-1):
     import torch.distributed as dist
     from datetime import timedelta
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
@@ -42,6 +42,7 @@ def _worker(rank, world, port, path, kv, out):
     states, lg, toks, err = [], None, None, None
     try:
         kb.set_device(rank)
+        kb.lib().kc_debug_ffn_split(ffn)
         m = kb.Model(path, upload=False).shard(rank, world)
         st = kb.State(m, kv_type=kv)
         states.append(st)
@@ -70,12 +71,12 @@ def _worker(rank, world, port, path, kv, out):
     dist.destroy_process_group()
 
 
-def _run(path, kv, world=2):
+def _run(path, kv, world=2, ffn=-1):
     import multiprocessing as mp
     ctx = mp.get_context("spawn")
     out = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_worker, args=(r, world, port, path, kv, out)) for r in range(world)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, path, kv, out, ffn)) for r in range(world)]
     for p in ps:
         p.start()
     res = {}
@@ -115,3 +116,15 @@ def test_tp2_kv_cache_types(kv):
     assert np.array_equal(t0, res[1][1])
     err = np.abs(lg0.astype(np.float64) - ref).max(axis=-1) / np.abs(ref).max(axis=-1)
     assert err.max() <= 1e-3, err
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
+def test_tp2_ffn_split_blocks():
+    """Each rank's gate|up rows shared in 4-row units with split blocks (the
+    mode cfg4's shards take) against whole blocks: equal logits bit for bit,
+    on every rank."""
+    path = os.path.join(GOLDEN, "models", "rand_q4.mlb")
+    whole, split = _run(path, kb.F32, ffn=0), _run(path, kb.F32, ffn=1)
+    for r in (0, 1):
+        assert np.array_equal(whole[r][0].view(np.uint32), split[r][0].view(np.uint32))
+        assert np.array_equal(whole[r][1], split[r][1])
