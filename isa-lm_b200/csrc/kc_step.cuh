@@ -1895,7 +1895,7 @@ __device__ __forceinline__ void attention_combine(const StepArgs &a, int U, int 
         const int h = o / hd, i = o - h * hd;
         const word_t *ps = a.partw + (size_t)(h0 + h) * a.nsplit * stride + i;
         const float *wh = sw + h * MAX_NSPLIT;
-        constexpr int CB = 16;   /* splits requested together */
+        constexpr int CB = MAX_NSPLIT;   /* splits requested together: one round trip */
         float num = 0.0f;
         bool ok = true;
 #pragma unroll 1
