@@ -815,10 +815,6 @@ static int setup_step_kernel(kc_state *s) {
         set_error("the model was uploaded for a device with another SM count");
         return KC_E_SHAPE;
     }
-    if (G > SSP_LOADS * 32) {
-        set_error("more SMs than the activation prologue's per-CTA sums cover");
-        return KC_E_SHAPE;
-    }
     if ((c.dim + G - 1) / G > OWN_MAX) {
         set_error("dim too large for the rows of x a CTA keeps in shared memory");
         return KC_E_SHAPE;

@@ -92,7 +92,6 @@ constexpr int GROUP_ROWS = 4;            /* rows per warp task (two gate|up pair
 constexpr int OWN_MAX = 128;             /* rows of x a CTA may own */
 static_assert((NCW & (NCW - 1)) == 0, "warp round-robin uses a mask");
 constexpr int ATT_CNT_STRIDE = 32;       /* words between attention unit counters (one 128-byte line each) */
-constexpr int SSP_LOADS = 8;             /* per-lane loads of per-CTA values (sums, flags): grids of up to 256 CTAs */
 
 /* Record bytes: quants, scales, the bias when present, padded to 16. */
 __host__ __device__ inline int rec_bytes(int type, int d16, int cols, int bias) {
@@ -1080,23 +1079,18 @@ __device__ __forceinline__ void put_quant(const ActW &o, int b, int nb, int j0, 
 /* The activation of a phase into shared memory: quantize_q8 of v, with
  * v = RMSNorm(x) * w (k_scalar.c:59-64: o = (x * inv) * w, inv =
  * 1 / sqrt(ss / n + eps)) when norm_w is set; x arrives as tagged words from
- * the CTAs that wrote it (tag: the phase output read). 1/rms: from ss = the
- * sum of the G per-CTA partial sums (tagged words sspw), else reduced here.
- * Every thread issues all its loads (up to 2 passes of 128 blocks, 4 lanes
- * per block, 8 values per lane) before it waits on any, so the prologue costs
- * one round trip to L2 once its input has landed. */
-__device__ __forceinline__ void act_float(float eps, const word_t *xw, unsigned tag, const float *norm_w,
-                                       const word_t *sspw, int cols, ActW o, float *red, const float *wstaged,
-                                       unsigned *err) {
+ * the CTAs that wrote it (tag: the phase output read), and every CTA reduces
+ * ss from the whole vector it loads, in the same order. Every thread issues
+ * all its loads (up to 2 passes of 64 blocks, 4 lanes per block, 8 values per
+ * lane) before it waits on any, so the prologue costs one round trip to L2
+ * once its input has landed. */
+__device__ __forceinline__ void act_float(float eps, const word_t *xw, unsigned tag, const float *norm_w, int cols,
+                                       ActW o, float *red, const float *wstaged, unsigned *err) {
     /* 4 lanes per block, 8 values per lane (four word pairs), passes of NCT / 4 blocks */
     const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 3) * 8;
     const int passes = (nb + NCT / 4 - 1) / (NCT / 4);
     const bool norm = norm_w != nullptr;
     if (tid == 0) ev(0, EV_ACT_ENTRY);
-    /* one warp per CTA loads the G per-CTA sums of squares (the same few
-     * lines read by every warp of every CTA would queue at their L2 slice) */
-    const int lane = tid & 31, warp = tid >> 5;
-    const bool ssw = norm && sspw && tid < (int)gridDim.x;   /* thread t reads CTA t's sum */
     constexpr int NP = ACT_PASSES / 2;   /* passes of NCT / 4 blocks */
     bool live[NP];
     const word_t *src[NP];
@@ -1108,7 +1102,7 @@ __device__ __forceinline__ void act_float(float eps, const word_t *xw, unsigned 
     }
     /* every word this thread reads, requested together; then, in one loop,
      * the stale ones again until all carry the tag */
-    word_t v[NP][8], part = mkword(tag, 0.0f);
+    word_t v[NP][8];
     bool fresh = false;
     for (unsigned it = 0;; it++) {
 #pragma unroll
@@ -1122,8 +1116,7 @@ __device__ __forceinline__ void act_float(float eps, const word_t *xw, unsigned 
                     ld_words4(src[p] + 4 * h, q[0], q[1], q[2], q[3]);
                 }
             }
-        if (ssw && (it == 0 || !wok(part, tag))) part = ld_word(sspw + tid);
-        fresh = wok(part, tag);
+        fresh = true;
 #pragma unroll
         for (int p = 0; p < NP; p++)
 #pragma unroll
@@ -1142,35 +1135,17 @@ __device__ __forceinline__ void act_float(float eps, const word_t *xw, unsigned 
     const float *wsrc = wstaged ? wstaged : norm_w;
     float inv = 1.0f;
     if (norm) {
-        if (sspw) {
-            /* the G sums through shared memory, then added by warp 0 as lane l
-             * adds CTAs l, l + 32, ... in order and the warp's tree adds lanes */
-            float *sums = red + 32;
-            if (ssw) sums[tid] = wval(part);
-            consumer_sync();
-            if (warp == 0) {
-                float t = 0.0f;
+        float t = 0.0f;
 #pragma unroll
-                for (int k = 0; k < SSP_LOADS; k++)
-                    if (k * 32 + lane < (int)gridDim.x) t += sums[k * 32 + lane];
-                const float ss = warp_sum(t);
-                if (lane == 0) red[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
+        for (int p = 0; p < NP; p++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const float a0 = wval(v[p][4 * h]), a1 = wval(v[p][4 * h + 1]), a2 = wval(v[p][4 * h + 2]),
+                            a3 = wval(v[p][4 * h + 3]);
+                t += a0 * a0 + a1 * a1 + a2 * a2 + a3 * a3;
             }
-            consumer_sync();
-            inv = red[0];
-        } else {
-            float t = 0.0f;
-#pragma unroll
-            for (int p = 0; p < NP; p++)
-#pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    const float a0 = wval(v[p][4 * h]), a1 = wval(v[p][4 * h + 1]), a2 = wval(v[p][4 * h + 2]),
-                                a3 = wval(v[p][4 * h + 3]);
-                    t += a0 * a0 + a1 * a1 + a2 * a2 + a3 * a3;
-                }
-            const float ss = block_sum(t, red);
-            inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
-        }
+        const float ss = block_sum(t, red);
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
     }
     if (tid == 0) ev(0, EV_ACT_INV);
     /* the passes in one copy of the code: the second pass's values move into
@@ -1261,20 +1236,16 @@ __device__ __noinline__ void act_loop(float eps, const float *x, const float *no
 }
 
 /* act_loop over tagged words: wider vectors in the step kernel, pass by pass. */
-__device__ __forceinline__ void act_loop_w(float eps, const word_t *xw, unsigned tag, const float *norm_w,
-                                        const word_t *sspw, int cols, ActW o, float *red, unsigned *err) {
+__device__ __forceinline__ void act_loop_w(float eps, const word_t *xw, unsigned tag, const float *norm_w, int cols,
+                                        ActW o, float *red, unsigned *err) {
     const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 7) * 4;
     float inv = 1.0f;
     if (norm_w) {
-        /* the sum of squares from the G per-CTA sums, else from x itself */
+        /* the sum of squares from x itself (a first pass over the words) */
         float t = 0.0f;
-        if (sspw) {
-            for (int g = tid; g < (int)gridDim.x; g += NCT) t += get_word(sspw + g, tag, err);
-        } else {
-            for (int i = tid; i < cols; i += NCT) {
-                const float v = get_word(xw + i, tag, err);
-                t += v * v;
-            }
+        for (int i = tid; i < cols; i += NCT) {
+            const float v = get_word(xw + i, tag, err);
+            t += v * v;
         }
         const float ss = block_sum(t, red);
         inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
@@ -1360,10 +1331,9 @@ __device__ __noinline__ void finish_post(const float *res, int nrows, int row0, 
  * phase output's tagged words; wstaged: norm_w already copied into shared
  * memory by prefetch_norm. */
 __device__ __forceinline__ void load_activation(const StepArgs &a, const word_t *x, unsigned tag, const float *norm_w,
-                                                const word_t *ssp, int cols, const ActW &o, float *red,
-                                                const float *wstaged = nullptr) {
-    if (cols <= ACT_PASSES * NCT / 8 * QK) act_float(a.eps, x, tag, norm_w, ssp, cols, o, red, wstaged, a.err);
-    else act_loop_w(a.eps, x, tag, norm_w, ssp, cols, o, red, a.err);
+                                                int cols, const ActW &o, float *red, const float *wstaged = nullptr) {
+    if (cols <= ACT_PASSES * NCT / 8 * QK) act_float(a.eps, x, tag, norm_w, cols, o, red, wstaged, a.err);
+    else act_loop_w(a.eps, x, tag, norm_w, cols, o, red, a.err);
 }
 
 /* The activation of a phase whose input arrives quantized (publish_qblock
@@ -1925,8 +1895,7 @@ __device__ __forceinline__ void attention_combine(const StepArgs &a, int U, int 
 /* ------------------------------------------------------------ shared layout */
 
 /* Dynamic shared memory of a streaming CTA: mbarriers [2][nstage], per-warp
- * argmax [NCW], flag, reduction scratch [32] and the per-CTA sums of squares
- * [32 * SSP_LOADS], the owned rows of x [OWN_MAX],
+ * argmax [NCW], flag, reduction scratch [32], the owned rows of x [OWN_MAX],
  * activation (or attention scratch) of act_bytes, then the ring (128 B
  * aligned). */
 struct Smem {
@@ -1944,7 +1913,7 @@ struct Smem {
 
 /* res_bytes: a phase's row results (16-byte multiple). */
 __host__ __device__ inline int smem_fixed_bytes(int nstage, int act_bytes, int res_bytes = 0, int wbuf_bytes = 0) {
-    return 16 * nstage + 8 * NCW + 16 + 4 * (32 + 32 * SSP_LOADS) + 8 * OWN_MAX + res_bytes + wbuf_bytes + act_bytes +
+    return 16 * nstage + 8 * NCW + 16 + 4 * 32 + 8 * OWN_MAX + res_bytes + wbuf_bytes + act_bytes +
            128;
 }
 
@@ -1956,7 +1925,7 @@ __device__ __forceinline__ Smem carve(unsigned char *smem, int nstage, int act_b
     s.cta_best = (unsigned long long *)(s.empty + nstage);
     s.flag = (int *)(s.cta_best + NCW);
     s.red = (float *)(s.flag + 4);
-    s.own = s.red + 32 + 32 * SSP_LOADS;
+    s.own = s.red + 32;
     s.yown = s.own + OWN_MAX;
     s.res = s.yown + OWN_MAX;
     s.wbuf = (float *)((unsigned char *)s.res + res_bytes);
@@ -2106,7 +2075,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const __grid_cons
                                      e ? s_lp[(gl - 1) & 1].post_ffn : L.post_attn, nw, a.dim, w, sh.red, sh.own, own0,
                                      own1);
                     else
-                        load_activation(a, e ? xw_e : xw_c, tin, nw, nullptr, cols, w, sh.red, nw ? sh.wbuf : nullptr);
+                        load_activation(a, e ? xw_e : xw_c, tin, nw, cols, w, sh.red, nw ? sh.wbuf : nullptr);
                 }
             }
             trace_mark(a, pidx, 0);
