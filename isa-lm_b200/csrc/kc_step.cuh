@@ -257,7 +257,9 @@ enum { EV_PRO_DONE = 2, EV_STAGE_READY = 3, EV_STAGE_DONE = 4, EV_ARRIVE = 5, EV
        EV_ATT_TILE = 14, EV_ATT_PART = 15, EV_ATT_COMBINE = 16, EV_ATT_DONE = 17,
        /* checkpoints inside an attention item */
        EV_ATT_ENTRY = 20, EV_ATT_ISSUED = 21, EV_ATT_QROPE = 22, EV_ATT_STORED = 23, EV_ATT_SYNCED = 24,
-       EV_ATT_SCORES = 25, EV_ATT_SOFTMAX = 26, EV_ATT_PARTIAL = 27, EV_ATT_ARRIVED = 28 };
+       EV_ATT_SCORES = 25, EV_ATT_SOFTMAX = 26, EV_ATT_PARTIAL = 27, EV_ATT_ARRIVED = 28,
+       /* tensor parallelism: a residual exchange's stores issued, every rank's words in */
+       EV_TP_SENT = 29, EV_TP_DONE = 30 };
 
 __device__ __forceinline__ void ev(int who, unsigned code) {
     unsigned long long *log = s_evp;
@@ -508,6 +510,7 @@ __device__ __noinline__ void tp_resid(const StepArgs &a, const float *res, int n
         for (int r = 0; r < W; r++)
             st_sys_u64((unsigned long long *)a.tp_box[r] + ((size_t)ph * W + me) * D + row0 + i, word);
     }
+    if (threadIdx.x == 0) ev(0, EV_TP_SENT);
     const unsigned long long *y = (const unsigned long long *)a.tp_box[me] + (size_t)ph * W * D;
     for (int i = threadIdx.x; i < nrows; i += NCT) {
         float tot = 0.0f;
@@ -526,6 +529,7 @@ __device__ __noinline__ void tp_resid(const StepArgs &a, const float *res, int n
         }
         own[i] = __fadd_rn(own[i], tot);
     }
+    if (threadIdx.x == 0) ev(0, EV_TP_DONE);
 }
 
 /* The rank's best logit key to every rank, then the maximum over ranks (one
