@@ -6,7 +6,7 @@
  * Q|K|V rows, the O rows, the gate|up row pairs, the down rows; then the
  * classifier rows — each row one record: quants, block scales, bias. The
  * producer warp of a CTA streams its own byte range into a ring of
- * shared-memory slots, one bulk copy per chunk of whole rows (<= 48 KB), the
+ * shared-memory slots, one bulk copy per chunk of whole rows (<= 56 KB), the
  * slots handed over with full/empty mbarriers, so HBM keeps streaming while
  * the consumers wait on their inputs.
  *
@@ -87,7 +87,7 @@ struct PhasePlan {
 };
 
 enum { PH_A = 0, PH_C = 1, PH_D = 2, PH_E = 3, PH_F = 4, NPHASE = 5 };
-constexpr int CHUNK_BYTES = 48 * 1024;   /* bytes per bulk copy (at least one record) */
+constexpr int CHUNK_BYTES = 56 * 1024;   /* bytes per bulk copy (at least one record): three ring slots */
 constexpr int GROUP_ROWS = 4;            /* rows per warp task (two gate|up pairs) */
 constexpr int OWN_MAX = 128;             /* rows of x a CTA may own */
 static_assert((NCW & (NCW - 1)) == 0, "warp round-robin uses a mask");
