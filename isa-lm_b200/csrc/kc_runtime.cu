@@ -836,16 +836,26 @@ static int setup_step_kernel(kc_state *s) {
         P.q_norm = L.q_norm; P.k_norm = L.k_norm;
         P.post_attn = L.post_attn_norm; P.post_ffn = L.post_ffn_norm;
     }
-    int slot = 0, res = 0;
+    int res = 0;
     for (int j = 0; j < G; j++) {
         PhasePlan P[NPHASE];
         make_plan(g, j, G, P);
-        slot = std::max(slot, plan_max_chunk(P));
         for (int p = 0; p < NPHASE; p++)
             res = std::max(res, plan_rows(P[p]) * (p == PH_D ? 8 : 4 * col_slices(P[p].cols / QK, false)));
     }
-    slot = (slot + 127) & ~127;
     res = (res + 15) & ~15;
+    /* the ring slot for bulk copies of up to `chunk` bytes: the largest chunk of any CTA's plan */
+    auto plan_slot = [&](int chunk) {
+        StreamGeom gc = g;
+        gc.chunk = chunk;
+        int sl = 0;
+        for (int j = 0; j < G; j++) {
+            PhasePlan P[NPHASE];
+            make_plan(gc, j, G, P);
+            sl = std::max(sl, plan_max_chunk(P));
+        }
+        return (sl + 127) & ~127;
+    };
     CK(cudaMalloc(&s->d_plan, sizeof(LayerPlan) * plan.size()));
     CK(cudaMemcpy(s->d_plan, plan.data(), sizeof(LayerPlan) * plan.size(), cudaMemcpyHostToDevice));
     const int group = c.n_heads / c.n_kv_heads;
@@ -867,7 +877,19 @@ static int setup_step_kernel(kc_state *s) {
     cudaFuncAttributes fa;
     CK(cudaFuncGetAttributes(&fa, (const void *)step_fn(s->kv_type, g.d16_q)));
     const int wbuf = 4 * c.dim;
-    const int nst = ring_stages(slot, act, (int)fa.sharedSizeBytes, res, wbuf);
+    /* the largest chunk (56 KB down to 32 KB) that leaves three ring slots beside
+     * the attention scratch, else the largest that leaves two */
+    int slot = 0, nst = 0;
+    for (int pass = 0; pass < 2 && nst == 0; pass++)
+        for (int kb = CHUNK_BYTES / 1024; kb >= 32; kb -= 4) {
+            const int sl = plan_slot(kb * 1024), n = ring_stages(sl, act, (int)fa.sharedSizeBytes, res, wbuf);
+            if (n >= (pass == 0 ? 3 : 2)) {
+                g.chunk = kb * 1024;
+                slot = sl;
+                nst = n;
+                break;
+            }
+        }
     if (nst < 2) {
         set_error("layer shapes leave no room for the weight ring in shared memory");
         return KC_E_SHAPE;

@@ -69,6 +69,7 @@ struct StreamGeom {
     int b_q, b_k, b_v;                                     /* rows carry a bias */
     int d_unit;   /* rows of the gate|up phase are shared in units of d_unit: 32 (whole blocks), or 4 when whole
                    * blocks would leave some CTAs with a block more (split blocks agree on their maximum) */
+    int chunk;    /* bytes per bulk copy (0: CHUNK_BYTES); the state picks the largest that leaves three ring slots */
 };
 
 /* A run of one matrix's rows in a CTA's stream. */
@@ -87,7 +88,7 @@ struct PhasePlan {
 };
 
 enum { PH_A = 0, PH_C = 1, PH_D = 2, PH_E = 3, PH_F = 4, NPHASE = 5 };
-constexpr int CHUNK_BYTES = 56 * 1024;   /* bytes per bulk copy (at least one record): three ring slots */
+constexpr int CHUNK_BYTES = 56 * 1024;   /* largest bulk copy (at least one record); a state may use smaller ones */
 constexpr int GROUP_ROWS = 4;            /* rows per warp task (two gate|up pairs) */
 constexpr int OWN_MAX = 128;             /* rows of x a CTA may own */
 static_assert((NCW & (NCW - 1)) == 0, "warp round-robin uses a mask");
@@ -105,7 +106,7 @@ __host__ __device__ inline void share_rows(int rows, int j, int G, int &r0, int 
     r1 = (int)((long long)rows * (j + 1) / G);
 }
 
-__host__ __device__ inline Seg make_seg(int rows, int row0, int type, int d16, int cols, int bias, int pair) {
+__host__ __device__ inline Seg make_seg(int rows, int row0, int type, int d16, int cols, int bias, int pair, int chunk) {
     Seg s;
     s.rows = rows;
     s.row0 = row0;
@@ -114,7 +115,7 @@ __host__ __device__ inline Seg make_seg(int rows, int row0, int type, int d16, i
     s.bias = bias;
     s.rec = rec_bytes(type, d16, cols, bias) * (pair ? 2 : 1);
     const int step = pair ? GROUP_ROWS / 2 : GROUP_ROWS;
-    int rpc = s.rec > 0 ? CHUNK_BYTES / s.rec : 1;
+    int rpc = s.rec > 0 ? chunk / s.rec : 1;
     if (rpc >= step) rpc -= rpc % step;
     s.rpc = rpc < 1 ? 1 : rpc;
     return s;
@@ -123,6 +124,7 @@ __host__ __device__ inline Seg make_seg(int rows, int row0, int type, int d16, i
 /* The phases of CTA j's stream for one layer (A, C, D, E) and the classifier (F). */
 __host__ __device__ inline void make_plan(const StreamGeom &g, int j, int G, PhasePlan *P) {
     int r0, r1;
+    const int ch = g.chunk > 0 ? g.chunk : CHUNK_BYTES;
     for (int p = 0; p < NPHASE; p++) {   /* unused segments read as empty */
         P[p].nseg = 0;
         P[p].cols = 0;
@@ -138,25 +140,25 @@ __host__ __device__ inline void make_plan(const StreamGeom &g, int j, int G, Pha
     const int ty[3] = { g.t_q, g.t_k, g.t_v }, dd[3] = { g.d16_q, g.d16_k, g.d16_v }, bb[3] = { g.b_q, g.b_k, g.b_v };
     for (int m = 0; m < 3; m++) {
         const int s0 = r0 > lo[m] ? r0 : lo[m], s1 = r1 < hi[m] ? r1 : hi[m];
-        if (s1 > s0) A.seg[A.nseg++] = make_seg(s1 - s0, s0, ty[m], dd[m], g.dim, bb[m], 0);
+        if (s1 > s0) A.seg[A.nseg++] = make_seg(s1 - s0, s0, ty[m], dd[m], g.dim, bb[m], 0, ch);
     }
     share_rows(g.dim, j, G, r0, r1);
     P[PH_C].nseg = 1;
     P[PH_C].cols = g.q_dim;
-    P[PH_C].seg[0] = make_seg(r1 - r0, r0, g.t_o, g.d16_o, g.q_dim, 0, 0);
+    P[PH_C].seg[0] = make_seg(r1 - r0, r0, g.t_o, g.d16_o, g.q_dim, 0, 0, ch);
     P[PH_E].nseg = 1;
     P[PH_E].cols = g.hidden;
-    P[PH_E].seg[0] = make_seg(r1 - r0, r0, g.t_down, g.d16_down, g.hidden, 0, 0);
+    P[PH_E].seg[0] = make_seg(r1 - r0, r0, g.t_down, g.d16_down, g.hidden, 0, 0, ch);
     share_rows(g.hidden / g.d_unit, j, G, r0, r1);   /* whole blocks, or 4-row units of split blocks */
     r0 *= g.d_unit;
     r1 *= g.d_unit;
     P[PH_D].nseg = 1;
     P[PH_D].cols = g.dim;
-    P[PH_D].seg[0] = make_seg(r1 - r0, r0, g.t_up, g.d16_up, g.dim, 0, 1);
+    P[PH_D].seg[0] = make_seg(r1 - r0, r0, g.t_up, g.d16_up, g.dim, 0, 1, ch);
     share_rows(g.vocab, j, G, r0, r1);
     P[PH_F].nseg = 1;
     P[PH_F].cols = g.dim;
-    P[PH_F].seg[0] = make_seg(r1 - r0, r0, g.t_cls, g.d16_cls, g.dim, 0, 0);
+    P[PH_F].seg[0] = make_seg(r1 - r0, r0, g.t_cls, g.d16_cls, g.dim, 0, 0, ch);
     for (int p = 0; p < NPHASE; p++) {
         long long b = 0;
         for (int s = 0; s < P[p].nseg; s++) b += (long long)P[p].seg[s].rows * P[p].seg[s].rec;
