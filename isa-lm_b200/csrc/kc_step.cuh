@@ -889,9 +889,10 @@ __device__ __forceinline__ int unit_owner(int u, int U, int G) { return (int)(((
  * the other covering CTAs' and quantizes its own rows with the block's maximum
  * (the max of the partials is exact, so the quants and scale are those of the
  * whole block); the block's first CTA writes the scale. Whole blocks as
- * finish_pair_q. */
-__device__ __forceinline__ void finish_pair_split(const float *res, int nrows, int row0, word_t *hw, int n, unsigned tag,
-                                                  int act, word_t *amaxw, int U, unsigned *err) {
+ * finish_pair_q. Out of line: inlined, its code slowed the models that never
+ * take it (cfg1 2.5%). */
+__device__ __noinline__ void finish_pair_split(const float *res, int nrows, int row0, word_t *hw, int n, unsigned tag,
+                                               int act, word_t *amaxw, int U, unsigned *err) {
     if (nrows <= 0) return;
     constexpr int UPB = QK / 4;   /* units per block */
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, G = gridDim.x, j = blockIdx.x;
@@ -1845,6 +1846,32 @@ __device__ __forceinline__ void attention_item_t(const StepArgs &a, const LayerP
  * into shared memory; then a thread per output sums the splits' partials in
  * split order with those weights; then a warp per block quantizes and
  * publishes the unit's blocks of the attention output (t_ao). */
+/* One output of the combine: the sum over the active splits of partial x
+ * weight, in split order, the splits' words requested CB at a time (one
+ * round trip per batch). */
+template <int CB>
+__device__ __forceinline__ float combine_sum(const word_t *ps, int stride, const float *wh, int active, unsigned t_part,
+                                             bool &ok) {
+    float num = 0.0f;
+#pragma unroll 1
+    for (int s0 = 0; s0 < active; s0 += CB) {
+        float pv[CB];
+#pragma unroll
+        for (int k = 0; k < CB; k++) {
+            pv[k] = 0.0f;
+            if (s0 + k < active) {
+                const word_t wv = ld_word(ps + (size_t)(s0 + k) * stride);
+                ok = ok && wok(wv, t_part);
+                pv[k] = wval(wv);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < CB; k++)
+            if (s0 + k < active) num = fmaf(pv[k], wh[s0 + k], num);
+    }
+    return num;
+}
+
 __device__ __forceinline__ void attention_combine(const StepArgs &a, int U, int active, float *fsm, unsigned t_part,
                                                   unsigned t_ao) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, hd = a.hd, stride = hd + 2;
@@ -1871,25 +1898,10 @@ __device__ __forceinline__ void attention_combine(const StepArgs &a, int U, int 
         const int h = o / hd, i = o - h * hd;
         const word_t *ps = a.partw + (size_t)(h0 + h) * a.nsplit * stride + i;
         const float *wh = sw + h * MAX_NSPLIT;
-        constexpr int CB = MAX_NSPLIT;   /* splits requested together: one round trip */
-        float num = 0.0f;
         bool ok = true;
-#pragma unroll 1
-        for (int s0 = 0; s0 < active; s0 += CB) {
-            float pv[CB];
-#pragma unroll
-            for (int k = 0; k < CB; k++) {
-                pv[k] = 0.0f;
-                if (s0 + k < active) {
-                    const word_t wv = ld_word(ps + (size_t)(s0 + k) * stride);
-                    ok = ok && wok(wv, t_part);
-                    pv[k] = wval(wv);
-                }
-            }
-#pragma unroll
-            for (int k = 0; k < CB; k++)
-                if (s0 + k < active) num = fmaf(pv[k], wh[s0 + k], num);
-        }
+        /* short contexts (a few splits) take the short batch: fewer predicated slots */
+        const float num = active <= 8 ? combine_sum<8>(ps, stride, wh, active, t_part, ok)
+                                      : combine_sum<MAX_NSPLIT>(ps, stride, wh, active, t_part, ok);
         if (!ok) atomicOr(a.err, ERR_POLL);
         out[o] = num;
     }
