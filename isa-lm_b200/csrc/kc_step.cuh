@@ -1189,8 +1189,9 @@ __device__ __forceinline__ void act_float(float eps, const word_t *xw, unsigned 
 }
 
 /* Layer 0's activation: the embedding row of tok, its 1/rms from the host
- * table (inv), times the norm weights. */
-__device__ __forceinline__ void act_embed(PMat emb, float embed_scale, int tok, const float *norm_w, float inv, int cols,
+ * table (inv), times the norm weights. Out of line: it runs once a step, and
+ * inlined its code slowed every layer (cfg1 2.3%). */
+__device__ __noinline__ void act_embed(PMat emb, float embed_scale, int tok, const float *norm_w, float inv, int cols,
                                        ActW o) {
     const int nb = cols / QK, tid = threadIdx.x, j0 = (tid & 7) * 4;
 #pragma unroll 1
